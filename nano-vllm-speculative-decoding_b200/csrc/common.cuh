@@ -1,0 +1,139 @@
+// Shared device/host helpers of the B200 verify/accept library.
+//
+// Everything here is written for sm_100a (B200).  The library is a C-ABI shared object: every entry point
+// returns an int status (0 = ok) and records a message for specdec_last_error() on failure.  No entry point
+// allocates device memory; callers pass a workspace.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdarg.h>
+
+namespace specdec {
+
+// ------------------------------------------------------------------------------------------- status codes
+enum Status : int {
+  kOk = 0,
+  kInvalidArgument = 1,   // a shape, dtype, pointer or size the host rejected before any launch
+  kWorkspaceTooSmall = 2, // the caller's workspace is smaller than the matching *_workspace_bytes query
+  kUnsupported = 3,       // a valid request this build does not implement (e.g. top_k above the cap)
+  kCudaError = 4,         // a CUDA runtime/driver call failed; the message carries cudaGetErrorString
+  kDeviceTimeout = 5,     // a bounded device-side wait gave up (error flag set by a kernel)
+};
+
+// Records a printf-style message for specdec_last_error() (thread-local) and returns `code`.
+int set_error(int code, const char* fmt, ...);
+
+#define SPECDEC_CHECK_ARG(cond, ...)                                         \
+  do {                                                                      \
+    if (!(cond)) return ::specdec::set_error(::specdec::kInvalidArgument, __VA_ARGS__); \
+  } while (0)
+
+#define SPECDEC_CUDA_TRY(call)                                                         \
+  do {                                                                                 \
+    cudaError_t err__ = (call);                                                        \
+    if (err__ != cudaSuccess)                                                          \
+      return ::specdec::set_error(::specdec::kCudaError, "%s failed: %s (%s:%d)", #call, \
+                                  cudaGetErrorString(err__), __FILE__, __LINE__);      \
+  } while (0)
+
+// Launch-error check right after a <<<>>> launch.
+#define SPECDEC_LAUNCH_CHECK() SPECDEC_CUDA_TRY(cudaGetLastError())
+
+// ------------------------------------------------------------------------------------------- dtypes
+// Element type codes shared with the Python wrapper (nanovllm_b200/_lib.py).
+enum DType : int { kF32 = 0, kBF16 = 1, kF16 = 2 };
+
+inline size_t dtype_bytes(int dtype) { return dtype == kF32 ? 4 : 2; }
+inline bool dtype_ok(int dtype) { return dtype == kF32 || dtype == kBF16 || dtype == kF16; }
+
+template <int DT> struct Elem;
+template <> struct Elem<kF32> { using T = float; };
+template <> struct Elem<kBF16> { using T = __nv_bfloat16; };
+template <> struct Elem<kF16> { using T = __half; };
+
+__device__ __forceinline__ float to_f32(float x) { return x; }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ float to_f32(__half x) { return __half2float(x); }
+
+// Loads one element bypassing nothing special; used for scattered single reads (draft tokens).
+template <typename T>
+__device__ __forceinline__ float load_f32(const T* p) { return to_f32(*p); }
+
+// 16-byte streaming load (read-once data: evict-first in L1/L2 is not wanted for rows re-read by the tail
+// pass, so this is a plain non-coherent global load).
+__device__ __forceinline__ uint4 ldg16(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+
+// Unpacks a 16-byte vector of T into floats; returns the number of lanes (4 for f32, 8 for 16-bit types).
+__device__ __forceinline__ void unpack16(const uint4& v, float (&out)[4]) {
+  out[0] = __uint_as_float(v.x); out[1] = __uint_as_float(v.y);
+  out[2] = __uint_as_float(v.z); out[3] = __uint_as_float(v.w);
+}
+__device__ __forceinline__ void unpack16_bf16(const uint4& v, float (&out)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    out[2 * i] = __uint_as_float(w[i] << 16);
+    out[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+__device__ __forceinline__ void unpack16_f16(const uint4& v, float (&out)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+    float2 f = __half22float2(h);
+    out[2 * i] = f.x;
+    out[2 * i + 1] = f.y;
+  }
+}
+
+// ------------------------------------------------------------------------------------------- ordering keys
+// Maps a float to a uint32 whose unsigned order is the float order (-inf < ... < +inf; +NaN above +inf).
+__device__ __forceinline__ uint32_t ordered_key(float f) {
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key_to_float(uint32_t k) {
+  uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+  return __uint_as_float(u);
+}
+// argmax key: larger value wins; on equal values the smaller index wins (torch's first-index rule).
+__device__ __forceinline__ unsigned long long argmax_key(float value, uint32_t index) {
+  return (static_cast<unsigned long long>(ordered_key(value)) << 32) | (0xffffffffu - index);
+}
+__device__ __forceinline__ uint32_t argmax_key_index(unsigned long long key) {
+  return 0xffffffffu - static_cast<uint32_t>(key & 0xffffffffull);
+}
+
+__device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    unsigned long long other = __shfl_xor_sync(0xffffffffu, v, o);
+    v = other > v ? other : v;
+  }
+  return v;
+}
+__device__ __forceinline__ float warp_max_f32(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum_f32(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Device properties the library needs (cached per device on first use).
+struct DeviceInfo {
+  int sm_count;
+  int max_threads_per_sm;
+  int cc_major, cc_minor;
+};
+int device_info(DeviceInfo* out);
+
+}  // namespace specdec

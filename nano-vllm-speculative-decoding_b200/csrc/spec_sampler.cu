@@ -1,0 +1,1072 @@
+// Kernel (1): the batched speculative sampler ("SpecSampler") for sm_100a.
+//
+// Reference behaviour restated here (nano-vllm-speculative-decoding, nanovllm/layers/spec_sampler.py):
+//   probs_from_logits / truncate_logits   :65-96   softmax(mask(logits.float() / T)), HF top-k (ties kept) then
+//                                                  top-p over the softmax of the top-k candidates
+//   exponential_noise_ / race / sample    :99-111  argmax(w / clamp_min(Exp(1), 1e-10)), first index on ties
+//   accept_random[_varlen]                :114-150 u * q_d < p_d & verified; prefix length; residual (p - q)+ at
+//                                                  the first rejection or the bonus row; tail by the race
+//   accept_greedy[_varlen]                :153-169 argmax match prefix; tail = argmax at start + n_accept
+//   _verified_positions                   :172-180 starts = exclusive cumsum(lens); positions clamped to the
+//                                                  bonus position; verified = j < len - 1
+//
+// Design (B200): the path is HBM-bound integer/float streaming, so it never touches the tensor cores.
+//   pass 1  (stats)  grid (chunks x rows): every verified row of logits is read once with 16-byte loads and
+//                    reduced to a softmax (max, sum) partial per chunk.  Rows that truncate (top_k > 0) are
+//                    handled by one 512-thread CTA per row that radix-selects the k-th value over L2-resident
+//                    re-reads.  The last CTA to finish a request (an atomic ticket per request) merges the
+//                    partials, computes p and q at the k drafts, draws or reads the uniforms, and decides the
+//                    accepted prefix - so acceptance costs no extra launch.
+//   pass 2  (tail)   grid = torch's own grid for exponential_ over [B, V]: thread i regenerates exactly the
+//                    Exp(1) numbers torch's CUDA generator would have written (Philox4x32-10 subsequence i,
+//                    curand_uniform4, torch's log transform, clamp at 1e-10), so the [B, V] noise is never
+//                    materialised in HBM.  Each element computes w = p (bonus) or (p - q)+, the ratio w / E in
+//                    IEEE fp32, and an argmax key; warps reduce per request into shared memory, CTAs into one
+//                    64-bit atomicMax per request, and the last CTA writes the tail tokens.
+// Explicit u / E pointers replace the in-kernel draws (parity mode) without changing anything else.
+#include "common.cuh"
+
+#include <curand_kernel.h>
+#include <math.h>
+
+namespace specdec {
+namespace sampler {
+
+constexpr int kThreads = 256;        // stats / tail / greedy CTAs
+constexpr int kTopkThreads = 512;    // one CTA per truncating row
+constexpr int kMaxRequests = 1024;   // B cap (shared-memory tables are sized by it)
+constexpr int kMaxRows = 16384;      // T cap (fixed-offset greedy key table)
+constexpr int kMaxChunks = 64;       // chunks per row in pass 1
+constexpr int kMaxTopK = 1024;       // top_k cap of the in-kernel radix select
+constexpr int kRngBlock = 256;       // torch's block_size_bound for distribution kernels
+
+// Device-side input checks (the host cannot see verified_lens or drafts without a sync).  A failing check makes
+// every kernel of the call return before touching memory it cannot bound, and leaves the code in the status word.
+constexpr int kStatusBadLens = 1;     // a length outside 1..k+1, or lengths not summing to T
+constexpr int kStatusBadDraft = 2;    // a draft id outside [0, V)
+constexpr int kStatusBadTopK = 3;     // a row's top_k above the in-kernel cap
+
+struct RowStat {   // per verified row: softmax max / sum over the kept entries, truncation threshold
+  float m, s, thr, pad;
+};
+struct ReqDesc {   // per request: where its tail distribution lives
+  long long x_row;   // flat row of x holding p_next
+  long long q_row;   // flat row of q for the residual, or -1 for the bonus row / plain race
+  float m, s, thr, temp;
+};
+
+// ---------------------------------------------------------------------------------------- workspace layout
+// Self-cleaning tables (tickets, argmax keys) sit at fixed offsets at the front, so a workspace zeroed once at
+// allocation stays valid across calls of any shape; per-call scratch follows.
+struct Layout {
+  size_t status, req_ticket, tail_key, tail_ticket, row_key, rows, partial, desc, total;
+};
+static Layout layout(int64_t T) {
+  Layout L{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off += (bytes + 255) & ~size_t(255);
+    return o;
+  };
+  L.status = take(256);
+  L.req_ticket = take(sizeof(unsigned) * kMaxRequests);
+  L.tail_key = take(sizeof(unsigned long long) * kMaxRequests);
+  L.tail_ticket = take(256);
+  L.row_key = take(sizeof(unsigned long long) * kMaxRows);
+  L.rows = take(sizeof(RowStat) * (size_t)(T > 0 ? T : 1));
+  L.partial = take(sizeof(float2) * (size_t)(T > 0 ? T : 1) * kMaxChunks);
+  L.desc = take(sizeof(ReqDesc) * kMaxRequests);
+  L.total = off;
+  return L;
+}
+
+struct Args {
+  // inputs
+  const void* x;            // [T, V] logits (dtype) or fp32 probabilities (probs_mode)
+  long long T, V;
+  int dtype, probs_mode;
+  const float* q;           // [B, k, V] fp32 draft probabilities (may be null for greedy / race)
+  const long long* drafts;  // [B, k]
+  int B, k;
+  const long long* lens;    // [B] verified lengths, or null = k + 1 each
+  int rows_per_param;       // probs-only calls: parameter row of x row t is t / rows_per_param
+  const float* temperature; // [B] (or [params]); null only in probs_mode / greedy
+  const long long* top_k;   // [B] or null
+  const float* top_p;       // [B] or null
+  int has_top_p, truncate;  // host flags: some row has top_p < 1; max_top_k > 0
+  const float* u;           // [B, k] uniforms or null (then drawn in-kernel)
+  const float* E;           // [B, V] exponential noise or null (then drawn in-kernel)
+  unsigned long long seed, offset_u, offset_E;
+  // outputs
+  long long* n_accept;      // [B]
+  long long* tail;          // [B]
+  float* probs_out;         // [T, V] for specdec_probs
+  // layout
+  int C, chunk, vec_ok;
+  int u_grid;               // torch grid (blocks of 256) of the [B, k] uniform draw
+  int e_grid, e_rounds;     // torch grid and grid-stride rounds of the [B, V] exponential draw
+  long long e_numel;
+  unsigned e_sq, e_sr;      // S / V and S % V for S = 256 * e_grid (incremental row tracking)
+  // workspace
+  int* status;              // device-side input check: 0 ok, else a kStatus* code (first writer wins)
+  unsigned* req_ticket;
+  unsigned long long* tail_key;
+  unsigned* tail_ticket;
+  unsigned long long* row_key;
+  RowStat* rows;
+  float2* partial;
+  ReqDesc* desc;
+};
+
+// ---------------------------------------------------------------------------------------- small helpers
+__device__ __forceinline__ float scale_logit(float x, float temp) {
+  // logits.float() / T, IEEE division (temperature 1 is the identity, as in fp32 division).
+  return __fdiv_rn(x, temp);
+}
+
+// torch.rand's transform of a curand_uniform4 lane: (0, 1] with 1 mapped to 0.
+__device__ __forceinline__ float torch_uniform(float r) { return r == 1.0f ? 0.0f : r; }
+
+// torch's CUDA exponential_(lambda = 1) transform of a curand_uniform4 lane, then clamp_min(1e-10).
+__device__ __forceinline__ float torch_exponential_clamped(float r) {
+  const float eps_half = 5.9604644775390625e-08f;  // numeric_limits<float>::epsilon() / 2
+  float lg = (r >= 1.0f - eps_half) ? -eps_half : logf(r);
+  float e = -1.0f * lg;
+  const float floor_v = 1e-10f;
+  return e < floor_v ? floor_v : e;
+}
+
+// Uniform number li of a torch.rand draw of `numel` floats whose grid has `grid` blocks of 256 threads.
+__device__ float torch_rand_at(unsigned long long seed, unsigned long long offset, long long li, int grid) {
+  const long long S = (long long)kRngBlock * grid;
+  const long long idx = li % S;
+  const long long m = li / S;       // grid-stride step: round m / 4, lane m % 4 of curand_uniform4
+  curandStatePhilox4_32_10_t st;
+  curand_init(seed, (unsigned long long)idx, offset + 4ull * (unsigned long long)(m / 4), &st);
+  float4 r = curand_uniform4(&st);
+  const int lane = (int)(m & 3);
+  float v = lane == 0 ? r.x : lane == 1 ? r.y : lane == 2 ? r.z : r.w;
+  return torch_uniform(v);
+}
+
+// Exclusive prefix sums of the verified lengths into s_start[0..B] (s_start[B] = T).  Returns false (in every
+// thread) when a length is outside 1..k1 or the lengths do not sum to T.
+template <int NT>
+__device__ bool starts_from_lens(const long long* lens, int B, int k1, long long T, int* s_start) {
+  constexpr int PER = (kMaxRequests + NT - 1) / NT;
+  __shared__ int warp_tot[NT / 32];
+  __shared__ int s_bad;
+  if (threadIdx.x == 0) s_bad = 0;
+  __syncthreads();
+  int vals[PER];
+  int local = 0;
+  const int base = threadIdx.x * PER;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    int idx = base + i;
+    int v = 0;
+    if (idx < B) {
+      long long raw = lens ? lens[idx] : k1;
+      if (raw < 1 || raw > k1) { s_bad = 1; raw = 1; }
+      v = (int)raw;
+    }
+    vals[i] = v;
+    local += v;
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += n;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < NT / 32 ? warp_tot[lane] : 0;
+    int wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int n = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += n;
+    }
+    if (lane < NT / 32) warp_tot[lane] = wi - w;
+  }
+  __syncthreads();
+  int run = warp_tot[warp] + incl - local;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    int idx = base + i;
+    if (idx < B) {
+      s_start[idx] = run;
+      run += vals[i];
+      if (idx == B - 1) s_start[B] = run;
+    }
+  }
+  __syncthreads();
+  return s_bad == 0 && s_start[B] == T;
+}
+
+__device__ __forceinline__ void report(const Args& a, int code) { atomicCAS(a.status, 0, code); }
+
+// Request holding flat row t: s_start[b] <= t < s_start[b + 1].
+__device__ __forceinline__ int request_of_row(const int* s_start, int B, int t) {
+  int lo = 0, hi = B - 1;
+  while (lo < hi) {
+    int mid = (lo + hi + 1) >> 1;
+    if (s_start[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ void ms_combine(float& m, float& s, float m2, float s2) {
+  if (m2 == -INFINITY) return;
+  if (m == -INFINITY) { m = m2; s = s2; return; }
+  if (m2 > m) { s = s * expf(m - m2) + s2; m = m2; }
+  else { s = s + s2 * expf(m2 - m); }
+}
+
+// Block-wide (max, sum) combine; result valid in every thread.
+template <int NT>
+__device__ void block_ms(float& m, float& s) {
+  __shared__ float sm_m[NT / 32], sm_s[NT / 32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    ms_combine(m, s, m2, s2);
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __syncthreads();
+  if (lane == 0) { sm_m[warp] = m; sm_s[warp] = s; }
+  __syncthreads();
+  m = sm_m[0];
+  s = sm_s[0];
+  for (int w = 1; w < NT / 32; ++w) ms_combine(m, s, sm_m[w], sm_s[w]);
+  __syncthreads();
+}
+
+// Online (max, sum of exp) over elements [lo, hi) of one row of scaled logits.
+template <typename T, int NT>
+__device__ void row_range_ms(const T* row, int lo, int hi, float temp, int vec_ok, float& m, float& s) {
+  m = -INFINITY;
+  s = 0.0f;
+  constexpr int VE = 16 / sizeof(T);  // elements per 16-byte vector
+  const bool unit_temp = temp == 1.0f;
+  if (vec_ok) {
+    // lo is a multiple of VE and the row base is 16-byte aligned.
+    const int nvec = (hi - lo) / VE;
+    const char* base = reinterpret_cast<const char*>(row + lo);
+    for (int i = threadIdx.x; i < nvec; i += NT * 4) {
+      uint4 raw[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        int j = i + u * NT;
+        if (j < nvec) raw[u] = ldg16(base + (size_t)j * 16);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        int j = i + u * NT;
+        if (j >= nvec) break;
+        float f[VE];
+        if constexpr (sizeof(T) == 4) {
+          float t4[4];
+          unpack16(raw[u], t4);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) f[e] = t4[e];
+        } else if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+          float t8[8];
+          unpack16_bf16(raw[u], t8);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) f[e] = t8[e];
+        } else {
+          float t8[8];
+          unpack16_f16(raw[u], t8);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) f[e] = t8[e];
+        }
+        float vm = -INFINITY;
+#pragma unroll
+        for (int e = 0; e < VE; ++e) {
+          if (!unit_temp) f[e] = scale_logit(f[e], temp);
+          vm = fmaxf(vm, f[e]);
+        }
+        if (vm > m) {
+          if (m != -INFINITY) s *= expf(m - vm);
+          m = vm;
+        }
+        if (m != -INFINITY) {
+#pragma unroll
+          for (int e = 0; e < VE; ++e) s += expf(f[e] - m);
+        }
+      }
+    }
+    // scalar tail of the range (fewer than VE elements)
+    for (int v = lo + nvec * VE + threadIdx.x; v < hi; v += NT) {
+      float f = to_f32(row[v]);
+      if (!unit_temp) f = scale_logit(f, temp);
+      if (f > m) {
+        if (m != -INFINITY) s *= expf(m - f);
+        m = f;
+      }
+      if (m != -INFINITY) s += expf(f - m);
+    }
+  } else {
+    for (int v = lo + threadIdx.x; v < hi; v += NT) {
+      float f = to_f32(row[v]);
+      if (!unit_temp) f = scale_logit(f, temp);
+      if (f > m) {
+        if (m != -INFINITY) s *= expf(m - f);
+        m = f;
+      }
+      if (m != -INFINITY) s += expf(f - m);
+    }
+  }
+}
+
+// p of one scaled logit f under row stats (masked entries give 0), exp(f - m) / s as ATen's softmax.
+__device__ __forceinline__ float prob_of_scaled(float f, const RowStat& r) {
+  return f >= r.thr ? __fdiv_rn(expf(f - r.m), r.s) : 0.0f;
+}
+
+template <typename T>
+__device__ __forceinline__ float prob_at(const Args& a, long long row, long long col, const RowStat& rs, float temp) {
+  float xv = to_f32(reinterpret_cast<const T*>(a.x)[row * a.V + col]);
+  if (a.probs_mode) return xv;
+  float f = temp == 1.0f ? xv : scale_logit(xv, temp);
+  return prob_of_scaled(f, rs);
+}
+
+// Merges the chunk partials of row t (one warp); the result is valid in every lane.
+__device__ RowStat merge_row_warp(const Args& a, int t) {
+  const int lane = threadIdx.x & 31;
+  float m = -INFINITY, s = 0.0f;
+  for (int c = lane; c < a.C; c += 32) {
+    float2 p = __ldcg(&a.partial[(size_t)t * kMaxChunks + c]);
+    ms_combine(m, s, p.x, p.y);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    ms_combine(m, s, m2, s2);
+  }
+  RowStat r;
+  r.m = m; r.s = s; r.thr = -INFINITY; r.pad = 0.0f;
+  return r;
+}
+
+// Acceptance of request b once every one of its rows has final stats (run by a whole CTA).  need_merge: the
+// rows' stats are still chunk partials, merged here into a.rows.  k <= 32 (one lane per draft).
+template <typename T>
+__device__ void decide_request(const Args& a, int b, int start, int len, bool need_merge) {
+  __shared__ RowStat s_rows[33];
+  const int warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  if (!a.probs_mode) {
+    for (int r = warp; r < len; r += nwarps) {
+      RowStat rs;
+      if (need_merge) {
+        rs = merge_row_warp(a, start + r);
+        if (lane == 0) a.rows[start + r] = rs;
+      } else {
+        float4 raw = __ldcg(reinterpret_cast<const float4*>(&a.rows[start + r]));
+        rs.m = raw.x; rs.s = raw.y; rs.thr = raw.z; rs.pad = raw.w;
+      }
+      if (lane == 0) s_rows[r] = rs;
+    }
+  }
+  __syncthreads();
+  if (warp != 0) return;
+  const float temp = a.probs_mode ? 1.0f : a.temperature[b];
+  const RowStat identity{0.f, 1.f, -INFINITY, 0.f};
+  bool accepted = false;
+  const int j = lane;
+  if (j < a.k) {
+    const bool verified = j < len - 1;
+    const int r = verified ? j : len - 1;
+    const long long d = a.drafts[(long long)b * a.k + j];
+    const long long li = (long long)b * a.k + j;
+    const float u = a.u ? a.u[li] : torch_rand_at(a.seed, a.offset_u, li, a.u_grid);
+    if (d < 0 || d >= a.V) {
+      report(a, kStatusBadDraft);
+    } else {
+      const RowStat rs = a.probs_mode ? identity : s_rows[r];
+      const float p_d = prob_at<T>(a, start + r, d, rs, temp);
+      const float q_d = a.q[((long long)b * a.k + j) * a.V + d];
+      accepted = (u * q_d < p_d) && verified;   // u < min(1, p/q) without dividing
+    }
+  }
+  const unsigned acc_mask = __ballot_sync(0xffffffffu, accepted);
+  // length of the accepted prefix: the trailing ones (lanes >= k never accept)
+  const int n_acc = (~acc_mask) ? __ffs(~acc_mask) - 1 : 32;
+  if (lane == 0) {
+    a.n_accept[b] = n_acc;
+    ReqDesc d;
+    d.x_row = start + n_acc;
+    d.q_row = (n_acc == len - 1) ? -1 : ((long long)b * a.k + (n_acc < a.k - 1 ? n_acc : a.k - 1));
+    const RowStat rs = a.probs_mode ? identity : s_rows[n_acc];
+    d.m = rs.m; d.s = rs.s; d.thr = rs.thr; d.temp = temp;
+    a.desc[b] = d;
+  }
+}
+
+// ---------------------------------------------------------------------------------------- pass 1: stats
+// grid (C, T).  mode 0: acceptance (decide when the request's last chunk lands); mode 1: probabilities only.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) stats_kernel(Args a, int mode) {
+  __shared__ int s_start[kMaxRequests + 1];
+  __shared__ int s_last;
+  const int c = blockIdx.x, t = blockIdx.y;
+  int b, start, len;
+  float temp;
+  if (mode == 0) {
+    if (!starts_from_lens<kThreads>(a.lens, a.B, a.k + 1, a.T, s_start)) {
+      if (threadIdx.x == 0) report(a, kStatusBadLens);
+      return;
+    }
+    b = request_of_row(s_start, a.B, t);
+    start = s_start[b];
+    len = s_start[b + 1] - start;
+    temp = a.temperature[b];
+  } else {
+    b = t / a.rows_per_param;
+    start = 0; len = 0;
+    temp = a.temperature[b];
+  }
+  const int lo = c * a.chunk;
+  const int hi = min((long long)lo + a.chunk, a.V);
+  const T* row = reinterpret_cast<const T*>(a.x) + (long long)t * a.V;
+  float m, s;
+  row_range_ms<T, kThreads>(row, lo, hi, temp, a.vec_ok, m, s);
+  block_ms<kThreads>(m, s);
+  if (threadIdx.x == 0) a.partial[(size_t)t * kMaxChunks + c] = make_float2(m, s);
+  if (mode != 0) return;
+  // last CTA of request b decides its acceptance
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned ticket = atomicAdd(&a.req_ticket[b], 1u);
+    s_last = ticket == (unsigned)(len * a.C - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  decide_request<T>(a, b, start, len, true);
+  if (threadIdx.x == 0) atomicExch(&a.req_ticket[b], 0u);
+}
+
+// ---------------------------------------------------------------------------------------- pass 1 (truncating)
+// One CTA per row: radix select of the k-th largest scaled logit over L2-resident re-reads, sorted top-k,
+// top-p over the top-k softmax, then (max, sum) over the kept entries.
+template <int NT>
+__device__ void select_digit(const unsigned* hist, int nbins, int rank, int* s_digit, int* s_above) {
+  // rank: 1-based rank (from the top) of the wanted element among the elements counted in hist.
+  __shared__ int warp_tot[NT / 32];
+  const int per = nbins / NT;
+  // thread i owns bins [i*per, (i+1)*per); suffix sums from the top
+  int local = 0;
+  for (int j = 0; j < per; ++j) local += hist[threadIdx.x * per + j];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // inclusive scan from the top: reverse the thread order
+  int incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int n = __shfl_down_sync(0xffffffffu, incl, o);
+    if (lane + o < 32) incl += n;
+  }
+  if (lane == 0) warp_tot[warp] = incl;
+  __syncthreads();
+  int above_warps = 0;
+  for (int w = warp + 1; w < NT / 32; ++w) above_warps += warp_tot[w];
+  int above = above_warps + incl - local;  // elements in bins above this thread's bins
+  for (int j = per - 1; j >= 0; --j) {
+    int h = hist[threadIdx.x * per + j];
+    if (above < rank && rank <= above + h) {
+      *s_digit = threadIdx.x * per + j;
+      *s_above = above;
+    }
+    above += h;
+  }
+  __syncthreads();
+}
+
+template <typename T>
+__device__ __forceinline__ float scaled_at(const T* row, int v, float temp) {
+  float f = to_f32(row[v]);
+  return temp == 1.0f ? f : scale_logit(f, temp);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kTopkThreads) topk_stats_kernel(Args a, int mode) {
+  constexpr int NT = kTopkThreads;
+  __shared__ int s_start[kMaxRequests + 1];
+  __shared__ unsigned hist[2048];
+  __shared__ float cand[kMaxTopK];
+  __shared__ int s_digit, s_above, s_cnt, s_last;
+  __shared__ float s_thr;
+  const int t = blockIdx.x;
+  int b, start = 0, len = 0;
+  if (mode == 0) {
+    if (!starts_from_lens<NT>(a.lens, a.B, a.k + 1, a.T, s_start)) {
+      if (threadIdx.x == 0) report(a, kStatusBadLens);
+      return;
+    }
+    b = request_of_row(s_start, a.B, t);
+    start = s_start[b];
+    len = s_start[b + 1] - start;
+  } else {
+    b = t / a.rows_per_param;
+  }
+  const float temp = a.temperature[b];
+  const long long tk = a.top_k ? a.top_k[b] : 0;
+  const int V = (int)a.V;
+  const T* row = reinterpret_cast<const T*>(a.x) + (long long)t * a.V;
+  float m, s, thr = -INFINITY;
+  if (tk <= 0) {
+    row_range_ms<T, NT>(row, 0, V, temp, a.vec_ok, m, s);
+    block_ms<NT>(m, s);
+  } else {
+    if (tk > kMaxTopK && V > kMaxTopK) {
+      if (threadIdx.x == 0) report(a, kStatusBadTopK);
+      return;
+    }
+    const int K = (int)(tk < V ? tk : V);
+    // ---- radix select of the K-th largest key over three digits (11, 11, 10 bits)
+    unsigned prefix = 0, pmask = 0;
+    int rank = K;
+    const int shifts[3] = {21, 10, 0};
+    const int widths[3] = {11, 11, 10};
+    for (int p = 0; p < 3; ++p) {
+      const int nb = 1 << widths[p];
+      for (int i = threadIdx.x; i < 2048; i += NT) hist[i] = 0;
+      __syncthreads();
+      for (int v = threadIdx.x; v < V; v += NT) {
+        unsigned key = ordered_key(scaled_at(row, v, temp));
+        if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shifts[p]) & (nb - 1)], 1u);
+      }
+      __syncthreads();
+      select_digit<NT>(hist, nb, rank, &s_digit, &s_above);
+      prefix |= (unsigned)s_digit << shifts[p];
+      pmask |= (unsigned)(nb - 1) << shifts[p];
+      rank -= s_above;
+      __syncthreads();
+    }
+    const unsigned key_k = prefix;        // key of the K-th largest value
+    const int n_gt = K - rank;            // elements strictly above it (< K)
+    // ---- collect the values above the K-th, fill the rest with it, sort descending
+    if (threadIdx.x == 0) s_cnt = 0;
+    __syncthreads();
+    for (int v = threadIdx.x; v < V; v += NT) {
+      float f = scaled_at(row, v, temp);
+      if (ordered_key(f) > key_k) {
+        int slot = atomicAdd(&s_cnt, 1);
+        if (slot < kMaxTopK) cand[slot] = f;
+      }
+    }
+    __syncthreads();
+    int P = 1;
+    while (P < K) P <<= 1;
+    const float kth = key_to_float(key_k);
+    for (int i = threadIdx.x; i < P; i += NT) {
+      if (i >= n_gt) cand[i] = i < K ? kth : -INFINITY;
+    }
+    __syncthreads();
+    // bitonic sort, descending
+    for (int size = 2; size <= P; size <<= 1) {
+      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+        for (int i = threadIdx.x; i < P; i += NT) {
+          int j = i ^ stride;
+          if (j > i) {
+            bool desc = (i & size) == 0;
+            float ci = cand[i], cj = cand[j];
+            if (desc ? (ci < cj) : (ci > cj)) { cand[i] = cj; cand[j] = ci; }
+          }
+        }
+        __syncthreads();
+      }
+    }
+    // ---- thresholds (one thread; K is small)
+    if (threadIdx.x == 0) {
+      float th = cand[K - 1];
+      if (a.has_top_p) {
+        const float tp = a.top_p[b];
+        const float c0 = cand[0];
+        float z = 0.0f;
+        for (int i = 0; i < K; ++i) z += expf(cand[i] - c0);
+        float cum = 0.0f;
+        int kept = 0;
+        for (int i = 0; i < K; ++i) {
+          float nu = __fdiv_rn(expf(cand[i] - c0), z);
+          cum += nu;
+          if (cum - nu < tp) ++kept;
+        }
+        if (kept >= 1 && kept <= K) th = fmaxf(th, cand[kept - 1]);
+      }
+      s_thr = th;
+    }
+    __syncthreads();
+    thr = s_thr;
+    m = cand[0];
+    // ---- sum over the kept entries
+    float ls = 0.0f;
+    for (int v = threadIdx.x; v < V; v += NT) {
+      float f = scaled_at(row, v, temp);
+      if (f >= thr) ls += expf(f - m);
+    }
+    ls = warp_sum_f32(ls);
+    __shared__ float sm_sum[NT / 32];
+    if ((threadIdx.x & 31) == 0) sm_sum[threadIdx.x >> 5] = ls;
+    __syncthreads();
+    s = 0.0f;
+    for (int w = 0; w < NT / 32; ++w) s += sm_sum[w];
+  }
+  if (threadIdx.x == 0) {
+    RowStat r;
+    r.m = m; r.s = s; r.thr = thr; r.pad = 0.0f;
+    a.rows[t] = r;
+  }
+  if (mode != 0) return;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned ticket = atomicAdd(&a.req_ticket[b], 1u);
+    s_last = ticket == (unsigned)(len - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  decide_request<T>(a, b, start, len, false);
+  if (threadIdx.x == 0) atomicExch(&a.req_ticket[b], 0u);
+}
+
+// ---------------------------------------------------------------------------------------- probs mode decide
+// accept_random_varlen with p given: one CTA (one warp working) per request.
+template <typename T>
+__global__ void __launch_bounds__(64) decide_probs_kernel(Args a) {
+  __shared__ int s_start[kMaxRequests + 1];
+  if (!starts_from_lens<64>(a.lens, a.B, a.k + 1, a.T, s_start)) {
+    if (threadIdx.x == 0) report(a, kStatusBadLens);
+    return;
+  }
+  const int b = blockIdx.x;
+  const int start = s_start[b], len = s_start[b + 1] - s_start[b];
+  decide_request<T>(a, b, start, len, false);
+}
+
+// ---------------------------------------------------------------------------------------- write probabilities
+template <typename T>
+__global__ void __launch_bounds__(kThreads) write_probs_kernel(Args a, int merged) {
+  __shared__ RowStat s_row;
+  const int c = blockIdx.x, t = blockIdx.y;
+  const int g = t / a.rows_per_param;
+  const float temp = a.temperature[g];
+  if (threadIdx.x < 32) {
+    RowStat rs;
+    if (merged) {
+      float4 raw = __ldcg(reinterpret_cast<const float4*>(&a.rows[t]));
+      rs.m = raw.x; rs.s = raw.y; rs.thr = raw.z; rs.pad = raw.w;
+    } else {
+      rs = merge_row_warp(a, t);
+    }
+    if (threadIdx.x == 0) s_row = rs;
+  }
+  __syncthreads();
+  const RowStat rs = s_row;
+  const int lo = c * a.chunk;
+  const int hi = min((long long)lo + a.chunk, a.V);
+  const T* row = reinterpret_cast<const T*>(a.x) + (long long)t * a.V;
+  float* out = a.probs_out + (long long)t * a.V;
+  for (int v = lo + threadIdx.x; v < hi; v += kThreads) {
+    float f = scaled_at(row, v, temp);
+    out[v] = prob_of_scaled(f, rs);
+  }
+}
+
+// ---------------------------------------------------------------------------------------- pass 2: tail race
+// grid = torch's exponential_ grid for e_numel = B * V elements (S = 256 * gridDim.x threads).  RACE: the
+// request's row is x row b itself, a plain race over given weights (sample()).
+__device__ __forceinline__ void warp_segment_reduce(unsigned long long key, int b, bool active,
+                                                    unsigned long long* s_best) {
+  const int lane = threadIdx.x & 31;
+  unsigned pending = __ballot_sync(0xffffffffu, active);
+  while (pending) {
+    const int leader = __ffs(pending) - 1;
+    const int bb = __shfl_sync(0xffffffffu, b, leader);
+    const bool mine = active && b == bb;
+    unsigned long long kk = warp_max_u64(mine ? key : 0ull);
+    if (lane == leader) atomicMax(&s_best[bb], kk);
+    pending &= ~__ballot_sync(0xffffffffu, mine);
+  }
+}
+
+template <typename T, bool RACE>
+__global__ void __launch_bounds__(kThreads) tail_kernel(Args a) {
+  __shared__ unsigned long long s_best[kMaxRequests];
+  __shared__ int s_last;
+  if (!RACE && *reinterpret_cast<volatile int*>(a.status) != 0) return;  // pass 1 rejected its inputs
+  for (int i = threadIdx.x; i < a.B; i += kThreads) s_best[i] = 0ull;
+  __syncthreads();
+  const long long S = (long long)kRngBlock * gridDim.x;
+  const long long idx = (long long)blockIdx.x * kRngBlock + threadIdx.x;
+  const long long warp_idx0 = idx - (threadIdx.x & 31);
+  const long long N = a.e_numel;
+  const unsigned V = (unsigned)a.V;
+  curandStatePhilox4_32_10_t st;
+  const bool gen = a.E == nullptr;
+  if (gen) curand_init(a.seed, (unsigned long long)idx, a.offset_E, &st);
+  // row / column of element idx, advanced by S per grid-stride step
+  unsigned b = (unsigned)(idx / V), v = (unsigned)(idx % V);
+  for (int n = 0; n < a.e_rounds; ++n) {
+    float4 r4 = make_float4(1.f, 1.f, 1.f, 1.f);
+    if (gen) r4 = curand_uniform4(&st);
+    const float rl[4] = {r4.x, r4.y, r4.z, r4.w};
+    if ((long long)(n * 4) * S + warp_idx0 >= N) break;
+#pragma unroll
+    for (int ii = 0; ii < 4; ++ii) {
+      const long long step = (long long)(n * 4 + ii);
+      if (step * S + warp_idx0 >= N) break;  // warp-uniform
+      const long long li = step * S + idx;
+      const bool active = li < N;
+      unsigned long long key = 0ull;
+      int bb = (int)b;
+      if (active) {
+        float w;
+        if (RACE) {
+          w = reinterpret_cast<const float*>(a.x)[(long long)b * a.V + v];
+        } else {
+          const ReqDesc d = a.desc[b];
+          const float xv = to_f32(reinterpret_cast<const T*>(a.x)[d.x_row * a.V + v]);
+          float p;
+          if (a.probs_mode) {
+            p = xv;
+          } else {
+            const float f = d.temp == 1.0f ? xv : scale_logit(xv, d.temp);
+            p = f >= d.thr ? __fdiv_rn(expf(f - d.m), d.s) : 0.0f;
+          }
+          if (d.q_row < 0) {
+            w = p;
+          } else {
+            const float qv = a.q[d.q_row * a.V + v];
+            w = fmaxf(p - qv, 0.0f);
+          }
+        }
+        const float e = gen ? torch_exponential_clamped(rl[ii]) : a.E[li];
+        float ratio = __fdiv_rn(w, e);
+        if (ratio == 0.0f) ratio = 0.0f;  // -0 and +0 compare equal in torch's argmax
+        key = argmax_key(ratio, v);
+      }
+      warp_segment_reduce(key, bb, active, s_best);
+      // advance to element li + S
+      b += a.e_sq;
+      v += a.e_sr;
+      if (v >= V) { v -= V; ++b; }
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < a.B; i += kThreads) {
+    unsigned long long kk = s_best[i];
+    if (kk) atomicMax(&a.tail_key[i], kk);
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned ticket = atomicAdd(a.tail_ticket, 1u);
+    s_last = ticket == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int i = threadIdx.x; i < a.B; i += kThreads) {
+    unsigned long long kk = atomicExch(&a.tail_key[i], 0ull);
+    a.tail[i] = (long long)argmax_key_index(kk);
+  }
+  if (threadIdx.x == 0) atomicExch(a.tail_ticket, 0u);
+}
+
+// ---------------------------------------------------------------------------------------- greedy
+// grid (C, T): per-chunk argmax folded into a per-row 64-bit key; the request's last CTA decides.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) greedy_kernel(Args a) {
+  __shared__ int s_start[kMaxRequests + 1];
+  __shared__ unsigned long long s_red[kThreads / 32];
+  __shared__ int s_last;
+  const int c = blockIdx.x, t = blockIdx.y;
+  if (!starts_from_lens<kThreads>(a.lens, a.B, a.k + 1, a.T, s_start)) {
+    if (threadIdx.x == 0) report(a, kStatusBadLens);
+    return;
+  }
+  const int b = request_of_row(s_start, a.B, t);
+  const int start = s_start[b], len = s_start[b + 1] - start;
+  const int lo = c * a.chunk;
+  const int hi = min((long long)lo + a.chunk, a.V);
+  const T* row = reinterpret_cast<const T*>(a.x) + (long long)t * a.V;
+  unsigned long long best = 0ull;
+  for (int v = lo + threadIdx.x; v < hi; v += kThreads) {
+    unsigned long long kk = argmax_key(to_f32(row[v]), (unsigned)v);
+    best = kk > best ? kk : best;
+  }
+  best = warp_max_u64(best);
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long m = 0ull;
+    for (int w = 0; w < kThreads / 32; ++w) m = s_red[w] > m ? s_red[w] : m;
+    atomicMax(&a.row_key[t], m);
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned ticket = atomicAdd(&a.req_ticket[b], 1u);
+    s_last = ticket == (unsigned)(len * a.C - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    bool accepted = false;
+    if (lane < a.k) {
+      const int pos = start + (lane < len - 1 ? lane : len - 1);
+      const unsigned long long kk = atomicAdd(&a.row_key[pos], 0ull);
+      const long long target = argmax_key_index(kk);
+      accepted = (target == a.drafts[(long long)b * a.k + lane]) && (lane < len - 1);
+    }
+    const unsigned acc_mask = __ballot_sync(0xffffffffu, accepted);
+    const int n_acc = (~acc_mask) ? __ffs(~acc_mask) - 1 : 32;
+    __syncwarp();
+    if (lane == 0) {
+      const unsigned long long kk = atomicAdd(&a.row_key[start + n_acc], 0ull);
+      a.n_accept[b] = n_acc;
+      a.tail[b] = argmax_key_index(kk);
+    }
+    __syncwarp();
+    // reset this request's row keys for the next call
+    for (int r = lane; r < len; r += 32) atomicExch(&a.row_key[start + r], 0ull);
+    if (lane == 0) atomicExch(&a.req_ticket[b], 0u);
+  }
+}
+
+// ---------------------------------------------------------------------------------------- host side
+static int torch_rng_grid(long long numel, const DeviceInfo& info) {
+  long long g = (numel + kRngBlock - 1) / kRngBlock;
+  long long cap = (long long)info.sm_count * (info.max_threads_per_sm / kRngBlock);
+  return (int)(g < cap ? g : cap);
+}
+static unsigned long long torch_rng_increment(long long numel, const DeviceInfo& info) {
+  if (numel <= 0) return 0;
+  const long long grid = torch_rng_grid(numel, info);
+  return (unsigned long long)(((numel - 1) / (kRngBlock * grid * 4) + 1) * 4);
+}
+
+static void choose_chunks(Args& a, const DeviceInfo& info) {
+  const long long target = (long long)info.sm_count * 8;
+  long long C = (target + a.T - 1) / a.T;
+  long long cmax = (a.V + 2047) / 2048;
+  if (C > cmax) C = cmax;
+  if (C > kMaxChunks) C = kMaxChunks;
+  if (C < 1) C = 1;
+  const int ve = a.dtype == kF32 ? 4 : 8;
+  long long chunk = (a.V + C - 1) / C;
+  chunk = (chunk + ve - 1) / ve * ve;
+  a.chunk = (int)chunk;
+  a.C = (int)((a.V + chunk - 1) / chunk);
+}
+
+static void bind_workspace(Args& a, void* ws) {
+  Layout L = layout(a.T);
+  char* base = static_cast<char*>(ws);
+  a.status = reinterpret_cast<int*>(base + L.status);
+  a.req_ticket = reinterpret_cast<unsigned*>(base + L.req_ticket);
+  a.tail_key = reinterpret_cast<unsigned long long*>(base + L.tail_key);
+  a.tail_ticket = reinterpret_cast<unsigned*>(base + L.tail_ticket);
+  a.row_key = reinterpret_cast<unsigned long long*>(base + L.row_key);
+  a.rows = reinterpret_cast<RowStat*>(base + L.rows);
+  a.partial = reinterpret_cast<float2*>(base + L.partial);
+  a.desc = reinterpret_cast<ReqDesc*>(base + L.desc);
+}
+
+template <typename T>
+static int launch_tail(Args& a, const DeviceInfo& info, bool race, cudaStream_t stream) {
+  a.e_numel = (long long)a.B * a.V;
+  a.e_grid = torch_rng_grid(a.e_numel, info);
+  const long long S = (long long)kRngBlock * a.e_grid;
+  a.e_rounds = (int)((a.e_numel - 1) / (S * 4) + 1);
+  a.e_sq = (unsigned)(S / a.V);
+  a.e_sr = (unsigned)(S % a.V);
+  if (race) tail_kernel<T, true><<<a.e_grid, kThreads, 0, stream>>>(a);
+  else tail_kernel<T, false><<<a.e_grid, kThreads, 0, stream>>>(a);
+  SPECDEC_LAUNCH_CHECK();
+  return kOk;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace sampler
+}  // namespace specdec
+
+using namespace specdec;
+using namespace specdec::sampler;
+
+#define SPECDEC_DISPATCH_DTYPE(dtype, ...)                 \
+  [&]() -> int {                                          \
+    switch (dtype) {                                      \
+      case kF32: { using Tx = float; return __VA_ARGS__(); }          \
+      case kBF16: { using Tx = __nv_bfloat16; return __VA_ARGS__(); } \
+      case kF16: { using Tx = __half; return __VA_ARGS__(); }         \
+      default: return set_error(kInvalidArgument, "unknown dtype code %d", dtype); \
+    }                                                     \
+  }()
+
+extern "C" {
+
+size_t specdec_sampler_workspace_bytes(long long T) { return layout(T).total; }
+
+unsigned long long specdec_philox_increment(long long numel) {
+  DeviceInfo info;
+  if (device_info(&info) != kOk) return 0;
+  return torch_rng_increment(numel, info);
+}
+
+int specdec_probs(const void* logits, int dtype, long long R, long long V, long long rows_per_param,
+                  const float* temperature, const long long* top_k, const float* top_p, int max_top_k,
+                  int has_top_p, float* probs, void* workspace, size_t workspace_bytes, void* stream) {
+  SPECDEC_CHECK_ARG(logits && probs && temperature, "logits, probs and temperature must be non-null");
+  SPECDEC_CHECK_ARG(dtype_ok(dtype), "dtype code %d is not f32/bf16/f16", dtype);
+  SPECDEC_CHECK_ARG(R >= 1 && R <= kMaxRows, "rows %lld out of range [1, %d]", R, kMaxRows);
+  SPECDEC_CHECK_ARG(V >= 1 && V < (1ll << 31), "vocabulary %lld out of range", V);
+  SPECDEC_CHECK_ARG(rows_per_param >= 1 && R % rows_per_param == 0, "rows_per_param must divide rows");
+  SPECDEC_CHECK_ARG(max_top_k >= 0, "max_top_k must be >= 0");
+  if (max_top_k > 0) {
+    SPECDEC_CHECK_ARG(top_k != nullptr, "top_k required when max_top_k > 0");
+    if (max_top_k > kMaxTopK && V > kMaxTopK)
+      return set_error(kUnsupported, "top_k %d above this build's cap %d", max_top_k, kMaxTopK);
+  }
+  SPECDEC_CHECK_ARG(!has_top_p || top_p != nullptr, "top_p required when has_top_p");
+  if (workspace_bytes < layout(R).total)
+    return set_error(kWorkspaceTooSmall, "workspace %zu < %zu bytes", workspace_bytes, layout(R).total);
+  DeviceInfo info;
+  if (int st = device_info(&info)) return st;
+  Args a{};
+  a.x = logits; a.T = R; a.V = V; a.dtype = dtype; a.probs_mode = 0;
+  a.B = (int)(R / rows_per_param); a.k = 0; a.rows_per_param = (int)rows_per_param;
+  a.temperature = temperature; a.top_k = top_k; a.top_p = top_p; a.has_top_p = has_top_p;
+  a.truncate = max_top_k > 0; a.probs_out = probs;
+  choose_chunks(a, info);
+  a.vec_ok = aligned16(logits) && ((V * (long long)dtype_bytes(dtype)) % 16 == 0);
+  bind_workspace(a, workspace);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  SPECDEC_CUDA_TRY(cudaMemsetAsync(a.status, 0, sizeof(int), s));
+  return SPECDEC_DISPATCH_DTYPE(dtype, [&] {
+    if (a.truncate) {
+      topk_stats_kernel<Tx><<<(unsigned)R, kTopkThreads, 0, s>>>(a, 1);
+    } else {
+      stats_kernel<Tx><<<dim3(a.C, (unsigned)R), kThreads, 0, s>>>(a, 1);
+    }
+    SPECDEC_LAUNCH_CHECK();
+    write_probs_kernel<Tx><<<dim3(a.C, (unsigned)R), kThreads, 0, s>>>(a, a.truncate ? 1 : 0);
+    SPECDEC_LAUNCH_CHECK();
+    return (int)kOk;
+  });
+}
+
+int specdec_accept(const void* x, int x_is_probs, int dtype, long long T, long long V, const float* q,
+                   const long long* drafts, long long B, long long k, const long long* verified_lens,
+                   const float* temperature, const long long* top_k, const float* top_p, int max_top_k,
+                   int has_top_p, const float* u, const float* E, unsigned long long seed,
+                   unsigned long long offset_u, unsigned long long offset_E, long long* n_accept,
+                   long long* tail, void* workspace, size_t workspace_bytes, void* stream) {
+  SPECDEC_CHECK_ARG(x && q && drafts && n_accept && tail, "x, q, drafts, n_accept and tail must be non-null");
+  SPECDEC_CHECK_ARG(dtype_ok(dtype), "dtype code %d is not f32/bf16/f16", dtype);
+  SPECDEC_CHECK_ARG(!x_is_probs || dtype == kF32, "probabilities must be fp32");
+  SPECDEC_CHECK_ARG(B >= 1 && B <= kMaxRequests, "batch %lld out of range [1, %d]", B, kMaxRequests);
+  SPECDEC_CHECK_ARG(k >= 1 && k <= 32, "num_drafts %lld out of range [1, 32]", k);
+  SPECDEC_CHECK_ARG(T >= B && T <= kMaxRows && T <= B * (k + 1), "rows %lld inconsistent with B=%lld, k=%lld",
+                    T, B, k);
+  SPECDEC_CHECK_ARG(verified_lens || T == B * (k + 1), "without verified_lens T must equal B * (k + 1)");
+  SPECDEC_CHECK_ARG(V >= 1 && B * V < (1ll << 31), "B * V must stay below 2^31");
+  SPECDEC_CHECK_ARG(x_is_probs || temperature, "temperature required for logits");
+  SPECDEC_CHECK_ARG(max_top_k >= 0, "max_top_k must be >= 0");
+  if (!x_is_probs && max_top_k > 0) {
+    SPECDEC_CHECK_ARG(top_k != nullptr, "top_k required when max_top_k > 0");
+    if (max_top_k > kMaxTopK && V > kMaxTopK)
+      return set_error(kUnsupported, "top_k %d above this build's cap %d", max_top_k, kMaxTopK);
+  }
+  SPECDEC_CHECK_ARG(!has_top_p || top_p != nullptr, "top_p required when has_top_p");
+  if (workspace_bytes < layout(T).total)
+    return set_error(kWorkspaceTooSmall, "workspace %zu < %zu bytes", workspace_bytes, layout(T).total);
+  DeviceInfo info;
+  if (int st = device_info(&info)) return st;
+  Args a{};
+  a.x = x; a.T = T; a.V = V; a.dtype = dtype; a.probs_mode = x_is_probs ? 1 : 0;
+  a.q = q; a.drafts = drafts; a.B = (int)B; a.k = (int)k; a.lens = verified_lens; a.rows_per_param = 1;
+  a.temperature = temperature; a.top_k = top_k; a.top_p = top_p; a.has_top_p = has_top_p;
+  a.truncate = (!x_is_probs && max_top_k > 0);
+  a.u = u; a.E = E; a.seed = seed; a.offset_u = offset_u; a.offset_E = offset_E;
+  a.u_grid = torch_rng_grid(B * k, info);
+  a.n_accept = n_accept; a.tail = tail;
+  choose_chunks(a, info);
+  a.vec_ok = aligned16(x) && ((V * (long long)dtype_bytes(dtype)) % 16 == 0);
+  bind_workspace(a, workspace);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  SPECDEC_CUDA_TRY(cudaMemsetAsync(a.status, 0, sizeof(int), s));
+  return SPECDEC_DISPATCH_DTYPE(dtype, [&] {
+    if (a.probs_mode) {
+      decide_probs_kernel<Tx><<<(unsigned)B, 64, 0, s>>>(a);
+    } else if (a.truncate) {
+      topk_stats_kernel<Tx><<<(unsigned)T, kTopkThreads, 0, s>>>(a, 0);
+    } else {
+      stats_kernel<Tx><<<dim3(a.C, (unsigned)T), kThreads, 0, s>>>(a, 0);
+    }
+    SPECDEC_LAUNCH_CHECK();
+    return launch_tail<Tx>(a, info, false, s);
+  });
+}
+
+int specdec_accept_greedy(const void* logits, int dtype, long long T, long long V, const long long* drafts,
+                          long long B, long long k, const long long* verified_lens, long long* n_accept,
+                          long long* tail, void* workspace, size_t workspace_bytes, void* stream) {
+  SPECDEC_CHECK_ARG(logits && drafts && n_accept && tail, "logits, drafts, n_accept and tail must be non-null");
+  SPECDEC_CHECK_ARG(dtype_ok(dtype), "dtype code %d is not f32/bf16/f16", dtype);
+  SPECDEC_CHECK_ARG(B >= 1 && B <= kMaxRequests, "batch %lld out of range [1, %d]", B, kMaxRequests);
+  SPECDEC_CHECK_ARG(k >= 1 && k <= 32, "num_drafts %lld out of range [1, 32]", k);
+  SPECDEC_CHECK_ARG(T >= B && T <= kMaxRows && T <= B * (k + 1), "rows %lld inconsistent with B=%lld, k=%lld",
+                    T, B, k);
+  SPECDEC_CHECK_ARG(verified_lens || T == B * (k + 1), "without verified_lens T must equal B * (k + 1)");
+  SPECDEC_CHECK_ARG(V >= 1 && V < (1ll << 31), "vocabulary %lld out of range", V);
+  if (workspace_bytes < layout(T).total)
+    return set_error(kWorkspaceTooSmall, "workspace %zu < %zu bytes", workspace_bytes, layout(T).total);
+  DeviceInfo info;
+  if (int st = device_info(&info)) return st;
+  Args a{};
+  a.x = logits; a.T = T; a.V = V; a.dtype = dtype; a.drafts = drafts; a.B = (int)B; a.k = (int)k;
+  a.lens = verified_lens; a.n_accept = n_accept; a.tail = tail;
+  choose_chunks(a, info);
+  bind_workspace(a, workspace);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  SPECDEC_CUDA_TRY(cudaMemsetAsync(a.status, 0, sizeof(int), s));
+  return SPECDEC_DISPATCH_DTYPE(dtype, [&] {
+    greedy_kernel<Tx><<<dim3(a.C, (unsigned)T), kThreads, 0, s>>>(a);
+    SPECDEC_LAUNCH_CHECK();
+    return (int)kOk;
+  });
+}
+
+int specdec_race(const float* weights, long long R, long long V, const float* E, unsigned long long seed,
+                 unsigned long long offset_E, long long* out, void* workspace, size_t workspace_bytes,
+                 void* stream) {
+  SPECDEC_CHECK_ARG(weights && out, "weights and out must be non-null");
+  SPECDEC_CHECK_ARG(R >= 1 && R <= kMaxRequests, "rows %lld out of range [1, %d]", R, kMaxRequests);
+  SPECDEC_CHECK_ARG(V >= 1 && R * V < (1ll << 31), "R * V must stay below 2^31");
+  if (workspace_bytes < layout(R).total)
+    return set_error(kWorkspaceTooSmall, "workspace %zu < %zu bytes", workspace_bytes, layout(R).total);
+  DeviceInfo info;
+  if (int st = device_info(&info)) return st;
+  Args a{};
+  a.x = weights; a.T = R; a.V = V; a.dtype = kF32; a.probs_mode = 1; a.B = (int)R; a.k = 0;
+  a.E = E; a.seed = seed; a.offset_E = offset_E; a.tail = out;
+  bind_workspace(a, workspace);
+  return launch_tail<float>(a, info, true, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,221 @@
+"""Generates the golden fixtures under tests/golden/ by running the reference itself on CPU torch.
+
+    python tests/golden/make_golden.py [--reference /path/to/nano-vllm-speculative-decoding]
+
+Needs the reference checkout (default: $SPECDEC_REFERENCE or ../reference next to this repository's parent);
+the fixtures it writes are committed, so nothing at test time reads the reference.
+
+Every random draw the reference makes is recorded next to its outputs: the generator's state is cloned before
+the call and the same draws are replayed in the reference's order (uniforms [B, k] first, then the [B, V]
+exponential noise of the tail race, clamped at 1e-10), and the script asserts that the replay leaves the
+generator where the reference left it.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+import zlib
+from pathlib import Path
+from types import SimpleNamespace
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+
+
+def import_reference(path: Path):
+    sys.path.insert(0, str(path))
+    sys.path.insert(0, str(path / "tests"))
+    import gpu_import_stubs  # noqa: F401  (flash_attn / triton stand-ins so nanovllm imports on CPU)
+    from nanovllm.layers import spec_sampler
+    return spec_sampler
+
+
+def sampling(ss, temps, top_k, top_p):
+    seqs = [SimpleNamespace(temperature=t, top_k=k, top_p=p) for t, k, p in zip(temps, top_k, top_p)]
+    return ss.sampling_tensors(seqs, torch.device("cpu"))
+
+
+def draws(generator: torch.Generator, batch: int, k: int, vocab: int):
+    clone = torch.Generator().manual_seed(0)
+    clone.set_state(generator.get_state())
+    u = torch.rand(batch, k, generator=clone)
+    noise = torch.empty(batch, vocab).exponential_(1.0, generator=clone).clamp_min_(1e-10)
+    return u, noise, clone
+
+
+def random_lens(rng: np.random.Generator, batch: int, k: int) -> np.ndarray:
+    return rng.integers(1, k + 2, size=batch).astype(np.int64)
+
+
+def accept_cases(ss) -> dict[str, np.ndarray]:
+    """accept_random[_varlen] on given probabilities (the reference functions' own inputs)."""
+    out: dict[str, np.ndarray] = {}
+    cases = []
+    # the pre-varlen equivalence cases of the reference's tests (B=6, k=7, V=5, seeds 0-4)
+    for seed in range(5):
+        torch.manual_seed(seed)
+        p = torch.softmax(torch.randn(6, 8, 5), dim=-1)
+        q = torch.softmax(torch.randn(6, 7, 5), dim=-1)
+        drafts = torch.randint(5, (6, 7))
+        cases.append((f"m3_seed{seed}", p.flatten(0, 1), q, drafts, None, seed))
+    # varlen point masses: rows verify 1, 2, 4 positions
+    point = torch.eye(4)
+    cases.append(("varlen_points", point[[3, 1, 2, 1, 2, 3, 0]], torch.eye(4)[torch.tensor([[1, 2, 3]] * 3)],
+                  torch.tensor([[1, 2, 3]] * 3), torch.tensor([1, 2, 4]), 0))
+    # random varlen / fixed cases at moderate vocabulary
+    rng = np.random.default_rng(7)
+    for name, batch, k, vocab, varlen, seed in [("fixed_b16_v600", 16, 7, 600, False, 11),
+                                                  ("varlen_b24_v377", 24, 7, 377, True, 12),
+                                                  ("varlen_b9_k3_v64", 9, 3, 64, True, 13),
+                                                  ("fixed_b4_k1_v33", 4, 1, 33, False, 14)]:
+        g = torch.Generator().manual_seed(seed)
+        lens = torch.from_numpy(random_lens(rng, batch, k)) if varlen else torch.full((batch,), k + 1)
+        total = int(lens.sum())
+        p = torch.softmax(torch.randn(total, vocab, generator=g) * 3, dim=-1)
+        q = torch.softmax(torch.randn(batch, k, vocab, generator=g) * 3, dim=-1)
+        # half the rows propose from p itself so long prefixes get accepted
+        starts = torch.cumsum(lens, 0) - lens
+        for b in range(0, batch, 2):
+            for j in range(k):
+                pos = int(starts[b]) + min(j, int(lens[b]) - 1)
+                q[b, j] = p[pos]
+        drafts = torch.stack([torch.multinomial(q[b], 1, generator=g).squeeze(-1) for b in range(batch)])
+        cases.append((name, p, q, drafts, lens if varlen else None, seed))
+    for name, p, q, drafts, lens, seed in cases:
+        batch, k = drafts.shape
+        g = torch.Generator().manual_seed(1000 + seed)
+        u, noise, clone = draws(g, batch, k, p.shape[-1])
+        if lens is None:
+            n_accept, tail = ss.accept_random(p.view(batch, k + 1, -1), q, drafts, g)
+            lens_out = torch.full((batch,), k + 1)
+        else:
+            n_accept, tail = ss.accept_random_varlen(p, q, drafts, lens, g)
+            lens_out = lens
+        assert torch.equal(g.get_state(), clone.get_state()), name
+        prefix = f"accept/{name}/"
+        for key, value in dict(p=p, q=q, drafts=drafts, lens=lens_out, u=u, noise=noise, n_accept=n_accept,
+                               tail=tail, fixed=torch.tensor(lens is None)).items():
+            out[prefix + key] = value.numpy()
+    return out
+
+
+def logits_cases(ss) -> dict[str, np.ndarray]:
+    """probs_from_logits + accept on logits: the fused _accept path (speculative.py:450-462)."""
+    out: dict[str, np.ndarray] = {}
+    rng = np.random.default_rng(21)
+    configs = [
+        # name, batch, k, vocab, dtype, temps, top_k, top_p, varlen
+        ("t1_fp32_v800", 8, 7, 800, torch.float32, [1.0] * 8, [0] * 8, [1.0] * 8, False),
+        ("protocol_fp32_v900", 8, 7, 900, torch.float32, [0.7] * 8, [20] * 8, [0.8] * 8, False),
+        ("mixed_bf16_v700", 6, 7, 700, torch.bfloat16, [1.0, 0.7, 0.5, 1.3, 0.9, 1.0], [0, 20, 5, 0, 64, 1],
+         [1.0, 0.8, 0.5, 1.0, 0.95, 1.0], True),
+        ("topk_only_fp16_v999", 5, 4, 999, torch.float16, [0.8] * 5, [3, 10, 50, 7, 1], [1.0] * 5, True),
+    ]
+    for name, batch, k, vocab, dtype, temps, top_k, top_p, varlen in configs:
+        g = torch.Generator().manual_seed(zlib.crc32(name.encode()) % 100000)
+        lens = torch.from_numpy(random_lens(rng, batch, k)) if varlen else torch.full((batch,), k + 1)
+        total = int(lens.sum())
+        logits = (torch.randn(total, vocab, generator=g) * 3).to(dtype)
+        samp = sampling(ss, temps, top_k, top_p)
+        per_token = ss.sampling_per_token(samp, lens, total)
+        p = ss.probs_from_logits(logits, per_token)
+        q_logits = torch.randn(batch, k, vocab, generator=g) * 3
+        q = ss.probs_from_logits(q_logits, samp)
+        drafts = ss.sample(q, g)
+        u, noise, clone = draws(g, batch, k, vocab)
+        n_accept, tail = ss.accept_random_varlen(p, q, drafts, lens, g)
+        assert torch.equal(g.get_state(), clone.get_state()), name
+        prefix = f"logits/{name}/"
+        for key, value in dict(logits=logits.float(), p=p, q=q, drafts=drafts, lens=lens, u=u, noise=noise,
+                               n_accept=n_accept, tail=tail, temperature=samp.temperatures, top_k=samp.top_k,
+                               top_p=samp.top_p).items():
+            out[prefix + key] = value.numpy()
+        out[prefix + "dtype"] = np.array(str(dtype).replace("torch.", ""))
+        out[prefix + "max_top_k"] = np.array(samp.max_top_k)
+        out[prefix + "has_top_p"] = np.array(samp.has_top_p)
+    return out
+
+
+def truncation_cases(ss) -> dict[str, np.ndarray]:
+    """probs_from_logits known answers, including the reference tests' tie and nucleus cases."""
+    out: dict[str, np.ndarray] = {}
+    g = torch.Generator().manual_seed(5)
+    tied = torch.randn(1, 200, generator=g).clamp(max=2.5)
+    tied[0, :32] = torch.tensor([5.0, 4.0] + [3.0] * 30)
+    cases = [
+        ("temperature", torch.tensor([[1.0, 0.0]]), [0.5], [0], [1.0]),
+        ("top_k_two", torch.tensor([[1.0, 3.0, 2.0, 0.0]]), [1.0], [2], [1.0]),
+        ("top_k_tie", torch.tensor([[2.0, 2.0, 1.0, 0.0]]), [1.0], [1], [1.0]),
+        ("top_p_half", torch.tensor([[0.4, 0.3, 0.2, 0.1]]).log(), [1.0], [4], [0.5]),
+        ("top_p_within_k", torch.tensor([[0.4, 0.3, 0.2, 0.1]]).log(), [1.0], [2], [0.99]),
+        ("mixed_rows", torch.tensor([[1.0, 2.0, 3.0], [1.0, 2.0, 3.0]]), [1.0, 1.0], [0, 1], [1.0, 1.0]),
+        ("thirty_tied_at_cut", tied, [0.7], [3], [1.0]),
+        ("top_k_above_vocab", torch.randn(2, 50, generator=g), [1.0, 0.9], [80, 3], [1.0, 0.7]),
+        ("wide_random", torch.randn(7, 1500, generator=g) * 4, [0.7, 1.0, 0.3, 2.0, 1.0, 0.7, 0.9],
+         [20, 0, 128, 1, 1000, 64, 7], [0.8, 1.0, 0.9, 1.0, 0.99, 0.3, 0.05]),
+    ]
+    for name, logits, temps, top_k, top_p in cases:
+        samp = sampling(ss, temps, top_k, top_p)
+        probs = ss.probs_from_logits(logits, samp)
+        prefix = f"trunc/{name}/"
+        out[prefix + "logits"] = logits.numpy()
+        out[prefix + "temperature"] = samp.temperatures.numpy()
+        out[prefix + "top_k"] = samp.top_k.numpy()
+        out[prefix + "top_p"] = samp.top_p.numpy()
+        out[prefix + "max_top_k"] = np.array(samp.max_top_k)
+        out[prefix + "has_top_p"] = np.array(samp.has_top_p)
+        out[prefix + "probs"] = probs.numpy()
+    return out
+
+
+def greedy_cases(ss) -> dict[str, np.ndarray]:
+    out: dict[str, np.ndarray] = {}
+    rng = np.random.default_rng(3)
+    for name, batch, k, vocab, varlen in [("fixed_b8_v500", 8, 7, 500, False), ("varlen_b12_v300", 12, 7, 300, True)]:
+        g = torch.Generator().manual_seed(batch)
+        lens = torch.from_numpy(random_lens(rng, batch, k)) if varlen else torch.full((batch,), k + 1)
+        total = int(lens.sum())
+        logits = torch.randn(total, vocab, generator=g)
+        target = logits.argmax(-1)
+        starts = torch.cumsum(lens, 0) - lens
+        drafts = torch.randint(vocab, (batch, k), generator=g)
+        for b in range(batch):   # agree with the target for a random prefix
+            agree = int(rng.integers(0, k + 1))
+            for j in range(min(agree, int(lens[b]) - 1)):
+                drafts[b, j] = target[int(starts[b]) + j]
+        n_accept, tail = ss.accept_greedy_varlen(logits, drafts, lens)
+        prefix = f"greedy/{name}/"
+        for key, value in dict(logits=logits, drafts=drafts, lens=lens, n_accept=n_accept, tail=tail).items():
+            out[prefix + key] = value.numpy()
+    # a tie: two equal maxima, the first index wins
+    logits = torch.zeros(2, 6)
+    logits[0, [2, 4]] = 1.0
+    logits[1, [1, 5]] = 2.0
+    n_accept, tail = ss.accept_greedy(logits.view(1, 2, 6), torch.tensor([[2]]))
+    for key, value in dict(logits=logits, drafts=torch.tensor([[2]]), lens=torch.tensor([2]), n_accept=n_accept,
+                           tail=tail).items():
+        out["greedy/ties/" + key] = value.numpy()
+    return out
+
+
+def main() -> int:
+    parser = argparse.ArgumentParser(description=__doc__)
+    default_ref = os.environ.get("SPECDEC_REFERENCE", str(HERE.parents[2] / "reference"))
+    parser.add_argument("--reference", default=default_ref)
+    args = parser.parse_args()
+    ss = import_reference(Path(args.reference))
+    fixtures = {}
+    fixtures.update(accept_cases(ss))
+    fixtures.update(logits_cases(ss))
+    fixtures.update(truncation_cases(ss))
+    fixtures.update(greedy_cases(ss))
+    np.savez_compressed(HERE / "sampler.npz", **fixtures)
+    print(f"wrote {len(fixtures)} arrays to {HERE / 'sampler.npz'}")
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
