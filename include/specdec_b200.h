@@ -72,6 +72,28 @@ int specdec_race(const float* weights, long long R, long long V, const float* E,
                  unsigned long long offset_E, long long* out, void* workspace, size_t workspace_bytes,
                  void* stream);
 
+/* ------------------------------------------------------------------------------------------ kernel 2: attention */
+/* store_kvcache (nanovllm/layers/attention.py:10-40, the Triton store_kvcache_kernel): key/value rows [N, Hkv, D]
+ * bf16 (row strides in elements) to flat slots slot_mapping[N] (int32) of k_cache / v_cache [num_slots, Hkv, D];
+ * slot -1 is skipped, a slot >= num_slots is skipped and recorded in *err (device int, first error wins). */
+int specdec_store_kvcache(const void* key, long long key_row_stride, const void* value, long long value_row_stride,
+                          void* k_cache, void* v_cache, const int* slot_mapping, long long N, int num_kv_heads,
+                          int head_dim, long long num_slots, int* err, void* stream);
+
+/* Attention.forward's paged branches (nanovllm/layers/attention.py:59-77): flash_attn_varlen_func with
+ * block_table (verify: cu_seqlens_q / cu_seqlens_k int32 [R + 1], causal bottom-right aligned) or
+ * flash_attn_with_kvcache (decode: context_lens int32 [R], q_per_seq queries per row, causal or not).
+ * q [T, H, 128] bf16 (row stride q_row_stride elements); caches [num_slots / block_size, block_size, Hkv, 128]
+ * bf16; block_tables int32 [R, W]; out [T, H, 128] bf16 (row stride out_row_stride).  Limits: head_dim 128,
+ * H / Hkv in {1, 2, 4, 8}, max_seqlen_q * H / Hkv <= 32, block_size a multiple of 128.  Rows whose metadata
+ * is inconsistent are skipped and recorded in *err. */
+int specdec_paged_attention(const void* q, long long T, long long q_row_stride, int num_heads, int num_kv_heads,
+                            int head_dim, const void* k_cache, const void* v_cache, long long num_slots,
+                            int block_size, const int* cu_seqlens_q, const int* cu_seqlens_k,
+                            const int* context_lens, int q_per_seq, int R, const int* block_tables, int W,
+                            int max_seqlen_q, float softmax_scale, int causal, void* out, long long out_row_stride,
+                            int* err, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -40,6 +40,11 @@ SIGNATURES = {
                                        _c_void_p, _c_void_p, _c_void_p, _c_size, _c_void_p]),
     "specdec_race": (_c_int, [_c_void_p, _c_ll, _c_ll, _c_void_p, _c_ull, _c_ull, _c_void_p, _c_void_p, _c_size,
                               _c_void_p]),
+    "specdec_store_kvcache": (_c_int, [_c_void_p, _c_ll, _c_void_p, _c_ll, _c_void_p, _c_void_p, _c_void_p, _c_ll,
+                                       _c_int, _c_int, _c_ll, _c_void_p, _c_void_p]),
+    "specdec_paged_attention": (_c_int, [_c_void_p, _c_ll, _c_ll, _c_int, _c_int, _c_int, _c_void_p, _c_void_p, _c_ll,
+                                         _c_int, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_int, _c_void_p, _c_int,
+                                         _c_int, _c_float, _c_int, _c_void_p, _c_ll, _c_void_p, _c_void_p]),
 }
 
 _lib = None

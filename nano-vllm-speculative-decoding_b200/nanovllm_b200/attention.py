@@ -1,0 +1,122 @@
+"""The reference's attention layer (nanovllm/layers/attention.py) on the B200 kernels of libspecdec_b200.so.
+
+    store_kvcache(key, value, k_cache, v_cache, slot_mapping)   attention.py:33-40   -> specdec_store_kvcache
+    Attention(num_heads, head_dim, scale, num_kv_heads).forward  attention.py:43-77   -> specdec_paged_attention
+
+Attention.forward reads the module-global context (nanovllm_b200.context, the reference's nanovllm/utils/context.py)
+and serves the two paged branches of the reference:
+  - verify (is_prefill with block_tables): varlen over cu_seqlens_q / cu_seqlens_k, causal bottom-right aligned;
+  - decode (not is_prefill): query_len_per_seq queries per row over context_lens, causal or not (the DFlash
+    draft block).
+Plain prefill without a block table is not on the verify/accept path and raises NotImplementedError.
+
+Shapes: q [T, H, 128], k / v [T, Hkv, 128] bf16; k_cache / v_cache [blocks, block_size, Hkv, 128] bf16 with
+block_size a multiple of 128; rows of at most 32 / (H / Hkv) queries (8 for Qwen3's GQA group of 4).
+"""
+from __future__ import annotations
+
+import torch
+from torch import nn
+
+from . import _lib
+from ._lib import Workspace, check, ptr, require_cuda, stream_of
+from .context import get_context
+
+
+def _err_word(device: torch.device) -> torch.Tensor:
+    return Workspace.get(device, 256, name="attention")[:4].view(torch.int32)
+
+
+def device_error(device: torch.device) -> int:
+    """First error code a paged-attention / K-V store kernel recorded on this device since the last reset
+    (synchronises): 0 none, 2 row metadata inconsistent with the block table width, 3 a slot past the cache,
+    11-17 a bounded pipeline wait gave up."""
+    return int(_err_word(device).item())
+
+
+def reset_device_error(device: torch.device) -> None:
+    _err_word(device).zero_()
+
+
+def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                  slot_mapping: torch.Tensor) -> None:
+    """attention.py:33-40: key/value [N, Hkv, D] rows to slot_mapping[N] of the paged caches; slot -1 skipped."""
+    device = require_cuda(key, value, k_cache, v_cache, slot_mapping)
+    N, num_heads, head_dim = key.shape
+    assert key.stride(-1) == 1 and value.stride(-1) == 1
+    assert key.stride(1) == head_dim and value.stride(1) == head_dim
+    assert slot_mapping.numel() == N
+    if key.dtype != torch.bfloat16 or k_cache.dtype != torch.bfloat16:
+        raise ValueError("the B200 K/V store takes bf16 keys, values and caches")
+    slots = slot_mapping.to(torch.int32).contiguous()
+    num_slots = k_cache.numel() // (num_heads * head_dim)
+    check(_lib.lib().specdec_store_kvcache(ptr(key), key.stride(0), ptr(value), value.stride(0), ptr(k_cache),
+                                           ptr(v_cache), ptr(slots), N, num_heads, head_dim, num_slots,
+                                           ptr(_err_word(device)), stream_of(device)))
+
+
+def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
+                    scale: float, *, cu_seqlens_q: torch.Tensor | None = None,
+                    cu_seqlens_k: torch.Tensor | None = None, max_seqlen_q: int | None = None,
+                    context_lens: torch.Tensor | None = None, query_len_per_seq: int = 1, causal: bool = True,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """Attention of q [T, H, D] over the paged caches.  Varlen (cu_seqlens_q/k, the verify forward) or decode
+    (context_lens with query_len_per_seq queries per row).  Returns out [T, H, D] bf16."""
+    device = require_cuda(q, k_cache, v_cache, block_tables)
+    T, H, D = q.shape
+    blocks, block_size, Hkv, Dc = k_cache.shape
+    if Dc != D or v_cache.shape != k_cache.shape:
+        raise ValueError("q, k_cache and v_cache disagree on head_dim or shape")
+    if q.stride(-1) != 1 or q.stride(1) != D:
+        q = q.contiguous()
+    tables = block_tables.to(torch.int32).contiguous()
+    R, W = tables.shape
+    if out is None:
+        out = torch.empty(T, H, D, dtype=torch.bfloat16, device=device)
+    if cu_seqlens_q is not None:
+        cq = cu_seqlens_q.to(torch.int32).contiguous()
+        ck = cu_seqlens_k.to(torch.int32).contiguous()
+        ctx = None
+        if max_seqlen_q is None:
+            raise ValueError("varlen attention needs max_seqlen_q")
+        R = cq.numel() - 1
+        q_per_seq = 0
+    else:
+        cq = ck = None
+        ctx = context_lens.to(torch.int32).contiguous()
+        R = ctx.numel()
+        q_per_seq = query_len_per_seq
+        max_seqlen_q = query_len_per_seq
+    check(_lib.lib().specdec_paged_attention(
+        ptr(q), T, q.stride(0), H, Hkv, D, ptr(k_cache), ptr(v_cache), blocks * block_size, block_size, ptr(cq),
+        ptr(ck), ptr(ctx), q_per_seq, R, ptr(tables), W, int(max_seqlen_q), float(scale), int(causal), ptr(out),
+        out.stride(0), ptr(_err_word(device)), stream_of(device)))
+    return out
+
+
+class Attention(nn.Module):
+    """attention.py:43-77: paged attention over this layer's k_cache / v_cache (bound by the model runner)."""
+
+    def __init__(self, num_heads, head_dim, scale, num_kv_heads):
+        super().__init__()
+        self.num_heads = num_heads
+        self.head_dim = head_dim
+        self.scale = scale
+        self.num_kv_heads = num_kv_heads
+        self.k_cache = self.v_cache = torch.tensor([])
+
+    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+        context = get_context()
+        k_cache, v_cache = self.k_cache, self.v_cache
+        if k_cache.numel() and v_cache.numel():
+            store_kvcache(k, v, k_cache, v_cache, context.slot_mapping)
+        q = q.view(-1, self.num_heads, self.head_dim)
+        if context.is_prefill:
+            if context.block_tables is None:
+                raise NotImplementedError("prefill without a block table is outside the B200 verify/accept path")
+            return paged_attention(q, k_cache, v_cache, context.block_tables, self.scale,
+                                   cu_seqlens_q=context.cu_seqlens_q, cu_seqlens_k=context.cu_seqlens_k,
+                                   max_seqlen_q=context.max_seqlen_q, causal=True)
+        return paged_attention(q, k_cache, v_cache, context.block_tables, self.scale,
+                               context_lens=context.context_lens, query_len_per_seq=context.query_len_per_seq,
+                               causal=context.causal)

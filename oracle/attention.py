@@ -1,0 +1,48 @@
+"""numpy restatement of the reference's paged attention -- test infrastructure only.
+
+store_kvcache            nanovllm/layers/attention.py:10-40 (and tests/fake_paged_attention.py:14-17)
+paged attention          nanovllm/layers/attention.py:59-77 restated by tests/fake_paged_attention.py:20-41: keys
+                         gathered through the block table up to the row's key length, SDPA in fp32, causal
+                         bottom-right aligned (query j of L_q sees keys 0 .. L_k - L_q + j).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+
+def store_kvcache(key, value, k_cache, v_cache, slot_mapping) -> None:
+    """attention.py:33-40: key/value [N, Hkv, D] rows to flat slots; slot -1 skipped (in place)."""
+    rows = slot_mapping >= 0
+    k_cache.reshape(-1, *key.shape[1:])[slot_mapping[rows]] = key[rows]
+    v_cache.reshape(-1, *value.shape[1:])[slot_mapping[rows]] = value[rows]
+
+
+def paged_attention(q, k_cache, v_cache, block_tables, q_starts, q_lens, k_lens, scale: float, causal: bool = True):
+    """q [T, H, D]; k_cache / v_cache [blocks, block_size, Hkv, D]; per row r: queries q[q_starts[r] :
+    q_starts[r] + q_lens[r]], keys 0 .. k_lens[r]-1 through block_tables[r].  Returns out [T, H, D] fp32 (rows
+    not covered stay 0)."""
+    q = q.astype(np.float32)
+    T, H, D = q.shape
+    block_size, Hkv = k_cache.shape[1], k_cache.shape[2]
+    group = H // Hkv
+    keys_all = k_cache.reshape(-1, Hkv, D).astype(np.float32)
+    values_all = v_cache.reshape(-1, Hkv, D).astype(np.float32)
+    out = np.zeros((T, H, D), dtype=np.float32)
+    for r in range(len(q_lens)):
+        ql, kl, qs = int(q_lens[r]), int(k_lens[r]), int(q_starts[r])
+        if ql == 0:
+            continue
+        positions = np.arange(kl)
+        slots = block_tables[r, positions // block_size].astype(np.int64) * block_size + positions % block_size
+        keys = np.repeat(keys_all[slots], group, axis=1)        # [L, H, D]
+        values = np.repeat(values_all[slots], group, axis=1)
+        queries = q[qs:qs + ql]                                  # [n, H, D]
+        scores = np.einsum("nhd,lhd->hnl", queries, keys) * np.float32(scale)
+        if causal:
+            allowed = positions[None, :] <= (kl - ql + np.arange(ql))[:, None]
+            scores = np.where(allowed[None], scores, -np.inf)
+        scores = scores - scores.max(axis=-1, keepdims=True)
+        weights = np.exp(scores)
+        weights /= weights.sum(axis=-1, keepdims=True)
+        out[qs:qs + ql] = np.einsum("hnl,lhd->nhd", weights, values)
+    return out

@@ -1,0 +1,167 @@
+"""Kernel (2), paged verify / decode attention and the paged K/V store, against the numpy oracle
+(oracle/attention.py, the reference's tests/fake_paged_attention.py rule).  Tolerance (north star): bf16
+attention outputs within 2e-2 absolute; the K/V store is a bit-exact copy."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention as OA
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+ATOL = 2e-2
+
+
+@pytest.fixture(scope="module")
+def A():
+    from nanovllm_b200 import attention
+    return attention
+
+
+def paged_case(q_lens, k_lens, H=32, Hkv=8, D=128, block_size=256, seed=0, stale_nan=True, pad_rows=0):
+    """Rows with q_lens queries and k_lens keys (the last q_len keys are the new tokens, stored through
+    store_kvcache), blocks drawn from a random permutation; unused slots hold NaN (stale cache)."""
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    R = len(q_lens)
+    blocks_per_row = [math.ceil(k / block_size) for k in k_lens]
+    W = max(blocks_per_row)
+    num_blocks = sum(blocks_per_row) + 3 + 1                         # + spare blocks + the pad block
+    perm = torch.randperm(num_blocks - 1, generator=torch.Generator().manual_seed(seed)).tolist()
+    pad_block = num_blocks - 1
+    k_cache = torch.full((num_blocks, block_size, Hkv, D), float("nan") if stale_nan else 0.0, dtype=torch.bfloat16,
+                         device=DEV)
+    v_cache = k_cache.clone()
+    k_cache[pad_block] = 0
+    v_cache[pad_block] = 0
+    tables = torch.full((R + pad_rows, W), pad_block, dtype=torch.int32)
+    used = 0
+    for r, nb in enumerate(blocks_per_row):
+        tables[r, :nb] = torch.tensor(perm[used:used + nb], dtype=torch.int32)
+        used += nb
+    # context keys / values (positions < k_len - q_len) written directly
+    for r, (ql, kl) in enumerate(zip(q_lens, k_lens)):
+        pos = torch.arange(kl - ql)
+        slots = tables[r, pos // block_size].long() * block_size + pos % block_size
+        k_cache.view(-1, Hkv, D)[slots.to(DEV)] = torch.randn(len(pos), Hkv, D, device=DEV, generator=g).bfloat16()
+        v_cache.view(-1, Hkv, D)[slots.to(DEV)] = torch.randn(len(pos), Hkv, D, device=DEV, generator=g).bfloat16()
+    # new tokens: q / k / v of every query position, slot mapping for the store
+    q_lens_all = list(q_lens) + [1] * pad_rows
+    k_lens_all = list(k_lens) + [1] * pad_rows
+    T = sum(q_lens_all)
+    q = torch.randn(T, H, D, device=DEV, generator=g).bfloat16()
+    k = torch.randn(T, Hkv, D, device=DEV, generator=g).bfloat16()
+    v = torch.randn(T, Hkv, D, device=DEV, generator=g).bfloat16()
+    slot_mapping = []
+    for r, (ql, kl) in enumerate(zip(q_lens_all, k_lens_all)):
+        for j in range(ql):
+            position = kl - ql + j
+            slot_mapping.append(int(tables[r, position // block_size]) * block_size + position % block_size
+                                if r < R else -1)
+    cu_q = torch.tensor([0] + np.cumsum(q_lens_all).tolist(), dtype=torch.int32, device=DEV)
+    cu_k = torch.tensor([0] + np.cumsum(k_lens_all).tolist(), dtype=torch.int32, device=DEV)
+    return dict(q=q, k=k, v=v, k_cache=k_cache, v_cache=v_cache, tables=tables.to(DEV), cu_q=cu_q, cu_k=cu_k,
+                slots=torch.tensor(slot_mapping, dtype=torch.int32, device=DEV), q_lens=q_lens_all,
+                k_lens=k_lens_all, scale=D ** -0.5)
+
+
+def oracle_out(c, causal=True):
+    k_cache = c["k_cache"].float().cpu().numpy()
+    v_cache = c["v_cache"].float().cpu().numpy()
+    starts = np.concatenate([[0], np.cumsum(c["q_lens"])[:-1]])
+    return OA.paged_attention(c["q"].float().cpu().numpy(), k_cache, v_cache, c["tables"].cpu().numpy(), starts,
+                              c["q_lens"], c["k_lens"], c["scale"], causal)
+
+
+def run_verify(A, c):
+    A.reset_device_error(DEV)
+    A.store_kvcache(c["k"], c["v"], c["k_cache"], c["v_cache"], c["slots"])
+    out = A.paged_attention(c["q"], c["k_cache"], c["v_cache"], c["tables"], c["scale"], cu_seqlens_q=c["cu_q"],
+                            cu_seqlens_k=c["cu_k"], max_seqlen_q=max(c["q_lens"]))
+    torch.cuda.synchronize()
+    assert A.device_error(DEV) == 0
+    return out
+
+
+def test_store_kvcache_is_an_exact_copy(A):
+    c = paged_case([3, 8], [40, 300], stale_nan=False)
+    expected_k = c["k_cache"].float().cpu().numpy()
+    expected_v = c["v_cache"].float().cpu().numpy()
+    A.store_kvcache(c["k"], c["v"], c["k_cache"], c["v_cache"], c["slots"])
+    OA.store_kvcache(c["k"].float().cpu().numpy(), c["v"].float().cpu().numpy(), expected_k, expected_v,
+                     c["slots"].cpu().numpy())
+    assert np.array_equal(c["k_cache"].float().cpu().numpy(), expected_k)
+    assert np.array_equal(c["v_cache"].float().cpu().numpy(), expected_v)
+
+
+def test_baseline_config2_verify_attention(A):
+    """32 rows x 8 queries, 32/8 heads, head_dim 128, contexts U[900, 1100], block size 256,
+    random block permutation, stale NaN in unused slots."""
+    rng = np.random.default_rng(0)
+    k_lens = rng.integers(900, 1101, size=32).tolist()
+    c = paged_case([8] * 32, k_lens, seed=1)
+    out = run_verify(A, c)
+    want = oracle_out(c)
+    got = out.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    np.testing.assert_allclose(got, want, atol=ATOL, rtol=0)
+
+
+@pytest.mark.parametrize("k_lens", [[1, 2, 8], [127, 128, 129], [255, 256, 257], [383, 512, 640]])
+def test_ragged_rows_and_tile_edges(A, k_lens):
+    q_lens = [min(k, q) for k, q in zip(k_lens, [1, 5, 8])]
+    c = paged_case(q_lens, k_lens, seed=sum(k_lens))
+    out = run_verify(A, c)
+    np.testing.assert_allclose(out.float().cpu().numpy(), oracle_out(c), atol=ATOL, rtol=0)
+
+
+def test_padding_rows_read_the_pad_block(A):
+    c = paged_case([8, 3], [700, 1000], pad_rows=2, seed=4)
+    out = run_verify(A, c)
+    got = out.float().cpu().numpy()
+    np.testing.assert_allclose(got[:11], oracle_out(c)[:11], atol=ATOL, rtol=0)
+    assert np.abs(got[11:]).max() == 0      # attention over the zero pad block
+
+
+@pytest.mark.parametrize("H,Hkv,ql", [(8, 8, 8), (16, 8, 8), (64, 8, 4), (32, 4, 4)])
+def test_gqa_groups(A, H, Hkv, ql):
+    c = paged_case([ql, ql, ql], [300, 129, 800], H=H, Hkv=Hkv, seed=H + Hkv)
+    out = run_verify(A, c)
+    np.testing.assert_allclose(out.float().cpu().numpy(), oracle_out(c), atol=ATOL, rtol=0)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_decode_branch_draft_block(A, causal):
+    """The decode branch: query_len_per_seq = 7 queries per row over context_lens (the DFlash draft block is
+    non-causal)."""
+    k_lens = [7, 100, 300, 1000]
+    c = paged_case([7] * 4, k_lens, seed=9)
+    A.store_kvcache(c["k"], c["v"], c["k_cache"], c["v_cache"], c["slots"])
+    ctx = torch.tensor(k_lens, dtype=torch.int32, device=DEV)
+    A.reset_device_error(DEV)
+    out = A.paged_attention(c["q"], c["k_cache"], c["v_cache"], c["tables"], c["scale"], context_lens=ctx,
+                            query_len_per_seq=7, causal=causal)
+    torch.cuda.synchronize()
+    assert A.device_error(DEV) == 0
+    np.testing.assert_allclose(out.float().cpu().numpy(), oracle_out(c, causal=causal), atol=ATOL, rtol=0)
+
+
+def test_attention_module_reads_the_context(A):
+    from nanovllm_b200.attention import Attention
+    from nanovllm_b200.context import reset_context, set_context
+    c = paged_case([8, 5], [600, 257], seed=12)
+    layer = Attention(32, 128, c["scale"], 8)
+    layer.k_cache, layer.v_cache = c["k_cache"], c["v_cache"]
+    set_context(True, c["cu_q"], c["cu_k"], 8, 4096, c["slots"], None, c["tables"])
+    out = layer(c["q"].view(-1, 32 * 128), c["k"], c["v"])
+    reset_context()
+    np.testing.assert_allclose(out.float().cpu().numpy(), oracle_out(c), atol=ATOL, rtol=0)
+
+
+def test_unsupported_shapes_raise(A):
+    from nanovllm_b200._lib import SpecdecError
+    c = paged_case([8], [100], seed=3)
+    with pytest.raises(SpecdecError):
+        A.paged_attention(c["q"], c["k_cache"], c["v_cache"], c["tables"], c["scale"], cu_seqlens_q=c["cu_q"],
+                          cu_seqlens_k=c["cu_k"], max_seqlen_q=9)
