@@ -94,6 +94,31 @@ int specdec_paged_attention(const void* q, long long T, long long q_row_stride, 
                             int max_seqlen_q, float softmax_scale, int causal, void* out, long long out_row_stride,
                             int* err, void* stream);
 
+/* ------------------------------------------------------------------------------------------ kernel 4: ctx_store */
+/* DFlashDraftModel.store_context_kv (nanovllm/models/dflash.py:88-96) for every draft layer in one launch, and
+ * the target's q_norm / k_norm + RoPE + store_kvcache (nanovllm/models/qwen3.py:77-86, attention.py:62-63).
+ * x [layers][T][(Hq + 2 Hkv) * 128] bf16 (layer / row strides in elements): Hq query heads, then Hkv K heads,
+ * then Hkv V heads.  Query heads: RMSNorm(q_norm [128]) then RoPE -> q_out [T][Hq][128].  K heads:
+ * RMSNorm(k_norm [layer][128]) then RoPE -> k_cache[layer][slot]; V heads copied to v_cache[layer][slot]; caches
+ * [layers][num_slots][Hkv][128] (layer stride in elements).  cos_sin [max_position][128] fp32 (cos | sin);
+ * positions [T] int64; slot_mapping [T] int32 (-1 skipped).  Out-of-range positions / slots are skipped and
+ * recorded in *err. */
+int specdec_norm_rope_store(const void* x, long long x_layer_stride, long long x_row_stride, int T, int layers,
+                            int num_q_heads, int num_kv_heads, const void* q_norm, const void* k_norm,
+                            long long k_norm_layer_stride, const float* cos_sin, long long max_position,
+                            const long long* positions, const int* slot_mapping, void* k_cache, void* v_cache,
+                            long long cache_layer_stride, long long num_slots, void* q_out, float eps, int* err,
+                            void* stream);
+
+/* ------------------------------------------------------------------------------------------ verify forward helpers */
+/* RMSNorm.rms_forward / add_rms_forward (nanovllm/layers/layernorm.py:16-40): rows of `width` bf16 (a multiple of
+ * 8, <= 8192).  With residual: s = x + residual, residual_out = s, out = norm(s) * weight; else out = norm(x). */
+int specdec_rmsnorm(const void* x, const void* residual, const void* weight, void* out, void* residual_out,
+                    long long T, int width, float eps, void* stream);
+
+/* SiluAndMul (nanovllm/layers/activation.py:8-11): gate_up [T, 2 I] bf16 -> out [T, I] = silu(gate) * up. */
+int specdec_silu_mul(const void* gate_up, void* out, long long T, int intermediate, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

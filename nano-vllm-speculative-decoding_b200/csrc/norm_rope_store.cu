@@ -1,0 +1,293 @@
+// Kernel (4) ctx_store, and the target-side siblings the verify forward needs around kernel (2).
+//
+// Reference behaviour (nano-vllm-speculative-decoding):
+//   DFlashDraftModel.store_context_kv    nanovllm/models/dflash.py:88-96    per draft layer: k, v = split(W_kv c);
+//                                        k = RoPE(k_norm(k)); store_kvcache(k, v, cache[layer], slot_mapping)
+//   Qwen3Attention.forward (q/k part)    nanovllm/models/qwen3.py:77-86     q = q_norm(q), k = k_norm(k),
+//                                        q, k = RoPE(positions, q, k), then Attention stores k, v
+//   RMSNorm.rms_forward / add_rms_forward nanovllm/layers/layernorm.py:16-40  fp32 mean of squares, x * rsqrt(var
+//                                        + eps), cast to the input dtype, times the weight
+//   apply_rotary_emb                     nanovllm/layers/rotary_embedding.py:6-14  (x1, x2) halves in fp32:
+//                                        (x1 cos - x2 sin, x2 cos + x1 sin), cast back
+//   SiluAndMul                           nanovllm/layers/activation.py:8-11  silu(x) * y over the two halves
+//
+// ctx_store design: one launch covers every draft layer.  A warp owns one (token, layer, head) row of 128 dims
+// (lane l holds dims l, l+32, l+64, l+96, so both RoPE partners l and l+64 sit in the same lane): the K row is
+// RMS-normalised with a warp reduction, rotated with the position's cos/sin, and written with the V row to the
+// slot; slot -1 rows are skipped before any load.  The kernel is HBM-bound (bytes: read kv, write cache).
+#include "common.cuh"
+
+#include <math.h>
+
+namespace specdec {
+namespace fused {
+
+constexpr int kHeadDim = 128;
+
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// RMSNorm of one 128-dim head row held as 4 values per lane (dims l, l+32, l+64, l+96), then the weight.
+__device__ __forceinline__ void head_rmsnorm(float (&x)[4], const __nv_bfloat16* weight, int lane, float eps) {
+  float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+  ss = warp_sum_f32(ss);
+  const float r = rsqrtf(ss / kHeadDim + eps);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float w = __bfloat162float(weight[lane + 32 * i]);
+    x[i] = bf16_round(bf16_round(x[i] * r) * w);   // x.to(bf16).mul_(weight) rounds twice
+  }
+}
+
+// RoPE on dims (l, l+64) and (l+32, l+96): cos/sin index = dim % 64.
+__device__ __forceinline__ void head_rope(float (&x)[4], const float* cos_sin, int lane) {
+  const float c0 = cos_sin[lane], s0 = cos_sin[64 + lane];
+  const float c1 = cos_sin[lane + 32], s1 = cos_sin[64 + lane + 32];
+  const float x1a = x[0], x2a = x[2], x1b = x[1], x2b = x[3];
+  x[0] = x1a * c0 - x2a * s0;
+  x[2] = x2a * c0 + x1a * s0;
+  x[1] = x1b * c1 - x2b * s1;
+  x[3] = x2b * c1 + x1b * s1;
+}
+
+struct NormRopeArgs {
+  const __nv_bfloat16* x;       // [layers][T][row] activations: (q heads,) k heads, v heads, 128 dims each
+  long long x_layer_stride, x_row_stride;
+  int T, layers, Hq, Hkv;
+  const __nv_bfloat16* q_norm;  // [128] (Hq > 0)
+  const __nv_bfloat16* k_norm;  // [layers][128]
+  long long k_norm_layer_stride;
+  const float* cos_sin;         // [max_position][128]: cos | sin
+  const long long* positions;   // [T]
+  const int* slot_mapping;      // [T]
+  __nv_bfloat16* k_cache;       // [layers][num_slots][Hkv][128]
+  __nv_bfloat16* v_cache;
+  long long cache_layer_stride, num_slots;
+  __nv_bfloat16* q_out;         // [T][Hq][128]
+  long long max_position;
+  float eps;
+  int* err;
+};
+
+// grid: (ceil(T * (Hq + Hkv) / 8), layers); 8 warps per CTA, one (token, head) row per warp; V rows are copied by
+// the warp that owns the K row of the same head.
+__global__ void __launch_bounds__(256) norm_rope_store_kernel(const NormRopeArgs a) {
+  const int lane = threadIdx.x & 31;
+  const long long item = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int heads = a.Hq + a.Hkv;
+  if (item >= (long long)a.T * heads) return;
+  const int layer = blockIdx.y;
+  const int t = (int)(item / heads);
+  const int hh = (int)(item % heads);
+  const long long pos = a.positions[t];
+  if (pos < 0 || pos >= a.max_position) {
+    if (lane == 0) atomicCAS(a.err, 0, 4);
+    return;
+  }
+  const float* cs = a.cos_sin + pos * kHeadDim;
+  const __nv_bfloat16* row = a.x + layer * a.x_layer_stride + (long long)t * a.x_row_stride;
+  if (hh < a.Hq) {
+    const __nv_bfloat16* src = row + hh * kHeadDim;
+    float x[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) x[i] = __bfloat162float(src[lane + 32 * i]);
+    head_rmsnorm(x, a.q_norm, lane, a.eps);
+    head_rope(x, cs, lane);
+    __nv_bfloat16* dst = a.q_out + ((long long)t * a.Hq + hh) * kHeadDim;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = __float2bfloat16_rn(x[i]);
+    return;
+  }
+  const int h = hh - a.Hq;
+  const long long slot = a.slot_mapping[t];
+  if (slot < 0) return;
+  if (slot >= a.num_slots) {
+    if (lane == 0) atomicCAS(a.err, 0, 3);
+    return;
+  }
+  const __nv_bfloat16* ksrc = row + (a.Hq + h) * kHeadDim;
+  const __nv_bfloat16* vsrc = row + (a.Hq + a.Hkv + h) * kHeadDim;
+  float x[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) x[i] = __bfloat162float(ksrc[lane + 32 * i]);
+  head_rmsnorm(x, a.k_norm + layer * a.k_norm_layer_stride, lane, a.eps);
+  head_rope(x, cs, lane);
+  const long long off = layer * a.cache_layer_stride + (slot * a.Hkv + h) * kHeadDim;
+  __nv_bfloat16* kdst = a.k_cache + off;
+  __nv_bfloat16* vdst = a.v_cache + off;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    kdst[lane + 32 * i] = __float2bfloat16_rn(x[i]);
+    vdst[lane + 32 * i] = vsrc[lane + 32 * i];
+  }
+}
+
+// ---------------------------------------------------------------------------------------- RMSNorm (+ residual)
+// One CTA per token row of `width` bf16 (width % 8 == 0, <= 8192).  With residual: s = x + residual (fp32),
+// residual_out = bf16(s), out = norm(s); without: out = norm(x).
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* x, const __nv_bfloat16* residual,
+                                                      const __nv_bfloat16* weight, __nv_bfloat16* out,
+                                                      __nv_bfloat16* residual_out, int width, float eps) {
+  constexpr int kMaxVec = 4;   // 4 x 8 elements per thread: width <= 256 * 32 = 8192
+  __shared__ float red[8];
+  const long long t = blockIdx.x;
+  const uint4* xv = reinterpret_cast<const uint4*>(x + t * width);
+  const uint4* rv = residual ? reinterpret_cast<const uint4*>(residual + t * width) : nullptr;
+  const int nvec = width / 8;
+  float v[kMaxVec][8];
+  float ss = 0.0f;
+#pragma unroll
+  for (int u = 0; u < kMaxVec; ++u) {
+    const int i = threadIdx.x + u * 256;
+    if (i < nvec) {
+      float a[8];
+      unpack16_bf16(xv[i], a);
+      if (rv) {
+        float r[8];
+        unpack16_bf16(rv[i], r);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) a[e] += r[e];
+        uint4 packed;
+        uint32_t* w = reinterpret_cast<uint32_t*>(&packed);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          __nv_bfloat162 p2 = __floats2bfloat162_rn(a[2 * e], a[2 * e + 1]);
+          w[e] = *reinterpret_cast<uint32_t*>(&p2);
+        }
+        reinterpret_cast<uint4*>(residual_out + t * width)[i] = packed;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        v[u][e] = a[e];
+        ss += a[e] * a[e];
+      }
+    }
+  }
+  ss = warp_sum_f32(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float total = 0.0f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) total += red[w];
+  const float rs = rsqrtf(total / width + eps);
+  const uint4* wv = reinterpret_cast<const uint4*>(weight);
+#pragma unroll
+  for (int u = 0; u < kMaxVec; ++u) {
+    const int i = threadIdx.x + u * 256;
+    if (i < nvec) {
+      float w8[8];
+      unpack16_bf16(wv[i], w8);
+      uint4 packed;
+      uint32_t* wd = reinterpret_cast<uint32_t*>(&packed);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float y0 = bf16_round(bf16_round(v[u][2 * e] * rs) * w8[2 * e]);
+        const float y1 = bf16_round(bf16_round(v[u][2 * e + 1] * rs) * w8[2 * e + 1]);
+        __nv_bfloat162 p2 = __floats2bfloat162_rn(y0, y1);
+        wd[e] = *reinterpret_cast<uint32_t*>(&p2);
+      }
+      reinterpret_cast<uint4*>(out + t * width)[i] = packed;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------- SiLU * mul
+// gate_up [T, 2I] -> out [T, I] = silu(gate) * up, computed in fp32 and rounded once.
+__global__ void __launch_bounds__(256) silu_mul_kernel(const __nv_bfloat16* gate_up, __nv_bfloat16* out, long long T,
+                                                       int I) {
+  const long long nvec_row = I / 8;
+  const long long i = (long long)blockIdx.x * 256 + threadIdx.x;
+  if (i >= T * nvec_row) return;
+  const long long t = i / nvec_row, c = i % nvec_row;
+  const uint4 g = reinterpret_cast<const uint4*>(gate_up + t * 2 * I)[c];
+  const uint4 u = reinterpret_cast<const uint4*>(gate_up + t * 2 * I + I)[c];
+  float gf[8], uf[8];
+  unpack16_bf16(g, gf);
+  unpack16_bf16(u, uf);
+  uint4 packed;
+  uint32_t* wd = reinterpret_cast<uint32_t*>(&packed);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float a0 = gf[2 * e], a1 = gf[2 * e + 1];
+    const float y0 = a0 / (1.0f + expf(-a0)) * uf[2 * e];
+    const float y1 = a1 / (1.0f + expf(-a1)) * uf[2 * e + 1];
+    __nv_bfloat162 p2 = __floats2bfloat162_rn(y0, y1);
+    wd[e] = *reinterpret_cast<uint32_t*>(&p2);
+  }
+  reinterpret_cast<uint4*>(out + t * I)[c] = packed;
+}
+
+}  // namespace fused
+}  // namespace specdec
+
+using namespace specdec;
+
+extern "C" {
+
+int specdec_norm_rope_store(const void* x, long long x_layer_stride, long long x_row_stride, int T, int layers,
+                            int num_q_heads, int num_kv_heads, const void* q_norm, const void* k_norm,
+                            long long k_norm_layer_stride, const float* cos_sin, long long max_position,
+                            const long long* positions, const int* slot_mapping, void* k_cache, void* v_cache,
+                            long long cache_layer_stride, long long num_slots, void* q_out, float eps, int* err,
+                            void* stream) {
+  SPECDEC_CHECK_ARG(x && k_norm && cos_sin && positions && slot_mapping && k_cache && v_cache && err,
+                    "null pointer argument");
+  SPECDEC_CHECK_ARG(T >= 0 && layers >= 1 && layers <= 65535 && num_kv_heads >= 1 && num_q_heads >= 0,
+                    "bad sizes");
+  SPECDEC_CHECK_ARG(num_q_heads == 0 || (q_norm && q_out), "q heads need q_norm and q_out");
+  if (T == 0) return kOk;
+  fused::NormRopeArgs a{};
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.x_layer_stride = x_layer_stride;
+  a.x_row_stride = x_row_stride;
+  a.T = T;
+  a.layers = layers;
+  a.Hq = num_q_heads;
+  a.Hkv = num_kv_heads;
+  a.q_norm = static_cast<const __nv_bfloat16*>(q_norm);
+  a.k_norm = static_cast<const __nv_bfloat16*>(k_norm);
+  a.k_norm_layer_stride = k_norm_layer_stride;
+  a.cos_sin = cos_sin;
+  a.positions = positions;
+  a.slot_mapping = slot_mapping;
+  a.k_cache = static_cast<__nv_bfloat16*>(k_cache);
+  a.v_cache = static_cast<__nv_bfloat16*>(v_cache);
+  a.cache_layer_stride = cache_layer_stride;
+  a.num_slots = num_slots;
+  a.q_out = static_cast<__nv_bfloat16*>(q_out);
+  a.max_position = max_position;
+  a.eps = eps;
+  a.err = err;
+  const long long items = (long long)T * (num_q_heads + num_kv_heads);
+  dim3 grid((unsigned)((items + 7) / 8), (unsigned)layers);
+  fused::norm_rope_store_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  SPECDEC_LAUNCH_CHECK();
+  return kOk;
+}
+
+int specdec_rmsnorm(const void* x, const void* residual, const void* weight, void* out, void* residual_out,
+                    long long T, int width, float eps, void* stream) {
+  SPECDEC_CHECK_ARG(x && weight && out, "null pointer argument");
+  SPECDEC_CHECK_ARG(!residual || residual_out, "residual needs residual_out");
+  SPECDEC_CHECK_ARG(width % 8 == 0 && width <= 8192 && width > 0, "width %d must be a multiple of 8 up to 8192",
+                    width);
+  if (T <= 0) return kOk;
+  fused::rmsnorm_kernel<<<(unsigned)T, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(residual),
+      static_cast<const __nv_bfloat16*>(weight), static_cast<__nv_bfloat16*>(out),
+      static_cast<__nv_bfloat16*>(residual_out), width, eps);
+  SPECDEC_LAUNCH_CHECK();
+  return kOk;
+}
+
+int specdec_silu_mul(const void* gate_up, void* out, long long T, int intermediate, void* stream) {
+  SPECDEC_CHECK_ARG(gate_up && out, "null pointer argument");
+  SPECDEC_CHECK_ARG(intermediate % 8 == 0 && intermediate > 0, "intermediate must be a positive multiple of 8");
+  if (T <= 0) return kOk;
+  const long long n = T * (intermediate / 8);
+  fused::silu_mul_kernel<<<(unsigned)((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(gate_up), static_cast<__nv_bfloat16*>(out), T, intermediate);
+  SPECDEC_LAUNCH_CHECK();
+  return kOk;
+}
+
+}  // extern "C"

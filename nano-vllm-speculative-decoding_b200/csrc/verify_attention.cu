@@ -17,7 +17,7 @@
 // both M = 128 UMMAs with fp32 accumulators in TMEM (S double-buffered, O resident for the whole row).  K and V
 // tiles of 128 keys (half a 256-slot block) arrive by TMA through one tensor map over the whole paged cache
 // (coordinates: dim, head, physical slot), so the block table is a coordinate, not a gather.
-//   warp 0      TMA producer (Q once, then K/V tiles into 2-stage rings)
+//   warp 0      TMA producer (Q once, then K/V tiles into 3-stage rings)
 //   warp 1      TMEM allocator + single-thread MMA issuer
 //   warps 4-7   softmax over keys (one TMEM lane = one key), P^T to shared memory, O rescale, epilogue
 // The softmax is online per query column with lazy rescaling (O is rescaled only when a column's running max
@@ -37,7 +37,7 @@ using namespace sm100;
 constexpr int kHeadDim = 128;
 constexpr int kKeysPerTile = 128;
 constexpr int kCols = 32;              // packed query columns (group x positions)
-constexpr int kStages = 2;             // K ring and V ring depth
+constexpr int kStages = 3;             // K ring and V ring depth
 constexpr int kThreads = 256;
 constexpr int kHalfTileBytes = kKeysPerTile * 128;     // 64 dims x 128 keys bf16 = 16 KB
 constexpr int kTileBytes = 2 * kHalfTileBytes;          // 32 KB
@@ -201,6 +201,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t idesc_o = idesc_bf16_f32(128, kCols, 1, 1);
       const uint32_t tmem_o = tmem + 64;
       bool ok = mbar_wait(&S.q_full, 0, abort, a.err, kErrTimeoutQ);
+      auto issue_s = [&](int t) -> bool {
+        const int stage = t % kStages;
+        if (!mbar_wait(&S.k_full[stage], (t / kStages) & 1, abort, a.err, kErrTimeoutK)) return false;
+        if (t >= 2 && !mbar_wait(&S.s_free[t & 1], ((t - 2) >> 1) & 1, abort, a.err, kErrTimeoutS)) return false;
+        tc_fence_after();
+        const unsigned char* kt = sK + stage * kTileBytes;
+        const uint32_t tmem_s = tmem + (t & 1) * 32;
+#pragma unroll
+        for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+          const int half = kk >> 2, sub = (kk & 3) * 32;
+          const uint64_t adesc = smem_desc(kt + half * kHalfTileBytes + sub, 16, 1024, kSwizzle128B);
+          const uint64_t bdesc = smem_desc(sQ + half * kQHalfBytes + sub, 16, 1024, kSwizzle128B);
+          mma_bf16_ss(tmem_s, adesc, bdesc, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(&S.s_full[t & 1]);
+        mma_commit(&S.k_empty[stage]);
+        return true;
+      };
       auto issue_pv = [&](int t) -> bool {
         const int stage = t % kStages;
         if (!mbar_wait(&S.p_full[t & 1], (t >> 1) & 1, abort, a.err, kErrTimeoutP)) return false;
@@ -218,28 +236,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(&S.v_empty[stage]);
         return true;
       };
+      // Two score tiles run ahead of the softmax: S(t + 2) is issued as soon as PV(t) is, so the softmax of
+      // tile t + 1 never waits for a score MMA issued after the softmax of tile t.
+      if (ok) ok = issue_s(0);
+      if (ok && nt > 1) ok = issue_s(1);
       for (int t = 0; t < nt && ok; ++t) {
-        const int stage = t % kStages;
-        if (!mbar_wait(&S.k_full[stage], (t / kStages) & 1, abort, a.err, kErrTimeoutK)) { ok = false; break; }
-        if (t >= 2 && !mbar_wait(&S.s_free[t & 1], ((t - 2) >> 1) & 1, abort, a.err, kErrTimeoutS)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const unsigned char* kt = sK + stage * kTileBytes;
-        const uint32_t tmem_s = tmem + (t & 1) * 32;
-#pragma unroll
-        for (int kk = 0; kk < kHeadDim / 16; ++kk) {
-          const int half = kk >> 2, sub = (kk & 3) * 32;
-          const uint64_t adesc = smem_desc(kt + half * kHalfTileBytes + sub, 16, 1024, kSwizzle128B);
-          const uint64_t bdesc = smem_desc(sQ + half * kQHalfBytes + sub, 16, 1024, kSwizzle128B);
-          mma_bf16_ss(tmem_s, adesc, bdesc, idesc_s, kk > 0 ? 1u : 0u);
-        }
-        mma_commit(&S.s_full[t & 1]);
-        mma_commit(&S.k_empty[stage]);
-        if (t >= 1 && !issue_pv(t - 1)) { ok = false; break; }
+        ok = issue_pv(t);
+        if (ok && t + 2 < nt) ok = issue_s(t + 2);
       }
-      if (ok) issue_pv(nt - 1);
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ softmax / correction / epilogue

@@ -45,6 +45,12 @@ SIGNATURES = {
     "specdec_paged_attention": (_c_int, [_c_void_p, _c_ll, _c_ll, _c_int, _c_int, _c_int, _c_void_p, _c_void_p, _c_ll,
                                          _c_int, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_int, _c_void_p, _c_int,
                                          _c_int, _c_float, _c_int, _c_void_p, _c_ll, _c_void_p, _c_void_p]),
+    "specdec_norm_rope_store": (_c_int, [_c_void_p, _c_ll, _c_ll, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_void_p,
+                                         _c_ll, _c_void_p, _c_ll, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_ll,
+                                         _c_ll, _c_void_p, _c_float, _c_void_p, _c_void_p]),
+    "specdec_rmsnorm": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_ll, _c_int, _c_float,
+                                 _c_void_p]),
+    "specdec_silu_mul": (_c_int, [_c_void_p, _c_void_p, _c_ll, _c_int, _c_void_p]),
 }
 
 _lib = None

@@ -1,0 +1,50 @@
+"""DFlash / DSpark draft context store (kernel 4, "ctx_store") on libspecdec_b200.so.
+
+Reference: DFlashDraftModel.store_context_kv (nanovllm/models/dflash.py:88-96), called by
+DFlashDrafter.after_verify (nanovllm/engine/speculative.py:326-337) for every verified position:
+
+    for layer in draft layers:
+        k, v = F.linear(features, W_kv[layer]).split(...)
+        k = RoPE(positions, k_norm[layer](k))
+        store_kvcache(k, v, kv_cache[0, layer], kv_cache[1, layer], slot_mapping)
+
+Here the five per-layer projections are one cuBLAS GEMM against the layers' stacked W_kv (a plain library GEMM),
+and every layer's k_norm + RoPE + paged scatter of K and V is a single kernel launch over (token, layer, head)
+rows (specdec_norm_rope_store with no query heads).  Slot -1 rows (padding) are skipped before any load.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import check, ptr, require_cuda, stream_of
+from .fused import err_word
+
+
+def stacked_kv_weight(layer_kv_weights: list[torch.Tensor]) -> torch.Tensor:
+    """[layers * 2 * Hkv * 128, hidden]: each draft layer's K then V rows of its packed qkv_proj
+    (qkv_proj.weight[q_size:] in dflash.py:92), stacked so one GEMM projects every layer."""
+    return torch.cat(layer_kv_weights, dim=0).contiguous()
+
+
+def store_context_kv(features: torch.Tensor, w_kv_stacked: torch.Tensor, k_norm: torch.Tensor,
+                     cos_sin: torch.Tensor, positions: torch.Tensor, slot_mapping: torch.Tensor,
+                     kv_cache: torch.Tensor, eps: float, *, kv_out: torch.Tensor | None = None) -> None:
+    """dflash.py:88-96 for all layers.  features [T, hidden] bf16; w_kv_stacked [L * 2 * Hkv * 128, hidden];
+    k_norm [L, 128] bf16; cos_sin [max_position, 128] fp32; positions [T] int64; slot_mapping [T] int32;
+    kv_cache [2, L, blocks, block_size, Hkv, 128] bf16 (the drafter's cache, sharing the target's block ids)."""
+    device = require_cuda(features, w_kv_stacked, k_norm, cos_sin, positions, slot_mapping, kv_cache)
+    T = features.shape[0]
+    _, layers, blocks, block_size, num_kv_heads, head_dim = kv_cache.shape
+    if head_dim != 128 or k_norm.shape != (layers, 128):
+        raise ValueError("ctx_store expects 128-dim heads and one k_norm row per layer")
+    width = 2 * num_kv_heads * head_dim
+    if w_kv_stacked.shape[0] != layers * width:
+        raise ValueError(f"stacked W_kv has {w_kv_stacked.shape[0]} rows, expected {layers * width}")
+    kv = torch.matmul(features, w_kv_stacked.t(), out=kv_out)        # [T, L * 2 * Hkv * 128] (cuBLAS)
+    k_cache, v_cache = kv_cache[0], kv_cache[1]
+    num_slots = blocks * block_size
+    check(_lib.lib().specdec_norm_rope_store(
+        ptr(kv), width, kv.stride(0), T, layers, 0, num_kv_heads, None, ptr(k_norm.contiguous()), 128,
+        ptr(cos_sin), cos_sin.shape[0], ptr(positions), ptr(slot_mapping.to(torch.int32)), ptr(k_cache),
+        ptr(v_cache), k_cache.stride(0), num_slots, None, float(eps), ptr(err_word(device)), stream_of(device)))

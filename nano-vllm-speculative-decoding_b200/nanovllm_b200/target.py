@@ -1,0 +1,151 @@
+"""A Qwen3-architecture target for the verify forward of a speculative round, on B200.
+
+Mirrors the reference's target model and verification (nano-vllm-speculative-decoding):
+    Qwen3DecoderLayer / Qwen3Model.forward     nanovllm/models/qwen3.py:133-213  (aux-layer export :174-191)
+    compute_logits (all positions)             nanovllm/models/qwen3.py:221-226
+    SpeculativeDecoder.verify_logits / graphs  nanovllm/engine/speculative.py:471-582
+    verify_varlen_metadata                     nanovllm/engine/batch_metadata.py:149-181
+
+The projections and the LM head are plain cuBLAS GEMMs (torch.matmul); everything between them runs on this
+package's kernels: RMSNorm(+residual), q/k norm + RoPE + paged K/V store, paged verify attention (kernel 2) and
+SiLU*mul.  Weights are random-initialised (no checkpoints here); the paged KV cache is [2, layers, blocks + 1,
+block_size, Hkv, 128] with the last block the zeroed pad block, as ModelRunner.allocate_kv_cache lays it out
+(nanovllm/engine/model_runner.py:142-169).  A whole verification (forward + logits) is captured as one CUDA
+graph per token count, replayed with the round's metadata copied into its static buffers.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import attention, fused
+
+
+@dataclass
+class Qwen3Shape:
+    hidden: int = 4096
+    layers: int = 36
+    heads: int = 32
+    kv_heads: int = 8
+    head_dim: int = 128
+    intermediate: int = 12288
+    vocab: int = 151936
+    eps: float = 1e-6
+    rope_theta: float = 1000000.0
+    max_position: int = 40960
+    aux_layer_ids: tuple[int, ...] = (1, 9, 17, 25, 33)    # DSpark / DFlash Qwen3-8B target_layer_ids
+
+
+class Qwen3Target:
+    def __init__(self, shape: Qwen3Shape, device: torch.device, num_blocks: int, block_size: int = 256,
+                 seed: int = 0, init_scale: float = 0.02):
+        self.shape = s = shape
+        self.device = device
+        self.block_size = block_size
+        self.num_blocks = num_blocks
+        self.pad_block_id = num_blocks
+        g = torch.Generator(device=device).manual_seed(seed)
+        bf = torch.bfloat16
+
+        def rand(*dims, scale=init_scale):
+            return (torch.randn(*dims, device=device, generator=g, dtype=torch.float32) * scale).to(bf)
+
+        def norm_weight(n):
+            return (1.0 + 0.05 * torch.randn(n, device=device, generator=g)).to(bf)
+
+        qkv_rows = (s.heads + 2 * s.kv_heads) * s.head_dim
+        self.embed = rand(s.vocab, s.hidden)
+        self.layers = []
+        for _ in range(s.layers):
+            self.layers.append(dict(
+                w_qkv=rand(qkv_rows, s.hidden), w_o=rand(s.hidden, s.heads * s.head_dim),
+                w_gate_up=rand(2 * s.intermediate, s.hidden), w_down=rand(s.hidden, s.intermediate),
+                in_norm=norm_weight(s.hidden), post_norm=norm_weight(s.hidden),
+                q_norm=norm_weight(s.head_dim), k_norm=norm_weight(s.head_dim)))
+        self.final_norm = norm_weight(s.hidden)
+        self.lm_head = rand(s.vocab, s.hidden)
+        self.kv_cache = torch.zeros(2, s.layers, num_blocks + 1, block_size, s.kv_heads, s.head_dim, dtype=bf,
+                                    device=device)
+        self.cos_sin = fused.rope_cache(s.head_dim, s.max_position, s.rope_theta, device)
+        self.scale = s.head_dim ** -0.5
+        # error words / workspaces exist before any graph capture
+        fused.err_word(device)
+        attention.reset_device_error(device)
+        self.graphs: dict[int, tuple[torch.cuda.CUDAGraph, dict]] = {}
+        self.graph_pool = None
+
+    # ------------------------------------------------------------------ eager forward
+    def forward(self, input_ids, positions, slot_mapping, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, block_tables,
+                aux_out: torch.Tensor | None = None) -> torch.Tensor:
+        """qwen3.py:201-213: hidden states [T, hidden] after the final norm; aux_out [T, 5 * hidden] receives the
+        aux layers' outputs (hidden + residual)."""
+        s = self.shape
+        T = input_ids.shape[0]
+        h = torch.nn.functional.embedding(input_ids, self.embed)
+        residual = None
+        for layer_id, w in enumerate(self.layers):
+            if residual is None:
+                x, residual = fused.rmsnorm(h, w["in_norm"], s.eps), h
+            else:
+                x, residual = fused.rmsnorm(h, w["in_norm"], s.eps, residual=residual)
+            qkv = torch.matmul(x, w["w_qkv"].t())
+            q = fused.qk_norm_rope_store(qkv, s.heads, s.kv_heads, w["q_norm"], w["k_norm"], self.cos_sin, positions,
+                                         slot_mapping, self.kv_cache[0, layer_id], self.kv_cache[1, layer_id], s.eps)
+            o = attention.paged_attention(q, self.kv_cache[0, layer_id], self.kv_cache[1, layer_id], block_tables,
+                                          self.scale, cu_seqlens_q=cu_seqlens_q, cu_seqlens_k=cu_seqlens_k,
+                                          max_seqlen_q=max_seqlen_q)
+            h = torch.matmul(o.view(T, -1), w["w_o"].t())
+            x, residual = fused.rmsnorm(h, w["post_norm"], s.eps, residual=residual)
+            h = torch.matmul(fused.silu_and_mul(torch.matmul(x, w["w_gate_up"].t())), w["w_down"].t())
+            if aux_out is not None and layer_id in s.aux_layer_ids:
+                seg = s.aux_layer_ids.index(layer_id)
+                aux_out[:, seg * s.hidden:(seg + 1) * s.hidden].copy_(h + residual)
+        h, _ = fused.rmsnorm(h, self.final_norm, s.eps, residual=residual)
+        return h
+
+    def compute_logits(self, hidden: torch.Tensor) -> torch.Tensor:
+        """qwen3.py:221-226 with all_logits: [T, vocab] bf16."""
+        return torch.matmul(hidden, self.lm_head.t())
+
+    # ------------------------------------------------------------------ graphs
+    def static_buffers(self, num_rows: int, num_tokens: int, width: int) -> dict:
+        d = self.device
+        return dict(input_ids=torch.zeros(num_tokens, dtype=torch.int64, device=d),
+                    positions=torch.zeros(num_tokens, dtype=torch.int64, device=d),
+                    slot_mapping=torch.full((num_tokens,), -1, dtype=torch.int32, device=d),
+                    cu_seqlens_q=torch.zeros(num_rows + 1, dtype=torch.int32, device=d),
+                    cu_seqlens_k=torch.zeros(num_rows + 1, dtype=torch.int32, device=d),
+                    block_tables=torch.full((num_rows, width), self.pad_block_id, dtype=torch.int32, device=d))
+
+    def capture(self, num_rows: int, num_tokens: int, width: int, max_seqlen_q: int,
+                load_padding) -> dict:
+        """Captures forward + logits for one (rows, tokens) shape; load_padding(buffers) fills a valid
+        all-padding metadata first (speculative.py:559-571).  Returns the graph's buffers (with "logits")."""
+        buffers = self.static_buffers(num_rows, num_tokens, width)
+        load_padding(buffers)
+
+        def body():
+            hidden = self.forward(buffers["input_ids"], buffers["positions"], buffers["slot_mapping"],
+                                  buffers["cu_seqlens_q"], buffers["cu_seqlens_k"], max_seqlen_q,
+                                  buffers["block_tables"])
+            return self.compute_logits(hidden)
+
+        body()   # warm-up (also configures the kernels' shared-memory attributes)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, self.graph_pool):
+            buffers["logits"] = body()
+        if self.graph_pool is None:
+            self.graph_pool = graph.pool()
+        torch.cuda.synchronize()
+        self.graphs[num_tokens] = (graph, buffers)
+        return buffers
+
+    def replay(self, num_tokens: int) -> torch.Tensor:
+        graph, buffers = self.graphs[num_tokens]
+        graph.replay()
+        return buffers["logits"]
+
+    def close(self) -> None:
+        self.graphs.clear()

@@ -20,7 +20,10 @@ from pathlib import Path
 from types import SimpleNamespace
 
 import numpy as np
-import torch
+
+# The reference's RMSNorm / RoPE / SiLU are torch.compile'd methods; the fixtures use their eager bodies.
+os.environ.setdefault("TORCHDYNAMO_DISABLE", "1")
+import torch  # noqa: E402
 
 HERE = Path(__file__).resolve().parent
 
@@ -201,6 +204,69 @@ def greedy_cases(ss) -> dict[str, np.ndarray]:
     return out
 
 
+def ctx_store_cases(reference: Path) -> dict[str, np.ndarray]:
+    """DFlashDraftModel.store_context_kv (dflash.py:88-96) on a small random draft: 2 layers, hidden 256, 4/2
+    heads of 128, bf16, with the CPU store_kvcache stand-in (tests/fake_paged_attention.py)."""
+    import torch.distributed as dist
+    from nanovllm.layers import attention as ref_attention
+    from nanovllm.models.dflash import DFlashDraftModel
+    import fake_paged_attention
+    if not dist.is_initialized():
+        dist.init_process_group("gloo", init_method="tcp://127.0.0.1:29517", world_size=1, rank=0)
+    config = SimpleNamespace(block_size=7, mask_token_id=99, target_layer_ids=[0, 1], vocab_size=128,
+                             hidden_size=256, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                             head_dim=128, rms_norm_eps=1e-6, intermediate_size=512, hidden_act="silu",
+                             max_position_embeddings=4096, markov_rank=0, enable_confidence_head=False,
+                             attention_bias=False, rope_theta=1000000, rope_scaling=None)
+    torch.manual_seed(0)
+    default_dtype = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        model = DFlashDraftModel(config)
+    finally:
+        torch.set_default_dtype(default_dtype)
+    with torch.no_grad():
+        for name, param in model.named_parameters():
+            if name.endswith("norm.weight"):
+                param.copy_(1.0 + 0.1 * torch.randn(param.shape))
+            else:
+                param.copy_(0.05 * torch.randn(param.shape))
+    blocks, block_size, hkv = 4, 256, 2
+    kv_cache = torch.zeros(2, 2, blocks, block_size, hkv, 128, dtype=torch.bfloat16)
+    for layer_id, layer in enumerate(model.layers):
+        layer.self_attn.attn.k_cache = kv_cache[0, layer_id]
+        layer.self_attn.attn.v_cache = kv_cache[1, layer_id]
+    T = 40
+    g = torch.Generator().manual_seed(3)
+    features = torch.randn(T, 256, generator=g).bfloat16()
+    positions = torch.randint(0, 3000, (T,), generator=g)
+    slots = torch.randperm(blocks * block_size, generator=g)[:T].to(torch.int32)
+    slots[[5, 17]] = -1                                   # padding rows are skipped
+    original = ref_attention.store_kvcache
+    ref_attention.store_kvcache = fake_paged_attention.store_kvcache
+    try:
+        with torch.no_grad():
+            model.store_context_kv(features, positions, slots)
+    finally:
+        ref_attention.store_kvcache = original
+    attn = model.layers[0].self_attn
+    model.requires_grad_(False)
+    w_kv = torch.cat([layer.self_attn.qkv_proj.weight[attn.q_size:] for layer in model.layers])
+    k_norm = torch.stack([layer.self_attn.k_norm.weight for layer in model.layers])
+    out = {"ctx/features": features.float().numpy(), "ctx/w_kv": w_kv.float().numpy(),
+           "ctx/k_norm": k_norm.float().numpy(), "ctx/positions": positions.numpy(),
+           "ctx/slots": slots.numpy(), "ctx/kv_cache": kv_cache.float().numpy(),
+           "ctx/eps": np.array(1e-6), "ctx/rope_base": np.array(1000000.0), "ctx/max_position": np.array(4096)}
+    # the target's q path: q_norm + RoPE of random queries (qwen3.py:77-84)
+    q = torch.randn(T, 4, 128, generator=g).bfloat16()
+    with torch.no_grad():
+        qn = attn.q_norm(q)
+        q_rot, _ = attn.rotary_emb(positions, qn, qn.clone())
+    out.update({"ctx/q": q.float().numpy(), "ctx/q_norm": attn.q_norm.weight.float().numpy(),
+                "ctx/q_out": q_rot.float().numpy()})
+    return out
+
+
 def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__)
     default_ref = os.environ.get("SPECDEC_REFERENCE", str(HERE.parents[2] / "reference"))
@@ -214,6 +280,9 @@ def main() -> int:
     fixtures.update(greedy_cases(ss))
     np.savez_compressed(HERE / "sampler.npz", **fixtures)
     print(f"wrote {len(fixtures)} arrays to {HERE / 'sampler.npz'}")
+    ctx = ctx_store_cases(Path(args.reference))
+    np.savez_compressed(HERE / "ctx_store.npz", **ctx)
+    print(f"wrote {len(ctx)} arrays to {HERE / 'ctx_store.npz'}")
     return 0
 
 
