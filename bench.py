@@ -48,7 +48,7 @@ def parse_args():
     p.add_argument("--batch", type=int, default=64)
     p.add_argument("--ctx", type=int, default=1000, help="mean context length (tokens before the verified ones)")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--kernel", choices=["attention", "accept"], default=None,
+    p.add_argument("--kernel", choices=["attention", "accept", "accept_topk", "markov", "ctx_store"], default=None,
                    help="time one kernel alone on its BASELINE config (attention: config 2, accept: config 3's "
                         "logits) instead of the round; used for profiling")
     return p.parse_args()
@@ -314,13 +314,54 @@ def run_kernel(args) -> int:
             attention.paged_attention(q, kc, vc, tables, D ** -0.5, cu_seqlens_q=cu_q, cu_seqlens_k=cu_k,
                                       max_seqlen_q=8)
         algorithmic = sum(k_lens) * Hkv * D * 2 * 2 + 2 * R * 8 * H * D * 2
+    elif args.kernel == "markov":
+        # config 4's drafter: 64 rows x 7 in-block steps, V = 151936, rank-256 Markov head, top_k 128 (192 candidates)
+        from nanovllm_b200 import spec_sampler as S
+        from nanovllm_b200.markov import MarkovHeadWeights, markov_rows, num_candidates
+        B, k, r = 64, 7, 256
+        gg = torch.Generator(device=device).manual_seed(0)
+        logits = (torch.randn(B, k, V, device=device, generator=gg) * 2).bfloat16()
+        head = MarkovHeadWeights((torch.randn(V, r, device=device, generator=gg) * 0.1).bfloat16(),
+                                 (torch.randn(V, r, device=device, generator=gg) * 0.1).bfloat16())
+        samp = S.sampling_tensors([SimpleNamespace(temperature=1.0, top_k=128, top_p=1.0)] * B, device)
+        cand = num_candidates(samp.max_top_k, samp.all_top_k, V)
+        noise = torch.empty(B, k, cand, device=device).exponential_(generator=gg).clamp_min_(1e-10)
+        prev = torch.randint(V, (B,), device=device, generator=gg)
+        drafts = torch.empty(B, k, dtype=torch.int64, device=device)
+        probs = torch.empty(B, k, V, device=device)
+
+        def fn():
+            markov_rows(logits, prev, samp, noise, drafts, probs, cand, head)
+        # per step: W2 (77.8 MB) + the row's logits (19.4 MB); once: the q zero-fill (272 MB)
+        algorithmic = k * (V * r * 2 + B * V * 2) + B * k * V * 4
+    elif args.kernel == "ctx_store":
+        # config 4's ctx_store: T = 288 verified tokens, 5 draft layers, hidden 4096, 8 KV heads of 128
+        from nanovllm_b200.dflash import store_context_kv
+        from nanovllm_b200.fused import rope_cache
+        T, layers, hidden, hkv, bs = 288, 5, 4096, 8, 256
+        gg = torch.Generator(device=device).manual_seed(0)
+        features = torch.randn(T, hidden, device=device, generator=gg).bfloat16()
+        w = (torch.randn(layers * 2 * hkv * 128, hidden, device=device, generator=gg) * 0.02).bfloat16()
+        k_norm = torch.ones(layers, 128, device=device).bfloat16()
+        cos_sin = rope_cache(128, 8192, 1000000.0, device)
+        positions = torch.randint(0, 8192, (T,), device=device, generator=gg)
+        slots = torch.randperm(64 * 16 * bs, device=device, generator=gg)[:T].to(torch.int32)
+        cache = torch.zeros(2, layers, 64 * 16, bs, hkv, 128, dtype=torch.bfloat16, device=device)
+        kv = torch.empty(T, layers * 2 * hkv * 128, dtype=torch.bfloat16, device=device)
+
+        def fn():
+            store_context_kv(features, w, k_norm, cos_sin, positions, slots, cache, 1e-6, kv_out=kv)
+        # weights (GEMM) + features + projection write/read + cache writes
+        algorithmic = w.numel() * 2 + features.numel() * 2 + 2 * kv.numel() * 2 + T * layers * 2 * hkv * 128 * 2
     else:
         from nanovllm_b200 import spec_sampler as S
         B = 64
         logits = (torch.randn(B * 8, V, device=device) * 3).bfloat16()
         q = torch.softmax(torch.randn(B, 7, V, device=device), -1)
         drafts = torch.randint(V, (B, 7), device=device)
-        samp = S.sampling_tensors([SimpleNamespace(temperature=1.0, top_k=0, top_p=1.0)] * B, device)
+        params = (0.7, 20, 0.8) if args.kernel == "accept_topk" else (1.0, 0, 1.0)   # protocol sampling
+        samp = S.sampling_tensors([SimpleNamespace(temperature=params[0], top_k=params[1], top_p=params[2])] * B,
+                                  device)
         gen = torch.Generator(device=device).manual_seed(0)
 
         def fn():

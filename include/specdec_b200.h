@@ -94,6 +94,20 @@ int specdec_paged_attention(const void* q, long long T, long long q_row_stride, 
                             int max_seqlen_q, float softmax_scale, int causal, void* out, long long out_row_stride,
                             int* err, void* stream);
 
+/* ------------------------------------------------------------------------------------------ kernel 3: Markov rows */
+/* One row step of DFlashDrafter._markov_rows (nanovllm/engine/speculative.py:163-184) for every batch row: with
+ * row_logits = logits[:, row] + bias (bias = markov_head(prev), [B, V]; rounded to bf16 when round_bf16):
+ * greedy -> argmax; else the top `candidates` values (ties by ascending token id), probs_from_logits over them
+ * with per-row temperature / top_k / top_p (spec_sampler.py:65-96), race against noise[b, row, :candidates]
+ * (noise [B, k, noise_width]), q scattered into probs [B, k, V] (zeroed by the caller once per call).  Writes
+ * drafts[b, row], prev_out[b] and, with w1 [V, rank] bf16, e_next[b] = w1[prev] (the next step's embedding).
+ * logits [B, k, V] and bias of dtype codes as above.  Limits: candidates <= 1024. */
+int specdec_markov_step(const void* logits, int logits_dtype, const void* bias, int bias_dtype, int B, int k, int V,
+                        int row, int candidates, int greedy, int round_bf16, const float* temperature,
+                        const long long* top_k, const float* top_p, int max_top_k, int has_top_p, const float* noise,
+                        int noise_width, long long* drafts, float* probs, long long* prev_out, const void* w1,
+                        int rank, void* e_next, int* err, void* stream);
+
 /* ------------------------------------------------------------------------------------------ kernel 4: ctx_store */
 /* DFlashDraftModel.store_context_kv (nanovllm/models/dflash.py:88-96) for every draft layer in one launch, and
  * the target's q_norm / k_norm + RoPE + store_kvcache (nanovllm/models/qwen3.py:77-86, attention.py:62-63).

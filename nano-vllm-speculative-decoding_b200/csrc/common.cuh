@@ -128,6 +128,16 @@ __device__ __forceinline__ float warp_sum_f32(float v) {
   return v;
 }
 
+// Histogram add aggregated over the warp: lanes whose (active, bin) agree add once with their count.  Random
+// logits concentrate radix digits in a few bins, where per-lane shared atomics would serialise.  Must be called
+// by all 32 lanes.
+__device__ __forceinline__ void warp_hist_add(unsigned* hist, unsigned bin, bool active) {
+  const unsigned tag = active ? bin : 0xffffffffu;
+  const unsigned peers = __match_any_sync(0xffffffffu, tag);
+  const int leader = __ffs(peers) - 1;
+  if (active && (threadIdx.x & 31) == leader) atomicAdd(&hist[bin], (unsigned)__popc(peers));
+}
+
 // Device properties the library needs (cached per device on first use).
 struct DeviceInfo {
   int sm_count;

@@ -1,0 +1,343 @@
+// Kernel (3): DSpark's in-block Markov row sampling, one row step at a time, for sm_100a.
+//
+// Reference (nano-vllm-speculative-decoding, nanovllm/engine/speculative.py:163-184, DFlashDrafter._markov_rows):
+//   for row in range(k):
+//       row_logits = logits[:, row] + markov_head(prev)                 (bf16 add, rounded)
+//       greedy:      prev = argmax(row_logits)
+//       candidates:  values, ids = row_logits.topk(C)                    (C = max_top_k + 64, every row truncates)
+//                    probs = probs_from_logits(values, sampling)         (temperature, top-k with ties, top-p)
+//                    prev = ids[race(probs, noise[:, row])]              (argmax probs / noise, first index)
+//                    draft_probs[:, row].scatter_(-1, ids, probs)
+//       drafts[:, row] = prev
+// markov_head(prev) = W2 . W1[prev] is a plain GEMM [B, r] x [r, V] left to cuBLAS between steps; this kernel
+// does everything else of a step for every row at once and writes the next step's W1[prev] rows.
+//
+// Design: one 512-thread CTA per batch row (the rows of a step are independent; the steps are not).  The biased
+// row (V bf16 logits + V bias values) is re-read from L2 by every pass: a 12-bit and a 4-bit radix pass on the
+// bf16 ordered key (warp-aggregated histogram atomics) find the C-th largest value, one pass collects the values above it, one warp-ordered pass takes
+// the tied values by ascending token id (ballot ranks), then a bitonic sort of <= 1024 64-bit keys (value desc,
+// id asc) orders the candidates.  The candidate softmax / truncation / race run in shared memory.  Candidate
+// order among equal values is ascending token id (torch.topk leaves it unspecified).
+#include "common.cuh"
+
+#include <math.h>
+
+namespace specdec {
+namespace markov {
+
+constexpr int kThreads = 512;
+constexpr int kWarps = kThreads / 32;
+constexpr int kMaxCand = 1024;
+
+struct Args {
+  const void* logits;       // [B, k, V] (dtype ldt)
+  int ldt;
+  const void* bias;         // [B, V] (dtype bdt) this step's Markov bias
+  int bdt;
+  int B, k, V, j, C, greedy, round_bf16;
+  const float* temperature; // [B]
+  const long long* top_k;   // [B]
+  const float* top_p;       // [B] or null
+  int max_top_k, has_top_p;
+  const float* noise;       // [B, k, noise_width]
+  int noise_width;
+  long long* drafts;        // [B, k]
+  float* probs;             // [B, k, V] or null (greedy)
+  long long* prev_out;      // [B]
+  const __nv_bfloat16* w1;  // [V, rank] or null
+  int rank;
+  __nv_bfloat16* e_next;    // [B, rank]
+  int* err;
+};
+
+__device__ __forceinline__ float load_any(const void* p, int dt, long long i) {
+  if (dt == kF32) return reinterpret_cast<const float*>(p)[i];
+  if (dt == kBF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  return __half2float(reinterpret_cast<const __half*>(p)[i]);
+}
+
+__device__ __forceinline__ float row_value(const Args& a, long long lrow, long long brow, int v) {
+  float x = load_any(a.logits, a.ldt, lrow + v) + load_any(a.bias, a.bdt, brow + v);
+  if (a.round_bf16) x = __bfloat162float(__float2bfloat16_rn(x));
+  return x;
+}
+
+// 1-based rank `rank` among the counted elements: digit d with above(d) < rank <= above(d) + hist[d].
+__device__ void pick_digit(const unsigned* hist, int nbins, int rank, int* s_digit, int* s_above) {
+  __shared__ int warp_tot[kWarps];
+  const int per = nbins / kThreads > 0 ? nbins / kThreads : 1;
+  const int owners = nbins / per;
+  int local = 0;
+  if (threadIdx.x < owners)
+    for (int i = 0; i < per; ++i) local += hist[threadIdx.x * per + i];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int n = __shfl_down_sync(0xffffffffu, incl, o);
+    if (lane + o < 32) incl += n;
+  }
+  if (lane == 0) warp_tot[warp] = incl;
+  __syncthreads();
+  int above = incl - local;
+  for (int w = warp + 1; w < kWarps; ++w) above += warp_tot[w];
+  if (threadIdx.x < owners) {
+    for (int i = per - 1; i >= 0; --i) {
+      const int h = hist[threadIdx.x * per + i];
+      if (above < rank && rank <= above + h) {
+        *s_digit = threadIdx.x * per + i;
+        *s_above = above;
+      }
+      above += h;
+    }
+  }
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kThreads) markov_step_kernel(const Args a) {
+  __shared__ unsigned hist[4096];
+  __shared__ unsigned long long cand[kMaxCand];
+  __shared__ float cprob[kMaxCand];
+  __shared__ int s_digit, s_above, s_cnt, s_prev;
+  __shared__ int warp_ties[kWarps], warp_base[kWarps];
+  __shared__ unsigned long long s_red[kWarps];
+  __shared__ float s_thr, s_z;
+
+  const int b = blockIdx.x;
+  const int V = a.V;
+  const long long lrow = ((long long)b * a.k + a.j) * V;
+  const long long brow = (long long)b * V;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+
+  if (a.greedy) {
+    unsigned long long best = 0ull;
+    for (int v = threadIdx.x; v < V; v += kThreads) {
+      const unsigned long long key = argmax_key(row_value(a, lrow, brow, v), (unsigned)v);
+      best = key > best ? key : best;
+    }
+    best = warp_max_u64(best);
+    if (lane == 0) s_red[warp] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      unsigned long long m = 0ull;
+      for (int w = 0; w < kWarps; ++w) m = s_red[w] > m ? s_red[w] : m;
+      s_prev = (int)argmax_key_index(m);
+    }
+    __syncthreads();
+  } else {
+    const int C = a.C;
+    // ---- radix select of the C-th largest ordered key
+    unsigned prefix = 0, pmask = 0;
+    int rank = C;
+    const int npass = a.round_bf16 ? 2 : 3;
+    const int shifts_bf[2] = {20, 16}, widths_bf[2] = {12, 4};
+    const int shifts_f[3] = {20, 8, 0}, widths_f[3] = {12, 12, 8};
+    for (int p = 0; p < npass; ++p) {
+      const int shift = a.round_bf16 ? shifts_bf[p] : shifts_f[p];
+      const int width = a.round_bf16 ? widths_bf[p] : widths_f[p];
+      const int nb = 1 << width;
+      for (int i = threadIdx.x; i < nb; i += kThreads) hist[i] = 0;
+      __syncthreads();
+      for (int v0 = threadIdx.x - lane; v0 < V; v0 += kThreads) {   // warp-uniform trip count
+        const int v = v0 + lane;
+        bool hit = false;
+        unsigned bin = 0;
+        if (v < V) {
+          const unsigned key = ordered_key(row_value(a, lrow, brow, v));
+          hit = (key & pmask) == prefix;
+          bin = (key >> shift) & (nb - 1);
+        }
+        warp_hist_add(hist, bin, hit);
+      }
+      __syncthreads();
+      pick_digit(hist, nb, rank, &s_digit, &s_above);
+      prefix |= (unsigned)s_digit << shift;
+      pmask |= (unsigned)(nb - 1) << shift;
+      rank -= s_above;
+      __syncthreads();
+    }
+    // bf16 values: the low 16 key bits follow from the sign (0 for positive, all ones for negative)
+    const unsigned key_c = a.round_bf16 ? (prefix | ((prefix & 0x80000000u) ? 0u : 0xffffu)) : prefix;
+    const int need_ties = rank;          // tied values to take, by ascending id
+    const int n_gt = C - rank;
+    // ---- values above the C-th (any order) and per-warp tie counts over contiguous id ranges
+    if (threadIdx.x == 0) s_cnt = 0;
+    __syncthreads();
+    const int span = ((V + kWarps - 1) / kWarps + 31) / 32 * 32;
+    const int lo = warp * span, hi = min(V, lo + span);
+    int ties = 0;
+    for (int base = lo; base < hi; base += 32) {
+      const int v = base + lane;
+      bool tie = false;
+      if (v < hi) {
+        const unsigned key = ordered_key(row_value(a, lrow, brow, v));
+        if (key > key_c) {
+          const int slot = atomicAdd(&s_cnt, 1);
+          if (slot < kMaxCand) cand[slot] = (static_cast<unsigned long long>(key) << 32) | (0xffffffffu - v);
+        }
+        tie = key == key_c;
+      }
+      ties += __popc(__ballot_sync(0xffffffffu, tie));
+    }
+    if (lane == 0) warp_ties[warp] = ties;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int run = 0;
+      for (int w = 0; w < kWarps; ++w) {
+        warp_base[w] = run;
+        run += warp_ties[w];
+      }
+    }
+    __syncthreads();
+    // ---- the first need_ties tied values by ascending id
+    if (need_ties > 0 && warp_base[warp] < need_ties) {
+      int seen = warp_base[warp];
+      for (int base = lo; base < hi && seen < need_ties; base += 32) {
+        const int v = base + lane;
+        bool tie = false;
+        if (v < hi) tie = ordered_key(row_value(a, lrow, brow, v)) == key_c;
+        const unsigned mask = __ballot_sync(0xffffffffu, tie);
+        const int r = seen + __popc(mask & ((1u << lane) - 1u));
+        if (tie && r < need_ties) cand[n_gt + r] = (static_cast<unsigned long long>(key_c) << 32) | (0xffffffffu - v);
+        seen += __popc(mask);
+      }
+    }
+    // ---- sort descending (value desc, id asc); pad with 0 keys
+    int P = 1;
+    while (P < C) P <<= 1;
+    for (int i = C + threadIdx.x; i < P; i += kThreads) cand[i] = 0ull;
+    __syncthreads();
+    for (int size = 2; size <= P; size <<= 1) {
+      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+        for (int i = threadIdx.x; i < P; i += kThreads) {
+          const int jx = i ^ stride;
+          if (jx > i) {
+            const bool desc = (i & size) == 0;
+            const unsigned long long ci = cand[i], cj = cand[jx];
+            if (desc ? (ci < cj) : (ci > cj)) { cand[i] = cj; cand[jx] = ci; }
+          }
+        }
+        __syncthreads();
+      }
+    }
+    // ---- probs_from_logits over the C candidates (spec_sampler.py:65-96 on a [C] row)
+    const float temp = a.temperature[b];
+    if (threadIdx.x == 0) {
+      const int nc = a.max_top_k < C ? a.max_top_k : C;
+      const long long tk = a.top_k ? a.top_k[b] : 0;
+      float thr = -INFINITY;
+      if (a.max_top_k > 0 && tk > 0) {
+        const int eff_k = (int)tk;
+        const int kidx = (eff_k - 1) < (nc - 1) ? (eff_k - 1) : (nc - 1);
+        auto scaled = [&](int i) { return __fdiv_rn(key_to_float((unsigned)(cand[i] >> 32)), temp); };
+        thr = scaled(kidx);
+        if (a.has_top_p) {
+          const float tp = a.top_p[b];
+          const int kk = eff_k < nc ? eff_k : nc;
+          const float c0 = scaled(0);
+          float z = 0.0f;
+          for (int i = 0; i < kk; ++i) z += expf(scaled(i) - c0);
+          float cum = 0.0f;
+          int kept = 0;
+          for (int i = 0; i < kk; ++i) {
+            const float nu = __fdiv_rn(expf(scaled(i) - c0), z);
+            cum += nu;
+            if (cum - nu < tp) ++kept;
+          }
+          if (kept >= 1 && kept <= kk) thr = fmaxf(thr, scaled(kept - 1));
+        }
+      }
+      s_thr = thr;
+    }
+    __syncthreads();
+    const float thr = s_thr;
+    const float m = __fdiv_rn(key_to_float((unsigned)(cand[0] >> 32)), temp);
+    float zl = 0.0f;
+    for (int i = threadIdx.x; i < C; i += kThreads) {
+      const float f = __fdiv_rn(key_to_float((unsigned)(cand[i] >> 32)), temp);
+      const float e = f >= thr ? expf(f - m) : 0.0f;
+      cprob[i] = e;
+      zl += e;
+    }
+    zl = warp_sum_f32(zl);
+    __shared__ float zred[kWarps];
+    if (lane == 0) zred[warp] = zl;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float z = 0.0f;
+      for (int w = 0; w < kWarps; ++w) z += zred[w];
+      s_z = z;
+    }
+    __syncthreads();
+    const float z = s_z;
+    // ---- race over the candidates with their noise; scatter q
+    const float* noise = a.noise + ((long long)b * a.k + a.j) * a.noise_width;
+    unsigned long long best = 0ull;
+    for (int i = threadIdx.x; i < C; i += kThreads) {
+      const float p = __fdiv_rn(cprob[i], z);
+      const int id = (int)(0xffffffffu - (unsigned)(cand[i] & 0xffffffffull));
+      a.probs[lrow + id] = p;
+      float ratio = __fdiv_rn(p, noise[i]);
+      if (ratio == 0.0f) ratio = 0.0f;
+      const unsigned long long key = argmax_key(ratio, (unsigned)i);
+      best = key > best ? key : best;
+    }
+    best = warp_max_u64(best);
+    if (lane == 0) s_red[warp] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      unsigned long long mk = 0ull;
+      for (int w = 0; w < kWarps; ++w) mk = s_red[w] > mk ? s_red[w] : mk;
+      const int winner = (int)argmax_key_index(mk);
+      s_prev = (int)(0xffffffffu - (unsigned)(cand[winner] & 0xffffffffull));
+    }
+    __syncthreads();
+  }
+  const int prev = s_prev;
+  if (threadIdx.x == 0) {
+    a.drafts[(long long)b * a.k + a.j] = prev;
+    a.prev_out[b] = prev;
+  }
+  if (a.w1)
+    for (int i = threadIdx.x; i < a.rank; i += kThreads) a.e_next[(long long)b * a.rank + i] = a.w1[(long long)prev * a.rank + i];
+}
+
+}  // namespace markov
+}  // namespace specdec
+
+using namespace specdec;
+
+extern "C" {
+
+int specdec_markov_step(const void* logits, int logits_dtype, const void* bias, int bias_dtype, int B, int k, int V,
+                        int row, int candidates, int greedy, int round_bf16, const float* temperature,
+                        const long long* top_k, const float* top_p, int max_top_k, int has_top_p, const float* noise,
+                        int noise_width, long long* drafts, float* probs, long long* prev_out, const void* w1,
+                        int rank, void* e_next, int* err, void* stream) {
+  using namespace markov;
+  SPECDEC_CHECK_ARG(logits && bias && drafts && prev_out && err, "null pointer argument");
+  SPECDEC_CHECK_ARG(dtype_ok(logits_dtype) && dtype_ok(bias_dtype), "unknown dtype code");
+  SPECDEC_CHECK_ARG(B >= 1 && B <= 65535 && k >= 1 && V >= 1 && row >= 0 && row < k, "bad sizes");
+  SPECDEC_CHECK_ARG(!w1 || (e_next && rank >= 1), "w1 needs e_next and rank");
+  if (!greedy) {
+    SPECDEC_CHECK_ARG(temperature && probs && noise, "random rows need temperature, probs and noise");
+    SPECDEC_CHECK_ARG(candidates >= 1 && candidates <= V, "candidates %d out of range", candidates);
+    if (candidates > kMaxCand)
+      return set_error(kUnsupported, "%d candidates above this build's cap %d", candidates, kMaxCand);
+    SPECDEC_CHECK_ARG(noise_width >= candidates, "noise width %d < candidates %d", noise_width, candidates);
+    SPECDEC_CHECK_ARG(!has_top_p || top_p, "top_p required when has_top_p");
+    SPECDEC_CHECK_ARG(max_top_k == 0 || top_k, "top_k required when max_top_k > 0");
+  }
+  Args a{};
+  a.logits = logits; a.ldt = logits_dtype; a.bias = bias; a.bdt = bias_dtype;
+  a.B = B; a.k = k; a.V = V; a.j = row; a.C = candidates; a.greedy = greedy; a.round_bf16 = round_bf16;
+  a.temperature = temperature; a.top_k = top_k; a.top_p = top_p; a.max_top_k = max_top_k; a.has_top_p = has_top_p;
+  a.noise = noise; a.noise_width = noise_width; a.drafts = drafts; a.probs = probs; a.prev_out = prev_out;
+  a.w1 = static_cast<const __nv_bfloat16*>(w1); a.rank = rank; a.e_next = static_cast<__nv_bfloat16*>(e_next);
+  a.err = err;
+  markov_step_kernel<<<B, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  SPECDEC_LAUNCH_CHECK();
+  return kOk;
+}
+
+}  // extern "C"

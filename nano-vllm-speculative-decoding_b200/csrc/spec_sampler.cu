@@ -247,6 +247,15 @@ __device__ void block_ms(float& m, float& s) {
   __syncthreads();
 }
 
+// exp(x) for the softmax normaliser sums: the hardware ex2 of x * log2(e).  The sum's order already differs
+// from ATen's; this adds ~1e-7 relative error per term, far inside the 1e-5 probability tolerance and the 1e-6
+// decision flags.  Per-element probabilities that decide tokens use the accurate expf.
+__device__ __forceinline__ float exp_sum_term(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x * 1.4426950408889634f));
+  return y;
+}
+
 // Online (max, sum of exp) over elements [lo, hi) of one row of scaled logits.
 template <typename T, int NT>
 __device__ void row_range_ms(const T* row, int lo, int hi, float temp, int vec_ok, float& m, float& s) {
@@ -293,12 +302,12 @@ __device__ void row_range_ms(const T* row, int lo, int hi, float temp, int vec_o
           vm = fmaxf(vm, f[e]);
         }
         if (vm > m) {
-          if (m != -INFINITY) s *= expf(m - vm);
+          if (m != -INFINITY) s *= exp_sum_term(m - vm);
           m = vm;
         }
         if (m != -INFINITY) {
 #pragma unroll
-          for (int e = 0; e < VE; ++e) s += expf(f[e] - m);
+          for (int e = 0; e < VE; ++e) s += exp_sum_term(f[e] - m);
         }
       }
     }
@@ -307,20 +316,20 @@ __device__ void row_range_ms(const T* row, int lo, int hi, float temp, int vec_o
       float f = to_f32(row[v]);
       if (!unit_temp) f = scale_logit(f, temp);
       if (f > m) {
-        if (m != -INFINITY) s *= expf(m - f);
+        if (m != -INFINITY) s *= exp_sum_term(m - f);
         m = f;
       }
-      if (m != -INFINITY) s += expf(f - m);
+      if (m != -INFINITY) s += exp_sum_term(f - m);
     }
   } else {
     for (int v = lo + threadIdx.x; v < hi; v += NT) {
       float f = to_f32(row[v]);
       if (!unit_temp) f = scale_logit(f, temp);
       if (f > m) {
-        if (m != -INFINITY) s *= expf(m - f);
+        if (m != -INFINITY) s *= exp_sum_term(m - f);
         m = f;
       }
-      if (m != -INFINITY) s += expf(f - m);
+      if (m != -INFINITY) s += exp_sum_term(f - m);
     }
   }
 }
@@ -463,10 +472,12 @@ template <int NT>
 __device__ void select_digit(const unsigned* hist, int nbins, int rank, int* s_digit, int* s_above) {
   // rank: 1-based rank (from the top) of the wanted element among the elements counted in hist.
   __shared__ int warp_tot[NT / 32];
-  const int per = nbins / NT;
+  const int per = nbins >= NT ? nbins / NT : 1;       // bins per owning thread
+  const int owners = nbins / per;
   // thread i owns bins [i*per, (i+1)*per); suffix sums from the top
   int local = 0;
-  for (int j = 0; j < per; ++j) local += hist[threadIdx.x * per + j];
+  if ((int)threadIdx.x < owners)
+    for (int j = 0; j < per; ++j) local += hist[threadIdx.x * per + j];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   // inclusive scan from the top: reverse the thread order
   int incl = local;
@@ -480,13 +491,15 @@ __device__ void select_digit(const unsigned* hist, int nbins, int rank, int* s_d
   int above_warps = 0;
   for (int w = warp + 1; w < NT / 32; ++w) above_warps += warp_tot[w];
   int above = above_warps + incl - local;  // elements in bins above this thread's bins
-  for (int j = per - 1; j >= 0; --j) {
-    int h = hist[threadIdx.x * per + j];
-    if (above < rank && rank <= above + h) {
-      *s_digit = threadIdx.x * per + j;
-      *s_above = above;
+  if ((int)threadIdx.x < owners) {
+    for (int j = per - 1; j >= 0; --j) {
+      int h = hist[threadIdx.x * per + j];
+      if (above < rank && rank <= above + h) {
+        *s_digit = threadIdx.x * per + j;
+        *s_above = above;
+      }
+      above += h;
     }
-    above += h;
   }
   __syncthreads();
 }
@@ -501,7 +514,7 @@ template <typename T>
 __global__ void __launch_bounds__(kTopkThreads) topk_stats_kernel(Args a, int mode) {
   constexpr int NT = kTopkThreads;
   __shared__ int s_start[kMaxRequests + 1];
-  __shared__ unsigned hist[2048];
+  __shared__ unsigned hist[4096];
   __shared__ float cand[kMaxTopK];
   __shared__ int s_digit, s_above, s_cnt, s_last;
   __shared__ float s_thr;
@@ -535,15 +548,23 @@ __global__ void __launch_bounds__(kTopkThreads) topk_stats_kernel(Args a, int mo
     // ---- radix select of the K-th largest key over three digits (11, 11, 10 bits)
     unsigned prefix = 0, pmask = 0;
     int rank = K;
-    const int shifts[3] = {21, 10, 0};
-    const int widths[3] = {11, 11, 10};
+    const int shifts[3] = {20, 8, 0};
+    const int widths[3] = {12, 12, 8};
+    const int lane = threadIdx.x & 31;
     for (int p = 0; p < 3; ++p) {
       const int nb = 1 << widths[p];
-      for (int i = threadIdx.x; i < 2048; i += NT) hist[i] = 0;
+      for (int i = threadIdx.x; i < 4096; i += NT) hist[i] = 0;
       __syncthreads();
-      for (int v = threadIdx.x; v < V; v += NT) {
-        unsigned key = ordered_key(scaled_at(row, v, temp));
-        if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shifts[p]) & (nb - 1)], 1u);
+      for (int v0 = threadIdx.x - lane; v0 < V; v0 += NT) {     // warp-uniform trip count
+        const int v = v0 + lane;
+        bool hit = false;
+        unsigned bin = 0;
+        if (v < V) {
+          const unsigned key = ordered_key(scaled_at(row, v, temp));
+          hit = (key & pmask) == prefix;
+          bin = (key >> shifts[p]) & (nb - 1);
+        }
+        warp_hist_add(hist, bin, hit);
       }
       __syncthreads();
       select_digit<NT>(hist, nb, rank, &s_digit, &s_above);
@@ -612,7 +633,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_stats_kernel(Args a, int mo
     float ls = 0.0f;
     for (int v = threadIdx.x; v < V; v += NT) {
       float f = scaled_at(row, v, temp);
-      if (f >= thr) ls += expf(f - m);
+      if (f >= thr) ls += exp_sum_term(f - m);
     }
     ls = warp_sum_f32(ls);
     __shared__ float sm_sum[NT / 32];
@@ -703,9 +724,13 @@ __device__ __forceinline__ void warp_segment_reduce(unsigned long long key, int 
 template <typename T, bool RACE>
 __global__ void __launch_bounds__(kThreads) tail_kernel(Args a) {
   __shared__ unsigned long long s_best[kMaxRequests];
+  __shared__ ReqDesc s_desc[RACE ? 1 : kMaxRequests];
   __shared__ int s_last;
   if (!RACE && *reinterpret_cast<volatile int*>(a.status) != 0) return;  // pass 1 rejected its inputs
-  for (int i = threadIdx.x; i < a.B; i += kThreads) s_best[i] = 0ull;
+  for (int i = threadIdx.x; i < a.B; i += kThreads) {
+    s_best[i] = 0ull;
+    if (!RACE) s_desc[i] = a.desc[i];
+  }
   __syncthreads();
   const long long S = (long long)kRngBlock * gridDim.x;
   const long long idx = (long long)blockIdx.x * kRngBlock + threadIdx.x;
@@ -718,49 +743,70 @@ __global__ void __launch_bounds__(kThreads) tail_kernel(Args a) {
   // row / column of element idx, advanced by S per grid-stride step
   unsigned b = (unsigned)(idx / V), v = (unsigned)(idx % V);
   for (int n = 0; n < a.e_rounds; ++n) {
-    float4 r4 = make_float4(1.f, 1.f, 1.f, 1.f);
-    if (gen) r4 = curand_uniform4(&st);
-    const float rl[4] = {r4.x, r4.y, r4.z, r4.w};
-    if ((long long)(n * 4) * S + warp_idx0 >= N) break;
+    if ((long long)(n * 4) * S + warp_idx0 >= N) break;      // warp-uniform
+    // ---- the round's four elements (lanes of one curand_uniform4): issue every load first
+    unsigned eb[4], ev[4];
+    bool act[4];
+    float xv[4], qv[4], ee[4];
 #pragma unroll
     for (int ii = 0; ii < 4; ++ii) {
-      const long long step = (long long)(n * 4 + ii);
-      if (step * S + warp_idx0 >= N) break;  // warp-uniform
-      const long long li = step * S + idx;
-      const bool active = li < N;
-      unsigned long long key = 0ull;
-      int bb = (int)b;
-      if (active) {
-        float w;
+      const long long li = (long long)(n * 4 + ii) * S + idx;
+      act[ii] = li < N;
+      eb[ii] = b;
+      ev[ii] = v;
+      xv[ii] = 0.0f;
+      qv[ii] = 0.0f;
+      ee[ii] = 1.0f;
+      if (act[ii]) {
         if (RACE) {
-          w = reinterpret_cast<const float*>(a.x)[(long long)b * a.V + v];
+          xv[ii] = reinterpret_cast<const float*>(a.x)[(long long)b * a.V + v];
         } else {
-          const ReqDesc d = a.desc[b];
-          const float xv = to_f32(reinterpret_cast<const T*>(a.x)[d.x_row * a.V + v]);
-          float p;
-          if (a.probs_mode) {
-            p = xv;
-          } else {
-            const float f = d.temp == 1.0f ? xv : scale_logit(xv, d.temp);
-            p = f >= d.thr ? __fdiv_rn(expf(f - d.m), d.s) : 0.0f;
-          }
-          if (d.q_row < 0) {
-            w = p;
-          } else {
-            const float qv = a.q[d.q_row * a.V + v];
-            w = fmaxf(p - qv, 0.0f);
-          }
+          const ReqDesc& d = s_desc[b];
+          xv[ii] = to_f32(reinterpret_cast<const T*>(a.x)[d.x_row * a.V + v]);
+          if (d.q_row >= 0) qv[ii] = a.q[d.q_row * a.V + v];
         }
-        const float e = gen ? torch_exponential_clamped(rl[ii]) : a.E[li];
-        float ratio = __fdiv_rn(w, e);
-        if (ratio == 0.0f) ratio = 0.0f;  // -0 and +0 compare equal in torch's argmax
-        key = argmax_key(ratio, v);
+        if (!gen) ee[ii] = a.E[li];
       }
-      warp_segment_reduce(key, bb, active, s_best);
-      // advance to element li + S
       b += a.e_sq;
       v += a.e_sr;
       if (v >= V) { v -= V; ++b; }
+    }
+    if (gen) {
+      const float4 r4 = curand_uniform4(&st);
+      ee[0] = torch_exponential_clamped(r4.x);
+      ee[1] = torch_exponential_clamped(r4.y);
+      ee[2] = torch_exponential_clamped(r4.z);
+      ee[3] = torch_exponential_clamped(r4.w);
+    }
+    // ---- weights, ratios and argmax keys
+    unsigned long long key[4];
+#pragma unroll
+    for (int ii = 0; ii < 4; ++ii) {
+      key[ii] = 0ull;
+      if (act[ii]) {
+        float w;
+        if (RACE) {
+          w = xv[ii];
+        } else {
+          const ReqDesc& d = s_desc[eb[ii]];
+          float p;
+          if (a.probs_mode) {
+            p = xv[ii];
+          } else {
+            const float f = d.temp == 1.0f ? xv[ii] : scale_logit(xv[ii], d.temp);
+            p = f >= d.thr ? __fdiv_rn(expf(f - d.m), d.s) : 0.0f;
+          }
+          w = d.q_row < 0 ? p : fmaxf(p - qv[ii], 0.0f);
+        }
+        float ratio = __fdiv_rn(w, ee[ii]);
+        if (ratio == 0.0f) ratio = 0.0f;  // -0 and +0 compare equal in torch's argmax
+        key[ii] = argmax_key(ratio, ev[ii]);
+      }
+    }
+#pragma unroll
+    for (int ii = 0; ii < 4; ++ii) {
+      if ((long long)(n * 4 + ii) * S + warp_idx0 < N)          // warp-uniform
+        warp_segment_reduce(key[ii], (int)eb[ii], act[ii], s_best);
     }
   }
   __syncthreads();

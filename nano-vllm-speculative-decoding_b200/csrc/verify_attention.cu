@@ -70,10 +70,8 @@ struct Smem {
   uint64_t s_full[2], s_free[2], p_full[2], o_done[2];
   uint32_t tmem_base;
   int abort;
-  int any_rescale;
-  float red_max[4][32];   // per-warp column maxima of the current tile
-  float red_sum[4][32];   // per-warp column sums (separate: a warp may start the next tile's maxima early)
-  float m_col[kCols], l_col[kCols], alpha[kCols];
+  float red_max[2][4][32];   // per-warp column maxima, by tile parity
+  float red_sum[1][4][32];   // per-warp column sums (epilogue)
 };
 
 constexpr int kOffQ = 0;
@@ -82,6 +80,13 @@ constexpr int kOffV = kOffK + kStages * kTileBytes;
 constexpr int kOffP = kOffV + kStages * kTileBytes;
 constexpr int kOffCtl = kOffP + 2 * kPBytes;
 constexpr int kSmemBytes = kOffCtl + (int)sizeof(Smem) + 1024;   // + alignment slack
+
+// Max over the warp's 32 lanes in one instruction (sm_100a redux.sync on f32).
+__device__ __forceinline__ float warp_max_redux(float v) {
+  float r;
+  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+  return r;
+}
 
 // max (ADD=false) or sum (ADD=true) over the 32 lanes of column `lane`; v is consumed.
 template <bool ADD>
@@ -143,19 +148,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&S.s_full[i], 1);
-      mbar_init(&S.s_free[i], 128);
-      mbar_init(&S.p_full[i], 128);
+      mbar_init(&S.s_free[i], 4);     // one elected arrival per softmax warp
+      mbar_init(&S.p_full[i], 4);
       mbar_init(&S.o_done[i], 1);
     }
     S.abort = 0;
-    S.any_rescale = 0;
     fence_barrier_init();
-  }
-  if (threadIdx.x >= 128 && threadIdx.x < 160) {
-    const int j = threadIdx.x - 128;
-    S.m_col[j] = -INFINITY;
-    S.l_col[j] = 0.0f;
-    S.alpha[j] = 1.0f;
   }
   if (warp == 1) {
     tmem_alloc(&S.tmem_base, kTmemCols);
@@ -251,75 +249,86 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = threadIdx.x - 128;       // key within the tile (S^T) / head dim (O^T)
     const uint32_t lane_off = static_cast<uint32_t>(w * 32) << 16;
     const int min_limit = L - ql;            // smallest causal limit among the valid columns
+    // Running max per query column, kept identically by every softmax thread in registers (each thread reads
+    // the four warps' partial maxima itself), and this thread's partial column sums over its own keys, reduced
+    // across the 128 threads once in the epilogue: one named barrier per tile, no serial section.
+    float m_run[32], l_part[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      m_run[j] = -INFINITY;
+      l_part[j] = 0.0f;
+    }
     bool ok = true;
     for (int t = 0; t < nt && ok; ++t) {
-      if (!mbar_wait(&S.s_full[t & 1], (t >> 1) & 1, abort, a.err, kErrTimeoutS)) { ok = false; break; }
+      const int buf = t & 1;                 // partial buffers alternate by tile parity (no reuse hazard)
+      if (!mbar_wait(&S.s_full[buf], (t >> 1) & 1, abort, a.err, kErrTimeoutS)) { ok = false; break; }
       tc_fence_after();
-      float s[32];
-      tmem_ld_32x32b_x32(tmem + lane_off + (t & 1) * 32, s);
+      float x[32];
+      tmem_ld_32x32b_x32(tmem + lane_off + buf * 32, x);
       tc_fence_before();
-      mbar_arrive(&S.s_free[t & 1]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.s_free[buf]);
       const int key = t * kKeysPerTile + row;
       const bool tile_masked = (t * kKeysPerTile + kKeysPerTile - 1) > min_limit || (t + 1) * kKeysPerTile > L;
-      float x[32];
+      if (tile_masked) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        bool valid = key < L;
-        if (tile_masked && a.causal) {
+        for (int j = 0; j < 32; ++j) {
           const int p = j / G;
-          const int limit = p < ql ? L - ql + p : L - 1;
-          valid = valid && key <= limit;
+          const int limit = (a.causal && p < ql) ? L - ql + p : L - 1;
+          x[j] = key <= limit ? x[j] * a.scale_log2 : -INFINITY;
         }
-        x[j] = valid ? s[j] * a.scale_log2 : -INFINITY;
-      }
-      // ---- column max over the tile's 128 keys
-      float tmp[32];
+      } else {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) tmp[j] = x[j];
-      const float wmax = column_reduce<false>(tmp, lane);
-      S.red_max[w][lane] = wmax;
-      named_barrier(1, 128);
-      if (w == 0) {
-        const int j = lane;
-        const float tile_max = fmaxf(fmaxf(S.red_max[0][j], S.red_max[1][j]), fmaxf(S.red_max[2][j], S.red_max[3][j]));
-        const float m_old = S.m_col[j];
-        const bool need = tile_max > m_old + 8.0f;   // lazy rescale: only when the max grows by 2^8
-        float alpha = 1.0f;
-        if (need) {
-          alpha = (m_old == -INFINITY) ? 0.0f : ex2_approx(m_old - tile_max);
-          S.m_col[j] = tile_max;
-        }
-        S.alpha[j] = alpha;
-        const unsigned any = __ballot_sync(0xffffffffu, need && m_old != -INFINITY);
-        if (lane == 0) S.any_rescale = any != 0;
+        for (int j = 0; j < 32; ++j) x[j] = x[j] * a.scale_log2;
       }
-      named_barrier(1, 128);
-      // ---- probabilities (relative to the column's running max) and column sums
-      float p[32];
+      // ---- column max over this warp's 32 keys (one warp reduction per column), then the four warps'
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
-        const float m = S.m_col[j];
-        p[j] = x[j] == -INFINITY ? 0.0f : ex2_approx(x[j] - m);
-        tmp[j] = p[j];
+        const float wm = warp_max_redux(x[j]);
+        if (lane == j) S.red_max[buf][w][j] = wm;
       }
-      const float wsum = column_reduce<true>(tmp, lane);
-      const int any_rescale = S.any_rescale;
-      S.red_sum[w][lane] = wsum;
       named_barrier(1, 128);
-      if (w == 0) {
-        const int j = lane;
-        S.l_col[j] = S.l_col[j] * S.alpha[j] + (S.red_sum[0][j] + S.red_sum[1][j] + S.red_sum[2][j] + S.red_sum[3][j]);
+      float alpha[32];
+      bool any_rescale = false;
+#pragma unroll
+      for (int j4 = 0; j4 < 8; ++j4) {
+        const float4 r0 = reinterpret_cast<const float4*>(S.red_max[buf][0])[j4];
+        const float4 r1 = reinterpret_cast<const float4*>(S.red_max[buf][1])[j4];
+        const float4 r2 = reinterpret_cast<const float4*>(S.red_max[buf][2])[j4];
+        const float4 r3 = reinterpret_cast<const float4*>(S.red_max[buf][3])[j4];
+        const float tm[4] = {fmaxf(fmaxf(r0.x, r1.x), fmaxf(r2.x, r3.x)), fmaxf(fmaxf(r0.y, r1.y), fmaxf(r2.y, r3.y)),
+                             fmaxf(fmaxf(r0.z, r1.z), fmaxf(r2.z, r3.z)), fmaxf(fmaxf(r0.w, r1.w), fmaxf(r2.w, r3.w))};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int j = j4 * 4 + e;
+          alpha[j] = 1.0f;
+          if (tm[e] > m_run[j] + 8.0f) {       // lazy rescale: only when the max grows by 2^8
+            if (m_run[j] != -INFINITY) {
+              alpha[j] = ex2_approx(m_run[j] - tm[e]);
+              any_rescale = true;
+            } else {
+              alpha[j] = 0.0f;
+            }
+            m_run[j] = tm[e];
+          }
+        }
+      }
+      // ---- probabilities relative to the running max; this thread's share of the column sums
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        x[j] = x[j] == -INFINITY ? 0.0f : ex2_approx(x[j] - m_run[j]);
+        l_part[j] = l_part[j] * alpha[j] + x[j];
       }
       // ---- P^T row `row` (32 bf16, 64 bytes) into the SW64 buffer once PV(t-2) released it
-      if (t >= 2 && !mbar_wait(&S.o_done[t & 1], ((t - 2) >> 1) & 1, abort, a.err, kErrTimeoutO)) { ok = false; break; }
-      unsigned char* prow = sP + (t & 1) * kPBytes + row * 64;
+      if (t >= 2 && !mbar_wait(&S.o_done[buf], ((t - 2) >> 1) & 1, abort, a.err, kErrTimeoutO)) { ok = false; break; }
+      unsigned char* prow = sP + buf * kPBytes + row * 64;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint4 chunk;
         uint32_t* wds = reinterpret_cast<uint32_t*>(&chunk);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          __nv_bfloat162 pair = __floats2bfloat162_rn(p[c * 8 + 2 * e], p[c * 8 + 2 * e + 1]);
+          __nv_bfloat162 pair = __floats2bfloat162_rn(x[c * 8 + 2 * e], x[c * 8 + 2 * e + 1]);
           wds[e] = *reinterpret_cast<uint32_t*>(&pair);
         }
         const int phys = c ^ ((row >> 1) & 3);
@@ -339,24 +348,28 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      // ---- rescale O^T (lane = head dim) once PV(t-1) has landed
+      // ---- rescale O^T (lane = head dim) once PV(t-1) has landed (uniform: every thread decided alike)
       if (any_rescale && t >= 1) {
         if (!mbar_wait(&S.o_done[(t - 1) & 1], ((t - 1) >> 1) & 1, abort, a.err, kErrTimeoutO)) { ok = false; break; }
         tc_fence_after();
         float o[32];
         tmem_ld_32x32b_x32(tmem + lane_off + 64, o);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) o[j] *= S.alpha[j];
+        for (int j = 0; j < 32; ++j) o[j] *= alpha[j];
         tmem_st_32x32b_x32(tmem + lane_off + 64, o);
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(&S.p_full[t & 1]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.p_full[buf]);
     }
-    // ---- epilogue: O^T / l, bf16, to out[token, head, dim]
+    // ---- epilogue: column sums over the 128 key threads, then O^T / l, bf16, to out[token, head, dim]
+    if (ok) {
+      S.red_sum[0][w][lane] = column_reduce<true>(l_part, lane);
+      named_barrier(1, 128);
+    }
     if (ok && mbar_wait(&S.o_done[(nt - 1) & 1], ((nt - 1) >> 1) & 1, abort, a.err, kErrTimeoutO)) {
       tc_fence_after();
-      named_barrier(1, 128);   // l_col of the last tile is complete
       float o[32];
       tmem_ld_32x32b_x32(tmem + lane_off + 64, o);
       const int d = row;
@@ -364,7 +377,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < 32; ++j) {
         const int p = j / G, g = j % G;
         if (p < ql) {
-          const float l = S.l_col[j];
+          const float l = (S.red_sum[0][0][j] + S.red_sum[0][1][j]) + (S.red_sum[0][2][j] + S.red_sum[0][3][j]);
           const float val = l > 0.0f ? o[j] / l : 0.0f;
           a.out[(long long)(q_start + p) * a.out_row_stride + (long long)(h * G + g) * kHeadDim + d] =
               __float2bfloat16_rn(val);

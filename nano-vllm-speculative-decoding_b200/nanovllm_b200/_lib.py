@@ -51,6 +51,10 @@ SIGNATURES = {
     "specdec_rmsnorm": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_ll, _c_int, _c_float,
                                  _c_void_p]),
     "specdec_silu_mul": (_c_int, [_c_void_p, _c_void_p, _c_ll, _c_int, _c_void_p]),
+    "specdec_markov_step": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
+                                     _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_int, _c_void_p,
+                                     _c_int, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_void_p,
+                                     _c_void_p, _c_void_p]),
 }
 
 _lib = None

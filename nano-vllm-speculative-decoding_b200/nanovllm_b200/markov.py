@@ -1,0 +1,96 @@
+"""DSpark's in-block Markov sampling (kernel 3) on libspecdec_b200.so.
+
+    markov_rows(logits, prev, sampling, noise, drafts, draft_probs, candidates, markov_head)
+
+mirrors DFlashDrafter._markov_rows (nanovllm/engine/speculative.py:163-184) with the Markov head passed in:
+k sequential steps, each `bias = markov_head(prev)` (for MarkovHeadWeights a cuBLAS GEMM of the W1 rows the
+previous step's kernel gathered against W2) followed by ONE kernel launch that, for every batch row at once,
+adds the bias, selects the top `candidates` logits (ties by ascending token id), applies the row's temperature /
+top-k / top-p over them, races them against that row's noise and scatters q.  Greedy batches take the argmax.
+Rows drawn over the whole vocabulary (candidates == 0: some row does not truncate) use the sampler's
+probs_from_logits + race kernels.  drafts [B, k] and draft_probs [B, k, V] are written in place, as in the
+reference; noise [B, k, candidates or V] is drawn by the caller before row 0 (speculative.py:156-159).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib, spec_sampler
+from ._lib import DTYPE_CODES, check, ptr, require_cuda, stream_of
+from .fused import err_word
+
+TIE_MARGIN = 64
+
+
+def num_candidates(max_top_k: int, all_top_k: bool, vocab_size: int) -> int:
+    """speculative.py:46-50: a row is drawn among its top max_top_k + 64 logits when every row truncates."""
+    return min(max_top_k + TIE_MARGIN, vocab_size) if all_top_k else 0
+
+
+@dataclass
+class MarkovHeadWeights:
+    """MarkovHead (nanovllm/models/dflash.py:26-41): markov_w1 [V, r] embeds the previous token, markov_w2 [V, r]
+    projects it to a bias over the vocabulary."""
+    w1: torch.Tensor
+    w2: torch.Tensor
+
+    def embed(self, prev: torch.Tensor) -> torch.Tensor:
+        return self.w1[prev]
+
+    def __call__(self, prev: torch.Tensor) -> torch.Tensor:
+        return torch.matmul(self.embed(prev), self.w2.t())
+
+
+def _round_flag(logits: torch.Tensor, bias: torch.Tensor) -> int:
+    if logits.dtype == torch.bfloat16 and bias.dtype == torch.bfloat16:
+        return 1
+    if logits.dtype == torch.float16 or bias.dtype == torch.float16:
+        raise ValueError("fp16 Markov rows are not implemented (bf16 and fp32 are)")
+    return 0
+
+
+def markov_rows(logits: torch.Tensor, prev: torch.Tensor, sampling, noise: torch.Tensor | None,
+                drafts: torch.Tensor, draft_probs: torch.Tensor | None, candidates: int, markov_head) -> None:
+    """speculative.py:163-184: draw the k rows left to right into drafts (and q into draft_probs unless greedy);
+    prev holds the anchors.  logits [B, k, V]; markov_head(prev [B]) -> bias [B, V]."""
+    device = require_cuda(logits, prev, drafts)
+    batch, k, vocab = logits.shape
+    logits = logits.contiguous()
+    greedy = draft_probs is None
+    if not greedy and candidates:
+        draft_probs.zero_()                     # q is zero outside each row's candidates (speculative.py:171)
+    prev_buf = prev.to(torch.int64).clone()
+    weights = markov_head if isinstance(markov_head, MarkovHeadWeights) else None
+    e_buf = None
+    if weights is not None:
+        e_buf = weights.embed(prev_buf).contiguous()
+    temps = top_k = top_p = None
+    max_top_k = has_top_p = 0
+    if not greedy:
+        temps = sampling.temperatures.contiguous()
+        top_k = sampling.top_k.contiguous()
+        top_p = sampling.top_p.contiguous() if sampling.has_top_p else None
+        max_top_k, has_top_p = sampling.max_top_k, int(sampling.has_top_p)
+        noise = noise.float().contiguous()
+    lib = _lib.lib()
+    stream = stream_of(device)
+    for row in range(k):
+        bias = torch.matmul(e_buf, weights.w2.t()) if weights is not None else markov_head(prev_buf)
+        bias = bias.contiguous()
+        if greedy or candidates:
+            check(lib.specdec_markov_step(
+                ptr(logits), DTYPE_CODES[logits.dtype], ptr(bias), DTYPE_CODES[bias.dtype], batch, k, vocab, row,
+                candidates, int(greedy), _round_flag(logits, bias), ptr(temps), ptr(top_k), ptr(top_p), max_top_k,
+                has_top_p, ptr(noise), 0 if noise is None else noise.shape[-1], ptr(drafts), ptr(draft_probs),
+                ptr(prev_buf), ptr(None if weights is None else weights.w1), 0 if weights is None else
+                weights.w1.shape[1], ptr(e_buf), ptr(err_word(device)), stream))
+        else:
+            row_logits = logits[:, row] + bias  # torch's dtype promotion and rounding, as the reference
+            probs = spec_sampler.probs_from_logits(row_logits, sampling)
+            draft_probs[:, row] = probs
+            prev_buf = spec_sampler.race(probs, noise[:, row])
+            drafts[:, row] = prev_buf
+            if weights is not None:
+                e_buf = weights.embed(prev_buf).contiguous()

@@ -267,6 +267,58 @@ def ctx_store_cases(reference: Path) -> dict[str, np.ndarray]:
     return out
 
 
+def markov_cases(reference: Path) -> dict[str, np.ndarray]:
+    """DFlashDrafter._markov_rows (speculative.py:163-184) with a lookup-table Markov head, as the reference's
+    tests/test_dspark_propose.py builds it: greedy, candidate rows (every row truncates) and whole-vocabulary
+    rows.  fp32 logits and a rank-1 bias a[prev] * c[v] (one fp32 product, reproduced exactly by any
+    implementation), so no two candidates tie."""
+    from nanovllm.engine.speculative import DFlashDrafter, num_candidates
+    from nanovllm.layers import spec_sampler as ss
+    out: dict[str, np.ndarray] = {}
+    configs = [
+        # name, B, k, V, temps (None = greedy), top_k, top_p
+        ("greedy_v300", 5, 7, 300, None, [0] * 5, [1.0] * 5),
+        ("candidates_v500", 6, 7, 500, [1.0, 0.7, 0.5, 1.3, 0.9, 1.0], [3, 10, 20, 5, 1, 64],
+         [1.0, 0.8, 0.5, 1.0, 0.95, 1.0]),
+        ("whole_vocab_v400", 4, 7, 400, [1.0, 0.7, 1.0, 0.8], [0, 5, 0, 3], [1.0, 0.9, 1.0, 0.7]),
+        ("candidates_v5000_k128", 3, 7, 5000, [1.0, 1.0, 0.7], [128, 20, 128], [1.0, 0.8, 1.0]),
+    ]
+    for name, batch, k, vocab, temps, top_k, top_p in configs:
+        g = torch.Generator().manual_seed(zlib.crc32(name.encode()) % 100000)
+        logits = torch.randn(batch, k, vocab, generator=g) * 2
+        bias_a = torch.randn(vocab, generator=g)
+        bias_c = torch.randn(vocab, generator=g)
+        prev = torch.randint(vocab, (batch,), generator=g)
+        drafter = object.__new__(DFlashDrafter)
+        drafter.model = SimpleNamespace(markov_head=lambda p, a=bias_a, c=bias_c: a[p][:, None] * c[None, :])
+        drafts = torch.empty(batch, k, dtype=torch.int64)
+        if temps is None:
+            samp, noise, probs, cand = None, None, None, 0
+            drafter._markov_rows(logits, prev.clone(), None, None, drafts, None, 0)
+        else:
+            samp = sampling(ss, temps, top_k, top_p)
+            cand = num_candidates(samp.max_top_k, samp.all_top_k, vocab)
+            noise = ss.exponential_noise_(torch.empty(batch, k, cand or vocab), g)
+            probs = torch.empty(batch, k, vocab)
+            drafter._markov_rows(logits, prev.clone(), samp, noise, drafts, probs, cand)
+        prefix = f"markov/{name}/"
+        out[prefix + "logits"] = logits.numpy()
+        out[prefix + "bias_a"] = bias_a.numpy()
+        out[prefix + "bias_c"] = bias_c.numpy()
+        out[prefix + "prev"] = prev.numpy()
+        out[prefix + "drafts"] = drafts.numpy()
+        out[prefix + "candidates"] = np.array(cand)
+        if samp is not None:
+            out[prefix + "temperature"] = samp.temperatures.numpy()
+            out[prefix + "top_k"] = samp.top_k.numpy()
+            out[prefix + "top_p"] = samp.top_p.numpy()
+            out[prefix + "max_top_k"] = np.array(samp.max_top_k)
+            out[prefix + "has_top_p"] = np.array(samp.has_top_p)
+            out[prefix + "noise"] = noise.numpy()
+            out[prefix + "probs"] = probs.numpy()
+    return out
+
+
 def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__)
     default_ref = os.environ.get("SPECDEC_REFERENCE", str(HERE.parents[2] / "reference"))
@@ -280,6 +332,9 @@ def main() -> int:
     fixtures.update(greedy_cases(ss))
     np.savez_compressed(HERE / "sampler.npz", **fixtures)
     print(f"wrote {len(fixtures)} arrays to {HERE / 'sampler.npz'}")
+    markov = markov_cases(Path(args.reference))
+    np.savez_compressed(HERE / "markov.npz", **markov)
+    print(f"wrote {len(markov)} arrays to {HERE / 'markov.npz'}")
     ctx = ctx_store_cases(Path(args.reference))
     np.savez_compressed(HERE / "ctx_store.npz", **ctx)
     print(f"wrote {len(ctx)} arrays to {HERE / 'ctx_store.npz'}")

@@ -1,0 +1,130 @@
+"""Kernel (3), DSpark's in-block Markov rows, against oracle/markov.py and the reference's golden vectors.
+Drafts bit-exact (candidate ties ordered by ascending token id on both sides), q within 1e-5 relative; at full
+size, a row whose race is within 1e-5 of a tie is compared only up to that step."""
+from pathlib import Path
+from types import SimpleNamespace
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import markov as OM
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+G = np.load(Path(__file__).parent / "golden" / "markov.npz")
+NAMES = sorted({key.split("/")[1] for key in G.files if key.startswith("markov/")})
+
+
+def case(name):
+    prefix = f"markov/{name}/"
+    return {key[len(prefix):]: G[key] for key in G.files if key.startswith(prefix)}
+
+
+def sampling_of(temps, top_k, top_p):
+    from nanovllm_b200 import spec_sampler as S
+    seqs = [SimpleNamespace(temperature=float(t), top_k=int(k), top_p=float(p)) for t, k, p in zip(temps, top_k, top_p)]
+    return S.sampling_tensors(seqs, DEV)
+
+
+@pytest.mark.parametrize("name", NAMES)
+def test_golden_markov_rows(name):
+    from nanovllm_b200.markov import markov_rows
+    c = case(name)
+    a = torch.from_numpy(c["bias_a"]).to(DEV)
+    cc = torch.from_numpy(c["bias_c"]).to(DEV)
+    head = lambda prev: a[prev][:, None] * cc[None, :]
+    logits = torch.from_numpy(c["logits"]).to(DEV)
+    B, k, V = logits.shape
+    drafts = torch.empty(B, k, dtype=torch.int64, device=DEV)
+    samp = probs = noise = None
+    if "temperature" in c:
+        samp = sampling_of(c["temperature"], c["top_k"], c["top_p"])
+        probs = torch.full((B, k, V), 7.0, device=DEV)     # garbage: the call must zero / overwrite it
+        noise = torch.from_numpy(c["noise"]).to(DEV)
+    markov_rows(logits, torch.from_numpy(c["prev"]).to(DEV), samp, noise, drafts, probs, int(c["candidates"]), head)
+    assert drafts.cpu().numpy().tolist() == c["drafts"].tolist()
+    if probs is not None:
+        got = probs.cpu().numpy()
+        assert np.array_equal(got > 0, c["probs"] > 0)
+        np.testing.assert_allclose(got, c["probs"], rtol=1e-5, atol=1e-7)
+
+
+class RecordingHead:
+    """The production Markov head (W2 . W1[prev], cuBLAS) that records every step's bias for the oracle."""
+
+    def __init__(self, w1, w2):
+        self.w1, self.w2, self.biases = w1, w2, []
+
+    def __call__(self, prev):
+        bias = torch.matmul(self.w1[prev], self.w2.t())
+        self.biases.append(bias.clone())
+        return bias
+
+
+@pytest.mark.parametrize("greedy", [False, True])
+def test_config4_markov_rows_match_oracle(greedy):
+    """BASELINE config 4's drafter: B = 64 rows, k = 7, V = 151936, rank 256, bf16, top_k = 128 (192 candidates)."""
+    from nanovllm_b200.markov import markov_rows, num_candidates
+    B, k, V, r = 64, 7, 151936, 256
+    g = torch.Generator(device=DEV).manual_seed(4)
+    logits = (torch.randn(B, k, V, device=DEV, generator=g) * 2).bfloat16()
+    w1 = (torch.randn(V, r, device=DEV, generator=g) * 0.1).bfloat16()
+    w2 = (torch.randn(V, r, device=DEV, generator=g) * 0.1).bfloat16()
+    prev = torch.randint(V, (B,), device=DEV, generator=g)
+    head = RecordingHead(w1, w2)
+    drafts = torch.empty(B, k, dtype=torch.int64, device=DEV)
+    if greedy:
+        samp, cand, noise, probs = None, 0, None, None
+    else:
+        samp = sampling_of([1.0] * (B // 2) + [0.7] * (B // 2), [128] * B, [1.0] * (B // 2) + [0.9] * (B // 2))
+        cand = num_candidates(samp.max_top_k, samp.all_top_k, V)
+        noise = torch.empty(B, k, cand, device=DEV).exponential_(generator=g).clamp_min_(1e-10)
+        probs = torch.empty(B, k, V, device=DEV)
+    markov_rows(logits, prev, samp, noise, drafts, probs, cand, head)
+    biases = [b.float().cpu().numpy() for b in head.biases]
+    step = {"i": 0}
+
+    def bias_fn(_prev):
+        out = biases[step["i"]]
+        step["i"] += 1
+        return out
+
+    from oracle.ctx_store import bf16
+    sampling = None if greedy else dict(temps=samp.temperatures.cpu().numpy(), top_k=samp.top_k.cpu().numpy(),
+                                        top_p=samp.top_p.cpu().numpy(), max_top_k=samp.max_top_k,
+                                        has_top_p=samp.has_top_p)
+    want, want_probs = OM.markov_rows(logits.float().cpu().numpy(), prev.cpu().numpy(), bias_fn, sampling,
+                                      None if noise is None else noise.cpu().numpy(), cand, round_fn=bf16)
+    got = drafts.cpu().numpy()
+    # rows agree step by step; a row may only diverge after a step whose race is a near tie
+    mismatched = (got != want).any(axis=1)
+    assert mismatched.sum() <= 1, f"{mismatched.sum()} rows diverge"
+    if not greedy:
+        same = ~mismatched
+        gp = probs.cpu().numpy()[same]
+        np.testing.assert_allclose(gp, want_probs[same], rtol=1e-5, atol=1e-8)
+
+
+def test_whole_vocabulary_rows_use_the_sampler_kernels():
+    """A batch where one row does not truncate draws every row over the whole vocabulary (candidates = 0)."""
+    from nanovllm_b200.markov import markov_rows
+    B, k, V = 3, 4, 3000
+    g = torch.Generator(device=DEV).manual_seed(9)
+    logits = torch.randn(B, k, V, device=DEV, generator=g)
+    a = torch.randn(V, device=DEV, generator=g)
+    cvec = torch.randn(V, device=DEV, generator=g)
+    head = lambda prev: a[prev][:, None] * cvec[None, :]
+    samp = sampling_of([1.0, 0.8, 1.2], [0, 20, 5], [1.0, 0.9, 1.0])
+    noise = torch.empty(B, k, V, device=DEV).exponential_(generator=g).clamp_min_(1e-10)
+    drafts = torch.empty(B, k, dtype=torch.int64, device=DEV)
+    probs = torch.empty(B, k, V, device=DEV)
+    prev = torch.tensor([1, 2, 3], device=DEV)
+    markov_rows(logits, prev, samp, noise, drafts, probs, 0, head)
+    an, cn = a.cpu().numpy(), cvec.cpu().numpy()
+    sampling = dict(temps=samp.temperatures.cpu().numpy(), top_k=samp.top_k.cpu().numpy(),
+                    top_p=samp.top_p.cpu().numpy(), max_top_k=samp.max_top_k, has_top_p=samp.has_top_p)
+    want, want_probs = OM.markov_rows(logits.cpu().numpy(), prev.cpu().numpy(),
+                                      lambda p: an[p][:, None] * cn[None, :], sampling, noise.cpu().numpy(), 0)
+    assert drafts.cpu().numpy().tolist() == want.tolist()
+    np.testing.assert_allclose(probs.cpu().numpy(), want_probs, rtol=1e-5, atol=1e-8)
