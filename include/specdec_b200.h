@@ -72,6 +72,21 @@ int specdec_race(const float* weights, long long R, long long V, const float* E,
                  unsigned long long offset_E, long long* out, void* workspace, size_t workspace_bytes,
                  void* stream);
 
+/* specdec_accept without a workspace, for callers that cannot allocate device memory: a plugin whose host owns
+ * the device memory budget and forbids cudaMalloc from extensions, or a latency-critical caller that may not
+ * call cudaMalloc (which can synchronise the device).  No counterpart in the reference (it allocates through
+ * torch).  Scratch is a fixed ~0.7 MB array in the library's device memory (held by every GPU that loads the
+ * library until exit); T is limited to 1024 verified rows, larger calls fail with status 3.  The first call on
+ * a device looks the array's address up (cudaGetSymbolAddress) and should come before any stream capture.
+ * Every call clears the array's tickets and keys first; calls that overlap on the GPU race on the array.
+ * Arguments and results as specdec_accept. */
+int specdec_accept_noalloc(const void* x, int x_is_probs, int dtype, long long T, long long V, const float* q,
+                           const long long* drafts, long long B, long long k, const long long* verified_lens,
+                           const float* temperature, const long long* top_k, const float* top_p, int max_top_k,
+                           int has_top_p, const float* u, const float* E, unsigned long long seed,
+                           unsigned long long offset_u, unsigned long long offset_E, long long* n_accept,
+                           long long* tail, void* stream);
+
 /* ------------------------------------------------------------------------------------------ kernel 2: attention */
 /* store_kvcache (nanovllm/layers/attention.py:10-40, the Triton store_kvcache_kernel): key/value rows [N, Hkv, D]
  * bf16 (row strides in elements) to flat slots slot_mapping[N] (int32) of k_cache / v_cache [num_slots, Hkv, D];

@@ -61,10 +61,10 @@ struct ReqDesc {   // per request: where its tail distribution lives
 struct Layout {
   size_t status, req_ticket, tail_key, tail_ticket, row_key, rows, partial, desc, total;
 };
-static Layout layout(int64_t T) {
+static constexpr Layout layout(int64_t T) {
   Layout L{};
   size_t off = 0;
-  auto take = [&](size_t bytes) {
+  auto take = [&off](size_t bytes) {
     size_t o = off;
     off += (bytes + 255) & ~size_t(255);
     return o;
@@ -1116,3 +1116,63 @@ int specdec_race(const float* weights, long long R, long long V, const float* E,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------- no-allocation entry
+// specdec_accept for callers that cannot allocate device memory at all, not even the workspace the other entry
+// points take: a plugin loaded into a host process that owns the whole device memory budget and forbids its
+// extensions from calling cudaMalloc, or a caller on a latency-critical path where cudaMalloc (which may
+// synchronise the device) is not allowed.  Its scratch is a fixed array in the library's own device memory,
+// sized for at most kNoAllocMaxRows verified rows; every GPU that loads the library holds it until exit.
+namespace specdec {
+namespace sampler {
+
+constexpr long long kNoAllocMaxRows = 1024;
+constexpr size_t kNoAllocBytes = layout(kNoAllocMaxRows).total;            // about 0.7 MB
+constexpr size_t kNoAllocHeaderBytes = layout(1).rows;                     // status, tickets and keys
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+// The array's device address, looked up once per device with that device current.  In host code the array's
+// name is only a host-side stand-in, so kernels always receive this looked-up address.
+static int noalloc_scratch(void** out) {
+  static void* addr[64] = {nullptr};
+  int dev = 0;
+  SPECDEC_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return set_error(kInvalidArgument, "device ordinal %d out of range", dev);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess)
+      return set_error(kCudaError, "cudaGetSymbolAddress of the no-allocation scratch failed: %s",
+                       cudaGetErrorString(e));
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return kOk;
+}
+
+}  // namespace sampler
+}  // namespace specdec
+
+extern "C" int specdec_accept_noalloc(const void* x, int x_is_probs, int dtype, long long T, long long V,
+                                      const float* q, const long long* drafts, long long B, long long k,
+                                      const long long* verified_lens, const float* temperature,
+                                      const long long* top_k, const float* top_p, int max_top_k, int has_top_p,
+                                      const float* u, const float* E, unsigned long long seed,
+                                      unsigned long long offset_u, unsigned long long offset_E,
+                                      long long* n_accept, long long* tail, void* stream) {
+  using namespace specdec::sampler;
+  if (T > kNoAllocMaxRows)
+    return set_error(kUnsupported,
+                     "specdec_accept_noalloc takes at most %lld verified rows (got %lld): its fixed scratch holds "
+                     "%zu bytes; use specdec_accept with a caller workspace for more",
+                     kNoAllocMaxRows, T, kNoAllocBytes);
+  void* scratch = nullptr;
+  if (int st = noalloc_scratch(&scratch)) return st;
+  // The array keeps the previous call's contents: clear the tickets and keys that must start at zero (a call
+  // that stopped part-way could have left some behind).  Calls whose work overlaps on the GPU race on the array.
+  SPECDEC_CUDA_TRY(cudaMemsetAsync(scratch, 0, kNoAllocHeaderBytes, static_cast<cudaStream_t>(stream)));
+  return specdec_accept(x, x_is_probs, dtype, T, V, q, drafts, B, k, verified_lens, temperature, top_k, top_p,
+                        max_top_k, has_top_p, u, E, seed, offset_u, offset_E, n_accept, tail, scratch,
+                        kNoAllocBytes, stream);
+}

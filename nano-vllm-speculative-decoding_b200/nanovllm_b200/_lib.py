@@ -36,6 +36,9 @@ SIGNATURES = {
     "specdec_accept": (_c_int, [_c_void_p, _c_int, _c_int, _c_ll, _c_ll, _c_void_p, _c_void_p, _c_ll, _c_ll,
                                 _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p,
                                 _c_ull, _c_ull, _c_ull, _c_void_p, _c_void_p, _c_void_p, _c_size, _c_void_p]),
+    "specdec_accept_noalloc": (_c_int, [_c_void_p, _c_int, _c_int, _c_ll, _c_ll, _c_void_p, _c_void_p, _c_ll, _c_ll,
+                                        _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_int, _c_void_p,
+                                        _c_void_p, _c_ull, _c_ull, _c_ull, _c_void_p, _c_void_p, _c_void_p]),
     "specdec_accept_greedy": (_c_int, [_c_void_p, _c_int, _c_ll, _c_ll, _c_void_p, _c_ll, _c_ll, _c_void_p,
                                        _c_void_p, _c_void_p, _c_void_p, _c_size, _c_void_p]),
     "specdec_race": (_c_int, [_c_void_p, _c_ll, _c_ll, _c_void_p, _c_ull, _c_ull, _c_void_p, _c_void_p, _c_size,
