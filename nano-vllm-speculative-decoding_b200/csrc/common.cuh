@@ -138,6 +138,83 @@ __device__ __forceinline__ void warp_hist_add(unsigned* hist, unsigned bin, bool
   if (active && (threadIdx.x & 31) == leader) atomicAdd(&hist[bin], (unsigned)__popc(peers));
 }
 
+// Descending bitonic sort of P (a power of two, <= 32 * blockDim) 64-bit keys in shared memory, whole block.
+__device__ __forceinline__ void block_sort_desc_u64(unsigned long long* keys, int P) {
+  for (int size = 2; size <= P; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < P; i += blockDim.x) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const bool desc = (i & size) == 0;
+          const unsigned long long ki = keys[i], kj = keys[j];
+          if (desc ? (ki < kj) : (ki > kj)) { keys[i] = kj; keys[j] = ki; }
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+__device__ __forceinline__ void block_sort_desc_f32(float* keys, int P) {
+  for (int size = 2; size <= P; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < P; i += blockDim.x) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const bool desc = (i & size) == 0;
+          const float ki = keys[i], kj = keys[j];
+          if (desc ? (ki < kj) : (ki > kj)) { keys[i] = kj; keys[j] = ki; }
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// Top-C selection by a thread-maxima bound (whole block of NT threads; C <= NT).  load(g, x) fills the 8 values
+// of element group g (missing ones -inf) and returns how many exist.  Every thread's maximum over its groups is
+// an element; the C-th largest of those NT maxima is therefore <= the row's C-th largest value, so collecting
+// every element at or above it keeps the top C and all of their ties.  Collected entries are 64-bit keys
+// (ordered value << 32 | ~id) in buf (capacity cap); returns the count, or -1 when more than cap elements reach
+// the bound (the caller falls back to an exact radix select).  tmax is NT floats of scratch.
+template <int NT, typename Load>
+__device__ int select_by_thread_max(int ngroups, int C, Load load, float* tmax, unsigned long long* buf, int cap,
+                                    int* s_count) {
+  float mx = -INFINITY;
+  for (int g = threadIdx.x; g < ngroups; g += NT) {
+    float x[8];
+    const int n = load(g, x);
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (e < n) mx = fmaxf(mx, x[e]);
+  }
+  tmax[threadIdx.x] = mx;
+  if (threadIdx.x == 0) *s_count = 0;
+  __syncthreads();
+  block_sort_desc_f32(tmax, NT);
+  const float bound = tmax[C - 1];
+  for (int g = threadIdx.x; g < ngroups; g += NT) {
+    float x[8];
+    const int n = load(g, x);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      if (e < n && x[e] >= bound) {
+        const int slot = atomicAdd(s_count, 1);
+        if (slot < cap)
+          buf[slot] = (static_cast<unsigned long long>(ordered_key(x[e])) << 32) | (0xffffffffu - (unsigned)(g * 8 + e));
+      }
+    }
+  }
+  __syncthreads();
+  const int count = *s_count;
+  if (count > cap) return -1;
+  int P = 1;
+  while (P < count) P <<= 1;
+  for (int i = count + threadIdx.x; i < P; i += NT) buf[i] = 0ull;
+  __syncthreads();
+  block_sort_desc_u64(buf, P);
+  return count;
+}
+
 // Device properties the library needs (cached per device on first use).
 struct DeviceInfo {
   int sm_count;

@@ -28,6 +28,7 @@ namespace markov {
 constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
 constexpr int kMaxCand = 1024;
+constexpr int kSelCap = 4096;          // elements the thread-maxima bound may admit before the radix fallback
 
 struct Args {
   const void* logits;       // [B, k, V] (dtype ldt)
@@ -48,6 +49,7 @@ struct Args {
   int rank;
   __nv_bfloat16* e_next;    // [B, rank]
   int* err;
+  int vec;                  // bf16 logits and bias, V % 8 == 0, 16-byte aligned rows: vector loads
 };
 
 __device__ __forceinline__ float load_any(const void* p, int dt, long long i) {
@@ -60,6 +62,24 @@ __device__ __forceinline__ float row_value(const Args& a, long long lrow, long l
   float x = load_any(a.logits, a.ldt, lrow + v) + load_any(a.bias, a.bdt, brow + v);
   if (a.round_bf16) x = __bfloat162float(__float2bfloat16_rn(x));
   return x;
+}
+
+// The biased values of the 8 consecutive elements of group g (16-byte loads on the vector path); returns how
+// many of them exist.
+__device__ __forceinline__ int load_group(const Args& a, long long lrow, long long brow, int g, float (&x)[8]) {
+  const int v0 = g * 8;
+  const int n = min(8, a.V - v0);
+  if (a.vec && n == 8) {
+    float l8[8], b8[8];
+    unpack16_bf16(ldg16(reinterpret_cast<const __nv_bfloat16*>(a.logits) + lrow + v0), l8);
+    unpack16_bf16(ldg16(reinterpret_cast<const __nv_bfloat16*>(a.bias) + brow + v0), b8);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) x[e] = __bfloat162float(__float2bfloat16_rn(l8[e] + b8[e]));
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) x[e] = e < n ? row_value(a, lrow, brow, v0 + e) : -INFINITY;
+  }
+  return n;
 }
 
 // 1-based rank `rank` among the counted elements: digit d with above(d) < rank <= above(d) + hist[d].
@@ -95,8 +115,11 @@ __device__ void pick_digit(const unsigned* hist, int nbins, int rank, int* s_dig
 }
 
 __global__ void __launch_bounds__(kThreads) markov_step_kernel(const Args a) {
-  __shared__ unsigned hist[4096];
+  __shared__ unsigned long long sel[kSelCap];            // fast-path candidates; the radix fallback's histogram
+  unsigned* hist = reinterpret_cast<unsigned*>(sel);      // (4096 bins) reuses the same bytes
   __shared__ unsigned long long cand[kMaxCand];
+  __shared__ float tmax[kThreads];
+  __shared__ int s_sel;
   __shared__ float cprob[kMaxCand];
   __shared__ int s_digit, s_above, s_cnt, s_prev;
   __shared__ int warp_ties[kWarps], warp_base[kWarps];
@@ -109,11 +132,21 @@ __global__ void __launch_bounds__(kThreads) markov_step_kernel(const Args a) {
   const long long brow = (long long)b * V;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 
+  // Passes over the row read 2 x 32 consecutive groups of 8 elements per warp per iteration (two 16-byte loads
+  // of logits and bias per group in flight per thread); trip counts are warp-uniform.
+  const int ngroups = (V + 7) / 8;
   if (a.greedy) {
     unsigned long long best = 0ull;
-    for (int v = threadIdx.x; v < V; v += kThreads) {
-      const unsigned long long key = argmax_key(row_value(a, lrow, brow, v), (unsigned)v);
-      best = key > best ? key : best;
+    for (int gb = warp * 64; gb < ngroups; gb += kWarps * 64) {
+      float x0[8], x1[8];
+      const int g0 = gb + lane, g1 = gb + 32 + lane;
+      const int n0 = g0 < ngroups ? load_group(a, lrow, brow, g0, x0) : 0;
+      const int n1 = g1 < ngroups ? load_group(a, lrow, brow, g1, x1) : 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        if (e < n0) { const unsigned long long k0 = argmax_key(x0[e], (unsigned)(g0 * 8 + e)); best = k0 > best ? k0 : best; }
+        if (e < n1) { const unsigned long long k1 = argmax_key(x1[e], (unsigned)(g1 * 8 + e)); best = k1 > best ? k1 : best; }
+      }
     }
     best = warp_max_u64(best);
     if (lane == 0) s_red[warp] = best;
@@ -126,6 +159,16 @@ __global__ void __launch_bounds__(kThreads) markov_step_kernel(const Args a) {
     __syncthreads();
   } else {
     const int C = a.C;
+    // ---- fast path: thread-maxima bound, collect, sort (two passes over the row)
+    int fast = -1;
+    if (C <= kThreads) {
+      fast = select_by_thread_max<kThreads>(
+          ngroups, C, [&](int g, float (&x)[8]) { return load_group(a, lrow, brow, g, x); }, tmax, sel, kSelCap,
+          &s_sel);
+      if (fast >= 0)
+        for (int i = threadIdx.x; i < C; i += kThreads) cand[i] = sel[i];
+    }
+    if (fast < 0) {
     // ---- radix select of the C-th largest ordered key
     unsigned prefix = 0, pmask = 0;
     int rank = C;
@@ -138,16 +181,18 @@ __global__ void __launch_bounds__(kThreads) markov_step_kernel(const Args a) {
       const int nb = 1 << width;
       for (int i = threadIdx.x; i < nb; i += kThreads) hist[i] = 0;
       __syncthreads();
-      for (int v0 = threadIdx.x - lane; v0 < V; v0 += kThreads) {   // warp-uniform trip count
-        const int v = v0 + lane;
-        bool hit = false;
-        unsigned bin = 0;
-        if (v < V) {
-          const unsigned key = ordered_key(row_value(a, lrow, brow, v));
-          hit = (key & pmask) == prefix;
-          bin = (key >> shift) & (nb - 1);
+      for (int gb = warp * 64; gb < ngroups; gb += kWarps * 64) {
+        float x0[8], x1[8];
+        const int g0 = gb + lane, g1 = gb + 32 + lane;
+        const int n0 = g0 < ngroups ? load_group(a, lrow, brow, g0, x0) : 0;
+        const int n1 = g1 < ngroups ? load_group(a, lrow, brow, g1, x1) : 0;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const unsigned k0 = ordered_key(x0[e]);
+          warp_hist_add(hist, (k0 >> shift) & (nb - 1), e < n0 && (k0 & pmask) == prefix);
+          const unsigned k1 = ordered_key(x1[e]);
+          warp_hist_add(hist, (k1 >> shift) & (nb - 1), e < n1 && (k1 & pmask) == prefix);
         }
-        warp_hist_add(hist, bin, hit);
       }
       __syncthreads();
       pick_digit(hist, nb, rank, &s_digit, &s_above);
@@ -160,25 +205,30 @@ __global__ void __launch_bounds__(kThreads) markov_step_kernel(const Args a) {
     const unsigned key_c = a.round_bf16 ? (prefix | ((prefix & 0x80000000u) ? 0u : 0xffffu)) : prefix;
     const int need_ties = rank;          // tied values to take, by ascending id
     const int n_gt = C - rank;
-    // ---- values above the C-th (any order) and per-warp tie counts over contiguous id ranges
+    // ---- values above the C-th (any order) and per-warp tie counts over contiguous group ranges
     if (threadIdx.x == 0) s_cnt = 0;
     __syncthreads();
-    const int span = ((V + kWarps - 1) / kWarps + 31) / 32 * 32;
-    const int lo = warp * span, hi = min(V, lo + span);
+    const int gspan = ((ngroups + kWarps - 1) / kWarps + 31) / 32 * 32;
+    const int glo = warp * gspan, ghi = min(ngroups, glo + gspan);
     int ties = 0;
-    for (int base = lo; base < hi; base += 32) {
-      const int v = base + lane;
-      bool tie = false;
-      if (v < hi) {
-        const unsigned key = ordered_key(row_value(a, lrow, brow, v));
-        if (key > key_c) {
-          const int slot = atomicAdd(&s_cnt, 1);
-          if (slot < kMaxCand) cand[slot] = (static_cast<unsigned long long>(key) << 32) | (0xffffffffu - v);
+    for (int gb = glo; gb < ghi; gb += 32) {
+      const int g = gb + lane;
+      float x[8];
+      const int n = g < ghi ? load_group(a, lrow, brow, g, x) : 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        if (e < n) {
+          const unsigned key = ordered_key(x[e]);
+          if (key > key_c) {
+            const int slot = atomicAdd(&s_cnt, 1);
+            if (slot < kMaxCand)
+              cand[slot] = (static_cast<unsigned long long>(key) << 32) | (0xffffffffu - (unsigned)(g * 8 + e));
+          }
+          ties += key == key_c;
         }
-        tie = key == key_c;
       }
-      ties += __popc(__ballot_sync(0xffffffffu, tie));
     }
+    ties = __reduce_add_sync(0xffffffffu, ties);
     if (lane == 0) warp_ties[warp] = ties;
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -189,17 +239,34 @@ __global__ void __launch_bounds__(kThreads) markov_step_kernel(const Args a) {
       }
     }
     __syncthreads();
-    // ---- the first need_ties tied values by ascending id
+    // ---- the first need_ties tied values by ascending id (lane order = id order within a step)
     if (need_ties > 0 && warp_base[warp] < need_ties) {
       int seen = warp_base[warp];
-      for (int base = lo; base < hi && seen < need_ties; base += 32) {
-        const int v = base + lane;
-        bool tie = false;
-        if (v < hi) tie = ordered_key(row_value(a, lrow, brow, v)) == key_c;
-        const unsigned mask = __ballot_sync(0xffffffffu, tie);
-        const int r = seen + __popc(mask & ((1u << lane) - 1u));
-        if (tie && r < need_ties) cand[n_gt + r] = (static_cast<unsigned long long>(key_c) << 32) | (0xffffffffu - v);
-        seen += __popc(mask);
+      for (int gb = glo; gb < ghi && seen < need_ties; gb += 32) {
+        const int g = gb + lane;
+        float x[8];
+        const int n = g < ghi ? load_group(a, lrow, brow, g, x) : 0;
+        unsigned mask = 0;
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (e < n && ordered_key(x[e]) == key_c) mask |= 1u << e;
+        const int cnt = __popc(mask);
+        int incl = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int nb = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += nb;
+        }
+        int r = seen + incl - cnt;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          if (mask & (1u << e)) {
+            if (r < need_ties) cand[n_gt + r] = (static_cast<unsigned long long>(key_c) << 32) |
+                                                (0xffffffffu - (unsigned)(g * 8 + e));
+            ++r;
+          }
+        }
+        seen += __shfl_sync(0xffffffffu, incl, 31);
       }
     }
     // ---- sort descending (value desc, id asc); pad with 0 keys
@@ -207,19 +274,9 @@ __global__ void __launch_bounds__(kThreads) markov_step_kernel(const Args a) {
     while (P < C) P <<= 1;
     for (int i = C + threadIdx.x; i < P; i += kThreads) cand[i] = 0ull;
     __syncthreads();
-    for (int size = 2; size <= P; size <<= 1) {
-      for (int stride = size >> 1; stride > 0; stride >>= 1) {
-        for (int i = threadIdx.x; i < P; i += kThreads) {
-          const int jx = i ^ stride;
-          if (jx > i) {
-            const bool desc = (i & size) == 0;
-            const unsigned long long ci = cand[i], cj = cand[jx];
-            if (desc ? (ci < cj) : (ci > cj)) { cand[i] = cj; cand[jx] = ci; }
-          }
-        }
-        __syncthreads();
-      }
-    }
+    block_sort_desc_u64(cand, P);
+    }  // radix fallback
+    __syncthreads();
     // ---- probs_from_logits over the C candidates (spec_sampler.py:65-96 on a [C] row)
     const float temp = a.temperature[b];
     if (threadIdx.x == 0) {
@@ -335,6 +392,8 @@ int specdec_markov_step(const void* logits, int logits_dtype, const void* bias, 
   a.noise = noise; a.noise_width = noise_width; a.drafts = drafts; a.probs = probs; a.prev_out = prev_out;
   a.w1 = static_cast<const __nv_bfloat16*>(w1); a.rank = rank; a.e_next = static_cast<__nv_bfloat16*>(e_next);
   a.err = err;
+  a.vec = logits_dtype == kBF16 && bias_dtype == kBF16 && V % 8 == 0 &&
+          ((reinterpret_cast<uintptr_t>(logits) | reinterpret_cast<uintptr_t>(bias)) & 15) == 0;
   markov_step_kernel<<<B, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
   SPECDEC_LAUNCH_CHECK();
   return kOk;

@@ -510,11 +510,43 @@ __device__ __forceinline__ float scaled_at(const T* row, int v, float temp) {
   return temp == 1.0f ? f : scale_logit(f, temp);
 }
 
+// Scaled logits (x / T) of the 8 consecutive elements of group g of a row (16-byte loads when vec); returns how
+// many exist; missing ones are -inf.
+template <typename T>
+__device__ __forceinline__ int load_group_scaled(const T* row, int g, int V, int vec, float temp, float (&f)[8]) {
+  const int v0 = g * 8;
+  const int n = min(8, V - v0);
+  if (vec && n == 8) {
+    if constexpr (sizeof(T) == 4) {
+      float lo[4], hi[4];
+      unpack16(ldg16(row + v0), lo);
+      unpack16(ldg16(row + v0 + 4), hi);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) { f[e] = lo[e]; f[e + 4] = hi[e]; }
+    } else if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      unpack16_bf16(ldg16(row + v0), f);
+    } else {
+      unpack16_f16(ldg16(row + v0), f);
+    }
+    if (temp != 1.0f) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] = scale_logit(f[e], temp);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) f[e] = e < n ? scaled_at(row, v0 + e, temp) : -INFINITY;
+  }
+  return n;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kTopkThreads) topk_stats_kernel(Args a, int mode) {
   constexpr int NT = kTopkThreads;
   __shared__ int s_start[kMaxRequests + 1];
-  __shared__ unsigned hist[4096];
+  __shared__ unsigned long long sel[4096];                // fast-path candidates; the radix fallback's histogram
+  unsigned* hist = reinterpret_cast<unsigned*>(sel);      // (4096 bins) reuses the same bytes
+  __shared__ float tmax[kTopkThreads];
+  __shared__ int s_sel;
   __shared__ float cand[kMaxTopK];
   __shared__ int s_digit, s_above, s_cnt, s_last;
   __shared__ float s_thr;
@@ -545,7 +577,19 @@ __global__ void __launch_bounds__(kTopkThreads) topk_stats_kernel(Args a, int mo
       return;
     }
     const int K = (int)(tk < V ? tk : V);
-    // ---- radix select of the K-th largest key over three digits (11, 11, 10 bits)
+    // ---- fast path: thread-maxima bound, collect, sort (two passes over the row)
+    int fast = -1;
+    if (K <= NT) {
+      fast = select_by_thread_max<NT>(
+          (V + 7) / 8, K, [&](int g, float (&x)[8]) { return load_group_scaled(row, g, V, a.vec_ok, temp, x); },
+          tmax, sel, 4096, &s_sel);
+      if (fast >= 0) {
+        for (int i = threadIdx.x; i < K; i += NT) cand[i] = key_to_float((unsigned)(sel[i] >> 32));
+        __syncthreads();
+      }
+    }
+    if (fast < 0) {
+    // ---- radix select of the K-th largest key over three digits (12, 12, 8 bits)
     unsigned prefix = 0, pmask = 0;
     int rank = K;
     const int shifts[3] = {20, 8, 0};
@@ -555,16 +599,19 @@ __global__ void __launch_bounds__(kTopkThreads) topk_stats_kernel(Args a, int mo
       const int nb = 1 << widths[p];
       for (int i = threadIdx.x; i < 4096; i += NT) hist[i] = 0;
       __syncthreads();
-      for (int v0 = threadIdx.x - lane; v0 < V; v0 += NT) {     // warp-uniform trip count
-        const int v = v0 + lane;
-        bool hit = false;
-        unsigned bin = 0;
-        if (v < V) {
-          const unsigned key = ordered_key(scaled_at(row, v, temp));
-          hit = (key & pmask) == prefix;
-          bin = (key >> shifts[p]) & (nb - 1);
+      const int ngroups = (V + 7) / 8;
+      for (int gb = (threadIdx.x - lane) * 2; gb < ngroups; gb += NT * 2) {   // warp-uniform trip count
+        float x0[8], x1[8];
+        const int g0 = gb + lane, g1 = gb + 32 + lane;
+        const int n0 = g0 < ngroups ? load_group_scaled(row, g0, V, a.vec_ok, temp, x0) : 0;
+        const int n1 = g1 < ngroups ? load_group_scaled(row, g1, V, a.vec_ok, temp, x1) : 0;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const unsigned k0 = ordered_key(x0[e]);
+          warp_hist_add(hist, (k0 >> shifts[p]) & (nb - 1), e < n0 && (k0 & pmask) == prefix);
+          const unsigned k1 = ordered_key(x1[e]);
+          warp_hist_add(hist, (k1 >> shifts[p]) & (nb - 1), e < n1 && (k1 & pmask) == prefix);
         }
-        warp_hist_add(hist, bin, hit);
       }
       __syncthreads();
       select_digit<NT>(hist, nb, rank, &s_digit, &s_above);
@@ -578,11 +625,18 @@ __global__ void __launch_bounds__(kTopkThreads) topk_stats_kernel(Args a, int mo
     // ---- collect the values above the K-th, fill the rest with it, sort descending
     if (threadIdx.x == 0) s_cnt = 0;
     __syncthreads();
-    for (int v = threadIdx.x; v < V; v += NT) {
-      float f = scaled_at(row, v, temp);
-      if (ordered_key(f) > key_k) {
-        int slot = atomicAdd(&s_cnt, 1);
-        if (slot < kMaxTopK) cand[slot] = f;
+    {
+      const int ngroups = (V + 7) / 8;
+      for (int g = threadIdx.x; g < ngroups; g += NT) {
+        float x[8];
+        const int n = load_group_scaled(row, g, V, a.vec_ok, temp, x);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          if (e < n && ordered_key(x[e]) > key_k) {
+            int slot = atomicAdd(&s_cnt, 1);
+            if (slot < kMaxTopK) cand[slot] = x[e];
+          }
+        }
       }
     }
     __syncthreads();
@@ -607,6 +661,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_stats_kernel(Args a, int mo
         __syncthreads();
       }
     }
+    }  // radix fallback
     // ---- thresholds (one thread; K is small)
     if (threadIdx.x == 0) {
       float th = cand[K - 1];
@@ -631,9 +686,15 @@ __global__ void __launch_bounds__(kTopkThreads) topk_stats_kernel(Args a, int mo
     m = cand[0];
     // ---- sum over the kept entries
     float ls = 0.0f;
-    for (int v = threadIdx.x; v < V; v += NT) {
-      float f = scaled_at(row, v, temp);
-      if (f >= thr) ls += exp_sum_term(f - m);
+    {
+      const int ngroups = (V + 7) / 8;
+      for (int g = threadIdx.x; g < ngroups; g += NT) {
+        float x[8];
+        const int n = load_group_scaled(row, g, V, a.vec_ok, temp, x);
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (e < n && x[e] >= thr) ls += exp_sum_term(x[e] - m);
+      }
     }
     ls = warp_sum_f32(ls);
     __shared__ float sm_sum[NT / 32];

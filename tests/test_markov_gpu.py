@@ -128,3 +128,30 @@ def test_whole_vocabulary_rows_use_the_sampler_kernels():
                                       lambda p: an[p][:, None] * cn[None, :], sampling, noise.cpu().numpy(), 0)
     assert drafts.cpu().numpy().tolist() == want.tolist()
     np.testing.assert_allclose(probs.cpu().numpy(), want_probs, rtol=1e-5, atol=1e-8)
+
+
+@pytest.mark.parametrize("top_k", [5, 500])
+def test_candidate_selection_paths(top_k):
+    """C = top_k + 64 candidates: <= 512 takes the thread-maxima selection, > 512 the exact radix fallback; both
+    must give the oracle's drafts and q (bf16 logits and bias, so many candidates tie)."""
+    from nanovllm_b200.markov import markov_rows, num_candidates
+    from oracle.ctx_store import bf16
+    B, k, V = 5, 3, 6000
+    g = torch.Generator(device=DEV).manual_seed(top_k)
+    logits = (torch.randn(B, k, V, device=DEV, generator=g) * 2).bfloat16()
+    table = (torch.randn(64, V, device=DEV, generator=g)).bfloat16()
+    head = lambda prev: table[prev % 64]
+    samp = sampling_of([1.0, 0.8, 1.0, 0.6, 1.2], [top_k] * B, [1.0, 0.9, 1.0, 0.5, 1.0])
+    cand = num_candidates(samp.max_top_k, samp.all_top_k, V)
+    noise = torch.empty(B, k, cand, device=DEV).exponential_(generator=g).clamp_min_(1e-10)
+    drafts = torch.empty(B, k, dtype=torch.int64, device=DEV)
+    probs = torch.empty(B, k, V, device=DEV)
+    prev = torch.randint(V, (B,), device=DEV, generator=g)
+    markov_rows(logits, prev, samp, noise, drafts, probs, cand, head)
+    tab = table.float().cpu().numpy()
+    sampling = dict(temps=samp.temperatures.cpu().numpy(), top_k=samp.top_k.cpu().numpy(),
+                    top_p=samp.top_p.cpu().numpy(), max_top_k=samp.max_top_k, has_top_p=samp.has_top_p)
+    want, want_probs = OM.markov_rows(logits.float().cpu().numpy(), prev.cpu().numpy(), lambda p: tab[p % 64],
+                                      sampling, noise.cpu().numpy(), cand, round_fn=bf16)
+    assert drafts.cpu().numpy().tolist() == want.tolist()
+    np.testing.assert_allclose(probs.cpu().numpy(), want_probs, rtol=1e-5, atol=1e-8)
