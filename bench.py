@@ -405,25 +405,13 @@ def main() -> int:
     def step_device():
         return rnd.verify_and_accept(num_tokens, batch, w.drafts, w.q, w.sampling, gen)
 
-    def barrier():
-        torch.cuda.synchronize()
-        if dist is not None:
-            dist.barrier()
-        torch.cuda.synchronize()
+    from nanovllm_b200.replicas import barrier, reduce_scalar
 
     def max_over_ranks(x: float) -> float:
-        if dist is None:
-            return x
-        t = torch.tensor([x], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return reduce_scalar(x, "max")
 
     def sum_over_ranks(x: float) -> float:
-        if dist is None:
-            return x
-        t = torch.tensor([x], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        return float(t.item())
+        return reduce_scalar(x, "sum")
 
     for _ in range(args.warmup):
         step_device()

@@ -117,6 +117,15 @@ __device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v)
   }
   return v;
 }
+// Max of a 64-bit key over the warp with two 32-bit warp reductions: the high words, then the low words of the
+// lanes holding the winning high word.  All 32 lanes must call it.
+__device__ __forceinline__ unsigned long long warp_max_u64_redux(unsigned long long v) {
+  const unsigned hi = static_cast<unsigned>(v >> 32), lo = static_cast<unsigned>(v);
+  const unsigned mhi = __reduce_max_sync(0xffffffffu, hi);
+  const unsigned mlo = __reduce_max_sync(0xffffffffu, hi == mhi ? lo : 0u);
+  return (static_cast<unsigned long long>(mhi) << 32) | mlo;
+}
+
 __device__ __forceinline__ float warp_max_f32(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

@@ -264,51 +264,61 @@ __device__ void row_range_ms(const T* row, int lo, int hi, float temp, int vec_o
   constexpr int VE = 16 / sizeof(T);  // elements per 16-byte vector
   const bool unit_temp = temp == 1.0f;
   if (vec_ok) {
-    // lo is a multiple of VE and the row base is 16-byte aligned.
+    // lo is a multiple of VE and the row base is 16-byte aligned.  Four 16-byte vectors per iteration: their
+    // maximum first (one rescale of the running sum), then exp2(x * log2e - m * log2e) per element.
     const int nvec = (hi - lo) / VE;
     const char* base = reinterpret_cast<const char*>(row + lo);
+    const float kLog2e = 1.4426950408889634f;
     for (int i = threadIdx.x; i < nvec; i += NT * 4) {
       uint4 raw[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         int j = i + u * NT;
-        if (j < nvec) raw[u] = ldg16(base + (size_t)j * 16);
+        raw[u] = j < nvec ? ldg16(base + (size_t)j * 16) : make_uint4(0xff800000u, 0xff800000u, 0xff800000u, 0xff800000u);
       }
+      float f[4][VE];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        int j = i + u * NT;
-        if (j >= nvec) break;
-        float f[VE];
+        const bool live = i + u * NT < nvec;
         if constexpr (sizeof(T) == 4) {
           float t4[4];
           unpack16(raw[u], t4);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) f[e] = t4[e];
+          for (int e = 0; e < 4; ++e) f[u][e] = live ? t4[e] : -INFINITY;
         } else if constexpr (std::is_same<T, __nv_bfloat16>::value) {
           float t8[8];
           unpack16_bf16(raw[u], t8);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) f[e] = t8[e];
+          for (int e = 0; e < 8; ++e) f[u][e] = live ? t8[e] : -INFINITY;
         } else {
           float t8[8];
           unpack16_f16(raw[u], t8);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) f[e] = t8[e];
+          for (int e = 0; e < 8; ++e) f[u][e] = live ? t8[e] : -INFINITY;
         }
-        float vm = -INFINITY;
+      }
+      float vm = -INFINITY;
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
 #pragma unroll
         for (int e = 0; e < VE; ++e) {
-          if (!unit_temp) f[e] = scale_logit(f[e], temp);
-          vm = fmaxf(vm, f[e]);
+          if (!unit_temp) f[u][e] = scale_logit(f[u][e], temp);
+          vm = fmaxf(vm, f[u][e]);
         }
-        if (vm > m) {
-          if (m != -INFINITY) s *= exp_sum_term(m - vm);
-          m = vm;
-        }
-        if (m != -INFINITY) {
+      if (vm > m) {
+        if (m != -INFINITY) s *= exp_sum_term(m - vm);
+        m = vm;
+      }
+      if (m != -INFINITY) {
+        const float mb = m * kLog2e;
 #pragma unroll
-          for (int e = 0; e < VE; ++e) s += exp_sum_term(f[e] - m);
-        }
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+          for (int e = 0; e < VE; ++e) {
+            float y;
+            asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(fmaf(f[u][e], kLog2e, -mb)));
+            s += y;
+          }
       }
     }
     // scalar tail of the range (fewer than VE elements)
@@ -771,12 +781,19 @@ __global__ void __launch_bounds__(kThreads) write_probs_kernel(Args a, int merge
 __device__ __forceinline__ void warp_segment_reduce(unsigned long long key, int b, bool active,
                                                     unsigned long long* s_best) {
   const int lane = threadIdx.x & 31;
-  unsigned pending = __ballot_sync(0xffffffffu, active);
+  const int b0 = __shfl_sync(0xffffffffu, b, 0);
+  const unsigned all = __ballot_sync(0xffffffffu, active);
+  if (all == 0xffffffffu && __all_sync(0xffffffffu, b == b0)) {   // the common case: one row, every lane active
+    const unsigned long long m = warp_max_u64_redux(key);
+    if (lane == 0) atomicMax(&s_best[b0], m);
+    return;
+  }
+  unsigned pending = all;
   while (pending) {
     const int leader = __ffs(pending) - 1;
     const int bb = __shfl_sync(0xffffffffu, b, leader);
     const bool mine = active && b == bb;
-    unsigned long long kk = warp_max_u64(mine ? key : 0ull);
+    const unsigned long long kk = warp_max_u64_redux(mine ? key : 0ull);
     if (lane == leader) atomicMax(&s_best[bb], kk);
     pending &= ~__ballot_sync(0xffffffffu, mine);
   }
