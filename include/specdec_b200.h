@@ -101,13 +101,16 @@ int specdec_store_kvcache(const void* key, long long key_row_stride, const void*
  * q [T, H, 128] bf16 (row stride q_row_stride elements); caches [num_slots / block_size, block_size, Hkv, 128]
  * bf16; block_tables int32 [R, W]; out [T, H, 128] bf16 (row stride out_row_stride).  Limits: head_dim 128,
  * H / Hkv in {1, 2, 4, 8}, max_seqlen_q * H / Hkv <= 32, block_size a multiple of 128.  Rows whose metadata
- * is inconsistent are skipped and recorded in *err. */
+ * is inconsistent are skipped and recorded in *err.  workspace: 256-byte aligned device bytes, zero-filled once
+ * before first use (the kernel leaves it zeroed), at least specdec_attention_workspace_bytes(R, Hkv); calls that
+ * share a workspace must not overlap on the GPU. */
+long long specdec_attention_workspace_bytes(int R, int num_kv_heads);
 int specdec_paged_attention(const void* q, long long T, long long q_row_stride, int num_heads, int num_kv_heads,
                             int head_dim, const void* k_cache, const void* v_cache, long long num_slots,
                             int block_size, const int* cu_seqlens_q, const int* cu_seqlens_k,
                             const int* context_lens, int q_per_seq, int R, const int* block_tables, int W,
                             int max_seqlen_q, float softmax_scale, int causal, void* out, long long out_row_stride,
-                            int* err, void* stream);
+                            void* workspace, long long workspace_bytes, int* err, void* stream);
 
 /* ------------------------------------------------------------------------------------------ kernel 3: Markov rows */
 /* One row step of DFlashDrafter._markov_rows (nanovllm/engine/speculative.py:163-184) for every batch row: with

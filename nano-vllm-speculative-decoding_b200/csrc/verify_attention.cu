@@ -11,14 +11,21 @@
 //                                          DFlash draft block passes causal=False)
 //   restated on CPU by tests/fake_paged_attention.py:14-41 (SDPA with the same mask rule).
 //
-// Design (B200).  One CTA per (row, KV head).  The row's <= 8 query positions times the GQA group's 4 query
-// heads are packed into N = 32 columns, so every K/V tile of that head is read from HBM exactly once.  The
-// tensor core runs swap-AB: S^T[128 keys x 32] = K_tile[128 x 128] . Q^T and O^T[128 dims x 32] += V^T . P^T,
-// both M = 128 UMMAs with fp32 accumulators in TMEM (S double-buffered, O resident for the whole row).  K and V
-// tiles of 128 keys (half a 256-slot block) arrive by TMA through one tensor map over the whole paged cache
-// (coordinates: dim, head, physical slot), so the block table is a coordinate, not a gather.
-//   warp 0      TMA producer (Q once, then K/V tiles into 3-stage rings)
+// Design (B200).  A persistent kernel, one CTA per SM.  Work item = (row, KV head): the row's <= 8 query
+// positions times the GQA group's 4 query heads are packed into N = 32 columns, so every K/V tile of that head is
+// read from HBM exactly once.  The items' 128-key tiles form one sequence that is cut into equal contiguous
+// shares, one per CTA (stream-K): no wave quantisation, and every SM streams the same number of tiles.  An item
+// cut between CTAs is finished by whichever of its CTAs arrives last (an atomic counter per item): each piece is
+// published as unnormalised O^T with its column maxima and sums, and the last one merges them in CTA order (the
+// output does not depend on arrival order); nobody waits.
+// The tensor core runs swap-AB: S^T[128 keys x 32] = K_tile[128 x 128] . Q^T and O^T[128 dims x 32] += V^T . P^T,
+// both M = 128 UMMAs with fp32 accumulators in TMEM (S and O double-buffered, O by item).  K and V tiles of 128
+// keys (half a 256-slot block) arrive by TMA through one tensor map over the whole paged cache (coordinates: dim,
+// head, physical slot), so the block table is a coordinate, not a gather.  The pipelines run across items: the
+// next item's Q (double-buffered) and first tiles load while the current item's epilogue runs.
+//   warp 0      TMA producer (Q per item, K/V tiles into 3-stage rings)
 //   warp 1      TMEM allocator + single-thread MMA issuer
+//   warp 2      prologue: this CTA's share of the tile sequence from the row metadata
 //   warps 4-7   softmax over keys (one TMEM lane = one key), P^T to shared memory, O rescale, epilogue
 // The softmax is online per query column with lazy rescaling (O is rescaled only when a column's running max
 // grows by more than 2^8), masked by key index (bottom-right causal or context length).  Keys past the row's
@@ -28,6 +35,7 @@
 
 #include <cudaTypedefs.h>
 #include <math.h>
+#include <stddef.h>
 
 namespace specdec {
 namespace attention {
@@ -38,22 +46,28 @@ constexpr int kHeadDim = 128;
 constexpr int kKeysPerTile = 128;
 constexpr int kCols = 32;              // packed query columns (group x positions)
 constexpr int kStages = 3;             // K ring and V ring depth
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;            // warps 0-3: TMA, MMA, prologue, idle; 4-11: softmax
 constexpr int kHalfTileBytes = kKeysPerTile * 128;     // 64 dims x 128 keys bf16 = 16 KB
 constexpr int kTileBytes = 2 * kHalfTileBytes;          // 32 KB
 constexpr int kQHalfBytes = kCols * 128;                // 32 rows x 64 dims bf16 = 4 KB
 constexpr int kPBytes = kKeysPerTile * kCols * 2;       // 8 KB
-constexpr uint32_t kTmemCols = 128;                     // S0 | S1 | O | spare
+constexpr uint32_t kTmemCols = 128;                     // S0 | S1 | O0 | O1
 
 // error codes written to the global error word
 constexpr int kErrTimeoutQ = 11, kErrTimeoutK = 12, kErrTimeoutV = 13, kErrTimeoutS = 14, kErrTimeoutP = 15,
               kErrTimeoutO = 16, kErrTimeoutEmpty = 17;
+
+// One piece of a split item: O^T columns (unnormalised, relative to the piece's running maxima) then the maxima m
+// and the sums l of the 32 columns.
+constexpr int kPartialFloats = kCols * kHeadDim + 2 * kCols;
+constexpr float kNegBig = -1.0e30f;    // start value of the running maxima (finite: no -inf arithmetic)
 
 struct Args {
   const int* cu_seqlens_q;   // [R + 1] or null (decode mode)
   const int* cu_seqlens_k;   // [R + 1] or null (decode mode)
   const int* context_lens;   // [R] (decode mode)
   int q_per_seq;             // decode mode: queries per row
+  int R;
   const int* block_tables;   // [R, W]
   int W, block_size;
   int H, Hkv;
@@ -61,25 +75,37 @@ struct Args {
   int causal;
   __nv_bfloat16* out;        // [T, H, D]
   long long out_row_stride;  // elements between tokens of out
+  int* counters;             // [R * Hkv] arrivals at split items; zero between launches (the last arrival resets)
+  float* partial;            // [2 * gridDim.x][kPartialFloats]: slot 2c = CTA c's first item, 2c + 1 its last
   int* err;                  // global error word (0 = ok)
 };
 
 struct Smem {
-  uint64_t q_full;
+  uint64_t q_full[2], q_empty[2];
   uint64_t k_full[kStages], k_empty[kStages], v_full[kStages], v_empty[kStages];
-  uint64_t s_full[2], s_free[2], p_full[2], o_done[2];
+  uint64_t s_full[2], s_free[2], p_full[2], o_done[2], o_free[2];
   uint32_t tmem_base;
   int abort;
-  float red_max[2][4][32];   // per-warp column maxima, by tile parity
-  float red_sum[1][4][32];   // per-warp column sums (epilogue)
+  long long total_tiles;     // tiles of all items
+  long long x_begin, x_end;  // this CTA's share [x_begin, x_end) of the tile sequence
+  long long row_tile0;       // sequence index of the first tile of row b_start
+  int b_start;               // row holding tile x_begin
+  int active;                // CTAs given tiles: min(gridDim.x, total_tiles)
+  int last_piece;            // the epilogue's broadcast: this CTA combines the split item
+  alignas(16) float red_max[2][32][4];   // [tile parity][column][warp] maxima (read as float4)
+  alignas(16) float red_sum[32][4];      // [column][warp] sums (epilogue)
 };
+static_assert(offsetof(Smem, red_max) % 16 == 0 && offsetof(Smem, red_sum) % 16 == 0, "float4 reads need 16 B");
+static_assert(offsetof(Smem, total_tiles) % 8 == 0, "64-bit fields need 8 B");
 
+constexpr int kQBytes = 2 * kQHalfBytes;                       // 8 KB, double-buffered by item
 constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + 2 * kQHalfBytes;                 // 8 KB
+constexpr int kOffK = kOffQ + 2 * kQBytes;                     // 16 KB
 constexpr int kOffV = kOffK + kStages * kTileBytes;
 constexpr int kOffP = kOffV + kStages * kTileBytes;
 constexpr int kOffCtl = kOffP + 2 * kPBytes;
 constexpr int kSmemBytes = kOffCtl + (int)sizeof(Smem) + 1024;   // + alignment slack
+static_assert(kSmemBytes <= 232448, "shared memory above the sm_100 per-CTA limit");
 
 // Max over the warp's 32 lanes in one instruction (sm_100a redux.sync on f32).
 __device__ __forceinline__ float warp_max_redux(float v) {
@@ -88,22 +114,108 @@ __device__ __forceinline__ float warp_max_redux(float v) {
   return r;
 }
 
-// max (ADD=false) or sum (ADD=true) over the 32 lanes of column `lane`; v is consumed.
-template <bool ADD>
-__device__ __forceinline__ float column_reduce(float (&v)[32], int lane) {
+// Sum over the 32 lanes of 16 columns held by every lane; lane j ends with column (j & 15)'s sum; v is consumed.
+__device__ __forceinline__ float column_reduce16(float (&v)[16], int lane) {
 #pragma unroll
-  for (int w = 16; w >= 1; w >>= 1) {
+  for (int c = 0; c < 16; ++c) v[c] += __shfl_xor_sync(0xffffffffu, v[c], 16);
+#pragma unroll
+  for (int w = 8; w >= 1; w >>= 1) {
     const bool upper = (lane & w) != 0;
 #pragma unroll
     for (int c = 0; c < w; ++c) {
       const float send = upper ? v[c] : v[c + w];
       const float keep = upper ? v[c + w] : v[c];
-      const float recv = __shfl_xor_sync(0xffffffffu, send, w);
-      v[c] = ADD ? keep + recv : fmaxf(keep, recv);
+      v[c] = keep + __shfl_xor_sync(0xffffffffu, send, w);
     }
   }
   return v[0];
 }
+
+// A row's queries and keys; nt = 0 when the row has no work (no queries, or metadata that the kernel rejects).
+struct RowInfo {
+  int q_start, ql, L, nt;
+};
+
+template <int QMAX>
+__device__ __forceinline__ RowInfo row_info(const Args& a, int b, bool report) {
+  RowInfo r;
+  if (a.cu_seqlens_q) {
+    r.q_start = a.cu_seqlens_q[b];
+    r.ql = a.cu_seqlens_q[b + 1] - r.q_start;
+    r.L = a.cu_seqlens_k[b + 1] - a.cu_seqlens_k[b];
+  } else {
+    r.q_start = b * a.q_per_seq;
+    r.ql = a.q_per_seq;
+    r.L = a.context_lens[b];
+  }
+  r.nt = 0;
+  if (r.ql > 0) {
+    if (r.ql > QMAX || r.L <= 0 || r.L > a.W * a.block_size) {   // inconsistent metadata: report, never read
+      if (report) atomicCAS(a.err, 0, 2);
+    } else {
+      r.nt = (r.L + kKeysPerTile - 1) / kKeysPerTile;
+    }
+  }
+  return r;
+}
+
+// The item sequence: items (row b, KV head h) in row-major order, item (b, h) holding the sequence's tiles
+// [A, A + r.nt).  Each role of a CTA walks it from the item holding x_begin to the one holding x_end - 1.
+template <int QMAX>
+struct Walk {
+  int b, h;
+  long long A;
+  RowInfo r;
+  __device__ __forceinline__ void start(const Args& a, const Smem& S) {
+    b = S.b_start;
+    r = row_info<QMAX>(a, b, false);
+    h = (int)((S.x_begin - S.row_tile0) / r.nt);
+    A = S.row_tile0 + (long long)h * r.nt;
+  }
+  __device__ __forceinline__ void next(const Args& a) {
+    A += r.nt;
+    if (++h == a.Hkv) {
+      h = 0;
+      do {
+        ++b;
+        r = b < a.R ? row_info<QMAX>(a, b, false) : RowInfo{0, 0, 0, 1};
+      } while (r.nt == 0);
+    }
+  }
+  // this CTA's tiles of the item: item-local [t0, t1)
+  __device__ __forceinline__ int t0(long long x_begin) const { return (int)(x_begin > A ? x_begin - A : 0); }
+  __device__ __forceinline__ int t1(long long x_end) const {
+    return (int)(x_end < A + r.nt ? x_end - A : (long long)r.nt);
+  }
+};
+
+// Tile-by-tile cursor over the CTA's share: the segment (item piece) index n of the current tile and whether the
+// tile is the segment's first / last.
+template <int QMAX>
+struct Cursor {
+  Walk<QMAX> w;
+  int n, left;
+  bool first;
+  __device__ __forceinline__ void start(const Args& a, const Smem& S) {
+    w.start(a, S);
+    n = 0;
+    left = w.t1(S.x_end) - w.t0(S.x_begin);
+    first = true;
+  }
+  __device__ __forceinline__ bool last() const { return left == 1; }
+  __device__ __forceinline__ void advance(const Args& a, long long x_begin, long long x_end) {
+    if (--left == 0) {
+      w.next(a);
+      ++n;
+      left = w.t1(x_end) - w.t0(x_begin);
+      first = true;
+    } else {
+      first = false;
+    }
+  }
+};
+
+__device__ __forceinline__ long long ceil_div(long long x, long long y) { return (x + y - 1) / y; }
 
 template <int G>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -117,40 +229,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   unsigned char* sV = base + kOffV;
   unsigned char* sP = base + kOffP;
   Smem& S = *reinterpret_cast<Smem*>(base + kOffCtl);
-
-  const int h = blockIdx.x;
-  const int b = blockIdx.y;
-  int q_start, ql, L;
-  if (a.cu_seqlens_q) {
-    q_start = a.cu_seqlens_q[b];
-    ql = a.cu_seqlens_q[b + 1] - q_start;
-    L = a.cu_seqlens_k[b + 1] - a.cu_seqlens_k[b];
-  } else {
-    q_start = b * a.q_per_seq;
-    ql = a.q_per_seq;
-    L = a.context_lens[b];
-  }
-  if (ql <= 0) return;
-  if (ql > QMAX || L <= 0 || L > a.W * a.block_size) {   // inconsistent metadata: report, never read past it
-    if (threadIdx.x == 0) atomicCAS(a.err, 0, 2);
-    return;
-  }
-  const int nt = (L + kKeysPerTile - 1) / kKeysPerTile;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    mbar_init(&S.q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&S.q_full[i], 1);
+      mbar_init(&S.q_empty[i], 1);
+      mbar_init(&S.s_full[i], 1);
+      mbar_init(&S.s_free[i], 8);     // one elected arrival per softmax warp
+      mbar_init(&S.p_full[i], 8);
+      mbar_init(&S.o_done[i], 1);
+      mbar_init(&S.o_free[i], 8);
+    }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&S.k_full[s], 1);
       mbar_init(&S.k_empty[s], 1);
       mbar_init(&S.v_full[s], 1);
       mbar_init(&S.v_empty[s], 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&S.s_full[i], 1);
-      mbar_init(&S.s_free[i], 4);     // one elected arrival per softmax warp
-      mbar_init(&S.p_full[i], 4);
-      mbar_init(&S.o_done[i], 1);
     }
     S.abort = 0;
     fence_barrier_init();
@@ -164,224 +259,355 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tensormap(&kmap);
     prefetch_tensormap(&vmap);
   }
+  if (warp == 2) {
+    // ---- this CTA's share: the tile sequence split evenly over min(grid, tiles) CTAs, then the row holding
+    // its first tile (two passes of 32 rows at a time over the row metadata)
+    long long row_tiles = 0;
+    for (int b0 = 0; b0 < a.R; b0 += 32) {
+      const int b = b0 + lane;
+      const int nt = b < a.R ? row_info<QMAX>(a, b, true).nt : 0;
+      row_tiles += __reduce_add_sync(0xffffffffu, (unsigned)nt);
+    }
+    const long long T = row_tiles * a.Hkv;
+    const long long Ge = T < (long long)gridDim.x ? T : (long long)gridDim.x;
+    const long long c = blockIdx.x;
+    long long xb = 0, xe = 0, row0 = 0;
+    int bstart = 0;
+    if (c < Ge) {
+      xb = T * c / Ge;
+      xe = T * (c + 1) / Ge;
+      long long pre = 0;
+      for (int b0 = 0; b0 < a.R; b0 += 32) {
+        const int b = b0 + lane;
+        const long long v = b < a.R ? (long long)row_info<QMAX>(a, b, false).nt * a.Hkv : 0;
+        long long inc = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const long long y = __shfl_up_sync(0xffffffffu, inc, o);
+          if (lane >= o) inc += y;
+        }
+        const long long first = pre + inc - v;
+        const unsigned hit = __ballot_sync(0xffffffffu, v > 0 && xb >= first && xb < first + v);
+        if (hit) {
+          const int src = __ffs(hit) - 1;
+          bstart = b0 + src;
+          row0 = __shfl_sync(0xffffffffu, first, src);
+          break;
+        }
+        pre += __shfl_sync(0xffffffffu, inc, 31);
+      }
+    }
+    if (lane == 0) {
+      S.total_tiles = T;
+      S.active = (int)Ge;
+      S.x_begin = xb;
+      S.x_end = xe;
+      S.row_tile0 = row0;
+      S.b_start = bstart;
+    }
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = S.tmem_base;
   volatile int* abort = &S.abort;
+  const long long x_begin = S.x_begin, x_end = S.x_end;
+  const int ntiles = (int)(x_end - x_begin);
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      mbar_arrive_expect_tx(&S.q_full, 2 * kQHalfBytes);
-      tma_load_3d(sQ, &qmap, 0, h * G, q_start, &S.q_full);
-      tma_load_3d(sQ + kQHalfBytes, &qmap, 64, h * G, q_start, &S.q_full);
-      const int* table = a.block_tables + (long long)b * a.W;
-      for (int t = 0; t < nt && !*abort; ++t) {
-        const int stage = t % kStages;
-        const uint32_t use = t / kStages;
-        const int key0 = t * kKeysPerTile;
-        const int slot = table[key0 / a.block_size] * a.block_size + key0 % a.block_size;
-        if (t >= kStages && !mbar_wait(&S.k_empty[stage], (use - 1) & 1, abort, a.err, kErrTimeoutEmpty)) break;
-        mbar_arrive_expect_tx(&S.k_full[stage], kTileBytes);
-        tma_load_3d(sK + stage * kTileBytes, &kmap, 0, h, slot, &S.k_full[stage]);
-        tma_load_3d(sK + stage * kTileBytes + kHalfTileBytes, &kmap, 64, h, slot, &S.k_full[stage]);
-        if (t >= kStages && !mbar_wait(&S.v_empty[stage], (use - 1) & 1, abort, a.err, kErrTimeoutEmpty)) break;
-        mbar_arrive_expect_tx(&S.v_full[stage], kTileBytes);
-        tma_load_3d(sV + stage * kTileBytes, &vmap, 0, h, slot, &S.v_full[stage]);
-        tma_load_3d(sV + stage * kTileBytes + kHalfTileBytes, &vmap, 64, h, slot, &S.v_full[stage]);
+    if (lane == 0 && ntiles > 0) {
+      Walk<QMAX> wk;
+      wk.start(a, S);
+      bool ok = true;
+      int g = 0;
+      for (int n = 0; ok && wk.A < x_end; wk.next(a), ++n) {
+        const int qb = n & 1;
+        if (n >= 2 && !mbar_wait(&S.q_empty[qb], ((n - 2) >> 1) & 1, abort, a.err, kErrTimeoutEmpty)) break;
+        unsigned char* q = sQ + qb * kQBytes;
+        mbar_arrive_expect_tx(&S.q_full[qb], kQBytes);
+        tma_load_3d(q, &qmap, 0, wk.h * G, wk.r.q_start, &S.q_full[qb]);
+        tma_load_3d(q + kQHalfBytes, &qmap, 64, wk.h * G, wk.r.q_start, &S.q_full[qb]);
+        const int* table = a.block_tables + (long long)wk.b * a.W;
+        const int t1 = wk.t1(x_end);
+        for (int t = wk.t0(x_begin); t < t1; ++t, ++g) {
+          const int stage = g % kStages;
+          const uint32_t use = g / kStages;
+          const int key0 = t * kKeysPerTile;
+          const int slot = table[key0 / a.block_size] * a.block_size + key0 % a.block_size;
+          if (g >= kStages && !mbar_wait(&S.k_empty[stage], (use - 1) & 1, abort, a.err, kErrTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&S.k_full[stage], kTileBytes);
+          tma_load_3d(sK + stage * kTileBytes, &kmap, 0, wk.h, slot, &S.k_full[stage]);
+          tma_load_3d(sK + stage * kTileBytes + kHalfTileBytes, &kmap, 64, wk.h, slot, &S.k_full[stage]);
+          if (g >= kStages && !mbar_wait(&S.v_empty[stage], (use - 1) & 1, abort, a.err, kErrTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&S.v_full[stage], kTileBytes);
+          tma_load_3d(sV + stage * kTileBytes, &vmap, 0, wk.h, slot, &S.v_full[stage]);
+          tma_load_3d(sV + stage * kTileBytes + kHalfTileBytes, &vmap, 64, wk.h, slot, &S.v_full[stage]);
+        }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && ntiles > 0) {
       const uint32_t idesc_s = idesc_bf16_f32(128, kCols, 0, 0);
       const uint32_t idesc_o = idesc_bf16_f32(128, kCols, 1, 1);
-      const uint32_t tmem_o = tmem + 64;
-      bool ok = mbar_wait(&S.q_full, 0, abort, a.err, kErrTimeoutQ);
-      auto issue_s = [&](int t) -> bool {
-        const int stage = t % kStages;
-        if (!mbar_wait(&S.k_full[stage], (t / kStages) & 1, abort, a.err, kErrTimeoutK)) return false;
-        if (t >= 2 && !mbar_wait(&S.s_free[t & 1], ((t - 2) >> 1) & 1, abort, a.err, kErrTimeoutS)) return false;
+      Cursor<QMAX> cs, cp;     // the score MMAs run two tiles ahead of the PV MMAs
+      cs.start(a, S);
+      cp.start(a, S);
+      auto issue_s = [&](int g) -> bool {
+        const int stage = g % kStages;
+        const int qb = cs.n & 1;
+        if (cs.first && !mbar_wait(&S.q_full[qb], (cs.n >> 1) & 1, abort, a.err, kErrTimeoutQ)) return false;
+        if (!mbar_wait(&S.k_full[stage], (g / kStages) & 1, abort, a.err, kErrTimeoutK)) return false;
+        if (g >= 2 && !mbar_wait(&S.s_free[g & 1], ((g - 2) >> 1) & 1, abort, a.err, kErrTimeoutS)) return false;
         tc_fence_after();
         const unsigned char* kt = sK + stage * kTileBytes;
-        const uint32_t tmem_s = tmem + (t & 1) * 32;
+        const unsigned char* qt = sQ + qb * kQBytes;
+        const uint32_t tmem_s = tmem + (g & 1) * 32;
 #pragma unroll
         for (int kk = 0; kk < kHeadDim / 16; ++kk) {
           const int half = kk >> 2, sub = (kk & 3) * 32;
           const uint64_t adesc = smem_desc(kt + half * kHalfTileBytes + sub, 16, 1024, kSwizzle128B);
-          const uint64_t bdesc = smem_desc(sQ + half * kQHalfBytes + sub, 16, 1024, kSwizzle128B);
+          const uint64_t bdesc = smem_desc(qt + half * kQHalfBytes + sub, 16, 1024, kSwizzle128B);
           mma_bf16_ss(tmem_s, adesc, bdesc, idesc_s, kk > 0 ? 1u : 0u);
         }
-        mma_commit(&S.s_full[t & 1]);
+        mma_commit(&S.s_full[g & 1]);
         mma_commit(&S.k_empty[stage]);
+        if (cs.last()) mma_commit(&S.q_empty[qb]);
+        cs.advance(a, x_begin, x_end);
         return true;
       };
-      auto issue_pv = [&](int t) -> bool {
-        const int stage = t % kStages;
-        if (!mbar_wait(&S.p_full[t & 1], (t >> 1) & 1, abort, a.err, kErrTimeoutP)) return false;
-        if (!mbar_wait(&S.v_full[stage], (t / kStages) & 1, abort, a.err, kErrTimeoutV)) return false;
+      auto issue_pv = [&](int g) -> bool {
+        const int stage = g % kStages;
+        const int ob = cp.n & 1;
+        if (cp.first && cp.n >= 2 && !mbar_wait(&S.o_free[ob], ((cp.n - 2) >> 1) & 1, abort, a.err, kErrTimeoutO))
+          return false;
+        if (!mbar_wait(&S.p_full[g & 1], (g >> 1) & 1, abort, a.err, kErrTimeoutP)) return false;
+        if (!mbar_wait(&S.v_full[stage], (g / kStages) & 1, abort, a.err, kErrTimeoutV)) return false;
         tc_fence_after();
         const unsigned char* vt = sV + stage * kTileBytes;
-        const unsigned char* pt = sP + (t & 1) * kPBytes;
+        const unsigned char* pt = sP + (g & 1) * kPBytes;
+        const uint32_t tmem_o = tmem + 64 + ob * 32;
+        const bool fresh = cp.first;
 #pragma unroll
         for (int kk = 0; kk < kKeysPerTile / 16; ++kk) {
           const uint64_t adesc = smem_desc(vt + kk * 2048, kHalfTileBytes, 1024, kSwizzle128B);
           const uint64_t bdesc = smem_desc(pt + kk * 1024, kPBytes, 512, kSwizzle64B);
-          mma_bf16_ss(tmem_o, adesc, bdesc, idesc_o, (t > 0 || kk > 0) ? 1u : 0u);
+          mma_bf16_ss(tmem_o, adesc, bdesc, idesc_o, (!fresh || kk > 0) ? 1u : 0u);
         }
-        mma_commit(&S.o_done[t & 1]);
+        mma_commit(&S.o_done[g & 1]);
         mma_commit(&S.v_empty[stage]);
+        cp.advance(a, x_begin, x_end);
         return true;
       };
-      // Two score tiles run ahead of the softmax: S(t + 2) is issued as soon as PV(t) is, so the softmax of
-      // tile t + 1 never waits for a score MMA issued after the softmax of tile t.
-      if (ok) ok = issue_s(0);
-      if (ok && nt > 1) ok = issue_s(1);
-      for (int t = 0; t < nt && ok; ++t) {
-        ok = issue_pv(t);
-        if (ok && t + 2 < nt) ok = issue_s(t + 2);
+      // S(g + 2) is issued right after PV(g), so the softmax of tile g + 1 never waits for a score MMA issued
+      // after the softmax of tile g, across item boundaries too.
+      bool ok = issue_s(0);
+      if (ok && ntiles > 1) ok = issue_s(1);
+      for (int g = 0; g < ntiles && ok; ++g) {
+        ok = issue_pv(g);
+        if (ok && g + 2 < ntiles) ok = issue_s(g + 2);
       }
     }
-  } else if (warp >= 4) {
+  } else if (warp >= 4 && ntiles > 0) {
     // ------------------------------------------------------------------ softmax / correction / epilogue
-    const int w = warp - 4;                  // TMEM lane quadrant
-    const int row = threadIdx.x - 128;       // key within the tile (S^T) / head dim (O^T)
+    // Two warpgroups split the 32 columns (16 each); warp w of either group reads TMEM lane quadrant w % 4.
+    const int wg = (warp - 4) >> 2;          // column group: columns cb .. cb + 15
+    const int cb = wg * 16;
+    const int w = warp & 3;                  // TMEM lane quadrant
+    const int row = (threadIdx.x - 128) & 127;   // key within the tile (S^T) / head dim (O^T)
+    const int col = cb + (lane & 15);        // the column lane j (and lane j + 16) speaks for
     const uint32_t lane_off = static_cast<uint32_t>(w * 32) << 16;
-    const int min_limit = L - ql;            // smallest causal limit among the valid columns
-    // Running max per query column, kept identically by every softmax thread in registers (each thread reads
-    // the four warps' partial maxima itself), and this thread's partial column sums over its own keys, reduced
-    // across the 128 threads once in the epilogue: one named barrier per tile, no serial section.
-    float m_run[32], l_part[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      m_run[j] = -INFINITY;
-      l_part[j] = 0.0f;
-    }
+    const int bar_wg = 1 + wg;               // named barrier of this group's 128 threads
+    const long long T = S.total_tiles, Ge = S.active;
+    const int c = blockIdx.x;
+    Walk<QMAX> wk;
+    wk.start(a, S);
     bool ok = true;
-    for (int t = 0; t < nt && ok; ++t) {
-      const int buf = t & 1;                 // partial buffers alternate by tile parity (no reuse hazard)
-      if (!mbar_wait(&S.s_full[buf], (t >> 1) & 1, abort, a.err, kErrTimeoutS)) { ok = false; break; }
-      tc_fence_after();
-      float x[32];
-      tmem_ld_32x32b_x32(tmem + lane_off + buf * 32, x);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&S.s_free[buf]);
-      const int key = t * kKeysPerTile + row;
-      const bool tile_masked = (t * kKeysPerTile + kKeysPerTile - 1) > min_limit || (t + 1) * kKeysPerTile > L;
-      if (tile_masked) {
+    int g = 0;
+    for (int n = 0; ok && wk.A < x_end; wk.next(a), ++n) {
+      const int L = wk.r.L, ql = wk.r.ql;
+      const int t0 = wk.t0(x_begin), t1 = wk.t1(x_end);
+      const uint32_t tmem_o = tmem + lane_off + 64 + (n & 1) * 32 + cb;
+      const int min_limit = L - ql;            // smallest causal limit among the valid columns
+      // Running maxima (log2 domain): lane j owns column cb + (j & 15)'s (m_lane) and every thread keeps a copy
+      // of its group's 16 (m_all), changed only when some column grows by more than 2^8 (lazy rescaling).  The
+      // start value is a large negative finite number, so no -inf arithmetic is needed.  l_part: this thread's
+      // share of the column sums over its own keys, reduced across the group once per item.
+      float m_lane = kNegBig, m_all[16], l_part[16];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int p = j / G;
-          const int limit = (a.causal && p < ql) ? L - ql + p : L - 1;
-          x[j] = key <= limit ? x[j] * a.scale_log2 : -INFINITY;
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) x[j] = x[j] * a.scale_log2;
+      for (int j = 0; j < 16; ++j) {
+        m_all[j] = kNegBig;
+        l_part[j] = 0.0f;
       }
-      // ---- column max over this warp's 32 keys (one warp reduction per column), then the four warps'
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float wm = warp_max_redux(x[j]);
-        if (lane == j) S.red_max[buf][w][j] = wm;
-      }
-      named_barrier(1, 128);
-      float alpha[32];
-      bool any_rescale = false;
-#pragma unroll
-      for (int j4 = 0; j4 < 8; ++j4) {
-        const float4 r0 = reinterpret_cast<const float4*>(S.red_max[buf][0])[j4];
-        const float4 r1 = reinterpret_cast<const float4*>(S.red_max[buf][1])[j4];
-        const float4 r2 = reinterpret_cast<const float4*>(S.red_max[buf][2])[j4];
-        const float4 r3 = reinterpret_cast<const float4*>(S.red_max[buf][3])[j4];
-        const float tm[4] = {fmaxf(fmaxf(r0.x, r1.x), fmaxf(r2.x, r3.x)), fmaxf(fmaxf(r0.y, r1.y), fmaxf(r2.y, r3.y)),
-                             fmaxf(fmaxf(r0.z, r1.z), fmaxf(r2.z, r3.z)), fmaxf(fmaxf(r0.w, r1.w), fmaxf(r2.w, r3.w))};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int j = j4 * 4 + e;
-          alpha[j] = 1.0f;
-          if (tm[e] > m_run[j] + 8.0f) {       // lazy rescale: only when the max grows by 2^8
-            if (m_run[j] != -INFINITY) {
-              alpha[j] = ex2_approx(m_run[j] - tm[e]);
-              any_rescale = true;
-            } else {
-              alpha[j] = 0.0f;
-            }
-            m_run[j] = tm[e];
-          }
-        }
-      }
-      // ---- probabilities relative to the running max; this thread's share of the column sums
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        x[j] = x[j] == -INFINITY ? 0.0f : ex2_approx(x[j] - m_run[j]);
-        l_part[j] = l_part[j] * alpha[j] + x[j];
-      }
-      // ---- P^T row `row` (32 bf16, 64 bytes) into the SW64 buffer once PV(t-2) released it
-      if (t >= 2 && !mbar_wait(&S.o_done[buf], ((t - 2) >> 1) & 1, abort, a.err, kErrTimeoutO)) { ok = false; break; }
-      unsigned char* prow = sP + buf * kPBytes + row * 64;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint4 chunk;
-        uint32_t* wds = reinterpret_cast<uint32_t*>(&chunk);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          __nv_bfloat162 pair = __floats2bfloat162_rn(x[c * 8 + 2 * e], x[c * 8 + 2 * e + 1]);
-          wds[e] = *reinterpret_cast<uint32_t*>(&pair);
-        }
-        const int phys = c ^ ((row >> 1) & 3);
-        *reinterpret_cast<uint4*>(prow + phys * 16) = chunk;
-      }
-      // ---- the last tile's V rows past the context are zeroed (they may hold stale bits, even NaN)
-      if ((t + 1) * kKeysPerTile > L) {
-        const int stage = t % kStages;
-        if (!mbar_wait(&S.v_full[stage], (t / kStages) & 1, abort, a.err, kErrTimeoutV)) { ok = false; break; }
-        if (key >= L) {
-          uint4 zero = make_uint4(0, 0, 0, 0);
-          unsigned char* v0 = sV + stage * kTileBytes + row * 128;
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            *reinterpret_cast<uint4*>(v0 + c * 16) = zero;
-            *reinterpret_cast<uint4*>(v0 + kHalfTileBytes + c * 16) = zero;
-          }
-        }
-      }
-      // ---- rescale O^T (lane = head dim) once PV(t-1) has landed (uniform: every thread decided alike)
-      if (any_rescale && t >= 1) {
-        if (!mbar_wait(&S.o_done[(t - 1) & 1], ((t - 1) >> 1) & 1, abort, a.err, kErrTimeoutO)) { ok = false; break; }
+      for (int t = t0; t < t1; ++t, ++g) {
+        const int buf = g & 1;               // partial buffers alternate by tile parity (no reuse hazard)
+        if (!mbar_wait(&S.s_full[buf], (g >> 1) & 1, abort, a.err, kErrTimeoutS)) { ok = false; break; }
         tc_fence_after();
-        float o[32];
-        tmem_ld_32x32b_x32(tmem + lane_off + 64, o);
+        float x[16];
+        tmem_ld_32x32b_x16(tmem + lane_off + buf * 32 + cb, x);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.s_free[buf]);
+        const int key = t * kKeysPerTile + row;
+        if ((t * kKeysPerTile + kKeysPerTile - 1) > min_limit || (t + 1) * kKeysPerTile > L) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) o[j] *= alpha[j];
-        tmem_st_32x32b_x32(tmem + lane_off + 64, o);
+          for (int j = 0; j < 16; ++j) {
+            const int p = (cb + j) / G;
+            const int limit = (a.causal && p < ql) ? L - ql + p : L - 1;
+            x[j] = key <= limit ? x[j] : -INFINITY;
+          }
+        }
+        // ---- column maxima of the raw scores: this warp's (lane j keeps column cb + j's), then the four warps'
+        float wmax = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float v = warp_max_redux(x[j]);
+          wmax = lane == j ? v : wmax;
+        }
+        if (lane < 16) S.red_max[buf][col][w] = wmax;
+        named_barrier(bar_wg, 128);
+        const float4 r4 = *reinterpret_cast<const float4*>(S.red_max[buf][col]);
+        const float tmax = fmaxf(fmaxf(r4.x, r4.y), fmaxf(r4.z, r4.w)) * a.scale_log2;
+        const bool grow = tmax > m_lane + 8.0f;
+        // every thread of the group reads the same maxima, so this branch is uniform over its 128 threads
+        if (__any_sync(0xffffffffu, grow)) {
+          const float m_new = grow ? tmax : m_lane;
+          const float alpha_lane = ex2_approx(m_lane - m_new);   // 1 if unchanged, 0 from the start value
+          m_lane = m_new;
+          float alpha[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            alpha[j] = __shfl_sync(0xffffffffu, alpha_lane, j);
+            m_all[j] = __shfl_sync(0xffffffffu, m_new, j);
+            l_part[j] *= alpha[j];
+          }
+          if (t > t0) {     // O holds this item's earlier tiles: rescale it once PV(g-1) has landed
+            if (!mbar_wait(&S.o_done[(g - 1) & 1], ((g - 1) >> 1) & 1, abort, a.err, kErrTimeoutO)) { ok = false; break; }
+            tc_fence_after();
+            float o[16];
+            tmem_ld_32x32b_x16(tmem_o, o);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) o[j] *= alpha[j];
+            tmem_st_32x32b_x16(tmem_o, o);
+          }
+        }
+        // ---- probabilities relative to the running maxima (masked scores give ex2(-inf) = 0)
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          x[j] = ex2_approx(fmaf(x[j], a.scale_log2, -m_all[j]));
+          l_part[j] += x[j];
+        }
+        // ---- this group's half of P^T row `row` (16 bf16, 32 bytes) into the SW64 buffer once PV(g-2) released it
+        if (g >= 2 && !mbar_wait(&S.o_done[buf], ((g - 2) >> 1) & 1, abort, a.err, kErrTimeoutO)) { ok = false; break; }
+        unsigned char* prow = sP + buf * kPBytes + row * 64;
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          uint4 chunk;
+          uint32_t* wds = reinterpret_cast<uint32_t*>(&chunk);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            __nv_bfloat162 pair = __floats2bfloat162_rn(x[h2 * 8 + 2 * e], x[h2 * 8 + 2 * e + 1]);
+            wds[e] = *reinterpret_cast<uint32_t*>(&pair);
+          }
+          const int phys = (2 * wg + h2) ^ ((row >> 1) & 3);
+          *reinterpret_cast<uint4*>(prow + phys * 16) = chunk;
+        }
+        // ---- the row's last tile: V rows past the context are zeroed (they may hold stale bits, even NaN);
+        // each group zeroes one 64-dim half of the row
+        if ((t + 1) * kKeysPerTile > L) {
+          const int stage = g % kStages;
+          if (!mbar_wait(&S.v_full[stage], (g / kStages) & 1, abort, a.err, kErrTimeoutV)) { ok = false; break; }
+          if (key >= L) {
+            uint4 zero = make_uint4(0, 0, 0, 0);
+            unsigned char* v0 = sV + stage * kTileBytes + wg * kHalfTileBytes + row * 128;
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc) *reinterpret_cast<uint4*>(v0 + cc * 16) = zero;
+          }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.p_full[buf]);
       }
-      fence_proxy_async_smem();
+      if (!ok) break;
+      // ---- item epilogue: column sums over the 128 key threads (lane j ends with column cb + (j & 15)'s), O^T
+      // out of TMEM (the buffer is then free for the item after next)
+      {
+        const float s = column_reduce16(l_part, lane);
+        if (lane < 16) S.red_sum[col][w] = s;
+      }
+      named_barrier(bar_wg, 128);
+      const int gl = g - 1;
+      if (!mbar_wait(&S.o_done[gl & 1], (gl >> 1) & 1, abort, a.err, kErrTimeoutO)) break;
+      tc_fence_after();
+      float o[16];
+      tmem_ld_32x32b_x16(tmem_o, o);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&S.p_full[buf]);
-    }
-    // ---- epilogue: column sums over the 128 key threads, then O^T / l, bf16, to out[token, head, dim]
-    if (ok) {
-      S.red_sum[0][w][lane] = column_reduce<true>(l_part, lane);
-      named_barrier(1, 128);
-    }
-    if (ok && mbar_wait(&S.o_done[(nt - 1) & 1], ((nt - 1) >> 1) & 1, abort, a.err, kErrTimeoutO)) {
-      tc_fence_after();
-      float o[32];
-      tmem_ld_32x32b_x32(tmem + lane_off + 64, o);
+      if (lane == 0) mbar_arrive(&S.o_free[n & 1]);
+      const float4 s4 = *reinterpret_cast<const float4*>(S.red_sum[col]);
+      float l_lane = (s4.x + s4.y) + (s4.z + s4.w);
+      // ---- an item split over CTAs c_lo..c_hi: every piece is published; the last to arrive merges them
+      const long long A = wk.A, B = wk.A + wk.r.nt;
+      const long long c_lo = ceil_div((A + 1) * Ge, T) - 1, c_hi = ceil_div(B * Ge, T) - 1;
+      if (c_lo != c_hi) {
+        float* mine = a.partial + (2LL * c + (x_begin < A ? 1 : 0)) * kPartialFloats;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) __stcg(mine + (cb + j) * kHeadDim + row, o[j]);
+        if (w == 0 && lane < 16) {
+          __stcg(mine + kCols * kHeadDim + col, m_lane);
+          __stcg(mine + kCols * kHeadDim + kCols + col, l_lane);
+        }
+        __threadfence();
+        named_barrier(3, 256);               // both groups published
+        if (threadIdx.x == 128) {
+          int* counter = a.counters + (long long)wk.b * a.Hkv + wk.h;
+          const int last = atomicAdd(counter, 1) == (int)(c_hi - c_lo);
+          if (last) atomicExch(counter, 0);
+          S.last_piece = last;
+        }
+        named_barrier(3, 256);
+        if (!S.last_piece) continue;        // rewritten only after every thread passes the next publish barrier
+        __threadfence();
+        // merged in CTA order from the published pieces (this CTA's own included), so the result does not depend
+        // on which CTA arrived last; lane j merges column cb + (j & 15)'s maximum and sum
+        float m_acc = kNegBig;
+        l_lane = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) o[j] = 0.0f;
+        for (long long cc = c_lo; cc <= c_hi; ++cc) {
+          const long long s_cc = T * cc / Ge;
+          const float* piece = a.partial + (2 * cc + (s_cc < A ? 1 : 0)) * kPartialFloats;
+          const float mp = __ldcg(piece + kCols * kHeadDim + col);
+          const float lp = __ldcg(piece + kCols * kHeadDim + kCols + col);
+          const float mn = fmaxf(m_acc, mp);
+          const float sa = ex2_approx(m_acc - mn), sb = ex2_approx(mp - mn);
+          m_acc = mn;
+          l_lane = l_lane * sa + lp * sb;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float op = __ldcg(piece + (cb + j) * kHeadDim + row);
+            o[j] = o[j] * __shfl_sync(0xffffffffu, sa, j) + op * __shfl_sync(0xffffffffu, sb, j);
+          }
+        }
+      }
+      // ---- O^T / l, bf16, to out[token, head, dim]
+      const float inv_lane = l_lane > 0.0f ? 1.0f / l_lane : 0.0f;
       const int d = row;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int p = j / G, g = j % G;
-        if (p < ql) {
-          const float l = (S.red_sum[0][0][j] + S.red_sum[0][1][j]) + (S.red_sum[0][2][j] + S.red_sum[0][3][j]);
-          const float val = l > 0.0f ? o[j] / l : 0.0f;
-          a.out[(long long)(q_start + p) * a.out_row_stride + (long long)(h * G + g) * kHeadDim + d] =
-              __float2bfloat16_rn(val);
-        }
+      for (int j = 0; j < 16; ++j) {
+        const int p = (cb + j) / G, gq = (cb + j) % G;
+        const float inv = __shfl_sync(0xffffffffu, inv_lane, j);
+        if (p < ql)
+          a.out[(long long)(wk.r.q_start + p) * a.out_row_stride + (long long)(wk.h * G + gq) * kHeadDim + d] =
+              __float2bfloat16_rn(o[j] * inv);
       }
     }
   }
@@ -453,7 +679,7 @@ static int make_map(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1
 }
 
 template <int G>
-static int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const Args& a, int R,
+static int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const Args& a, int grid,
                   cudaStream_t stream) {
   static bool configured = false;
   if (!configured) {
@@ -461,10 +687,15 @@ static int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMa
                                           kSmemBytes));
     configured = true;
   }
-  dim3 grid(a.Hkv, R);
   verify_attention_kernel<G><<<grid, kThreads, kSmemBytes, stream>>>(qm, km, vm, a);
   SPECDEC_LAUNCH_CHECK();
   return kOk;
+}
+
+// Workspace: R * Hkv arrival counters (256-byte padded), then two piece slots per CTA.
+static long long counters_bytes(long long R, int Hkv) { return (R * Hkv * 4 + 255) / 256 * 256; }
+static long long workspace_bytes(long long R, int Hkv, int grid) {
+  return counters_bytes(R, Hkv) + 2LL * grid * kPartialFloats * 4;
 }
 
 }  // namespace attention
@@ -495,14 +726,21 @@ int specdec_store_kvcache(const void* key, long long key_row_stride, const void*
   return kOk;
 }
 
+long long specdec_attention_workspace_bytes(int R, int num_kv_heads) {
+  DeviceInfo info;
+  if (R < 1 || num_kv_heads < 1 || device_info(&info) != kOk) return -1;
+  return attention::workspace_bytes(R, num_kv_heads, info.sm_count);
+}
+
 int specdec_paged_attention(const void* q, long long T, long long q_row_stride, int num_heads, int num_kv_heads,
                             int head_dim, const void* k_cache, const void* v_cache, long long num_slots,
                             int block_size, const int* cu_seqlens_q, const int* cu_seqlens_k,
                             const int* context_lens, int q_per_seq, int R, const int* block_tables, int W,
                             int max_seqlen_q, float softmax_scale, int causal, void* out, long long out_row_stride,
-                            int* err, void* stream) {
+                            void* workspace, long long workspace_bytes, int* err, void* stream) {
   using namespace attention;
-  SPECDEC_CHECK_ARG(q && k_cache && v_cache && block_tables && out && err, "null pointer argument");
+  SPECDEC_CHECK_ARG(q && k_cache && v_cache && block_tables && out && workspace && err, "null pointer argument");
+  SPECDEC_CHECK_ARG((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "workspace must be 256-byte aligned");
   SPECDEC_CHECK_ARG(head_dim == kHeadDim, "head_dim %d: this build implements 128", head_dim);
   SPECDEC_CHECK_ARG(num_kv_heads >= 1 && num_heads % num_kv_heads == 0, "heads %d not a multiple of kv heads %d",
                     num_heads, num_kv_heads);
@@ -545,12 +783,23 @@ int specdec_paged_attention(const void* q, long long T, long long q_row_stride, 
   a.out = static_cast<__nv_bfloat16*>(out);
   a.out_row_stride = out_row_stride;
   a.err = err;
+  a.R = R;
+  // One CTA per SM, fewer when every row's table holds fewer tiles in total.
+  DeviceInfo info;
+  if (int st = device_info(&info)) return st;
+  const long long max_tiles = (long long)R * num_kv_heads * ((long long)W * block_size / kKeysPerTile);
+  const int grid = (int)(max_tiles < info.sm_count ? max_tiles : info.sm_count);
+  const long long need = attention::workspace_bytes(R, num_kv_heads, grid);
+  if (workspace_bytes < need)
+    return set_error(kWorkspaceTooSmall, "attention workspace of %lld bytes, %lld needed", workspace_bytes, need);
+  a.counters = static_cast<int*>(workspace);
+  a.partial = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + counters_bytes(R, num_kv_heads));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (G) {
-    case 1: return launch<1>(qm, km, vm, a, R, s);
-    case 2: return launch<2>(qm, km, vm, a, R, s);
-    case 4: return launch<4>(qm, km, vm, a, R, s);
-    default: return launch<8>(qm, km, vm, a, R, s);
+    case 1: return launch<1>(qm, km, vm, a, grid, s);
+    case 2: return launch<2>(qm, km, vm, a, grid, s);
+    case 4: return launch<4>(qm, km, vm, a, grid, s);
+    default: return launch<8>(qm, km, vm, a, grid, s);
   }
 }
 

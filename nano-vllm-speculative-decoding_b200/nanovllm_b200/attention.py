@@ -35,7 +35,23 @@ def device_error(device: torch.device) -> int:
 
 
 def reset_device_error(device: torch.device) -> None:
+    """Clears the error word and the split-item counters (a launch that gave up may leave counters behind)."""
     _err_word(device).zero_()
+    Workspace.get(device, _SPLIT_MIN_BYTES, name="attention_split").zero_()
+
+
+# Split-item workspace of the persistent attention kernel (arrival counters + two piece slots per SM), shared by
+# every launch on the device; allocated once at a size covering R * Hkv up to ~1.3M so that a captured CUDA graph
+# keeps a valid pointer.
+_SPLIT_MIN_BYTES = 8 << 20
+
+
+def _split_workspace(device: torch.device, R: int, Hkv: int) -> torch.Tensor:
+    with torch.cuda.device(device):
+        need = int(_lib.lib().specdec_attention_workspace_bytes(R, Hkv))
+    if need < 0:
+        raise _lib.SpecdecError(_lib.lib().specdec_last_error().decode())
+    return Workspace.get(device, max(need, _SPLIT_MIN_BYTES), name="attention_split")
 
 
 def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
@@ -87,10 +103,11 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
         R = ctx.numel()
         q_per_seq = query_len_per_seq
         max_seqlen_q = query_len_per_seq
+    ws = _split_workspace(device, R, Hkv)
     check(_lib.lib().specdec_paged_attention(
         ptr(q), T, q.stride(0), H, Hkv, D, ptr(k_cache), ptr(v_cache), blocks * block_size, block_size, ptr(cq),
         ptr(ck), ptr(ctx), q_per_seq, R, ptr(tables), W, int(max_seqlen_q), float(scale), int(causal), ptr(out),
-        out.stride(0), ptr(_err_word(device)), stream_of(device)))
+        out.stride(0), ptr(ws), ws.numel(), ptr(_err_word(device)), stream_of(device)))
     return out
 
 

@@ -165,3 +165,37 @@ def test_unsupported_shapes_raise(A):
     with pytest.raises(SpecdecError):
         A.paged_attention(c["q"], c["k_cache"], c["v_cache"], c["tables"], c["scale"], cu_seqlens_q=c["cu_q"],
                           cu_seqlens_k=c["cu_k"], max_seqlen_q=9)
+
+
+@pytest.mark.parametrize("k_lens", [[20000], [15000, 3000, 40]])
+def test_long_rows_split_over_many_ctas(A, k_lens):
+    """Rows far longer than one CTA's share of the tile sequence: every item is cut into many pieces that the
+    last-arriving CTA merges."""
+    c = paged_case([8] * len(k_lens), k_lens, seed=len(k_lens) + 20)
+    out = run_verify(A, c)
+    got = out.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    np.testing.assert_allclose(got, oracle_out(c), atol=ATOL, rtol=0)
+
+
+def test_repeated_launches_are_bitwise_identical(A):
+    """Split-item counters clean themselves and pieces merge in a fixed order: three launches agree bit for bit."""
+    rng = np.random.default_rng(5)
+    c = paged_case([8] * 24, rng.integers(500, 3000, size=24).tolist(), seed=31)
+    first = run_verify(A, c)
+    for _ in range(2):
+        again = A.paged_attention(c["q"], c["k_cache"], c["v_cache"], c["tables"], c["scale"],
+                                  cu_seqlens_q=c["cu_q"], cu_seqlens_k=c["cu_k"], max_seqlen_q=8)
+        torch.cuda.synchronize()
+        assert torch.equal(again, first)
+    assert A.device_error(DEV) == 0
+    np.testing.assert_allclose(first.float().cpu().numpy(), oracle_out(c), atol=ATOL, rtol=0)
+
+
+def test_workspace_query(A):
+    from nanovllm_b200 import _lib
+    lib = _lib.lib()
+    need = lib.specdec_attention_workspace_bytes(64, 8)
+    sms = torch.cuda.get_device_properties(DEV).multi_processor_count
+    assert need == (64 * 8 * 4 + 255) // 256 * 256 + 2 * sms * (32 * 128 + 64) * 4
+    assert lib.specdec_attention_workspace_bytes(0, 8) == -1
