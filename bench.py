@@ -151,6 +151,10 @@ def build_workload(torch, device, batch: int, ctx: int, seed: int):
                            lengths=lengths, width=width, shape=shape)
 
 
+CFG2_TRAFFIC_BYTES = 148_173_056       # 143.241984 MB read + 4.931072 MB written, one launch
+CFG2_ALGORITHMIC_BYTES = 135_319_552
+
+
 def time_events(torch, fn, iters: int) -> float:
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
@@ -190,9 +194,13 @@ def attention_roofline(torch, w, hbm_peak: float) -> dict:
     qo_bytes = 2 * num_tokens * s.heads * s.head_dim * 2
     algorithmic = kv_bytes + qo_bytes
     achieved = algorithmic / (per_launch_us * 1e-6) / 1e9
+    # DRAM traffic from one ncu capture of the config-2 launch (148.17 MB read + written for 135.32 MB
+    # algorithmic), scaled to this launch by its algorithmic bytes (traffic grows with the keys)
+    traffic = round(algorithmic * CFG2_TRAFFIC_BYTES / CFG2_ALGORITHMIC_BYTES)
     return {"kernel": "specdec::attention::verify_attention_kernel<4>", "bound": "hbm",
             "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
-            "frac": round(achieved / hbm_peak, 4), "traffic": None,
+            "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of config 2, scaled by keys",
             "algorithmic_bytes_per_launch": algorithmic, "us_per_launch": round(per_launch_us, 2),
             "launches_per_step": s.layers}
 

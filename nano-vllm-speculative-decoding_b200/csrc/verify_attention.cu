@@ -23,10 +23,12 @@
 // keys (half a 256-slot block) arrive by TMA through one tensor map over the whole paged cache (coordinates: dim,
 // head, physical slot), so the block table is a coordinate, not a gather.  The pipelines run across items: the
 // next item's Q (double-buffered) and first tiles load while the current item's epilogue runs.
-//   warp 0      TMA producer (Q per item, K/V tiles into 3-stage rings)
+//   warp 0      TMA producer: Q per item and the K tiles (3-stage ring)
 //   warp 1      TMEM allocator + single-thread MMA issuer
 //   warp 2      prologue: this CTA's share of the tile sequence from the row metadata
-//   warps 4-7   softmax over keys (one TMEM lane = one key), P^T to shared memory, O rescale, epilogue
+//   warp 3      TMA producer: the V tiles (3-stage ring)
+//   warps 4-11  softmax over keys (one TMEM lane = one key; two warpgroups of 16 columns each), P^T to shared
+//               memory, O rescale, epilogue
 // The softmax is online per query column with lazy rescaling (O is rescaled only when a column's running max
 // grows by more than 2^8), masked by key index (bottom-right causal or context length).  Keys past the row's
 // context in its last tile are never read as values: their P is 0 and their V rows are zeroed in shared memory.
@@ -46,7 +48,7 @@ constexpr int kHeadDim = 128;
 constexpr int kKeysPerTile = 128;
 constexpr int kCols = 32;              // packed query columns (group x positions)
 constexpr int kStages = 3;             // K ring and V ring depth
-constexpr int kThreads = 384;            // warps 0-3: TMA, MMA, prologue, idle; 4-11: softmax
+constexpr int kThreads = 384;            // warps 0-3: TMA (Q, K), MMA, prologue, TMA (V); 4-11: softmax
 constexpr int kHalfTileBytes = kKeysPerTile * 128;     // 64 dims x 128 keys bf16 = 16 KB
 constexpr int kTileBytes = 2 * kHalfTileBytes;          // 32 KB
 constexpr int kQHalfBytes = kCols * 128;                // 32 rows x 64 dims bf16 = 4 KB
@@ -314,20 +316,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   const long long x_begin = S.x_begin, x_end = S.x_end;
   const int ntiles = (int)(x_end - x_begin);
 
-  if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
+  if (warp == 0 || warp == 3) {
+    // ------------------------------------------------------------------ TMA producers
+    // warp 0: Q per item and the K ring (a K slot frees as soon as its score MMA completes); warp 3: the V ring
+    // (a V slot frees only after its PV MMA, so V waits never hold back the K loads)
+    const bool kq = warp == 0;
     if (lane == 0 && ntiles > 0) {
+      uint64_t* full = kq ? S.k_full : S.v_full;
+      uint64_t* empty = kq ? S.k_empty : S.v_empty;
+      unsigned char* ring = kq ? sK : sV;
+      const CUtensorMap* map = kq ? &kmap : &vmap;
       Walk<QMAX> wk;
       wk.start(a, S);
       bool ok = true;
       int g = 0;
       for (int n = 0; ok && wk.A < x_end; wk.next(a), ++n) {
-        const int qb = n & 1;
-        if (n >= 2 && !mbar_wait(&S.q_empty[qb], ((n - 2) >> 1) & 1, abort, a.err, kErrTimeoutEmpty)) break;
-        unsigned char* q = sQ + qb * kQBytes;
-        mbar_arrive_expect_tx(&S.q_full[qb], kQBytes);
-        tma_load_3d(q, &qmap, 0, wk.h * G, wk.r.q_start, &S.q_full[qb]);
-        tma_load_3d(q + kQHalfBytes, &qmap, 64, wk.h * G, wk.r.q_start, &S.q_full[qb]);
+        if (kq) {
+          const int qb = n & 1;
+          if (n >= 2 && !mbar_wait(&S.q_empty[qb], ((n - 2) >> 1) & 1, abort, a.err, kErrTimeoutEmpty)) break;
+          unsigned char* q = sQ + qb * kQBytes;
+          mbar_arrive_expect_tx(&S.q_full[qb], kQBytes);
+          tma_load_3d(q, &qmap, 0, wk.h * G, wk.r.q_start, &S.q_full[qb]);
+          tma_load_3d(q + kQHalfBytes, &qmap, 64, wk.h * G, wk.r.q_start, &S.q_full[qb]);
+        }
         const int* table = a.block_tables + (long long)wk.b * a.W;
         const int t1 = wk.t1(x_end);
         for (int t = wk.t0(x_begin); t < t1; ++t, ++g) {
@@ -335,20 +346,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t use = g / kStages;
           const int key0 = t * kKeysPerTile;
           const int slot = table[key0 / a.block_size] * a.block_size + key0 % a.block_size;
-          if (g >= kStages && !mbar_wait(&S.k_empty[stage], (use - 1) & 1, abort, a.err, kErrTimeoutEmpty)) {
+          if (g >= kStages && !mbar_wait(&empty[stage], (use - 1) & 1, abort, a.err, kErrTimeoutEmpty)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&S.k_full[stage], kTileBytes);
-          tma_load_3d(sK + stage * kTileBytes, &kmap, 0, wk.h, slot, &S.k_full[stage]);
-          tma_load_3d(sK + stage * kTileBytes + kHalfTileBytes, &kmap, 64, wk.h, slot, &S.k_full[stage]);
-          if (g >= kStages && !mbar_wait(&S.v_empty[stage], (use - 1) & 1, abort, a.err, kErrTimeoutEmpty)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(&S.v_full[stage], kTileBytes);
-          tma_load_3d(sV + stage * kTileBytes, &vmap, 0, wk.h, slot, &S.v_full[stage]);
-          tma_load_3d(sV + stage * kTileBytes + kHalfTileBytes, &vmap, 64, wk.h, slot, &S.v_full[stage]);
+          mbar_arrive_expect_tx(&full[stage], kTileBytes);
+          tma_load_3d(ring + stage * kTileBytes, map, 0, wk.h, slot, &full[stage]);
+          tma_load_3d(ring + stage * kTileBytes + kHalfTileBytes, map, 64, wk.h, slot, &full[stage]);
         }
       }
     }
@@ -406,13 +410,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         cp.advance(a, x_begin, x_end);
         return true;
       };
-      // S(g + 2) is issued right after PV(g), so the softmax of tile g + 1 never waits for a score MMA issued
-      // after the softmax of tile g, across item boundaries too.
+      // S(g + 2) goes out as soon as the softmax has read S(g) (its buffer), before PV(g), which waits for the
+      // softmax of tile g to finish: the score tiles stay two ahead of the softmax, across item boundaries too.
       bool ok = issue_s(0);
       if (ok && ntiles > 1) ok = issue_s(1);
       for (int g = 0; g < ntiles && ok; ++g) {
-        ok = issue_pv(g);
-        if (ok && g + 2 < ntiles) ok = issue_s(g + 2);
+        if (g + 2 < ntiles) ok = issue_s(g + 2);
+        if (ok) ok = issue_pv(g);
       }
     }
   } else if (warp >= 4 && ntiles > 0) {
