@@ -34,6 +34,7 @@ namespace sampler {
 
 constexpr int kThreads = 256;        // stats / tail / greedy CTAs
 constexpr int kTopkThreads = 512;    // one CTA per truncating row
+constexpr int kStatsCtasPerSm = 4;   // stats_kernel residency its launch bounds guarantee (<= 64 registers)
 constexpr int kMaxRequests = 1024;   // B cap (shared-memory tables are sized by it)
 constexpr int kMaxRows = 16384;      // T cap (fixed-offset greedy key table)
 constexpr int kMaxChunks = 64;       // chunks per row in pass 1
@@ -264,47 +265,49 @@ __device__ void row_range_ms(const T* row, int lo, int hi, float temp, int vec_o
   constexpr int VE = 16 / sizeof(T);  // elements per 16-byte vector
   const bool unit_temp = temp == 1.0f;
   if (vec_ok) {
-    // lo is a multiple of VE and the row base is 16-byte aligned.  Four 16-byte vectors per iteration: their
-    // maximum first (one rescale of the running sum), then exp2(x * log2e - m * log2e) per element.
+    // lo is a multiple of VE and the row base is 16-byte aligned.  Four 16-byte vectors per batch, the next
+    // batch's loads in flight while this one is reduced: the batch maximum first (one rescale of the running
+    // sum), then exp2(x * log2e - m * log2e) per element; vectors are unpacked where they are used.
     const int nvec = (hi - lo) / VE;
     const char* base = reinterpret_cast<const char*>(row + lo);
     const float kLog2e = 1.4426950408889634f;
+    // -inf in every element of a vector past the range (f32 0xff800000, bf16 0xff80, f16 0xfc00)
+    constexpr unsigned kNegInfWord = sizeof(T) == 4 ? 0xff800000u
+                                   : std::is_same<T, __nv_bfloat16>::value ? 0xff80ff80u : 0xfc00fc00u;
+    const uint4 kNegInf = make_uint4(kNegInfWord, kNegInfWord, kNegInfWord, kNegInfWord);
+    auto load_batch = [&](int i, uint4 (&r)[4]) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = i + u * NT;
+        r[u] = j < nvec ? ldg16(base + (size_t)j * 16) : kNegInf;
+      }
+    };
+    auto unpack = [&](const uint4& r, float (&f)[VE]) {
+      if constexpr (sizeof(T) == 4) {
+        unpack16(r, f);
+      } else if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        unpack16_bf16(r, f);
+      } else {
+        unpack16_f16(r, f);
+      }
+#pragma unroll
+      for (int e = 0; e < VE; ++e)
+        if (!unit_temp) f[e] = scale_logit(f[e], temp);
+    };
+    uint4 cur[4];
+    if ((int)threadIdx.x < nvec) load_batch(threadIdx.x, cur);
     for (int i = threadIdx.x; i < nvec; i += NT * 4) {
-      uint4 raw[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        int j = i + u * NT;
-        raw[u] = j < nvec ? ldg16(base + (size_t)j * 16) : make_uint4(0xff800000u, 0xff800000u, 0xff800000u, 0xff800000u);
-      }
-      float f[4][VE];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const bool live = i + u * NT < nvec;
-        if constexpr (sizeof(T) == 4) {
-          float t4[4];
-          unpack16(raw[u], t4);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) f[u][e] = live ? t4[e] : -INFINITY;
-        } else if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-          float t8[8];
-          unpack16_bf16(raw[u], t8);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) f[u][e] = live ? t8[e] : -INFINITY;
-        } else {
-          float t8[8];
-          unpack16_f16(raw[u], t8);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) f[u][e] = live ? t8[e] : -INFINITY;
-        }
-      }
+      uint4 nxt[4];
+      const int inext = i + NT * 4;
+      if (inext < nvec) load_batch(inext, nxt);
       float vm = -INFINITY;
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
+      for (int u = 0; u < 4; ++u) {
+        float f[VE];
+        unpack(cur[u], f);
 #pragma unroll
-        for (int e = 0; e < VE; ++e) {
-          if (!unit_temp) f[u][e] = scale_logit(f[u][e], temp);
-          vm = fmaxf(vm, f[u][e]);
-        }
+        for (int e = 0; e < VE; ++e) vm = fmaxf(vm, f[e]);
+      }
       if (vm > m) {
         if (m != -INFINITY) s *= exp_sum_term(m - vm);
         m = vm;
@@ -312,14 +315,19 @@ __device__ void row_range_ms(const T* row, int lo, int hi, float temp, int vec_o
       if (m != -INFINITY) {
         const float mb = m * kLog2e;
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
+        for (int u = 0; u < 4; ++u) {
+          float f[VE];
+          unpack(cur[u], f);
 #pragma unroll
           for (int e = 0; e < VE; ++e) {
             float y;
-            asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(fmaf(f[u][e], kLog2e, -mb)));
+            asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(fmaf(f[e], kLog2e, -mb)));
             s += y;
           }
+        }
       }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) cur[u] = nxt[u];
     }
     // scalar tail of the range (fewer than VE elements)
     for (int v = lo + nvec * VE + threadIdx.x; v < hi; v += NT) {
@@ -433,13 +441,18 @@ __device__ void decide_request(const Args& a, int b, int start, int len, bool ne
 // ---------------------------------------------------------------------------------------- pass 1: stats
 // grid (C, T).  mode 0: acceptance (decide when the request's last chunk lands); mode 1: probabilities only.
 template <typename T>
-__global__ void __launch_bounds__(kThreads) stats_kernel(Args a, int mode) {
+__global__ void __launch_bounds__(kThreads, kStatsCtasPerSm) stats_kernel(Args a, int mode) {
   __shared__ int s_start[kMaxRequests + 1];
   __shared__ int s_last;
   const int c = blockIdx.x, t = blockIdx.y;
   int b, start, len;
   float temp;
-  if (mode == 0) {
+  if (mode == 0 && a.lens == nullptr) {        // every request verifies k + 1 rows (checked on the host)
+    b = t / (a.k + 1);
+    start = b * (a.k + 1);
+    len = a.k + 1;
+    temp = a.temperature[b];
+  } else if (mode == 0) {
     if (!starts_from_lens<kThreads>(a.lens, a.B, a.k + 1, a.T, s_start)) {
       if (threadIdx.x == 0) report(a, kStatusBadLens);
       return;
@@ -908,6 +921,212 @@ __global__ void __launch_bounds__(kThreads) tail_kernel(Args a) {
   if (threadIdx.x == 0) atomicExch(a.tail_ticket, 0u);
 }
 
+// ---------------------------------------------------------------------------------------- pass 2: accept tail
+// The tail race of the accept path (not race()): the same torch exponential_ grid and the same in-kernel draws
+// as tail_kernel, with the per-element arithmetic cut down.  p = e^(f - m) / s as exp_compensated(f - m) * (1/s)
+// and w / E as a fast quotient: both within a few ulp (a few 1e-7 relative), inside the 1e-6 relative p
+// uncertainty the parity rule allows for the race (a winner within that of another candidate is a near tie).
+// The draws themselves (Philox, then torch's -log transform) are exact.  One 32-bit max per warp and element
+// round, the first lane among equals keeps torch's first-index rule.
+struct alignas(16) TailDesc {    // per request, in shared memory (32 B: one float4 + two row pointers)
+  float m, inv_s, thr, temp;
+  const void* xrow;   // row of x holding p_next
+  const float* qrow;  // row of q for the residual, or null (bonus row, plain p)
+};
+static_assert(sizeof(TailDesc) == 32, "TailDesc is read as float4 + two pointers");
+
+// e^y to a few ulp: 2^(y log2 e) with the rounding error of the product y * log2(e) recovered by an FMA (the
+// exact two-product of Dekker / Kahan, as in Muller et al., Handbook of Floating-Point Arithmetic) plus the low
+// part of log2(e), applied as 2^t * (1 + err ln 2).  ex2.approx carries the remaining ~2 ulp.
+__device__ __forceinline__ float exp_compensated(float y) {
+  const float kL = 1.44269502162933349609375f;   // log2(e) rounded to float
+  const float kLlo = 1.925963033500011e-08f;     // log2(e) - kL
+  const float t = y * kL;
+  const float err = fmaf(y, kL, -t) + y * kLlo;
+  float p;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(p) : "f"(t));
+  return p * fmaf(err, 0.6931471805599453f, 1.0f);
+}
+
+// One round's four elements (lane ii = grid-stride step ii of the round): loaded x and q values and where the
+// round starts.  Element indices stay below 2^32 (B * V < 2^31 and S < 2^21), so they are 32-bit.
+struct TailLoads {
+  float x[4], q[4];
+  unsigned b0, v0;
+};
+
+__device__ __forceinline__ void tail_step(const Args& a, unsigned& b, unsigned& v) {
+  b += a.e_sq;
+  v += a.e_sr;
+  if (v >= (unsigned)a.V) { v -= (unsigned)a.V; ++b; }
+}
+
+template <typename T>
+__device__ __forceinline__ void tail_issue_loads(const Args& a, const TailDesc* s_td, unsigned& b, unsigned& v,
+                                                 unsigned li0, unsigned S, unsigned N, TailLoads& L) {
+  L.b0 = b;
+  L.v0 = v;
+#pragma unroll
+  for (int ii = 0; ii < 4; ++ii) {
+    L.x[ii] = 0.0f;
+    L.q[ii] = 0.0f;
+    if (li0 + ii * S < N) {
+      const TailDesc& d = s_td[b];
+      L.x[ii] = to_f32(static_cast<const T*>(d.xrow)[v]);
+      if (d.qrow) L.q[ii] = d.qrow[v];
+    }
+    tail_step(a, b, v);
+  }
+}
+
+// The four uniforms of call n of curand's Philox4x32-10 stream (seed, subsequence idx, offset 4 c0): the Philox
+// block (Salmon et al., SC 2011) at counter (c0 + n, idx) under key seed, computed by curand's own block function
+// and uniform transform, without the state bookkeeping of curand_uniform4.
+__device__ __forceinline__ float4 philox_uniform4(unsigned long long seed, unsigned long long c0, unsigned idx,
+                                                  int n) {
+  const unsigned long long c = c0 + (unsigned long long)n;
+  const uint4 ctr = make_uint4((unsigned)c, (unsigned)(c >> 32), idx, 0u);
+  const uint2 key = make_uint2((unsigned)seed, (unsigned)(seed >> 32));
+  return _curand_uniform4(curand_Philox4x32_10(ctr, key));
+}
+
+// Accept-tail race.  Work per element: the Philox draw and torch's -log transform (exact), p = e^(f - m) / s as
+// exp_compensated(f - m) * (1/s), the residual, w / E as a fast quotient (p and the quotient within a few 1e-7
+// relative: inside the 1e-6 relative p uncertainty the parity rule allows for the race, where a winner within
+// that of another candidate is a near tie), then one 32-bit max per warp; the first lane among equals keeps
+// torch's first-index rule.  Round n + 1's loads are issued before round n is computed.
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 4) tail_accept_kernel(Args a) {
+  extern __shared__ __align__(16) unsigned char tail_smem[];
+  TailDesc* s_td = reinterpret_cast<TailDesc*>(tail_smem);
+  unsigned long long* s_best = reinterpret_cast<unsigned long long*>(tail_smem + sizeof(TailDesc) * a.B);
+  __shared__ int s_last;
+  if (*reinterpret_cast<volatile int*>(a.status) != 0) return;  // pass 1 rejected its inputs
+  for (int i = threadIdx.x; i < a.B; i += kThreads) {
+    s_best[i] = 0ull;
+    const ReqDesc d = a.desc[i];
+    TailDesc t;
+    t.m = d.m;
+    t.inv_s = 1.0f / d.s;
+    t.thr = d.thr;
+    t.temp = d.temp;
+    t.xrow = static_cast<const T*>(a.x) + d.x_row * a.V;
+    t.qrow = d.q_row < 0 ? nullptr : a.q + d.q_row * a.V;
+    s_td[i] = t;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const unsigned S = kRngBlock * gridDim.x;
+  const unsigned idx = blockIdx.x * kRngBlock + threadIdx.x;
+  const unsigned N = (unsigned)a.e_numel;
+  const unsigned V = (unsigned)a.V;
+  const bool gen = a.E == nullptr;
+  const bool direct = (a.offset_E & 3ull) == 0;     // torch's offsets are multiples of 4
+  curandStatePhilox4_32_10_t st;
+  if (gen && !direct) curand_init(a.seed, idx, a.offset_E, &st);
+  const unsigned long long c0 = a.offset_E >> 2;
+  unsigned b = idx / V, v = idx % V;
+  unsigned li0 = idx;                      // element of lane ii = 0 in the current round
+  unsigned warp0 = idx - lane;             // the warp's first element in the current round
+  TailLoads cur{}, nxt{};
+  if (a.e_rounds > 0 && warp0 < N) tail_issue_loads<T>(a, s_td, b, v, li0, S, N, cur);
+  for (int n = 0; n < a.e_rounds; ++n) {
+    if (warp0 >= N) break;                                     // warp-uniform
+    if (n + 1 < a.e_rounds && warp0 + 4 * S < N) tail_issue_loads<T>(a, s_td, b, v, li0 + 4 * S, S, N, nxt);
+    float ee[4];
+    if (gen) {
+      const float4 r4 = direct ? philox_uniform4(a.seed, c0, idx, n) : curand_uniform4(&st);
+      ee[0] = torch_exponential_clamped(r4.x);
+      ee[1] = torch_exponential_clamped(r4.y);
+      ee[2] = torch_exponential_clamped(r4.z);
+      ee[3] = torch_exponential_clamped(r4.w);
+    }
+    unsigned bb = cur.b0, vv = cur.v0;
+    if (!a.probs_mode && warp0 + 3 * S + 32 <= N) {
+      // full round: every element in range for the whole warp; selects instead of branches
+#pragma unroll
+      for (int ii = 0; ii < 4; ++ii) {
+        const float4 d = *reinterpret_cast<const float4*>(&s_td[bb]);   // m, inv_s, thr, temp
+        const float* qrow = s_td[bb].qrow;
+        const float f = d.w == 1.0f ? cur.x[ii] : scale_logit(cur.x[ii], d.w);
+        const float p = f >= d.z ? exp_compensated(f - d.x) * d.y : 0.0f;
+        const float w = qrow ? fmaxf(p - cur.q[ii], 0.0f) : p;
+        const float e = gen ? ee[ii] : a.E[li0 + ii * S];
+        const unsigned bits = __float_as_uint(__fdividef(w, e)) & 0x7fffffffu;
+        if (__all_sync(0xffffffffu, vv >= (unsigned)lane)) {
+          // 32 consecutive columns vv(lane 0) + lane of one row
+          const unsigned mx = __reduce_max_sync(0xffffffffu, bits);
+          const unsigned first = __ffs(__ballot_sync(0xffffffffu, bits == mx)) - 1;
+          if (lane == 0)
+            atomicMax(&s_best[bb],
+                      (static_cast<unsigned long long>(mx | 0x80000000u) << 32) | (0xffffffffu - (vv + first)));
+        } else {
+          warp_segment_reduce((static_cast<unsigned long long>(bits | 0x80000000u) << 32) | (0xffffffffu - vv),
+                              (int)bb, true, s_best);
+        }
+        tail_step(a, bb, vv);
+      }
+    } else {
+#pragma unroll
+      for (int ii = 0; ii < 4; ++ii) {
+        if (warp0 + ii * S < N) {                                // warp-uniform
+          const unsigned li = li0 + ii * S;
+          const bool act = li < N;
+          unsigned bits = 0u;
+          if (act) {
+            const float4 d = *reinterpret_cast<const float4*>(&s_td[bb]);   // m, inv_s, thr, temp
+            float p;
+            if (a.probs_mode) {
+              p = cur.x[ii];
+            } else {
+              const float f = d.w == 1.0f ? cur.x[ii] : scale_logit(cur.x[ii], d.w);
+              p = f >= d.z ? exp_compensated(f - d.x) * d.y : 0.0f;
+            }
+            const float w = s_td[bb].qrow ? fmaxf(p - cur.q[ii], 0.0f) : p;
+            const float e = gen ? ee[ii] : a.E[li];
+            bits = __float_as_uint(__fdividef(w, e)) & 0x7fffffffu;   // w >= 0: clears a -0
+          }
+          const unsigned b0 = __shfl_sync(0xffffffffu, bb, 0);
+          if (__all_sync(0xffffffffu, act && bb == b0)) {
+            const unsigned mx = __reduce_max_sync(0xffffffffu, bits);
+            const unsigned first = __ffs(__ballot_sync(0xffffffffu, bits == mx)) - 1;
+            if (lane == 0)
+              atomicMax(&s_best[bb],
+                        (static_cast<unsigned long long>(mx | 0x80000000u) << 32) | (0xffffffffu - (vv + first)));
+          } else {
+            const unsigned long long key =
+                act ? (static_cast<unsigned long long>(bits | 0x80000000u) << 32) | (0xffffffffu - vv) : 0ull;
+            warp_segment_reduce(key, (int)bb, act, s_best);
+          }
+        }
+        tail_step(a, bb, vv);
+      }
+    }
+    cur = nxt;
+    li0 += 4 * S;
+    warp0 += 4 * S;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < a.B; i += kThreads) {
+    unsigned long long kk = s_best[i];
+    if (kk) atomicMax(&a.tail_key[i], kk);
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned ticket = atomicAdd(a.tail_ticket, 1u);
+    s_last = ticket == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int i = threadIdx.x; i < a.B; i += kThreads) {
+    unsigned long long kk = atomicExch(&a.tail_key[i], 0ull);
+    a.tail[i] = (long long)argmax_key_index(kk);
+  }
+  if (threadIdx.x == 0) atomicExch(a.tail_ticket, 0u);
+}
+
 // ---------------------------------------------------------------------------------------- greedy
 // grid (C, T): per-chunk argmax folded into a per-row 64-bit key; the request's last CTA decides.
 template <typename T>
@@ -984,8 +1203,10 @@ static unsigned long long torch_rng_increment(long long numel, const DeviceInfo&
 }
 
 static void choose_chunks(Args& a, const DeviceInfo& info) {
-  const long long target = (long long)info.sm_count * 8;
-  long long C = (target + a.T - 1) / a.T;
+  // (row, chunk) CTAs of 256 threads, kStatsCtasPerSm resident per SM: as many chunks per row as fit one wave
+  // (a second, partial wave would run at a fraction of the occupancy), at least one
+  const long long slots = (long long)info.sm_count * kStatsCtasPerSm;
+  long long C = slots / a.T;
   long long cmax = (a.V + 2047) / 2048;
   if (C > cmax) C = cmax;
   if (C > kMaxChunks) C = kMaxChunks;
@@ -1018,8 +1239,12 @@ static int launch_tail(Args& a, const DeviceInfo& info, bool race, cudaStream_t 
   a.e_rounds = (int)((a.e_numel - 1) / (S * 4) + 1);
   a.e_sq = (unsigned)(S / a.V);
   a.e_sr = (unsigned)(S % a.V);
-  if (race) tail_kernel<T, true><<<a.e_grid, kThreads, 0, stream>>>(a);
-  else tail_kernel<T, false><<<a.e_grid, kThreads, 0, stream>>>(a);
+  if (race) {
+    tail_kernel<T, true><<<a.e_grid, kThreads, 0, stream>>>(a);
+  } else {
+    const size_t smem = (sizeof(TailDesc) + sizeof(unsigned long long)) * a.B;
+    tail_accept_kernel<T><<<a.e_grid, kThreads, smem, stream>>>(a);
+  }
   SPECDEC_LAUNCH_CHECK();
   return kOk;
 }
