@@ -119,12 +119,16 @@ int specdec_paged_attention(const void* q, long long T, long long q_row_stride, 
  * with per-row temperature / top_k / top_p (spec_sampler.py:65-96), race against noise[b, row, :candidates]
  * (noise [B, k, noise_width]), q scattered into probs [B, k, V] (zeroed by the caller once per call).  Writes
  * drafts[b, row], prev_out[b] and, with w1 [V, rank] bf16, e_next[b] = w1[prev] (the next step's embedding).
- * logits [B, k, V] and bias of dtype codes as above.  Limits: candidates <= 1024. */
+ * logits [B, k, V] and bias of dtype codes as above.  Limits: candidates <= 1024.  Each row is split over several
+ * CTAs; workspace: 256-byte aligned device bytes, zero-filled once before first use (the kernel leaves its
+ * counters zeroed), at least specdec_markov_workspace_bytes(B, V, candidates, greedy); calls sharing it must not
+ * overlap on the GPU. */
+long long specdec_markov_workspace_bytes(int B, int V, int candidates, int greedy);
 int specdec_markov_step(const void* logits, int logits_dtype, const void* bias, int bias_dtype, int B, int k, int V,
                         int row, int candidates, int greedy, int round_bf16, const float* temperature,
                         const long long* top_k, const float* top_p, int max_top_k, int has_top_p, const float* noise,
                         int noise_width, long long* drafts, float* probs, long long* prev_out, const void* w1,
-                        int rank, void* e_next, int* err, void* stream);
+                        int rank, void* e_next, void* workspace, long long workspace_bytes, int* err, void* stream);
 
 /* ------------------------------------------------------------------------------------------ kernel 4: ctx_store */
 /* DFlashDraftModel.store_context_kv (nanovllm/models/dflash.py:88-96) for every draft layer in one launch, and

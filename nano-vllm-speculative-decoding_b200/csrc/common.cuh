@@ -179,43 +179,135 @@ __device__ __forceinline__ void block_sort_desc_f32(float* keys, int P) {
   }
 }
 
+// Bitonic sort of one 64-bit key per lane across the warp, descending (lane 0 ends with the largest): shuffles
+// only, no block barrier.
+__device__ __forceinline__ unsigned long long warp_sort_desc_u64(unsigned long long key, int lane) {
+#pragma unroll
+  for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, stride);
+      const bool up = (lane & size) == 0 || size == 32;
+      const bool lower = (lane & stride) == 0;
+      const unsigned long long hi = key > other ? key : other, lo = key > other ? other : key;
+      key = (lower == up) ? hi : lo;
+    }
+  }
+  return key;
+}
+
+// Number of keys in a descending list of 32 that are larger than key.
+__device__ __forceinline__ int count_larger32(const unsigned long long* list, unsigned long long key) {
+  int lo = 0, hi = 32;             // the answer is in [0, 32]: six halvings
+#pragma unroll
+  for (int s = 0; s < 6; ++s) {
+    if (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (list[mid] > key) lo = mid + 1; else hi = mid;
+    }
+  }
+  return lo;
+}
+
+// The top C of n distinct nonzero keys keys[0..n), descending, into out[0..C) (C <= n): every 32-key chunk is
+// sorted by one warp (shuffles), then each key's rank in the
+// whole set is its position in its chunk plus, per other chunk, the count of larger keys there (binary search).
+// keys is rewritten (chunks sorted, padded with 0 keys to whole chunks: keys needs room for that).  Two barriers.
+template <int NT>
+__device__ void block_top_sorted(unsigned long long* keys, int n, int C, unsigned long long* out) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nchunks = (n + 31) / 32;
+  for (int c = warp; c < nchunks; c += NT / 32) {
+    const int i = c * 32 + lane;
+    const unsigned long long k = i < n ? keys[i] : 0ull;
+    keys[i] = warp_sort_desc_u64(k, lane);
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < nchunks * 32; t += NT) {
+    const unsigned long long key = keys[t];
+    if (key == 0ull) continue;                       // padding
+    const int c = t >> 5;
+    int r = t & 31;
+    for (int q = 0; q < nchunks; ++q)
+      if (q != c) r += count_larger32(keys + q * 32, key);
+    if (r < C) out[r] = key;
+  }
+  __syncthreads();
+}
+
 // Top-C selection by a thread-maxima bound (whole block of NT threads; C <= NT).  load(g, x) fills the 8 values
 // of element group g (missing ones -inf) and returns how many exist.  Every thread's maximum over its groups is
 // an element; the C-th largest of those NT maxima is therefore <= the row's C-th largest value, so collecting
 // every element at or above it keeps the top C and all of their ties.  Collected entries are 64-bit keys
-// (ordered value << 32 | ~id) in buf (capacity cap); returns the count, or -1 when more than cap elements reach
-// the bound (the caller falls back to an exact radix select).  tmax is NT floats of scratch.
-template <int NT, typename Load>
+// (ordered value << 32 | ~id, all distinct) in buf (capacity cap); on return buf[0..C) holds the top C keys in
+// descending order and the count is returned, or -1 when more than cap elements reach the bound (the caller
+// falls back to an exact radix select).  tmax is NT floats of scratch.  Both orderings (the C-th thread maximum,
+// the top C of up to 1024 collected keys) are warp sorts plus binary-search ranks: a few block barriers.
+template <int NT, int UNROLL, typename Load>
 __device__ int select_by_thread_max(int ngroups, int C, Load load, float* tmax, unsigned long long* buf, int cap,
                                     int* s_count) {
+  __shared__ float s_bound;
   float mx = -INFINITY;
-  for (int g = threadIdx.x; g < ngroups; g += NT) {
-    float x[8];
-    const int n = load(g, x);
+  // UNROLL groups per thread in flight per iteration (their loads are independent)
+  for (int g0 = threadIdx.x; g0 < ngroups; g0 += UNROLL * NT) {
+    float x[UNROLL][8];
+    int n[UNROLL];
 #pragma unroll
-    for (int e = 0; e < 8; ++e)
-      if (e < n) mx = fmaxf(mx, x[e]);
+    for (int u = 0; u < UNROLL; ++u) {
+      const int g = g0 + u * NT;
+      n[u] = g < ngroups ? load(g, x[u]) : 0;
+    }
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u)
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (e < n[u]) mx = fmaxf(mx, x[u][e]);
   }
-  tmax[threadIdx.x] = mx;
   if (threadIdx.x == 0) *s_count = 0;
-  __syncthreads();
-  block_sort_desc_f32(tmax, NT);
-  const float bound = tmax[C - 1];
-  for (int g = threadIdx.x; g < ngroups; g += NT) {
-    float x[8];
-    const int n = load(g, x);
+  {  // the C-th largest thread maximum (ties by thread index): warp-sorted keys in buf, ranks by binary search
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const unsigned long long mine = (static_cast<unsigned long long>(ordered_key(mx)) << 32) | (0xffffffffu - threadIdx.x);
+    const unsigned long long sorted = warp_sort_desc_u64(mine, lane);
+    buf[threadIdx.x] = sorted;
+    __syncthreads();
+    int r = lane;
+    for (int q = 0; q < NT / 32; ++q)
+      if (q != warp) r += count_larger32(buf + q * 32, sorted);
+    if (r == C - 1) s_bound = key_to_float(static_cast<unsigned>(sorted >> 32));
+    __syncthreads();
+  }
+  const float bound = s_bound;
+  for (int g0 = threadIdx.x; g0 < ngroups; g0 += UNROLL * NT) {
+    float x[UNROLL][8];
+    int n[UNROLL];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      if (e < n && x[e] >= bound) {
-        const int slot = atomicAdd(s_count, 1);
-        if (slot < cap)
-          buf[slot] = (static_cast<unsigned long long>(ordered_key(x[e])) << 32) | (0xffffffffu - (unsigned)(g * 8 + e));
+    for (int u = 0; u < UNROLL; ++u) {
+      const int g = g0 + u * NT;
+      n[u] = g < ngroups ? load(g, x[u]) : 0;
+    }
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      const int g = g0 + u * NT;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        if (e < n[u] && x[u][e] >= bound) {
+          const int slot = atomicAdd(s_count, 1);
+          if (slot < cap)
+            buf[slot] = (static_cast<unsigned long long>(ordered_key(x[u][e])) << 32) | (0xffffffffu - (unsigned)(g * 8 + e));
+        }
       }
     }
   }
   __syncthreads();
   const int count = *s_count;
   if (count > cap) return -1;
+  const int padded = (count + 31) / 32 * 32;
+  if (count <= 1024 && padded + C <= cap) {
+    block_top_sorted<NT>(buf, count, C, buf + cap - C);
+    for (int i = threadIdx.x; i < C; i += NT) buf[i] = buf[cap - C + i];
+    __syncthreads();
+    return count;
+  }
   int P = 1;
   while (P < count) P <<= 1;
   for (int i = count + threadIdx.x; i < P; i += NT) buf[i] = 0ull;

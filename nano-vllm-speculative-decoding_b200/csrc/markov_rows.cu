@@ -50,7 +50,18 @@ struct Args {
   __nv_bfloat16* e_next;    // [B, rank]
   int* err;
   int vec;                  // bf16 logits and bias, V % 8 == 0, 16-byte aligned rows: vector loads
+  int P;                    // CTAs per row (grid.x); piece p covers groups [p * gchunk, (p + 1) * gchunk)
+  int gchunk;               // groups of 8 elements per piece
+  unsigned* tickets;        // [B] arrivals per row; the last CTA resets its entry
+  unsigned long long* best; // [B] greedy argmax keys; reset by the last CTA
+  unsigned long long* keys; // [B][P][C] each piece's top C keys (value << 32 | ~id), descending
 };
+
+// Workspace: tickets and greedy keys (zeroed once, self-cleaning), then the pieces' candidate keys.
+constexpr long long kHeaderAlign = 256;
+__host__ __device__ inline long long ws_head_bytes(int B) {
+  return ((long long)B * (4 + 8) + kHeaderAlign - 1) / kHeaderAlign * kHeaderAlign;
+}
 
 __device__ __forceinline__ float load_any(const void* p, int dt, long long i) {
   if (dt == kF32) return reinterpret_cast<const float*>(p)[i];
@@ -115,37 +126,42 @@ __device__ void pick_digit(const unsigned* hist, int nbins, int rank, int* s_dig
 }
 
 __global__ void __launch_bounds__(kThreads) markov_step_kernel(const Args a) {
-  __shared__ unsigned long long sel[kSelCap];            // fast-path candidates; the radix fallback's histogram
-  unsigned* hist = reinterpret_cast<unsigned*>(sel);      // (4096 bins) reuses the same bytes
+  __shared__ unsigned long long sel[kSelCap];            // fast-path candidates, the pieces' keys when merging;
+  unsigned* hist = reinterpret_cast<unsigned*>(sel);      // the radix fallback's histogram (4096 bins) reuses it
   __shared__ unsigned long long cand[kMaxCand];
   __shared__ float tmax[kThreads];
   __shared__ int s_sel;
   __shared__ float cprob[kMaxCand];
-  __shared__ int s_digit, s_above, s_cnt, s_prev;
+  __shared__ int s_digit, s_above, s_cnt, s_prev, s_last;
   __shared__ int warp_ties[kWarps], warp_base[kWarps];
   __shared__ unsigned long long s_red[kWarps];
   __shared__ float s_thr, s_z;
 
-  const int b = blockIdx.x;
+  const int piece = blockIdx.x, b = blockIdx.y;
   const int V = a.V;
   const long long lrow = ((long long)b * a.k + a.j) * V;
   const long long brow = (long long)b * V;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int C = a.C;
 
-  // Passes over the row read 2 x 32 consecutive groups of 8 elements per warp per iteration (two 16-byte loads
-  // of logits and bias per group in flight per thread); trip counts are warp-uniform.
-  const int ngroups = (V + 7) / 8;
+  // This CTA's piece of the row: groups [g_lo, g_lo + ngroups) of 8 elements.  Passes over it read 2 x 32
+  // consecutive groups per warp per iteration (two 16-byte loads of logits and bias per group in flight per
+  // thread); trip counts are warp-uniform.  Ids below are piece-local (group * 8 + e) until published.
+  const int ngroups_row = (V + 7) / 8;
+  const int g_lo = piece * a.gchunk;
+  const int ngroups = min(ngroups_row - g_lo, a.gchunk);
+  auto load = [&](int g, float (&x)[8]) { return load_group(a, lrow, brow, g_lo + g, x); };
   if (a.greedy) {
     unsigned long long best = 0ull;
     for (int gb = warp * 64; gb < ngroups; gb += kWarps * 64) {
       float x0[8], x1[8];
       const int g0 = gb + lane, g1 = gb + 32 + lane;
-      const int n0 = g0 < ngroups ? load_group(a, lrow, brow, g0, x0) : 0;
-      const int n1 = g1 < ngroups ? load_group(a, lrow, brow, g1, x1) : 0;
+      const int n0 = g0 < ngroups ? load(g0, x0) : 0;
+      const int n1 = g1 < ngroups ? load(g1, x1) : 0;
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        if (e < n0) { const unsigned long long k0 = argmax_key(x0[e], (unsigned)(g0 * 8 + e)); best = k0 > best ? k0 : best; }
-        if (e < n1) { const unsigned long long k1 = argmax_key(x1[e], (unsigned)(g1 * 8 + e)); best = k1 > best ? k1 : best; }
+        if (e < n0) { const unsigned long long k0 = argmax_key(x0[e], (unsigned)((g_lo + g0) * 8 + e)); best = k0 > best ? k0 : best; }
+        if (e < n1) { const unsigned long long k1 = argmax_key(x1[e], (unsigned)((g_lo + g1) * 8 + e)); best = k1 > best ? k1 : best; }
       }
     }
     best = warp_max_u64(best);
@@ -154,17 +170,13 @@ __global__ void __launch_bounds__(kThreads) markov_step_kernel(const Args a) {
     if (threadIdx.x == 0) {
       unsigned long long m = 0ull;
       for (int w = 0; w < kWarps; ++w) m = s_red[w] > m ? s_red[w] : m;
-      s_prev = (int)argmax_key_index(m);
+      atomicMax(&a.best[b], m);
     }
-    __syncthreads();
   } else {
-    const int C = a.C;
-    // ---- fast path: thread-maxima bound, collect, sort (two passes over the row)
+    // ---- the piece's top C, descending: thread-maxima bound + collect + sort, or an exact radix select
     int fast = -1;
     if (C <= kThreads) {
-      fast = select_by_thread_max<kThreads>(
-          ngroups, C, [&](int g, float (&x)[8]) { return load_group(a, lrow, brow, g, x); }, tmax, sel, kSelCap,
-          &s_sel);
+      fast = select_by_thread_max<kThreads, 1>(ngroups, C, load, tmax, sel, kSelCap, &s_sel);
       if (fast >= 0)
         for (int i = threadIdx.x; i < C; i += kThreads) cand[i] = sel[i];
     }
@@ -184,8 +196,8 @@ __global__ void __launch_bounds__(kThreads) markov_step_kernel(const Args a) {
       for (int gb = warp * 64; gb < ngroups; gb += kWarps * 64) {
         float x0[8], x1[8];
         const int g0 = gb + lane, g1 = gb + 32 + lane;
-        const int n0 = g0 < ngroups ? load_group(a, lrow, brow, g0, x0) : 0;
-        const int n1 = g1 < ngroups ? load_group(a, lrow, brow, g1, x1) : 0;
+        const int n0 = g0 < ngroups ? load(g0, x0) : 0;
+        const int n1 = g1 < ngroups ? load(g1, x1) : 0;
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const unsigned k0 = ordered_key(x0[e]);
@@ -214,7 +226,7 @@ __global__ void __launch_bounds__(kThreads) markov_step_kernel(const Args a) {
     for (int gb = glo; gb < ghi; gb += 32) {
       const int g = gb + lane;
       float x[8];
-      const int n = g < ghi ? load_group(a, lrow, brow, g, x) : 0;
+      const int n = g < ghi ? load(g, x) : 0;
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         if (e < n) {
@@ -245,7 +257,7 @@ __global__ void __launch_bounds__(kThreads) markov_step_kernel(const Args a) {
       for (int gb = glo; gb < ghi && seen < need_ties; gb += 32) {
         const int g = gb + lane;
         float x[8];
-        const int n = g < ghi ? load_group(a, lrow, brow, g, x) : 0;
+        const int n = g < ghi ? load(g, x) : 0;
         unsigned mask = 0;
 #pragma unroll
         for (int e = 0; e < 8; ++e)
@@ -270,12 +282,56 @@ __global__ void __launch_bounds__(kThreads) markov_step_kernel(const Args a) {
       }
     }
     // ---- sort descending (value desc, id asc); pad with 0 keys
-    int P = 1;
-    while (P < C) P <<= 1;
-    for (int i = C + threadIdx.x; i < P; i += kThreads) cand[i] = 0ull;
+    int P2 = 1;
+    while (P2 < C) P2 <<= 1;
+    for (int i = C + threadIdx.x; i < P2; i += kThreads) cand[i] = 0ull;
     __syncthreads();
-    block_sort_desc_u64(cand, P);
+    block_sort_desc_u64(cand, P2);
     }  // radix fallback
+    __syncthreads();
+    // ---- publish the piece's top C with row-global ids (the low word holds ~id)
+    unsigned long long* out = a.keys + ((long long)b * a.P + piece) * C;
+    const unsigned shift_ids = (unsigned)g_lo * 8u;
+    for (int i = threadIdx.x; i < C; i += kThreads) out[i] = cand[i] ? cand[i] - shift_ids : 0ull;
+  }
+  // ---- the last CTA of the row finishes it
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned ticket = atomicAdd(&a.tickets[b], 1u);
+    s_last = ticket == (unsigned)(a.P - 1);
+    if (s_last) a.tickets[b] = 0u;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  if (a.greedy) {
+    if (threadIdx.x == 0) s_prev = (int)argmax_key_index(atomicExch(&a.best[b], 0ull));
+    __syncthreads();
+  } else {
+    // ---- merge: the row's top C among the pieces' sorted top C lists.  Keys are distinct (value, then ~id), so
+    // a key's rank in the union is its index in its own list plus, per other list, the count of larger keys
+    // there (binary search); ties stay by ascending id because the keys say so.
+    const int n = a.P * C;
+    const unsigned long long* in = a.keys + (long long)b * a.P * C;
+    for (int i = threadIdx.x; i < n; i += kThreads) sel[i] = __ldcg(in + i);
+    __syncthreads();
+    for (int t = threadIdx.x; t < n; t += kThreads) {
+      const int p = t / C, i = t - p * C;
+      const unsigned long long key = sel[t];
+      int r = i;
+      for (int q = 0; q < a.P; ++q) {
+        if (q == p) continue;
+        const unsigned long long* list = sel + q * C;
+        int lo = 0, hi = C;
+        while (lo < hi) {
+          const int mid = (lo + hi) >> 1;
+          if (list[mid] > key) lo = mid + 1; else hi = mid;
+        }
+        r += lo;
+      }
+      if (r < C) cand[r] = key;
+    }
     __syncthreads();
     // ---- probs_from_logits over the C candidates (spec_sampler.py:65-96 on a [C] row)
     const float temp = a.temperature[b];
@@ -359,6 +415,26 @@ __global__ void __launch_bounds__(kThreads) markov_step_kernel(const Args a) {
     for (int i = threadIdx.x; i < a.rank; i += kThreads) a.e_next[(long long)b * a.rank + i] = a.w1[(long long)prev * a.rank + i];
 }
 
+// CTAs per row: enough to fill every SM twice over the batch, the pieces' keys fitting the merge buffer and
+// each piece keeping at least 4096 elements (so the thread-maxima bound sees every thread, and every piece has
+// C real keys, all distinct, for the merge's ranks).
+static int pieces_per_row(int B, int V, int C, int greedy, int sm_count) {
+  long long P = (2LL * sm_count) / B;
+  const long long by_len = V / 4096;
+  if (P > by_len) P = by_len;
+  if (!greedy) {
+    const long long by_merge = kSelCap / C;
+    if (P > by_merge) P = by_merge;
+  }
+  if (P < 1) P = 1;
+  return (int)P;
+}
+
+static long long workspace_bytes(int B, int V, int C, int greedy, int sm_count) {
+  const int P = pieces_per_row(B, V, C, greedy, sm_count);
+  return ws_head_bytes(B) + (greedy ? 0 : (long long)B * P * C * 8);
+}
+
 }  // namespace markov
 }  // namespace specdec
 
@@ -370,9 +446,10 @@ int specdec_markov_step(const void* logits, int logits_dtype, const void* bias, 
                         int row, int candidates, int greedy, int round_bf16, const float* temperature,
                         const long long* top_k, const float* top_p, int max_top_k, int has_top_p, const float* noise,
                         int noise_width, long long* drafts, float* probs, long long* prev_out, const void* w1,
-                        int rank, void* e_next, int* err, void* stream) {
+                        int rank, void* e_next, void* workspace, long long workspace_bytes, int* err, void* stream) {
   using namespace markov;
-  SPECDEC_CHECK_ARG(logits && bias && drafts && prev_out && err, "null pointer argument");
+  SPECDEC_CHECK_ARG(logits && bias && drafts && prev_out && err && workspace, "null pointer argument");
+  SPECDEC_CHECK_ARG((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "workspace must be 256-byte aligned");
   SPECDEC_CHECK_ARG(dtype_ok(logits_dtype) && dtype_ok(bias_dtype), "unknown dtype code");
   SPECDEC_CHECK_ARG(B >= 1 && B <= 65535 && k >= 1 && V >= 1 && row >= 0 && row < k, "bad sizes");
   SPECDEC_CHECK_ARG(!w1 || (e_next && rank >= 1), "w1 needs e_next and rank");
@@ -394,9 +471,27 @@ int specdec_markov_step(const void* logits, int logits_dtype, const void* bias, 
   a.err = err;
   a.vec = logits_dtype == kBF16 && bias_dtype == kBF16 && V % 8 == 0 &&
           ((reinterpret_cast<uintptr_t>(logits) | reinterpret_cast<uintptr_t>(bias)) & 15) == 0;
-  markov_step_kernel<<<B, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  DeviceInfo info;
+  if (int st = device_info(&info)) return st;
+  const int C = greedy ? 1 : candidates;
+  const long long need = markov::workspace_bytes(B, V, C, greedy, info.sm_count);
+  if (workspace_bytes < need)
+    return set_error(kWorkspaceTooSmall, "Markov workspace of %lld bytes, %lld needed", workspace_bytes, need);
+  a.P = pieces_per_row(B, V, C, greedy, info.sm_count);
+  a.gchunk = ((V + 7) / 8 + a.P - 1) / a.P;
+  char* ws = static_cast<char*>(workspace);
+  a.tickets = reinterpret_cast<unsigned*>(ws);
+  a.best = reinterpret_cast<unsigned long long*>(ws + (((long long)B * 4 + 7) / 8 * 8));
+  a.keys = reinterpret_cast<unsigned long long*>(ws + ws_head_bytes(B));
+  markov_step_kernel<<<dim3(a.P, B), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
   SPECDEC_LAUNCH_CHECK();
   return kOk;
+}
+
+long long specdec_markov_workspace_bytes(int B, int V, int candidates, int greedy) {
+  DeviceInfo info;
+  if (B < 1 || V < 1 || (!greedy && candidates < 1) || device_info(&info) != kOk) return -1;
+  return markov::workspace_bytes(B, V, greedy ? 1 : candidates, greedy, info.sm_count);
 }
 
 }  // extern "C"

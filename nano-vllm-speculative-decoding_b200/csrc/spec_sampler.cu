@@ -563,7 +563,7 @@ __device__ __forceinline__ int load_group_scaled(const T* row, int g, int V, int
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kTopkThreads) topk_stats_kernel(Args a, int mode) {
+__global__ void __launch_bounds__(kTopkThreads, 2) topk_stats_kernel(Args a, int mode) {
   constexpr int NT = kTopkThreads;
   __shared__ int s_start[kMaxRequests + 1];
   __shared__ unsigned long long sel[4096];                // fast-path candidates; the radix fallback's histogram
@@ -603,7 +603,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_stats_kernel(Args a, int mo
     // ---- fast path: thread-maxima bound, collect, sort (two passes over the row)
     int fast = -1;
     if (K <= NT) {
-      fast = select_by_thread_max<NT>(
+      fast = select_by_thread_max<NT, 2>(
           (V + 7) / 8, K, [&](int g, float (&x)[8]) { return load_group_scaled(row, g, V, a.vec_ok, temp, x); },
           tmax, sel, 4096, &s_sel);
       if (fast >= 0) {

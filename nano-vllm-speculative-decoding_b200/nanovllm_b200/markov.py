@@ -18,7 +18,7 @@ from dataclasses import dataclass
 import torch
 
 from . import _lib, spec_sampler
-from ._lib import DTYPE_CODES, check, ptr, require_cuda, stream_of
+from ._lib import DTYPE_CODES, Workspace, check, ptr, require_cuda, stream_of
 from .fused import err_word
 
 TIE_MARGIN = 64
@@ -76,6 +76,13 @@ def markov_rows(logits: torch.Tensor, prev: torch.Tensor, sampling, noise: torch
         noise = noise.float().contiguous()
     lib = _lib.lib()
     stream = stream_of(device)
+    ws = None
+    if greedy or candidates:
+        with torch.cuda.device(device):
+            need = int(lib.specdec_markov_workspace_bytes(batch, vocab, max(candidates, 1), int(greedy)))
+        if need < 0:
+            raise _lib.SpecdecError(lib.specdec_last_error().decode())
+        ws = Workspace.get(device, need, name="markov")    # zeroed once; the kernel keeps its counters zeroed
     for row in range(k):
         bias = torch.matmul(e_buf, weights.w2.t()) if weights is not None else markov_head(prev_buf)
         bias = bias.contiguous()
@@ -85,7 +92,7 @@ def markov_rows(logits: torch.Tensor, prev: torch.Tensor, sampling, noise: torch
                 candidates, int(greedy), _round_flag(logits, bias), ptr(temps), ptr(top_k), ptr(top_p), max_top_k,
                 has_top_p, ptr(noise), 0 if noise is None else noise.shape[-1], ptr(drafts), ptr(draft_probs),
                 ptr(prev_buf), ptr(None if weights is None else weights.w1), 0 if weights is None else
-                weights.w1.shape[1], ptr(e_buf), ptr(err_word(device)), stream))
+                weights.w1.shape[1], ptr(e_buf), ptr(ws), ws.numel(), ptr(err_word(device)), stream))
         else:
             row_logits = logits[:, row] + bias  # torch's dtype promotion and rounding, as the reference
             probs = spec_sampler.probs_from_logits(row_logits, sampling)

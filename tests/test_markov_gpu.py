@@ -155,3 +155,37 @@ def test_candidate_selection_paths(top_k):
                                       sampling, noise.cpu().numpy(), cand, round_fn=bf16)
     assert drafts.cpu().numpy().tolist() == want.tolist()
     np.testing.assert_allclose(probs.cpu().numpy(), want_probs, rtol=1e-5, atol=1e-8)
+
+
+@pytest.mark.parametrize("top_k", [100, 500, 0])
+def test_rows_split_over_many_ctas_keep_ties_by_id(top_k):
+    """V = 40000 rows are split over several CTAs (9 pieces at C = 164, 7 at C = 564); values drawn from a
+    handful of levels tie across piece boundaries, and the merged candidates must still be the oracle's (ties by
+    ascending token id).  top_k = 0 runs the greedy rows (argmax, first index)."""
+    from nanovllm_b200.markov import markov_rows, num_candidates
+    from oracle.ctx_store import bf16
+    B, k, V = 2, 3, 40000
+    g = torch.Generator(device=DEV).manual_seed(100 + top_k)
+    logits = (torch.randint(-3, 4, (B, k, V), device=DEV, generator=g).float() * 0.5).bfloat16()
+    table = (torch.randint(-2, 3, (8, V), device=DEV, generator=g).float() * 0.25).bfloat16()
+    head = lambda prev: table[prev % 8]
+    drafts = torch.empty(B, k, dtype=torch.int64, device=DEV)
+    prev = torch.randint(V, (B,), device=DEV, generator=g)
+    tab = table.float().cpu().numpy()
+    if top_k == 0:
+        markov_rows(logits, prev, None, None, drafts, None, 0, head)
+        want, _ = OM.markov_rows(logits.float().cpu().numpy(), prev.cpu().numpy(), lambda p: tab[p % 8], None, None,
+                                 0, round_fn=bf16)
+        assert drafts.cpu().numpy().tolist() == want.tolist()
+        return
+    samp = sampling_of([1.0, 0.8], [top_k] * B, [1.0, 0.9])
+    cand = num_candidates(samp.max_top_k, samp.all_top_k, V)
+    noise = torch.empty(B, k, cand, device=DEV).exponential_(generator=g).clamp_min_(1e-10)
+    probs = torch.empty(B, k, V, device=DEV)
+    markov_rows(logits, prev, samp, noise, drafts, probs, cand, head)
+    sampling = dict(temps=samp.temperatures.cpu().numpy(), top_k=samp.top_k.cpu().numpy(),
+                    top_p=samp.top_p.cpu().numpy(), max_top_k=samp.max_top_k, has_top_p=samp.has_top_p)
+    want, want_probs = OM.markov_rows(logits.float().cpu().numpy(), prev.cpu().numpy(), lambda p: tab[p % 8],
+                                      sampling, noise.cpu().numpy(), cand, round_fn=bf16)
+    assert drafts.cpu().numpy().tolist() == want.tolist()
+    np.testing.assert_allclose(probs.cpu().numpy(), want_probs, rtol=1e-5, atol=1e-8)
