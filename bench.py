@@ -325,7 +325,7 @@ def run_kernel(args) -> int:
     elif args.kernel == "markov":
         # config 4's drafter: 64 rows x 7 in-block steps, V = 151936, rank-256 Markov head, top_k 128 (192 candidates)
         from nanovllm_b200 import spec_sampler as S
-        from nanovllm_b200.markov import MarkovHeadWeights, markov_rows, num_candidates
+        from nanovllm_b200.markov import MarkovHeadWeights, MarkovQBuffer, markov_rows, num_candidates
         B, k, r = 64, 7, 256
         gg = torch.Generator(device=device).manual_seed(0)
         logits = (torch.randn(B, k, V, device=device, generator=gg) * 2).bfloat16()
@@ -336,12 +336,12 @@ def run_kernel(args) -> int:
         noise = torch.empty(B, k, cand, device=device).exponential_(generator=gg).clamp_min_(1e-10)
         prev = torch.randint(V, (B,), device=device, generator=gg)
         drafts = torch.empty(B, k, dtype=torch.int64, device=device)
-        probs = torch.empty(B, k, V, device=device)
+        qbuf = MarkovQBuffer(B, k, V, cand, device)     # persistent q: only the last call's candidates cleared
 
         def fn():
-            markov_rows(logits, prev, samp, noise, drafts, probs, cand, head)
-        # per step: W2 (77.8 MB) + the row's logits (19.4 MB); once: the q zero-fill (272 MB)
-        algorithmic = k * (V * r * 2 + B * V * 2) + B * k * V * 4
+            markov_rows(logits, prev, samp, noise, drafts, qbuf, cand, head)
+        # per step: W2 (77.8 MB) + the row's logits (19.4 MB); q is scattered (C values per row), not zero-filled
+        algorithmic = k * (V * r * 2 + B * V * 2)
     elif args.kernel == "ctx_store":
         # config 4's ctx_store: T = 288 verified tokens, 5 draft layers, hidden 4096, 8 KV heads of 128
         from nanovllm_b200.dflash import store_context_kv

@@ -122,13 +122,17 @@ int specdec_paged_attention(const void* q, long long T, long long q_row_stride, 
  * logits [B, k, V] and bias of dtype codes as above.  Limits: candidates <= 1024.  Each row is split over several
  * CTAs; workspace: 256-byte aligned device bytes, zero-filled once before first use (the kernel leaves its
  * counters zeroed), at least specdec_markov_workspace_bytes(B, V, candidates, greedy); calls sharing it must not
- * overlap on the GPU. */
+ * overlap on the GPU.  last_ids (int32 [B, k, candidates], or null): with it, probs is a persistent buffer that
+ * is zero except where this row scattered q on the previous call, listed in last_ids (-1 = none; all -1 and a
+ * zeroed probs at first use); those entries are cleared and the new ids recorded, so the caller need not zero
+ * the [B, k, V] probs (the reference's speculative.py:170-171 zero-fill) every call. */
 long long specdec_markov_workspace_bytes(int B, int V, int candidates, int greedy);
 int specdec_markov_step(const void* logits, int logits_dtype, const void* bias, int bias_dtype, int B, int k, int V,
                         int row, int candidates, int greedy, int round_bf16, const float* temperature,
                         const long long* top_k, const float* top_p, int max_top_k, int has_top_p, const float* noise,
                         int noise_width, long long* drafts, float* probs, long long* prev_out, const void* w1,
-                        int rank, void* e_next, void* workspace, long long workspace_bytes, int* err, void* stream);
+                        int rank, void* e_next, int* last_ids, void* workspace, long long workspace_bytes, int* err,
+                        void* stream);
 
 /* ------------------------------------------------------------------------------------------ kernel 4: ctx_store */
 /* DFlashDraftModel.store_context_kv (nanovllm/models/dflash.py:88-96) for every draft layer in one launch, and

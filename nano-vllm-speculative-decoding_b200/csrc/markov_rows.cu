@@ -55,6 +55,8 @@ struct Args {
   unsigned* tickets;        // [B] arrivals per row; the last CTA resets its entry
   unsigned long long* best; // [B] greedy argmax keys; reset by the last CTA
   unsigned long long* keys; // [B][P][C] each piece's top C keys (value << 32 | ~id), descending
+  int* last_ids;            // [B][k][C] ids this row scattered q to last time (-1: none), or null: the caller
+                            // zeroed probs; with it, probs stays zero elsewhere and only these are cleared
 };
 
 // Workspace: tickets and greedy keys (zeroed once, self-cleaning), then the pieces' candidate keys.
@@ -383,13 +385,23 @@ __global__ void __launch_bounds__(kThreads) markov_step_kernel(const Args a) {
     }
     __syncthreads();
     const float z = s_z;
-    // ---- race over the candidates with their noise; scatter q
+    // ---- race over the candidates with their noise; scatter q (after clearing the previous call's entries of
+    // this row when probs is a persistent buffer)
     const float* noise = a.noise + ((long long)b * a.k + a.j) * a.noise_width;
+    int* last = a.last_ids ? a.last_ids + ((long long)b * a.k + a.j) * C : nullptr;
+    if (last) {
+      for (int i = threadIdx.x; i < C; i += kThreads) {
+        const int old = last[i];
+        if (old >= 0 && old < V) a.probs[lrow + old] = 0.0f;
+      }
+      __syncthreads();
+    }
     unsigned long long best = 0ull;
     for (int i = threadIdx.x; i < C; i += kThreads) {
       const float p = __fdiv_rn(cprob[i], z);
       const int id = (int)(0xffffffffu - (unsigned)(cand[i] & 0xffffffffull));
       a.probs[lrow + id] = p;
+      if (last) last[i] = id;
       float ratio = __fdiv_rn(p, noise[i]);
       if (ratio == 0.0f) ratio = 0.0f;
       const unsigned long long key = argmax_key(ratio, (unsigned)i);
@@ -446,7 +458,8 @@ int specdec_markov_step(const void* logits, int logits_dtype, const void* bias, 
                         int row, int candidates, int greedy, int round_bf16, const float* temperature,
                         const long long* top_k, const float* top_p, int max_top_k, int has_top_p, const float* noise,
                         int noise_width, long long* drafts, float* probs, long long* prev_out, const void* w1,
-                        int rank, void* e_next, void* workspace, long long workspace_bytes, int* err, void* stream) {
+                        int rank, void* e_next, int* last_ids, void* workspace, long long workspace_bytes, int* err,
+                        void* stream) {
   using namespace markov;
   SPECDEC_CHECK_ARG(logits && bias && drafts && prev_out && err && workspace, "null pointer argument");
   SPECDEC_CHECK_ARG((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "workspace must be 256-byte aligned");
@@ -469,6 +482,7 @@ int specdec_markov_step(const void* logits, int logits_dtype, const void* bias, 
   a.noise = noise; a.noise_width = noise_width; a.drafts = drafts; a.probs = probs; a.prev_out = prev_out;
   a.w1 = static_cast<const __nv_bfloat16*>(w1); a.rank = rank; a.e_next = static_cast<__nv_bfloat16*>(e_next);
   a.err = err;
+  a.last_ids = greedy ? nullptr : last_ids;
   a.vec = logits_dtype == kBF16 && bias_dtype == kBF16 && V % 8 == 0 &&
           ((reinterpret_cast<uintptr_t>(logits) | reinterpret_cast<uintptr_t>(bias)) & 15) == 0;
   DeviceInfo info;

@@ -59,7 +59,7 @@ SIGNATURES = {
     "specdec_markov_step": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
                                      _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_int, _c_void_p,
                                      _c_int, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_void_p,
-                                     _c_void_p, _c_ll, _c_void_p, _c_void_p]),
+                                     _c_void_p, _c_void_p, _c_ll, _c_void_p, _c_void_p]),
     "specdec_markov_workspace_bytes": (_c_ll, [_c_int, _c_int, _c_int, _c_int]),
 }
 

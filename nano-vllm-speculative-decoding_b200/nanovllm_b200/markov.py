@@ -51,6 +51,20 @@ def _round_flag(logits: torch.Tensor, bias: torch.Tensor) -> int:
     return 0
 
 
+class MarkovQBuffer:
+    """A persistent q buffer for markov_rows: probs [B, k, V] fp32 is zero except where each row scattered q on the
+    previous call, recorded in ids [B, k, C] int32 (-1: none), so a call clears just those entries instead of
+    zero-filling the whole buffer (the reference zero-fills a fresh [B, k, V] tensor every call,
+    speculative.py:170-171).  Pass it as draft_probs; read q from .probs.  Tied to one (B, k, V, C)."""
+
+    def __init__(self, batch: int, k: int, vocab: int, candidates: int, device: torch.device):
+        if candidates < 1:
+            raise ValueError("a persistent q buffer needs candidate rows (candidates >= 1)")
+        self.probs = torch.zeros(batch, k, vocab, dtype=torch.float32, device=device)
+        self.ids = torch.full((batch, k, candidates), -1, dtype=torch.int32, device=device)
+        self.candidates = candidates
+
+
 def markov_rows(logits: torch.Tensor, prev: torch.Tensor, sampling, noise: torch.Tensor | None,
                 drafts: torch.Tensor, draft_probs: torch.Tensor | None, candidates: int, markov_head) -> None:
     """speculative.py:163-184: draw the k rows left to right into drafts (and q into draft_probs unless greedy);
@@ -58,8 +72,13 @@ def markov_rows(logits: torch.Tensor, prev: torch.Tensor, sampling, noise: torch
     device = require_cuda(logits, prev, drafts)
     batch, k, vocab = logits.shape
     logits = logits.contiguous()
+    qbuf = None
+    if isinstance(draft_probs, MarkovQBuffer):
+        qbuf, draft_probs = draft_probs, draft_probs.probs
+        if candidates != qbuf.candidates or tuple(draft_probs.shape) != (batch, k, vocab):
+            raise ValueError("the persistent q buffer was made for another batch shape or candidate count")
     greedy = draft_probs is None
-    if not greedy and candidates:
+    if not greedy and candidates and qbuf is None:
         draft_probs.zero_()                     # q is zero outside each row's candidates (speculative.py:171)
     prev_buf = prev.to(torch.int64).clone()
     weights = markov_head if isinstance(markov_head, MarkovHeadWeights) else None
@@ -92,7 +111,8 @@ def markov_rows(logits: torch.Tensor, prev: torch.Tensor, sampling, noise: torch
                 candidates, int(greedy), _round_flag(logits, bias), ptr(temps), ptr(top_k), ptr(top_p), max_top_k,
                 has_top_p, ptr(noise), 0 if noise is None else noise.shape[-1], ptr(drafts), ptr(draft_probs),
                 ptr(prev_buf), ptr(None if weights is None else weights.w1), 0 if weights is None else
-                weights.w1.shape[1], ptr(e_buf), ptr(ws), ws.numel(), ptr(err_word(device)), stream))
+                weights.w1.shape[1], ptr(e_buf), ptr(None if qbuf is None else qbuf.ids), ptr(ws), ws.numel(),
+                ptr(err_word(device)), stream))
         else:
             row_logits = logits[:, row] + bias  # torch's dtype promotion and rounding, as the reference
             probs = spec_sampler.probs_from_logits(row_logits, sampling)

@@ -189,3 +189,28 @@ def test_rows_split_over_many_ctas_keep_ties_by_id(top_k):
                                       sampling, noise.cpu().numpy(), cand, round_fn=bf16)
     assert drafts.cpu().numpy().tolist() == want.tolist()
     np.testing.assert_allclose(probs.cpu().numpy(), want_probs, rtol=1e-5, atol=1e-8)
+
+
+def test_persistent_q_buffer_matches_fresh_zeroed_buffers():
+    """A MarkovQBuffer clears only the previous call's candidates: two calls in a row give exactly the drafts and
+    q of two calls on freshly zeroed tensors, and the buffer stays zero outside the current candidates."""
+    from nanovllm_b200.markov import MarkovQBuffer, markov_rows, num_candidates
+    B, k, V = 6, 4, 20000
+    g = torch.Generator(device=DEV).manual_seed(77)
+    table = (torch.randn(16, V, device=DEV, generator=g)).bfloat16()
+    head = lambda prev: table[prev % 16]
+    samp = sampling_of([1.0, 0.8, 1.0, 0.6, 1.2, 0.9], [40] * B, [1.0, 0.9, 1.0, 0.5, 1.0, 0.95])
+    cand = num_candidates(samp.max_top_k, samp.all_top_k, V)
+    qbuf = MarkovQBuffer(B, k, V, cand, DEV)
+    for call in range(3):
+        logits = (torch.randn(B, k, V, device=DEV, generator=g) * 2).bfloat16()
+        noise = torch.empty(B, k, cand, device=DEV).exponential_(generator=g).clamp_min_(1e-10)
+        prev = torch.randint(V, (B,), device=DEV, generator=g)
+        d_ref = torch.empty(B, k, dtype=torch.int64, device=DEV)
+        q_ref = torch.full((B, k, V), float("nan"), device=DEV)      # garbage: markov_rows zero-fills it
+        markov_rows(logits, prev, samp, noise, d_ref, q_ref, cand, head)
+        d = torch.empty(B, k, dtype=torch.int64, device=DEV)
+        markov_rows(logits, prev, samp, noise, d, qbuf, cand, head)
+        assert torch.equal(d, d_ref)
+        assert torch.equal(qbuf.probs, q_ref)
+        assert int((qbuf.probs != 0).sum(dim=-1).max()) <= cand
