@@ -4,8 +4,9 @@ nanovllm/engine/speculative.py:411-512) on the B200 kernels.
     round = VerifyRound(target, num_drafts=7, graph_rows=[64])
     appended = round.run_round(rows, drafts, draft_probs, sampling, generator=gen)   # list[list[int]]
 
-A round: the rows' metadata (host lists, batch_metadata.verify_varlen_metadata) is copied once into the
-captured graph's static buffers from pinned memory, the drafts are placed on the device, the graph replays the
+A round: the rows' metadata (batch_metadata.pack_verify_metadata: the values of verify_varlen_metadata, built
+with array operations into a pinned staging copy of the graph's two packed metadata buffers) reaches the device in
+two host-to-device copies, the drafts are placed on the device, the graph replays the
 target's verification forward and LM head (logits [T, V] bf16), the fused sampler (kernel 1) accepts straight
 from the logits - probabilities, uniforms and the race noise never materialise - and the single D2H copy of
 [drafts | n_accept | tail] returns each row's accepted drafts followed by its tail token.
@@ -17,7 +18,7 @@ from collections import Counter
 import torch
 
 from . import spec_sampler
-from .batch_metadata import RowState, verify_varlen_metadata
+from .batch_metadata import RowState, pack_verify_metadata
 from .spec_sampler import SamplingTensors
 from .target import Qwen3Target
 
@@ -29,34 +30,29 @@ class VerifyRound:
         self.block_size = target.block_size
         self.max_num_blocks = max_num_blocks
         self.stats: Counter = Counter()
-        self.pinned: dict[str, torch.Tensor] = {}
+        self.pinned: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
         query_len = num_drafts + 1
         for rows in sorted(graph_rows):
             tokens = rows * query_len
-            target.capture(rows, tokens, max_num_blocks, query_len, lambda b, r=rows, t=tokens: self._load(
-                b, verify_varlen_metadata([], [], num_drafts, self.block_size, r, t, target.pad_block_id,
-                                          max_num_blocks), r, t))
+            target.capture(rows, tokens, max_num_blocks, query_len,
+                           lambda b, r=rows, t=tokens: self._load(b, [], [], r, t))
 
     # ------------------------------------------------------------------ metadata
-    def _host(self, name: str, values, dtype) -> torch.Tensor:
-        """The values in a reusable pinned host tensor (one per name and length)."""
-        flat = torch.tensor(values, dtype=dtype)
-        key = f"{name}:{flat.numel()}:{dtype}"
-        buf = self.pinned.get(key)
-        if buf is None:
-            buf = torch.empty(flat.shape, dtype=dtype, pin_memory=True)
-            self.pinned[key] = buf
-        buf.copy_(flat)
-        return buf
-
-    def _load(self, buffers: dict, m, num_rows: int, num_tokens: int) -> None:
-        """speculative.py:519-527: the metadata into the graph's buffers (H2D from pinned memory)."""
-        buffers["input_ids"][:num_tokens].copy_(self._host("ids", m.input_ids, torch.int64), non_blocking=True)
-        buffers["positions"][:num_tokens].copy_(self._host("pos", m.positions, torch.int64), non_blocking=True)
-        buffers["slot_mapping"][:num_tokens].copy_(self._host("slot", m.slot_mapping, torch.int32), non_blocking=True)
-        buffers["cu_seqlens_q"][:num_rows + 1].copy_(self._host("cuq", m.cu_seqlens_q, torch.int32), non_blocking=True)
-        buffers["cu_seqlens_k"][:num_rows + 1].copy_(self._host("cuk", m.cu_seqlens_k, torch.int32), non_blocking=True)
-        buffers["block_tables"][:num_rows].copy_(self._host("bt", m.block_tables, torch.int32), non_blocking=True)
+    def _load(self, buffers: dict, rows: list[RowState], lens: list[int], num_rows: int, num_tokens: int) -> None:
+        """speculative.py:519-527: the metadata (batch_metadata.py:149-181) into the graph's two packed buffers:
+        built in a pinned staging copy (one per graph), then two non-blocking host-to-device copies.  The staging
+        copy is rewritten only after the previous round's D2H read, which follows these copies on the stream."""
+        dev64, dev32 = buffers["_packed64"], buffers["_packed32"]
+        staging = self.pinned.get(num_tokens)
+        if staging is None:
+            staging = (torch.empty(dev64.shape, dtype=torch.int64, pin_memory=True),
+                       torch.empty(dev32.shape, dtype=torch.int32, pin_memory=True))
+            self.pinned[num_tokens] = staging
+        host64, host32 = staging
+        pack_verify_metadata(rows, lens, self.num_drafts, self.block_size, num_rows, num_tokens,
+                             self.target.pad_block_id, self.max_num_blocks, host64.numpy(), host32.numpy())
+        dev64.copy_(host64, non_blocking=True)
+        dev32.copy_(host32, non_blocking=True)
 
     def load(self, rows: list[RowState], verified_lens: list[int] | None = None) -> int:
         """Loads a round's metadata into the smallest fitting graph; returns its token count."""
@@ -64,9 +60,7 @@ class VerifyRound:
         num_verified = sum(lens)
         num_tokens = next(t for t in sorted(self.target.graphs) if t >= num_verified)
         num_rows = num_tokens // (self.num_drafts + 1)
-        m = verify_varlen_metadata(rows, lens, self.num_drafts, self.block_size, num_rows, num_tokens,
-                                   self.target.pad_block_id, self.max_num_blocks)
-        self._load(self.target.graphs[num_tokens][1], m, num_rows, num_tokens)
+        self._load(self.target.graphs[num_tokens][1], rows, lens, num_rows, num_tokens)
         return num_tokens
 
     def place_drafts(self, num_tokens: int, drafts: torch.Tensor) -> None:

@@ -110,13 +110,17 @@ class Qwen3Target:
 
     # ------------------------------------------------------------------ graphs
     def static_buffers(self, num_rows: int, num_tokens: int, width: int) -> dict:
-        d = self.device
-        return dict(input_ids=torch.zeros(num_tokens, dtype=torch.int64, device=d),
-                    positions=torch.zeros(num_tokens, dtype=torch.int64, device=d),
-                    slot_mapping=torch.full((num_tokens,), -1, dtype=torch.int32, device=d),
-                    cu_seqlens_q=torch.zeros(num_rows + 1, dtype=torch.int32, device=d),
-                    cu_seqlens_k=torch.zeros(num_rows + 1, dtype=torch.int32, device=d),
-                    block_tables=torch.full((num_rows, width), self.pad_block_id, dtype=torch.int32, device=d))
+        """The graph's metadata inputs as views of one int64 and one int32 device buffer, so a round's metadata
+        arrives in two host-to-device copies (batch_metadata.packed_views gives the layout)."""
+        from .batch_metadata import packed_sizes, packed_views
+        n64, n32 = packed_sizes(num_rows, num_tokens, width)
+        packed64 = torch.zeros(n64, dtype=torch.int64, device=self.device)
+        packed32 = torch.zeros(n32, dtype=torch.int32, device=self.device)
+        buffers = packed_views(packed64, packed32, num_rows, num_tokens, width)
+        buffers["slot_mapping"].fill_(-1)
+        buffers["block_tables"].fill_(self.pad_block_id)
+        buffers["_packed64"], buffers["_packed32"] = packed64, packed32
+        return buffers
 
     def capture(self, num_rows: int, num_tokens: int, width: int, max_seqlen_q: int,
                 load_padding) -> dict:
