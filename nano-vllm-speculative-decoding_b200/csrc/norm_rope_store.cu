@@ -12,9 +12,10 @@
 //   SiluAndMul                           nanovllm/layers/activation.py:8-11  silu(x) * y over the two halves
 //
 // ctx_store design: one launch covers every draft layer.  A warp owns one (token, layer, head) row of 128 dims
-// (lane l holds dims l, l+32, l+64, l+96, so both RoPE partners l and l+64 sit in the same lane): the K row is
-// RMS-normalised with a warp reduction, rotated with the position's cos/sin, and written with the V row to the
-// slot; slot -1 rows are skipped before any load.  The kernel is HBM-bound (bytes: read kv, write cache).
+// (lane l holds dims 2l, 2l+1 and their RoPE partners 2l+64, 2l+65, as two bf16 pairs, so the row moves in
+// 4-byte loads and stores and both partners of each rotation sit in the same lane): the K row is RMS-normalised
+// with a warp reduction, rotated with the position's cos/sin, and written with the V row to the slot; slot -1
+// rows are skipped before any load.  The kernel is HBM-bound (bytes: read kv, write cache).
 #include "common.cuh"
 
 #include <math.h>
@@ -26,27 +27,41 @@ constexpr int kHeadDim = 128;
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
-// RMSNorm of one 128-dim head row held as 4 values per lane (dims l, l+32, l+64, l+96), then the weight.
+// A head row's 4 dims of lane l: x[0], x[1] = dims 2l, 2l+1; x[2], x[3] = dims 2l+64, 2l+65.
+__device__ __forceinline__ void load_head(const __nv_bfloat16* row, int lane, float (&x)[4]) {
+  const __nv_bfloat162 a = reinterpret_cast<const __nv_bfloat162*>(row)[lane];
+  const __nv_bfloat162 b = reinterpret_cast<const __nv_bfloat162*>(row + 64)[lane];
+  x[0] = __low2float(a);
+  x[1] = __high2float(a);
+  x[2] = __low2float(b);
+  x[3] = __high2float(b);
+}
+__device__ __forceinline__ void store_head(__nv_bfloat16* row, int lane, const float (&x)[4]) {
+  reinterpret_cast<__nv_bfloat162*>(row)[lane] = __floats2bfloat162_rn(x[0], x[1]);
+  reinterpret_cast<__nv_bfloat162*>(row + 64)[lane] = __floats2bfloat162_rn(x[2], x[3]);
+}
+
+// RMSNorm of one 128-dim head row (lane layout of load_head), then the weight.
 __device__ __forceinline__ void head_rmsnorm(float (&x)[4], const __nv_bfloat16* weight, int lane, float eps) {
+  const __nv_bfloat162 wa = reinterpret_cast<const __nv_bfloat162*>(weight)[lane];
+  const __nv_bfloat162 wb = reinterpret_cast<const __nv_bfloat162*>(weight + 64)[lane];
+  const float w[4] = {__low2float(wa), __high2float(wa), __low2float(wb), __high2float(wb)};
   float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
   ss = warp_sum_f32(ss);
   const float r = rsqrtf(ss / kHeadDim + eps);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float w = __bfloat162float(weight[lane + 32 * i]);
-    x[i] = bf16_round(bf16_round(x[i] * r) * w);   // x.to(bf16).mul_(weight) rounds twice
-  }
+  for (int i = 0; i < 4; ++i) x[i] = bf16_round(bf16_round(x[i] * r) * w[i]);   // x.to(bf16).mul_(weight)
 }
 
-// RoPE on dims (l, l+64) and (l+32, l+96): cos/sin index = dim % 64.
+// RoPE on the pairs (2l, 2l+64) and (2l+1, 2l+65): cos/sin index = dim % 64.
 __device__ __forceinline__ void head_rope(float (&x)[4], const float* cos_sin, int lane) {
-  const float c0 = cos_sin[lane], s0 = cos_sin[64 + lane];
-  const float c1 = cos_sin[lane + 32], s1 = cos_sin[64 + lane + 32];
+  const float2 c = reinterpret_cast<const float2*>(cos_sin)[lane];
+  const float2 sn = reinterpret_cast<const float2*>(cos_sin + 64)[lane];
   const float x1a = x[0], x2a = x[2], x1b = x[1], x2b = x[3];
-  x[0] = x1a * c0 - x2a * s0;
-  x[2] = x2a * c0 + x1a * s0;
-  x[1] = x1b * c1 - x2b * s1;
-  x[3] = x2b * c1 + x1b * s1;
+  x[0] = x1a * c.x - x2a * sn.x;
+  x[2] = x2a * c.x + x1a * sn.x;
+  x[1] = x1b * c.y - x2b * sn.y;
+  x[3] = x2b * c.y + x1b * sn.y;
 }
 
 struct NormRopeArgs {
@@ -86,15 +101,11 @@ __global__ void __launch_bounds__(256) norm_rope_store_kernel(const NormRopeArgs
   const float* cs = a.cos_sin + pos * kHeadDim;
   const __nv_bfloat16* row = a.x + layer * a.x_layer_stride + (long long)t * a.x_row_stride;
   if (hh < a.Hq) {
-    const __nv_bfloat16* src = row + hh * kHeadDim;
     float x[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) x[i] = __bfloat162float(src[lane + 32 * i]);
+    load_head(row + hh * kHeadDim, lane, x);
     head_rmsnorm(x, a.q_norm, lane, a.eps);
     head_rope(x, cs, lane);
-    __nv_bfloat16* dst = a.q_out + ((long long)t * a.Hq + hh) * kHeadDim;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = __float2bfloat16_rn(x[i]);
+    store_head(a.q_out + ((long long)t * a.Hq + hh) * kHeadDim, lane, x);
     return;
   }
   const int h = hh - a.Hq;
@@ -106,19 +117,14 @@ __global__ void __launch_bounds__(256) norm_rope_store_kernel(const NormRopeArgs
   }
   const __nv_bfloat16* ksrc = row + (a.Hq + h) * kHeadDim;
   const __nv_bfloat16* vsrc = row + (a.Hq + a.Hkv + h) * kHeadDim;
+  const uint2 vv = reinterpret_cast<const uint2*>(vsrc)[lane];     // 8 bytes of the V row per lane
   float x[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) x[i] = __bfloat162float(ksrc[lane + 32 * i]);
+  load_head(ksrc, lane, x);
   head_rmsnorm(x, a.k_norm + layer * a.k_norm_layer_stride, lane, a.eps);
   head_rope(x, cs, lane);
   const long long off = layer * a.cache_layer_stride + (slot * a.Hkv + h) * kHeadDim;
-  __nv_bfloat16* kdst = a.k_cache + off;
-  __nv_bfloat16* vdst = a.v_cache + off;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    kdst[lane + 32 * i] = __float2bfloat16_rn(x[i]);
-    vdst[lane + 32 * i] = vsrc[lane + 32 * i];
-  }
+  store_head(a.k_cache + off, lane, x);
+  reinterpret_cast<uint2*>(a.v_cache + off)[lane] = vv;
 }
 
 // ---------------------------------------------------------------------------------------- RMSNorm (+ residual)
@@ -134,6 +140,13 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* x, co
   const uint4* rv = residual ? reinterpret_cast<const uint4*>(residual + t * width) : nullptr;
   const int nvec = width / 8;
   float v[kMaxVec][8];
+  uint4 wraw[kMaxVec];
+  const uint4* wv = reinterpret_cast<const uint4*>(weight);
+#pragma unroll
+  for (int u = 0; u < kMaxVec; ++u) {          // the weights load while the row is reduced
+    const int i = threadIdx.x + u * 256;
+    if (i < nvec) wraw[u] = wv[i];
+  }
   float ss = 0.0f;
 #pragma unroll
   for (int u = 0; u < kMaxVec; ++u) {
@@ -169,13 +182,12 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* x, co
 #pragma unroll
   for (int w = 0; w < 8; ++w) total += red[w];
   const float rs = rsqrtf(total / width + eps);
-  const uint4* wv = reinterpret_cast<const uint4*>(weight);
 #pragma unroll
   for (int u = 0; u < kMaxVec; ++u) {
     const int i = threadIdx.x + u * 256;
     if (i < nvec) {
       float w8[8];
-      unpack16_bf16(wv[i], w8);
+      unpack16_bf16(wraw[u], w8);
       uint4 packed;
       uint32_t* wd = reinterpret_cast<uint32_t*>(&packed);
 #pragma unroll
@@ -191,7 +203,8 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* x, co
 }
 
 // ---------------------------------------------------------------------------------------- SiLU * mul
-// gate_up [T, 2I] -> out [T, I] = silu(gate) * up, computed in fp32 and rounded once.
+// gate_up [T, 2I] -> out [T, I] = silu(gate) * up, computed in fp32 and rounded once to bf16.  silu(a) =
+// a / (1 + e^-a) with the hardware exp2 and a fast quotient: a few fp32 ulp, far below the bf16 rounding.
 __global__ void __launch_bounds__(256) silu_mul_kernel(const __nv_bfloat16* gate_up, __nv_bfloat16* out, long long T,
                                                        int I) {
   const long long nvec_row = I / 8;
@@ -208,8 +221,8 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const __nv_bfloat16* gate
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
     const float a0 = gf[2 * e], a1 = gf[2 * e + 1];
-    const float y0 = a0 / (1.0f + expf(-a0)) * uf[2 * e];
-    const float y1 = a1 / (1.0f + expf(-a1)) * uf[2 * e + 1];
+    const float y0 = __fdividef(a0, 1.0f + __expf(-a0)) * uf[2 * e];
+    const float y1 = __fdividef(a1, 1.0f + __expf(-a1)) * uf[2 * e + 1];
     __nv_bfloat162 p2 = __floats2bfloat162_rn(y0, y1);
     wd[e] = *reinterpret_cast<uint32_t*>(&p2);
   }
@@ -234,6 +247,14 @@ int specdec_norm_rope_store(const void* x, long long x_layer_stride, long long x
   SPECDEC_CHECK_ARG(T >= 0 && layers >= 1 && layers <= 65535 && num_kv_heads >= 1 && num_q_heads >= 0,
                     "bad sizes");
   SPECDEC_CHECK_ARG(num_q_heads == 0 || (q_norm && q_out), "q heads need q_norm and q_out");
+  // rows move as 4-byte bf16 pairs (8-byte V chunks), cos/sin as float2: 8-byte aligned rows and tables
+  auto a8 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7) == 0; };
+  SPECDEC_CHECK_ARG(a8(x) && a8(k_cache) && a8(v_cache) && a8(cos_sin) && (!q_out || a8(q_out)) &&
+                        (reinterpret_cast<uintptr_t>(k_norm) & 3) == 0 && (!q_norm || (reinterpret_cast<uintptr_t>(q_norm) & 3) == 0),
+                    "x, caches, q_out and cos_sin must be 8-byte aligned, the norm weights 4-byte aligned");
+  SPECDEC_CHECK_ARG(x_layer_stride % 4 == 0 && x_row_stride % 4 == 0 && cache_layer_stride % 4 == 0 &&
+                        k_norm_layer_stride % 2 == 0,
+                    "row, layer and cache strides must keep 8-byte alignment");
   if (T == 0) return kOk;
   fused::NormRopeArgs a{};
   a.x = static_cast<const __nv_bfloat16*>(x);
