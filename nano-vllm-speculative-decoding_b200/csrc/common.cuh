@@ -238,14 +238,18 @@ __device__ void block_top_sorted(unsigned long long* keys, int n, int C, unsigne
 // Top-C selection by a thread-maxima bound (whole block of NT threads; C <= NT).  load(g, x) fills the 8 values
 // of element group g (missing ones -inf) and returns how many exist.  Every thread's maximum over its groups is
 // an element; the C-th largest of those NT maxima is therefore <= the row's C-th largest value, so collecting
-// every element at or above it keeps the top C and all of their ties.  Collected entries are 64-bit keys
-// (ordered value << 32 | ~id, all distinct) in buf (capacity cap); on return buf[0..C) holds the top C keys in
-// descending order and the count is returned, or -1 when more than cap elements reach the bound (the caller
-// falls back to an exact radix select).  tmax is NT floats of scratch.  Both orderings (the C-th thread maximum,
-// the top C of up to 1024 collected keys) are warp sorts plus binary-search ranks: a few block barriers.
+// every element at or above it keeps the top C and all of their ties.  slack_rel widens the collection to
+// values >= bound - |bound| * slack_rel - 1e-30 (for callers that rank a monotone transform of the loaded values,
+// where rounding may tie a slightly smaller value with the bound).  Collected entries are 64-bit keys (ordered value << 32 | ~id, all
+// distinct) in buf (capacity cap); the count is returned, or -1 when more than cap elements reach the bound (the
+// caller falls back to an exact radix select).  On return buf[0..count) still holds every collected key (in some
+// order, padded with 0 keys to a multiple of 32) and *top points at the top C in descending order: inside buf
+// past the collected keys, or at buf itself when the count exceeded 1024 (then all of buf[0..count) is sorted).
+// tmax is NT floats of scratch.  Both orderings (the C-th thread maximum, the top C of up to 1024 collected
+// keys) are warp sorts plus binary-search ranks: a few block barriers.
 template <int NT, int UNROLL, typename Load>
 __device__ int select_by_thread_max(int ngroups, int C, Load load, float* tmax, unsigned long long* buf, int cap,
-                                    int* s_count) {
+                                    int* s_count, unsigned long long** top, float slack_rel = 0.0f) {
   __shared__ float s_bound;
   float mx = -INFINITY;
   // UNROLL groups per thread in flight per iteration (their loads are independent)
@@ -276,7 +280,7 @@ __device__ int select_by_thread_max(int ngroups, int C, Load load, float* tmax, 
     if (r == C - 1) s_bound = key_to_float(static_cast<unsigned>(sorted >> 32));
     __syncthreads();
   }
-  const float bound = s_bound;
+  const float bound = slack_rel > 0.0f ? s_bound - fabsf(s_bound) * slack_rel - 1e-30f : s_bound;
   for (int g0 = threadIdx.x; g0 < ngroups; g0 += UNROLL * NT) {
     float x[UNROLL][8];
     int n[UNROLL];
@@ -303,9 +307,8 @@ __device__ int select_by_thread_max(int ngroups, int C, Load load, float* tmax, 
   if (count > cap) return -1;
   const int padded = (count + 31) / 32 * 32;
   if (count <= 1024 && padded + C <= cap) {
-    block_top_sorted<NT>(buf, count, C, buf + cap - C);
-    for (int i = threadIdx.x; i < C; i += NT) buf[i] = buf[cap - C + i];
-    __syncthreads();
+    *top = buf + cap - C;
+    block_top_sorted<NT>(buf, count, C, *top);
     return count;
   }
   int P = 1;
@@ -313,6 +316,7 @@ __device__ int select_by_thread_max(int ngroups, int C, Load load, float* tmax, 
   for (int i = count + threadIdx.x; i < P; i += NT) buf[i] = 0ull;
   __syncthreads();
   block_sort_desc_u64(buf, P);
+  *top = buf;
   return count;
 }
 

@@ -178,9 +178,10 @@ __global__ void __launch_bounds__(kThreads) markov_step_kernel(const Args a) {
     // ---- the piece's top C, descending: thread-maxima bound + collect + sort, or an exact radix select
     int fast = -1;
     if (C <= kThreads) {
-      fast = select_by_thread_max<kThreads, 1>(ngroups, C, load, tmax, sel, kSelCap, &s_sel);
+      unsigned long long* top = nullptr;
+      fast = select_by_thread_max<kThreads, 1>(ngroups, C, load, tmax, sel, kSelCap, &s_sel, &top);
       if (fast >= 0)
-        for (int i = threadIdx.x; i < C; i += kThreads) cand[i] = sel[i];
+        for (int i = threadIdx.x; i < C; i += kThreads) cand[i] = top[i];
     }
     if (fast < 0) {
     // ---- radix select of the C-th largest ordered key

@@ -600,14 +600,35 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_stats_kernel(Args a, int
       return;
     }
     const int K = (int)(tk < V ? tk : V);
-    // ---- fast path: thread-maxima bound, collect, sort (two passes over the row)
+    // ---- fast path: thread-maxima bound and collection over the raw logits (x / T is monotone in x: the
+    // collection margin of 2^-22 relative covers values whose quotient rounds onto the bound's), then the
+    // collected candidates re-keyed by x / T and ranked: two passes over the row, no division in them
     int fast = -1;
+    unsigned long long* top = nullptr;
     if (K <= NT) {
       fast = select_by_thread_max<NT, 2>(
-          (V + 7) / 8, K, [&](int g, float (&x)[8]) { return load_group_scaled(row, g, V, a.vec_ok, temp, x); },
-          tmax, sel, 4096, &s_sel);
+          (V + 7) / 8, K, [&](int g, float (&x)[8]) { return load_group_scaled(row, g, V, a.vec_ok, 1.0f, x); },
+          tmax, sel, 4096, &s_sel, &top, temp == 1.0f ? 0.0f : 2.384185791015625e-07f);
+      if (fast >= 0 && temp != 1.0f) {
+        const int n = top == sel ? fast : (fast + 31) / 32 * 32;
+        for (int i = threadIdx.x; i < n; i += NT) {
+          const unsigned long long key = sel[i];
+          if (key) {
+            const float f = scale_logit(key_to_float((unsigned)(key >> 32)), temp);
+            sel[i] = (static_cast<unsigned long long>(ordered_key(f)) << 32) | (key & 0xffffffffull);
+          }
+        }
+        __syncthreads();
+        if (top == sel) {
+          int P2 = 1;
+          while (P2 < fast) P2 <<= 1;
+          block_sort_desc_u64(sel, P2);
+        } else {
+          block_top_sorted<NT>(sel, fast, K, top);
+        }
+      }
       if (fast >= 0) {
-        for (int i = threadIdx.x; i < K; i += NT) cand[i] = key_to_float((unsigned)(sel[i] >> 32));
+        for (int i = threadIdx.x; i < K; i += NT) cand[i] = key_to_float((unsigned)(top[i] >> 32));
         __syncthreads();
       }
     }
@@ -707,9 +728,19 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_stats_kernel(Args a, int
     __syncthreads();
     thr = s_thr;
     m = cand[0];
-    // ---- sum over the kept entries
+    // ---- sum over the kept entries: every one of them (>= the K-th value) is among the collected candidates on
+    // the fast path; the radix path re-reads the row
     float ls = 0.0f;
-    {
+    if (fast >= 0) {
+      const int n = top == sel ? fast : (fast + 31) / 32 * 32;
+      for (int i = threadIdx.x; i < n; i += NT) {
+        const unsigned long long key = sel[i];
+        if (key) {
+          const float f = key_to_float((unsigned)(key >> 32));
+          if (f >= thr) ls += exp_sum_term(f - m);
+        }
+      }
+    } else {
       const int ngroups = (V + 7) / 8;
       for (int g = threadIdx.x; g < ngroups; g += NT) {
         float x[8];
@@ -789,8 +820,7 @@ __global__ void __launch_bounds__(kThreads) write_probs_kernel(Args a, int merge
 }
 
 // ---------------------------------------------------------------------------------------- pass 2: tail race
-// grid = torch's exponential_ grid for e_numel = B * V elements (S = 256 * gridDim.x threads).  RACE: the
-// request's row is x row b itself, a plain race over given weights (sample()).
+// Race keys of a warp's 32 elements, which may belong to two rows, folded into the rows' shared-memory maxima.
 __device__ __forceinline__ void warp_segment_reduce(unsigned long long key, int b, bool active,
                                                     unsigned long long* s_best) {
   const int lane = threadIdx.x & 31;
@@ -812,122 +842,13 @@ __device__ __forceinline__ void warp_segment_reduce(unsigned long long key, int 
   }
 }
 
-template <typename T, bool RACE>
-__global__ void __launch_bounds__(kThreads) tail_kernel(Args a) {
-  __shared__ unsigned long long s_best[kMaxRequests];
-  __shared__ ReqDesc s_desc[RACE ? 1 : kMaxRequests];
-  __shared__ int s_last;
-  if (!RACE && *reinterpret_cast<volatile int*>(a.status) != 0) return;  // pass 1 rejected its inputs
-  for (int i = threadIdx.x; i < a.B; i += kThreads) {
-    s_best[i] = 0ull;
-    if (!RACE) s_desc[i] = a.desc[i];
-  }
-  __syncthreads();
-  const long long S = (long long)kRngBlock * gridDim.x;
-  const long long idx = (long long)blockIdx.x * kRngBlock + threadIdx.x;
-  const long long warp_idx0 = idx - (threadIdx.x & 31);
-  const long long N = a.e_numel;
-  const unsigned V = (unsigned)a.V;
-  curandStatePhilox4_32_10_t st;
-  const bool gen = a.E == nullptr;
-  if (gen) curand_init(a.seed, (unsigned long long)idx, a.offset_E, &st);
-  // row / column of element idx, advanced by S per grid-stride step
-  unsigned b = (unsigned)(idx / V), v = (unsigned)(idx % V);
-  for (int n = 0; n < a.e_rounds; ++n) {
-    if ((long long)(n * 4) * S + warp_idx0 >= N) break;      // warp-uniform
-    // ---- the round's four elements (lanes of one curand_uniform4): issue every load first
-    unsigned eb[4], ev[4];
-    bool act[4];
-    float xv[4], qv[4], ee[4];
-#pragma unroll
-    for (int ii = 0; ii < 4; ++ii) {
-      const long long li = (long long)(n * 4 + ii) * S + idx;
-      act[ii] = li < N;
-      eb[ii] = b;
-      ev[ii] = v;
-      xv[ii] = 0.0f;
-      qv[ii] = 0.0f;
-      ee[ii] = 1.0f;
-      if (act[ii]) {
-        if (RACE) {
-          xv[ii] = reinterpret_cast<const float*>(a.x)[(long long)b * a.V + v];
-        } else {
-          const ReqDesc& d = s_desc[b];
-          xv[ii] = to_f32(reinterpret_cast<const T*>(a.x)[d.x_row * a.V + v]);
-          if (d.q_row >= 0) qv[ii] = a.q[d.q_row * a.V + v];
-        }
-        if (!gen) ee[ii] = a.E[li];
-      }
-      b += a.e_sq;
-      v += a.e_sr;
-      if (v >= V) { v -= V; ++b; }
-    }
-    if (gen) {
-      const float4 r4 = curand_uniform4(&st);
-      ee[0] = torch_exponential_clamped(r4.x);
-      ee[1] = torch_exponential_clamped(r4.y);
-      ee[2] = torch_exponential_clamped(r4.z);
-      ee[3] = torch_exponential_clamped(r4.w);
-    }
-    // ---- weights, ratios and argmax keys
-    unsigned long long key[4];
-#pragma unroll
-    for (int ii = 0; ii < 4; ++ii) {
-      key[ii] = 0ull;
-      if (act[ii]) {
-        float w;
-        if (RACE) {
-          w = xv[ii];
-        } else {
-          const ReqDesc& d = s_desc[eb[ii]];
-          float p;
-          if (a.probs_mode) {
-            p = xv[ii];
-          } else {
-            const float f = d.temp == 1.0f ? xv[ii] : scale_logit(xv[ii], d.temp);
-            p = f >= d.thr ? __fdiv_rn(expf(f - d.m), d.s) : 0.0f;
-          }
-          w = d.q_row < 0 ? p : fmaxf(p - qv[ii], 0.0f);
-        }
-        float ratio = __fdiv_rn(w, ee[ii]);
-        if (ratio == 0.0f) ratio = 0.0f;  // -0 and +0 compare equal in torch's argmax
-        key[ii] = argmax_key(ratio, ev[ii]);
-      }
-    }
-#pragma unroll
-    for (int ii = 0; ii < 4; ++ii) {
-      if ((long long)(n * 4 + ii) * S + warp_idx0 < N)          // warp-uniform
-        warp_segment_reduce(key[ii], (int)eb[ii], act[ii], s_best);
-    }
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < a.B; i += kThreads) {
-    unsigned long long kk = s_best[i];
-    if (kk) atomicMax(&a.tail_key[i], kk);
-  }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    unsigned ticket = atomicAdd(a.tail_ticket, 1u);
-    s_last = ticket == gridDim.x - 1;
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  for (int i = threadIdx.x; i < a.B; i += kThreads) {
-    unsigned long long kk = atomicExch(&a.tail_key[i], 0ull);
-    a.tail[i] = (long long)argmax_key_index(kk);
-  }
-  if (threadIdx.x == 0) atomicExch(a.tail_ticket, 0u);
-}
-
 // ---------------------------------------------------------------------------------------- pass 2: accept tail
-// The tail race of the accept path (not race()): the same torch exponential_ grid and the same in-kernel draws
-// as tail_kernel, with the per-element arithmetic cut down.  p = e^(f - m) / s as exp_compensated(f - m) * (1/s)
+// The tail race of the accept path: torch's exponential_ grid of the [B, V] noise with its draws regenerated
+// in-kernel (exactly: Philox blocks, then torch's -log transform), the rest of the per-element arithmetic cut
+// down.  p = e^(f - m) / s as exp_compensated(f - m) * (1/s)
 // and w / E as a fast quotient: both within a few ulp (a few 1e-7 relative), inside the 1e-6 relative p
 // uncertainty the parity rule allows for the race (a winner within that of another candidate is a near tie).
-// The draws themselves (Philox, then torch's -log transform) are exact.  One 32-bit max per warp and element
-// round, the first lane among equals keeps torch's first-index rule.
+// One 32-bit max per warp and element round, the first lane among equals keeps torch's first-index rule.
 struct alignas(16) TailDesc {    // per request, in shared memory (32 B: one float4 + two row pointers)
   float m, inv_s, thr, temp;
   const void* xrow;   // row of x holding p_next
@@ -1127,6 +1048,77 @@ __global__ void __launch_bounds__(kThreads, 4) tail_accept_kernel(Args a) {
   if (threadIdx.x == 0) atomicExch(a.tail_ticket, 0u);
 }
 
+// race() / sample(): w fp32 [B, V] (row b is request b), argmax over v of w / E with torch's exact quotient and
+// its first-index rule; E drawn in-kernel (Philox blocks at torch's counters) on the exponential_ grid, or given.
+__global__ void __launch_bounds__(kThreads) race_kernel(Args a) {
+  __shared__ unsigned long long s_best[kMaxRequests];
+  __shared__ int s_last;
+  for (int i = threadIdx.x; i < a.B; i += kThreads) s_best[i] = 0ull;
+  __syncthreads();
+  const unsigned S = kRngBlock * gridDim.x;
+  const unsigned idx = blockIdx.x * kRngBlock + threadIdx.x;
+  const unsigned N = (unsigned)a.e_numel;
+  const unsigned V = (unsigned)a.V;
+  const float* w = reinterpret_cast<const float*>(a.x);
+  const bool gen = a.E == nullptr;
+  const bool direct = (a.offset_E & 3ull) == 0;     // torch's offsets are multiples of 4
+  curandStatePhilox4_32_10_t st;
+  if (gen && !direct) curand_init(a.seed, idx, a.offset_E, &st);
+  unsigned b = idx / V, v = idx % V;
+  unsigned li0 = idx, warp0 = idx - (threadIdx.x & 31);
+  for (int n = 0; n < a.e_rounds; ++n) {
+    if (warp0 >= N) break;                                     // warp-uniform
+    float x[4], e[4];
+    unsigned bb[4], vv[4];
+#pragma unroll
+    for (int ii = 0; ii < 4; ++ii) {                            // every load of the round first
+      bb[ii] = b;
+      vv[ii] = v;
+      const bool act = li0 + ii * S < N;
+      x[ii] = act ? w[(long long)b * V + v] : 0.0f;
+      e[ii] = act && !gen ? a.E[li0 + ii * S] : 1.0f;
+      tail_step(a, b, v);
+    }
+    if (gen) {
+      const float4 r4 = direct ? philox_uniform4(a.seed, a.offset_E >> 2, idx, n) : curand_uniform4(&st);
+      e[0] = torch_exponential_clamped(r4.x);
+      e[1] = torch_exponential_clamped(r4.y);
+      e[2] = torch_exponential_clamped(r4.z);
+      e[3] = torch_exponential_clamped(r4.w);
+    }
+#pragma unroll
+    for (int ii = 0; ii < 4; ++ii) {
+      if (warp0 + ii * S < N) {                                // warp-uniform
+        const bool act = li0 + ii * S < N;
+        float ratio = __fdiv_rn(x[ii], e[ii]);
+        if (ratio == 0.0f) ratio = 0.0f;                        // -0 and +0 compare equal in torch's argmax
+        warp_segment_reduce(act ? argmax_key(ratio, vv[ii]) : 0ull, (int)bb[ii], act, s_best);
+      }
+    }
+    li0 += 4 * S;
+    warp0 += 4 * S;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < a.B; i += kThreads) {
+    unsigned long long kk = s_best[i];
+    if (kk) atomicMax(&a.tail_key[i], kk);
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned ticket = atomicAdd(a.tail_ticket, 1u);
+    s_last = ticket == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int i = threadIdx.x; i < a.B; i += kThreads) {
+    unsigned long long kk = atomicExch(&a.tail_key[i], 0ull);
+    a.tail[i] = (long long)argmax_key_index(kk);
+  }
+  if (threadIdx.x == 0) atomicExch(a.tail_ticket, 0u);
+}
+
 // ---------------------------------------------------------------------------------------- greedy
 // grid (C, T): per-chunk argmax folded into a per-row 64-bit key; the request's last CTA decides.
 template <typename T>
@@ -1240,7 +1232,7 @@ static int launch_tail(Args& a, const DeviceInfo& info, bool race, cudaStream_t 
   a.e_sq = (unsigned)(S / a.V);
   a.e_sr = (unsigned)(S % a.V);
   if (race) {
-    tail_kernel<T, true><<<a.e_grid, kThreads, 0, stream>>>(a);
+    race_kernel<<<a.e_grid, kThreads, 0, stream>>>(a);
   } else {
     const size_t smem = (sizeof(TailDesc) + sizeof(unsigned long long)) * a.B;
     tail_accept_kernel<T><<<a.e_grid, kThreads, smem, stream>>>(a);
