@@ -401,7 +401,9 @@ def run_kernel(args) -> int:
 
         def fn():
             S.accept_from_logits(logits, q, drafts, samp, None, gen)
-        algorithmic = logits.numel() * 2 + B * V * (4 + 2)
+        # logits once, plus the tail rows' q and logits for the full-row race (a truncating batch races only its
+        # rows' kept tokens: a few KB)
+        algorithmic = logits.numel() * 2 + (B * V * (4 + 2) if args.kernel == "accept" else 0)
     for _ in range(args.warmup):
         fn()
     us = time_events(torch, fn, args.steps)

@@ -75,7 +75,7 @@ int specdec_race(const float* weights, long long R, long long V, const float* E,
 /* specdec_accept without a workspace, for callers that cannot allocate device memory: a plugin whose host owns
  * the device memory budget and forbids cudaMalloc from extensions, or a latency-critical caller that may not
  * call cudaMalloc (which can synchronise the device).  No counterpart in the reference (it allocates through
- * torch).  Scratch is a fixed ~0.7 MB array in the library's device memory (held by every GPU that loads the
+ * torch).  Scratch is a fixed ~2.8 MB array in the library's device memory (held by every GPU that loads the
  * library until exit); T is limited to 1024 verified rows, larger calls fail with status 3.  The first call on
  * a device looks the array's address up (cudaGetSymbolAddress) and should come before any stream capture.
  * Every call clears the array's tickets and keys first; calls that overlap on the GPU race on the array.

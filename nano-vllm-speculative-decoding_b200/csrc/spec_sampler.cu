@@ -38,6 +38,7 @@ constexpr int kStatsCtasPerSm = 4;   // stats_kernel residency its launch bounds
 constexpr int kMaxRequests = 1024;   // B cap (shared-memory tables are sized by it)
 constexpr int kMaxRows = 16384;      // T cap (fixed-offset greedy key table)
 constexpr int kMaxChunks = 64;       // chunks per row in pass 1
+constexpr int kKeptCap = kTopkThreads; // ids of a truncated row's kept tokens recorded for the candidate tail race
 constexpr int kMaxTopK = 1024;       // top_k cap of the in-kernel radix select
 constexpr int kRngBlock = 256;       // torch's block_size_bound for distribution kernels
 
@@ -60,7 +61,7 @@ struct ReqDesc {   // per request: where its tail distribution lives
 // Self-cleaning tables (tickets, argmax keys) sit at fixed offsets at the front, so a workspace zeroed once at
 // allocation stays valid across calls of any shape; per-call scratch follows.
 struct Layout {
-  size_t status, req_ticket, tail_key, tail_ticket, row_key, rows, partial, desc, total;
+  size_t status, req_ticket, tail_key, tail_ticket, row_key, rows, partial, desc, kept_n, kept_ids, total;
 };
 static constexpr Layout layout(int64_t T) {
   Layout L{};
@@ -78,6 +79,8 @@ static constexpr Layout layout(int64_t T) {
   L.rows = take(sizeof(RowStat) * (size_t)(T > 0 ? T : 1));
   L.partial = take(sizeof(float2) * (size_t)(T > 0 ? T : 1) * kMaxChunks);
   L.desc = take(sizeof(ReqDesc) * kMaxRequests);
+  L.kept_n = take(sizeof(int) * (size_t)(T > 0 ? T : 1));
+  L.kept_ids = take(sizeof(int) * (size_t)(T > 0 ? T : 1) * kKeptCap);
   L.total = off;
   return L;
 }
@@ -110,7 +113,9 @@ struct Args {
   long long e_numel;
   unsigned e_sq, e_sr;      // S / V and S % V for S = 256 * e_grid (incremental row tracking)
   // workspace
-  int* status;              // device-side input check: 0 ok, else a kStatus* code (first writer wins)
+  int* status;              // [0] device-side input check: 0 ok, else a kStatus* code (first writer wins);
+                            // [1] set when some request's tail row has no recorded kept set (full-row race)
+  int tail_gate;            // tail_accept_kernel runs only if status[1] is set (truncating calls)
   unsigned* req_ticket;
   unsigned long long* tail_key;
   unsigned* tail_ticket;
@@ -118,6 +123,8 @@ struct Args {
   RowStat* rows;
   float2* partial;
   ReqDesc* desc;
+  int* kept_n;              // [T] tokens a truncated row keeps (ids in kept_ids), or -1: not recorded
+  int* kept_ids;            // [T][kKeptCap]
 };
 
 // ---------------------------------------------------------------------------------------- small helpers
@@ -435,6 +442,8 @@ __device__ void decide_request(const Args& a, int b, int start, int len, bool ne
     const RowStat rs = a.probs_mode ? identity : s_rows[n_acc];
     d.m = rs.m; d.s = rs.s; d.thr = rs.thr; d.temp = temp;
     a.desc[b] = d;
+    // the tail row's kept set (written by its CTA before that CTA's ticket) decides which tail kernel races
+    if (a.truncate && __ldcg(&a.kept_n[d.x_row]) < 0) atomicExch(a.status + 1, 1);
   }
 }
 
@@ -594,6 +603,7 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_stats_kernel(Args a, int
   if (tk <= 0) {
     row_range_ms<T, NT>(row, 0, V, temp, a.vec_ok, m, s);
     block_ms<NT>(m, s);
+    if (threadIdx.x == 0) a.kept_n[t] = -1;
   } else {
     if (tk > kMaxTopK && V > kMaxTopK) {
       if (threadIdx.x == 0) report(a, kStatusBadTopK);
@@ -729,18 +739,28 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_stats_kernel(Args a, int
     thr = s_thr;
     m = cand[0];
     // ---- sum over the kept entries: every one of them (>= the K-th value) is among the collected candidates on
-    // the fast path; the radix path re-reads the row
+    // the fast path, whose ids are also recorded for the candidate tail race; the radix path re-reads the row
     float ls = 0.0f;
     if (fast >= 0) {
+      if (threadIdx.x == 0) s_cnt = 0;
+      __syncthreads();
+      int* ids = a.kept_ids + (long long)t * kKeptCap;
       const int n = top == sel ? fast : (fast + 31) / 32 * 32;
       for (int i = threadIdx.x; i < n; i += NT) {
         const unsigned long long key = sel[i];
         if (key) {
           const float f = key_to_float((unsigned)(key >> 32));
-          if (f >= thr) ls += exp_sum_term(f - m);
+          if (f >= thr) {
+            ls += exp_sum_term(f - m);
+            const int slot = atomicAdd(&s_cnt, 1);
+            if (slot < kKeptCap) ids[slot] = (int)(0xffffffffu - (unsigned)(key & 0xffffffffull));
+          }
         }
       }
+      __syncthreads();
+      if (threadIdx.x == 0) a.kept_n[t] = s_cnt <= kKeptCap ? s_cnt : -1;
     } else {
+      if (threadIdx.x == 0) a.kept_n[t] = -1;
       const int ngroups = (V + 7) / 8;
       for (int g = threadIdx.x; g < ngroups; g += NT) {
         float x[8];
@@ -922,7 +942,9 @@ __global__ void __launch_bounds__(kThreads, 4) tail_accept_kernel(Args a) {
   TailDesc* s_td = reinterpret_cast<TailDesc*>(tail_smem);
   unsigned long long* s_best = reinterpret_cast<unsigned long long*>(tail_smem + sizeof(TailDesc) * a.B);
   __shared__ int s_last;
-  if (*reinterpret_cast<volatile int*>(a.status) != 0) return;  // pass 1 rejected its inputs
+  const volatile int* status = a.status;
+  if (status[0] != 0) return;                   // pass 1 rejected its inputs
+  if (a.tail_gate && status[1] == 0) return;    // every request raced among its kept tokens
   for (int i = threadIdx.x; i < a.B; i += kThreads) {
     s_best[i] = 0ull;
     const ReqDesc d = a.desc[i];
@@ -1119,6 +1141,70 @@ __global__ void __launch_bounds__(kThreads) race_kernel(Args a) {
   if (threadIdx.x == 0) atomicExch(a.tail_ticket, 0u);
 }
 
+// ---------------------------------------------------------------------------------------- pass 2: truncated tail
+// Exp(1) draw li of torch's exponential_ over the [B, V] noise (S = 256 * e_grid threads): call li / S / 4 of
+// thread li % S's Philox stream, lane (li / S) % 4.
+__device__ __forceinline__ float torch_exponential_at(const Args& a, unsigned li) {
+  const unsigned S = kRngBlock * (unsigned)a.e_grid;
+  const unsigned idx = li % S, m = li / S;
+  float4 r;
+  if ((a.offset_E & 3ull) == 0) {
+    r = philox_uniform4(a.seed, a.offset_E >> 2, idx, (int)(m >> 2));
+  } else {
+    curandStatePhilox4_32_10_t st;
+    curand_init(a.seed, idx, a.offset_E + 4ull * (m >> 2), &st);
+    r = curand_uniform4(&st);
+  }
+  const unsigned lane = m & 3u;
+  return torch_exponential_clamped(lane == 0 ? r.x : lane == 1 ? r.y : lane == 2 ? r.z : r.w);
+}
+
+// The tail race of requests whose rows truncate (top-k / top-p): p is zero outside the row's kept tokens, so the
+// residual max(p - q, 0) (or p itself on the bonus row) is too, and the race over the whole vocabulary is
+// decided among the kept tokens (recorded by the stats pass) with their draws regenerated at their positions of
+// the noise: the largest ratio wins (first index among equals); if every kept ratio is 0 the whole row ties at
+// 0 and torch's first index, 0, wins.  Exact arithmetic (IEEE quotients, expf).  One CTA per request.  When some
+// tail row has no recorded kept set (no top-k on its request, or a set above kKeptCap) the decision pass set
+// status[1]: this kernel then does nothing and tail_accept_kernel races every request over its whole row.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) tail_kept_kernel(Args a) {
+  __shared__ unsigned long long s_red[kThreads / 32];
+  const volatile int* status = a.status;
+  if (status[0] != 0 || status[1] != 0) return;   // rejected inputs, or the full-row race runs instead
+  const int b = blockIdx.x;
+  const ReqDesc d = a.desc[b];
+  const T* xrow = reinterpret_cast<const T*>(a.x) + d.x_row * a.V;
+  const float* qrow = d.q_row < 0 ? nullptr : a.q + d.q_row * a.V;
+  const int n = a.kept_n[d.x_row];
+  const int* ids = a.kept_ids + d.x_row * kKeptCap;
+  auto key_of = [&](int v) -> unsigned long long {
+    const float xv = to_f32(xrow[v]);
+    const float f = d.temp == 1.0f ? xv : scale_logit(xv, d.temp);
+    const float p = f >= d.thr ? __fdiv_rn(expf(f - d.m), d.s) : 0.0f;
+    const float w = qrow ? fmaxf(p - qrow[v], 0.0f) : p;
+    const unsigned li = (unsigned)b * (unsigned)a.V + (unsigned)v;
+    const float e = a.E ? a.E[li] : torch_exponential_at(a, li);
+    float ratio = __fdiv_rn(w, e);
+    if (ratio == 0.0f) ratio = 0.0f;                              // -0 and +0 compare equal in torch's argmax
+    return argmax_key(ratio, (unsigned)v);
+  };
+  unsigned long long best = 0ull;
+  for (int i = threadIdx.x; i < n; i += kThreads) {   // n >= 1 here (status[1] clear)
+    const unsigned long long k = key_of(ids[i]);
+    best = k > best ? k : best;
+  }
+  best = warp_max_u64(best);
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long m = 0ull;
+    for (int w = 0; w < kThreads / 32; ++w) m = s_red[w] > m ? s_red[w] : m;
+    // a zero best ratio (or no kept token) leaves the whole row tied at 0: index 0 wins
+    const bool zero = m == 0ull || key_to_float(static_cast<unsigned>(m >> 32)) == 0.0f;
+    a.tail[b] = zero ? 0 : (long long)argmax_key_index(m);
+  }
+}
+
 // ---------------------------------------------------------------------------------------- greedy
 // grid (C, T): per-chunk argmax folded into a per-row 64-bit key; the request's last CTA decides.
 template <typename T>
@@ -1221,6 +1307,8 @@ static void bind_workspace(Args& a, void* ws) {
   a.rows = reinterpret_cast<RowStat*>(base + L.rows);
   a.partial = reinterpret_cast<float2*>(base + L.partial);
   a.desc = reinterpret_cast<ReqDesc*>(base + L.desc);
+  a.kept_n = reinterpret_cast<int*>(base + L.kept_n);
+  a.kept_ids = reinterpret_cast<int*>(base + L.kept_ids);
 }
 
 template <typename T>
@@ -1350,7 +1438,7 @@ int specdec_accept(const void* x, int x_is_probs, int dtype, long long T, long l
   a.vec_ok = aligned16(x) && ((V * (long long)dtype_bytes(dtype)) % 16 == 0);
   bind_workspace(a, workspace);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  SPECDEC_CUDA_TRY(cudaMemsetAsync(a.status, 0, sizeof(int), s));
+  SPECDEC_CUDA_TRY(cudaMemsetAsync(a.status, 0, 2 * sizeof(int), s));
   return SPECDEC_DISPATCH_DTYPE(dtype, [&] {
     if (a.probs_mode) {
       decide_probs_kernel<Tx><<<(unsigned)B, 64, 0, s>>>(a);
@@ -1360,6 +1448,13 @@ int specdec_accept(const void* x, int x_is_probs, int dtype, long long T, long l
       stats_kernel<Tx><<<dim3(a.C, (unsigned)T), kThreads, 0, s>>>(a, 0);
     }
     SPECDEC_LAUNCH_CHECK();
+    if (a.truncate) {   // truncating rows: the race over each request's kept tokens, or (gated) over whole rows
+      a.e_numel = (long long)a.B * a.V;
+      a.e_grid = torch_rng_grid(a.e_numel, info);
+      tail_kept_kernel<Tx><<<(unsigned)B, kThreads, 0, s>>>(a);
+      SPECDEC_LAUNCH_CHECK();
+      a.tail_gate = 1;
+    }
     return launch_tail<Tx>(a, info, false, s);
   });
 }
@@ -1422,7 +1517,7 @@ namespace specdec {
 namespace sampler {
 
 constexpr long long kNoAllocMaxRows = 1024;
-constexpr size_t kNoAllocBytes = layout(kNoAllocMaxRows).total;            // about 0.7 MB
+constexpr size_t kNoAllocBytes = layout(kNoAllocMaxRows).total;            // about 2.8 MB
 constexpr size_t kNoAllocHeaderBytes = layout(1).rows;                     // status, tickets and keys
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];

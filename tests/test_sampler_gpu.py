@@ -114,10 +114,19 @@ def test_in_kernel_noise_reproduces_torch_exponential(S, rows, vocab):
     assert g.get_offset() == g_torch.get_offset()
 
 
-@pytest.mark.parametrize("batch,k,vocab,varlen", [(8, 7, V_FULL, False), (64, 7, V_FULL, True), (5, 3, 1000, True)])
-def test_in_kernel_draws_match_torch_draws(S, batch, k, vocab, varlen):
+MIXED_TOPK = ([0.7, 1.0, 1.3, 0.9] * 16, [20, 0, 128, 600] * 16, [0.8, 1.0, 1.0, 0.95] * 16)
+
+
+@pytest.mark.parametrize("batch,k,vocab,varlen,params", [
+    (8, 7, V_FULL, False, None), (64, 7, V_FULL, True, None), (5, 3, 1000, True, None),
+    (64, 7, V_FULL, True, ([0.7] * 64, [20] * 64, [0.8] * 64)),       # every tail raced among its kept tokens
+    (64, 7, V_FULL, True, MIXED_TOPK),                                 # rows without a kept set: full-row race
+])
+def test_in_kernel_draws_match_torch_draws(S, batch, k, vocab, varlen, params):
     gen = torch.Generator(device=DEV).manual_seed(99)
-    logits, q, drafts, lens, samp = synthetic_round(S, batch, k, vocab, torch.float32, varlen, seed=3)
+    temps, top_k, top_p = params or (None, None, None)
+    logits, q, drafts, lens, samp = synthetic_round(S, batch, k, vocab, torch.float32, varlen, seed=3,
+                                                    temps=temps, top_k=top_k, top_p=top_p)
     g1 = torch.Generator(device=DEV).manual_seed(5)
     g2 = torch.Generator(device=DEV).manual_seed(5)
     a = S.accept_from_logits(logits, q, drafts, samp, lens, g1, draws="kernel")
@@ -152,6 +161,8 @@ def synthetic_round(S, batch, k, vocab, dtype, varlen, seed, temps=None, top_k=N
     (64, 7, torch.bfloat16, False, None),                                   # config 3's accept
     (64, 7, torch.bfloat16, True, None),                                    # config 4's varlen lengths
     (16, 7, torch.bfloat16, True, ([0.7] * 16, [20] * 16, [0.8] * 16)),    # protocol sampling
+    (64, 7, torch.bfloat16, True, ([0.7] * 64, [20] * 64, [0.8] * 64)),    # tails raced among kept tokens
+    (64, 7, torch.bfloat16, True, MIXED_TOPK),                             # top-k off / radix rows mixed in
 ])
 def test_full_vocab_accept_matches_oracle(S, batch, k, dtype, varlen, params):
     temps, top_k, top_p = params or (None, None, None)
