@@ -235,6 +235,51 @@ __device__ void block_top_sorted(unsigned long long* keys, int n, int C, unsigne
   __syncthreads();
 }
 
+// The C-th largest of the block's NT thread maxima (ties by thread index), returned to every thread.  buf holds
+// NT keys of scratch; it is free again when this returns.
+template <int NT>
+__device__ float block_cth_thread_max(float mx, int C, unsigned long long* buf) {
+  __shared__ float s_bound;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const unsigned long long mine = (static_cast<unsigned long long>(ordered_key(mx)) << 32) | (0xffffffffu - threadIdx.x);
+  const unsigned long long sorted = warp_sort_desc_u64(mine, lane);
+  buf[threadIdx.x] = sorted;
+  __syncthreads();
+  int r = lane;
+  for (int q = 0; q < NT / 32; ++q)
+    if (q != warp) r += count_larger32(buf + q * 32, sorted);
+  if (r == C - 1) s_bound = key_to_float(static_cast<unsigned>(sorted >> 32));
+  __syncthreads();
+  return s_bound;
+}
+
+// Collection bound: the C-th thread maximum, widened by slack_rel when that is positive.
+__device__ __forceinline__ float widened_bound(float b, float slack_rel) {
+  return slack_rel > 0.0f ? b - fabsf(b) * slack_rel - 1e-30f : b;
+}
+
+// Last phase of a thread-maxima selection: the top C of the *s_count collected keys in buf, in order.
+template <int NT>
+__device__ int finish_thread_max_selection(int C, unsigned long long* buf, int cap, int* s_count,
+                                           unsigned long long** top) {
+  __syncthreads();
+  const int count = *s_count;
+  if (count > cap) return -1;
+  const int padded = (count + 31) / 32 * 32;
+  if (count <= 1024 && padded + C <= cap) {
+    *top = buf + cap - C;
+    block_top_sorted<NT>(buf, count, C, *top);
+    return count;
+  }
+  int P = 1;
+  while (P < count) P <<= 1;
+  for (int i = count + threadIdx.x; i < P; i += NT) buf[i] = 0ull;
+  __syncthreads();
+  block_sort_desc_u64(buf, P);
+  *top = buf;
+  return count;
+}
+
 // Top-C selection by a thread-maxima bound (whole block of NT threads; C <= NT).  load(g, x) fills the 8 values
 // of element group g (missing ones -inf) and returns how many exist.  Every thread's maximum over its groups is
 // an element; the C-th largest of those NT maxima is therefore <= the row's C-th largest value, so collecting
@@ -245,12 +290,11 @@ __device__ void block_top_sorted(unsigned long long* keys, int n, int C, unsigne
 // caller falls back to an exact radix select).  On return buf[0..count) still holds every collected key (in some
 // order, padded with 0 keys to a multiple of 32) and *top points at the top C in descending order: inside buf
 // past the collected keys, or at buf itself when the count exceeded 1024 (then all of buf[0..count) is sorted).
-// tmax is NT floats of scratch.  Both orderings (the C-th thread maximum, the top C of up to 1024 collected
-// keys) are warp sorts plus binary-search ranks: a few block barriers.
+// Both orderings (the C-th thread maximum, the top C of up to 1024 collected keys) are warp sorts plus
+// binary-search ranks: a few block barriers.
 template <int NT, int UNROLL, typename Load>
-__device__ int select_by_thread_max(int ngroups, int C, Load load, float* tmax, unsigned long long* buf, int cap,
-                                    int* s_count, unsigned long long** top, float slack_rel = 0.0f) {
-  __shared__ float s_bound;
+__device__ int select_by_thread_max(int ngroups, int C, Load load, unsigned long long* buf, int cap, int* s_count,
+                                    unsigned long long** top, float slack_rel = 0.0f) {
   float mx = -INFINITY;
   // UNROLL groups per thread in flight per iteration (their loads are independent)
   for (int g0 = threadIdx.x; g0 < ngroups; g0 += UNROLL * NT) {
@@ -268,19 +312,7 @@ __device__ int select_by_thread_max(int ngroups, int C, Load load, float* tmax, 
         if (e < n[u]) mx = fmaxf(mx, x[u][e]);
   }
   if (threadIdx.x == 0) *s_count = 0;
-  {  // the C-th largest thread maximum (ties by thread index): warp-sorted keys in buf, ranks by binary search
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const unsigned long long mine = (static_cast<unsigned long long>(ordered_key(mx)) << 32) | (0xffffffffu - threadIdx.x);
-    const unsigned long long sorted = warp_sort_desc_u64(mine, lane);
-    buf[threadIdx.x] = sorted;
-    __syncthreads();
-    int r = lane;
-    for (int q = 0; q < NT / 32; ++q)
-      if (q != warp) r += count_larger32(buf + q * 32, sorted);
-    if (r == C - 1) s_bound = key_to_float(static_cast<unsigned>(sorted >> 32));
-    __syncthreads();
-  }
-  const float bound = slack_rel > 0.0f ? s_bound - fabsf(s_bound) * slack_rel - 1e-30f : s_bound;
+  const float bound = widened_bound(block_cth_thread_max<NT>(mx, C, buf), slack_rel);
   for (int g0 = threadIdx.x; g0 < ngroups; g0 += UNROLL * NT) {
     float x[UNROLL][8];
     int n[UNROLL];
@@ -302,22 +334,78 @@ __device__ int select_by_thread_max(int ngroups, int C, Load load, float* tmax, 
       }
     }
   }
-  __syncthreads();
-  const int count = *s_count;
-  if (count > cap) return -1;
-  const int padded = (count + 31) / 32 * 32;
-  if (count <= 1024 && padded + C <= cap) {
-    *top = buf + cap - C;
-    block_top_sorted<NT>(buf, count, C, *top);
-    return count;
+  return finish_thread_max_selection<NT>(C, buf, cap, s_count, top);
+}
+
+// Packed 16-bit pairs (bf16 or f16) and their -inf.
+template <typename H2> struct Packed16;
+template <> struct Packed16<__nv_bfloat162> {
+  static constexpr unsigned kNegInf = 0xff80ff80u;
+  __device__ static __forceinline__ void unpack(const uint4& v, float (&out)[8]) { unpack16_bf16(v, out); }
+};
+template <> struct Packed16<__half2> {
+  static constexpr unsigned kNegInf = 0xfc00fc00u;
+  __device__ static __forceinline__ void unpack(const uint4& v, float (&out)[8]) { unpack16_f16(v, out); }
+};
+template <typename H2>
+__device__ __forceinline__ H2 as_h2(unsigned u) {
+  H2 h;
+  memcpy(&h, &u, sizeof(h));
+  return h;
+}
+template <typename H2>
+__device__ __forceinline__ H2 group_max_h2(const uint4& w) {
+  return __hmax2(__hmax2(as_h2<H2>(w.x), as_h2<H2>(w.y)), __hmax2(as_h2<H2>(w.z), as_h2<H2>(w.w)));
+}
+
+// select_by_thread_max over a row of 16-bit values stored as ngroups 16-byte groups of 8 (16-byte aligned, no
+// ragged end), with the same result: thread maxima and the per-group test run on packed pairs (__hmax2 drops NaN
+// as fmaxf does, and the maximum of 16-bit values is exact), so each 16-byte group costs one load and a few
+// packed max instructions; only a group whose maximum reaches the bound is unpacked and its elements collected.
+template <int NT, int UNROLL, typename H2>
+__device__ int select_by_thread_max_x16(const uint4* groups, int ngroups, int C, unsigned long long* buf, int cap,
+                                        int* s_count, unsigned long long** top, float slack_rel = 0.0f) {
+  const unsigned neg = Packed16<H2>::kNegInf;
+  H2 mx2 = as_h2<H2>(neg);
+  for (int g0 = threadIdx.x; g0 < ngroups; g0 += UNROLL * NT) {
+    uint4 w[UNROLL];
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      const int g = g0 + u * NT;
+      w[u] = g < ngroups ? __ldg(groups + g) : make_uint4(neg, neg, neg, neg);
+    }
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) mx2 = __hmax2(mx2, group_max_h2<H2>(w[u]));
   }
-  int P = 1;
-  while (P < count) P <<= 1;
-  for (int i = count + threadIdx.x; i < P; i += NT) buf[i] = 0ull;
-  __syncthreads();
-  block_sort_desc_u64(buf, P);
-  *top = buf;
-  return count;
+  const float mx = fmaxf(__low2float(mx2), __high2float(mx2));
+  if (threadIdx.x == 0) *s_count = 0;
+  const float bound = widened_bound(block_cth_thread_max<NT>(mx, C, buf), slack_rel);
+  for (int g0 = threadIdx.x; g0 < ngroups; g0 += UNROLL * NT) {
+    uint4 w[UNROLL];
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      const int g = g0 + u * NT;
+      w[u] = g < ngroups ? __ldg(groups + g) : make_uint4(neg, neg, neg, neg);
+    }
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      const H2 m2 = group_max_h2<H2>(w[u]);
+      if (fmaxf(__low2float(m2), __high2float(m2)) >= bound) {   // rare: a candidate in this group
+        const int g = g0 + u * NT;
+        float x[8];
+        Packed16<H2>::unpack(w[u], x);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          if (x[e] >= bound) {
+            const int slot = atomicAdd(s_count, 1);
+            if (slot < cap)
+              buf[slot] = (static_cast<unsigned long long>(ordered_key(x[e])) << 32) | (0xffffffffu - (unsigned)(g * 8 + e));
+          }
+        }
+      }
+    }
+  }
+  return finish_thread_max_selection<NT>(C, buf, cap, s_count, top);
 }
 
 // Device properties the library needs (cached per device on first use).

@@ -131,7 +131,6 @@ __global__ void __launch_bounds__(kThreads) markov_step_kernel(const Args a) {
   __shared__ unsigned long long sel[kSelCap];            // fast-path candidates, the pieces' keys when merging;
   unsigned* hist = reinterpret_cast<unsigned*>(sel);      // the radix fallback's histogram (4096 bins) reuses it
   __shared__ unsigned long long cand[kMaxCand];
-  __shared__ float tmax[kThreads];
   __shared__ int s_sel;
   __shared__ float cprob[kMaxCand];
   __shared__ int s_digit, s_above, s_cnt, s_prev, s_last;
@@ -179,7 +178,7 @@ __global__ void __launch_bounds__(kThreads) markov_step_kernel(const Args a) {
     int fast = -1;
     if (C <= kThreads) {
       unsigned long long* top = nullptr;
-      fast = select_by_thread_max<kThreads, 1>(ngroups, C, load, tmax, sel, kSelCap, &s_sel, &top);
+      fast = select_by_thread_max<kThreads, 1>(ngroups, C, load, sel, kSelCap, &s_sel, &top);
       if (fast >= 0)
         for (int i = threadIdx.x; i < C; i += kThreads) cand[i] = top[i];
     }

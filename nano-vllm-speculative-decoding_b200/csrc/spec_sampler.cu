@@ -577,7 +577,6 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_stats_kernel(Args a, int
   __shared__ int s_start[kMaxRequests + 1];
   __shared__ unsigned long long sel[4096];                // fast-path candidates; the radix fallback's histogram
   unsigned* hist = reinterpret_cast<unsigned*>(sel);      // (4096 bins) reuses the same bytes
-  __shared__ float tmax[kTopkThreads];
   __shared__ int s_sel;
   __shared__ float cand[kMaxTopK];
   __shared__ int s_digit, s_above, s_cnt, s_last;
@@ -616,9 +615,17 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_stats_kernel(Args a, int
     int fast = -1;
     unsigned long long* top = nullptr;
     if (K <= NT) {
-      fast = select_by_thread_max<NT, 2>(
-          (V + 7) / 8, K, [&](int g, float (&x)[8]) { return load_group_scaled(row, g, V, a.vec_ok, 1.0f, x); },
-          tmax, sel, 4096, &s_sel, &top, temp == 1.0f ? 0.0f : 2.384185791015625e-07f);
+      const float slack = temp == 1.0f ? 0.0f : 2.384185791015625e-07f;
+      if constexpr (sizeof(T) == 2) {
+        using H2 = typename std::conditional<std::is_same<T, __half>::value, __half2, __nv_bfloat162>::type;
+        if (a.vec_ok)   // 16-byte groups, no ragged end: packed maxima
+          fast = select_by_thread_max_x16<NT, 4, H2>(reinterpret_cast<const uint4*>(row), V / 8, K, sel, 4096,
+                                                     &s_sel, &top, slack);
+      }
+      if (fast < 0 && (sizeof(T) == 4 || !a.vec_ok))
+        fast = select_by_thread_max<NT, 2>(
+            (V + 7) / 8, K, [&](int g, float (&x)[8]) { return load_group_scaled(row, g, V, a.vec_ok, 1.0f, x); },
+            sel, 4096, &s_sel, &top, slack);
       if (fast >= 0 && temp != 1.0f) {
         const int n = top == sel ? fast : (fast + 31) / 32 * 32;
         for (int i = threadIdx.x; i < n; i += NT) {
