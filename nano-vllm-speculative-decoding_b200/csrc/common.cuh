@@ -358,12 +358,13 @@ __device__ __forceinline__ H2 group_max_h2(const uint4& w) {
   return __hmax2(__hmax2(as_h2<H2>(w.x), as_h2<H2>(w.y)), __hmax2(as_h2<H2>(w.z), as_h2<H2>(w.w)));
 }
 
-// select_by_thread_max over a row of 16-bit values stored as ngroups 16-byte groups of 8 (16-byte aligned, no
-// ragged end), with the same result: thread maxima and the per-group test run on packed pairs (__hmax2 drops NaN
-// as fmaxf does, and the maximum of 16-bit values is exact), so each 16-byte group costs one load and a few
-// packed max instructions; only a group whose maximum reaches the bound is unpacked and its elements collected.
-template <int NT, int UNROLL, typename H2>
-__device__ int select_by_thread_max_x16(const uint4* groups, int ngroups, int C, unsigned long long* buf, int cap,
+// select_by_thread_max over 16-bit values (bf16 or f16) delivered as packed 16-byte groups of 8: load(g) returns
+// group g (0 <= g < ngroups, every group full).  Same result as select_by_thread_max on the unpacked values:
+// thread maxima and the per-group test run on packed pairs (__hmax2 drops NaN as fmaxf does, and the maximum of
+// 16-bit values is exact), so a group costs its loads and a few packed instructions; only a group whose maximum
+// reaches the bound is unpacked and its elements collected.
+template <int NT, int UNROLL, typename H2, typename LoadPacked>
+__device__ int select_by_thread_max_x16(int ngroups, int C, LoadPacked load, unsigned long long* buf, int cap,
                                         int* s_count, unsigned long long** top, float slack_rel = 0.0f) {
   const unsigned neg = Packed16<H2>::kNegInf;
   H2 mx2 = as_h2<H2>(neg);
@@ -372,7 +373,7 @@ __device__ int select_by_thread_max_x16(const uint4* groups, int ngroups, int C,
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) {
       const int g = g0 + u * NT;
-      w[u] = g < ngroups ? __ldg(groups + g) : make_uint4(neg, neg, neg, neg);
+      w[u] = g < ngroups ? load(g) : make_uint4(neg, neg, neg, neg);
     }
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) mx2 = __hmax2(mx2, group_max_h2<H2>(w[u]));
@@ -385,7 +386,7 @@ __device__ int select_by_thread_max_x16(const uint4* groups, int ngroups, int C,
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) {
       const int g = g0 + u * NT;
-      w[u] = g < ngroups ? __ldg(groups + g) : make_uint4(neg, neg, neg, neg);
+      w[u] = g < ngroups ? load(g) : make_uint4(neg, neg, neg, neg);
     }
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) {

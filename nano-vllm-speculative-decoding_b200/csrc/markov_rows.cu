@@ -95,6 +95,17 @@ __device__ __forceinline__ int load_group(const Args& a, long long lrow, long lo
   return n;
 }
 
+// Eight bf16 sums, pairwise (one rounding each).
+__device__ __forceinline__ uint4 bf16x8_add(const uint4& x, const uint4& y) {
+  auto add = [](unsigned a, unsigned b) {
+    const __nv_bfloat162 r = __hadd2(as_h2<__nv_bfloat162>(a), as_h2<__nv_bfloat162>(b));
+    unsigned u;
+    memcpy(&u, &r, sizeof(u));
+    return u;
+  };
+  return make_uint4(add(x.x, y.x), add(x.y, y.y), add(x.z, y.z), add(x.w, y.w));
+}
+
 // 1-based rank `rank` among the counted elements: digit d with above(d) < rank <= above(d) + hist[d].
 __device__ void pick_digit(const unsigned* hist, int nbins, int rank, int* s_digit, int* s_above) {
   __shared__ int warp_tot[kWarps];
@@ -178,7 +189,18 @@ __global__ void __launch_bounds__(kThreads) markov_step_kernel(const Args a) {
     int fast = -1;
     if (C <= kThreads) {
       unsigned long long* top = nullptr;
-      fast = select_by_thread_max<kThreads, 1>(ngroups, C, load, sel, kSelCap, &s_sel, &top);
+      if (a.vec) {
+        // bf16 logits and bias: the biased row as packed pairs.  The bf16x2 add rounds the exact sum once, which
+        // is what torch's bf16 add gives (its fp32 sum of two bf16 values is exact, or off only far below half
+        // a bf16 ulp of the larger term).
+        const uint4* lg = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.logits) + lrow) + g_lo;
+        const uint4* bg = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.bias) + brow) + g_lo;
+        fast = select_by_thread_max_x16<kThreads, 2, __nv_bfloat162>(
+            ngroups, C, [&](int g) { return bf16x8_add(__ldg(lg + g), __ldg(bg + g)); }, sel, kSelCap, &s_sel,
+            &top);
+      } else {
+        fast = select_by_thread_max<kThreads, 1>(ngroups, C, load, sel, kSelCap, &s_sel, &top);
+      }
       if (fast >= 0)
         for (int i = threadIdx.x; i < C; i += kThreads) cand[i] = top[i];
     }

@@ -619,8 +619,9 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_stats_kernel(Args a, int
       if constexpr (sizeof(T) == 2) {
         using H2 = typename std::conditional<std::is_same<T, __half>::value, __half2, __nv_bfloat162>::type;
         if (a.vec_ok)   // 16-byte groups, no ragged end: packed maxima
-          fast = select_by_thread_max_x16<NT, 4, H2>(reinterpret_cast<const uint4*>(row), V / 8, K, sel, 4096,
-                                                     &s_sel, &top, slack);
+          fast = select_by_thread_max_x16<NT, 4, H2>(
+              V / 8, K, [&](int g) { return __ldg(reinterpret_cast<const uint4*>(row) + g); }, sel, 4096, &s_sel,
+              &top, slack);
       }
       if (fast < 0 && (sizeof(T) == 4 || !a.vec_ok))
         fast = select_by_thread_max<NT, 2>(
