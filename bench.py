@@ -168,7 +168,8 @@ def time_events(torch, fn, iters: int) -> float:
 
 def attention_roofline(torch, w, hbm_peak: float) -> dict:
     """The dominant kernel of this package in a round: paged verify attention, 36 launches per round.  Timed
-    live over every layer's cache (each launch reads a different 262 MB of K/V, beyond L2)."""
+    live over every layer's cache (each launch reads a different 262 MB of K/V, beyond L2), as one CUDA graph of
+    the 36 launches replayed (like the round's own graph)."""
     from nanovllm_b200 import attention
     t = w.target
     num_tokens = w.q.shape[0] * (K_DRAFTS + 1)
@@ -187,8 +188,13 @@ def attention_roofline(torch, w, hbm_peak: float) -> dict:
         for layer in range(s.layers):
             one_layer(layer)
 
-    all_layers()
-    per_launch_us = time_events(torch, all_layers, 3) / s.layers
+    all_layers()                                   # warm-up (allocates the split workspace)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()                 # the 36 launches replayed as in the round: no host gaps
+    with torch.cuda.graph(graph):
+        all_layers()
+    graph.replay()
+    per_launch_us = time_events(torch, graph.replay, 5) / s.layers
     keys = sum(n + K_DRAFTS for n in w.lengths)       # row r verifies positions len-1 .. len+6
     kv_bytes = keys * s.kv_heads * s.head_dim * 2 * 2
     qo_bytes = 2 * num_tokens * s.heads * s.head_dim * 2

@@ -196,18 +196,15 @@ __device__ __forceinline__ unsigned long long warp_sort_desc_u64(unsigned long l
   return key;
 }
 
-// Number of keys in a descending list of 32 that are larger than key.
+// Number of keys in a descending list of 32 that are larger than key: branch-free binary lifting (five steps
+// find min(count, 31), a sixth adds the 32nd), so independent counts can run interleaved.
 __device__ __forceinline__ int count_larger32(const unsigned long long* list, unsigned long long key) {
-  int lo = 0, hi = 32;             // the answer is in [0, 32]: six halvings
+  int pos = 0;
 #pragma unroll
-  for (int s = 0; s < 6; ++s) {
-    if (lo < hi) {
-      const int mid = (lo + hi) >> 1;
-      if (list[mid] > key) lo = mid + 1; else hi = mid;
-    }
-  }
-  return lo;
+  for (int step = 16; step >= 1; step >>= 1) pos += list[pos + step - 1] > key ? step : 0;
+  return pos + (list[pos] > key ? 1 : 0);
 }
+
 
 // The top C of n distinct nonzero keys keys[0..n), descending, into out[0..C) (C <= n): every 32-key chunk is
 // sorted by one warp (shuffles), then each key's rank in the
@@ -226,10 +223,12 @@ __device__ void block_top_sorted(unsigned long long* keys, int n, int C, unsigne
   for (int t = threadIdx.x; t < nchunks * 32; t += NT) {
     const unsigned long long key = keys[t];
     if (key == 0ull) continue;                       // padding
-    const int c = t >> 5;
-    int r = t & 31;
-    for (int q = 0; q < nchunks; ++q)
-      if (q != c) r += count_larger32(keys + q * 32, key);
+    int r = 0;                                       // own chunk included: it counts t & 31 (keys are distinct)
+    for (int q0 = 0; q0 < nchunks; q0 += 4) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        r += q0 + u < nchunks ? count_larger32(keys + (q0 + u) * 32, key) : 0;
+    }
     if (r < C) out[r] = key;
   }
   __syncthreads();
@@ -245,9 +244,10 @@ __device__ float block_cth_thread_max(float mx, int C, unsigned long long* buf) 
   const unsigned long long sorted = warp_sort_desc_u64(mine, lane);
   buf[threadIdx.x] = sorted;
   __syncthreads();
-  int r = lane;
-  for (int q = 0; q < NT / 32; ++q)
-    if (q != warp) r += count_larger32(buf + q * 32, sorted);
+  int r = 0;                         // own list included: it counts lane (keys are distinct)
+#pragma unroll
+  for (int q = 0; q < NT / 32; ++q) r += count_larger32(buf + q * 32, sorted);
+  (void)warp;
   if (r == C - 1) s_bound = key_to_float(static_cast<unsigned>(sorted >> 32));
   __syncthreads();
   return s_bound;

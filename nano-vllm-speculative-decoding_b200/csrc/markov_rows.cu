@@ -138,7 +138,7 @@ __device__ void pick_digit(const unsigned* hist, int nbins, int rank, int* s_dig
   __syncthreads();
 }
 
-__global__ void __launch_bounds__(kThreads) markov_step_kernel(const Args a) {
+__global__ void __launch_bounds__(kThreads, 2) markov_step_kernel(const Args a) {
   __shared__ unsigned long long sel[kSelCap];            // fast-path candidates, the pieces' keys when merging;
   unsigned* hist = reinterpret_cast<unsigned*>(sel);      // the radix fallback's histogram (4096 bins) reuses it
   __shared__ unsigned long long cand[kMaxCand];
@@ -195,7 +195,7 @@ __global__ void __launch_bounds__(kThreads) markov_step_kernel(const Args a) {
         // a bf16 ulp of the larger term).
         const uint4* lg = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.logits) + lrow) + g_lo;
         const uint4* bg = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.bias) + brow) + g_lo;
-        fast = select_by_thread_max_x16<kThreads, 2, __nv_bfloat162>(
+        fast = select_by_thread_max_x16<kThreads, 4, __nv_bfloat162>(
             ngroups, C, [&](int g) { return bf16x8_add(__ldg(lg + g), __ldg(bg + g)); }, sel, kSelCap, &s_sel,
             &top);
       } else {

@@ -558,49 +558,70 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&S.o_free[n & 1]);
       const float4 s4 = *reinterpret_cast<const float4*>(S.red_sum[col]);
       float l_lane = (s4.x + s4.y) + (s4.z + s4.w);
-      // ---- an item split over CTAs c_lo..c_hi: every piece is published; the last to arrive merges them
+      // ---- an item split over CTAs c_lo..c_hi: every piece but the last to arrive is published; the last merges
+      // them in CTA order (its own from registers when it holds the first piece and finds every other piece already
+      // published; from its published copy otherwise), so the output does not depend on which CTA arrived last
       const long long A = wk.A, B = wk.A + wk.r.nt;
       const long long c_lo = ceil_div((A + 1) * Ge, T) - 1, c_hi = ceil_div(B * Ge, T) - 1;
       if (c_lo != c_hi) {
-        float* mine = a.partial + (2LL * c + (x_begin < A ? 1 : 0)) * kPartialFloats;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) __stcg(mine + (cb + j) * kHeadDim + row, o[j]);
-        if (w == 0 && lane < 16) {
-          __stcg(mine + kCols * kHeadDim + col, m_lane);
-          __stcg(mine + kCols * kHeadDim + kCols + col, l_lane);
-        }
-        __threadfence();
-        named_barrier(3, 256);               // both groups published
+        int* counter = a.counters + (long long)wk.b * a.Hkv + wk.h;
         if (threadIdx.x == 128) {
-          int* counter = a.counters + (long long)wk.b * a.Hkv + wk.h;
-          const int last = atomicAdd(counter, 1) == (int)(c_hi - c_lo);
-          if (last) atomicExch(counter, 0);
-          S.last_piece = last;
+          // the first piece arriving last (the usual case: it ends this CTA's share) skips its own publication
+          S.last_piece = (c == c_lo && ld_acquire_gpu(counter) == (int)(c_hi - c_lo)) ? 2 : 0;
         }
         named_barrier(3, 256);
-        if (!S.last_piece) continue;        // rewritten only after every thread passes the next publish barrier
-        __threadfence();
-        // merged in CTA order from the published pieces (this CTA's own included), so the result does not depend
-        // on which CTA arrived last; lane j merges column cb + (j & 15)'s maximum and sum
-        float m_acc = kNegBig;
-        l_lane = 0.0f;
+        const bool own_in_registers = S.last_piece == 2;
+        if (!own_in_registers) {
+          float* mine = a.partial + (2LL * c + (x_begin < A ? 1 : 0)) * kPartialFloats;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) o[j] = 0.0f;
-        for (long long cc = c_lo; cc <= c_hi; ++cc) {
-          const long long s_cc = T * cc / Ge;
-          const float* piece = a.partial + (2 * cc + (s_cc < A ? 1 : 0)) * kPartialFloats;
-          const float mp = __ldcg(piece + kCols * kHeadDim + col);
-          const float lp = __ldcg(piece + kCols * kHeadDim + kCols + col);
+          for (int j = 0; j < 16; ++j) __stcg(mine + (cb + j) * kHeadDim + row, o[j]);
+          if (w == 0 && lane < 16) {
+            __stcg(mine + kCols * kHeadDim + col, m_lane);
+            __stcg(mine + kCols * kHeadDim + kCols + col, l_lane);
+          }
+          __threadfence();
+          named_barrier(3, 256);             // both groups published
+          if (threadIdx.x == 128) {
+            const int last = atomicAdd(counter, 1) == (int)(c_hi - c_lo);
+            if (last) atomicExch(counter, 0);
+            S.last_piece = last;
+          }
+          named_barrier(3, 256);
+          // S.last_piece is next written at the next split item's epilogue, which thread 128 reaches only after
+          // every softmax warp has handed over P for that item's tiles (so after every thread's read here)
+          if (!S.last_piece) continue;
+        } else if (threadIdx.x == 128) {
+          atomicExch(counter, 0);            // every other piece has arrived: nobody else touches it
+        }
+        __threadfence();
+        // lane j merges column cb + (j & 15)'s maximum and sum; one merge step per piece, the same arithmetic for
+        // a piece from registers or from memory
+        float m_acc = kNegBig, l_acc = 0.0f;
+        const float m_own = m_lane, l_own = l_lane;
+        auto merge = [&](float mp, float lp, const float* op) {
           const float mn = fmaxf(m_acc, mp);
           const float sa = ex2_approx(m_acc - mn), sb = ex2_approx(mp - mn);
           m_acc = mn;
-          l_lane = l_lane * sa + lp * sb;
+          l_acc = __fmaf_rn(lp, sb, __fmul_rn(l_acc, sa));
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const float op = __ldcg(piece + (cb + j) * kHeadDim + row);
-            o[j] = o[j] * __shfl_sync(0xffffffffu, sa, j) + op * __shfl_sync(0xffffffffu, sb, j);
-          }
+          for (int j = 0; j < 16; ++j)
+            o[j] = __fmaf_rn(op ? __ldcg(op + (cb + j) * kHeadDim + row) : o[j], __shfl_sync(0xffffffffu, sb, j),
+                             __fmul_rn(op ? o[j] : 0.0f, __shfl_sync(0xffffffffu, sa, j)));
+        };
+        long long cc = c_lo;
+        if (own_in_registers) {
+          merge(m_own, l_own, nullptr);      // piece c_lo = this CTA's
+          ++cc;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) o[j] = 0.0f;
         }
+        for (; cc <= c_hi; ++cc) {
+          const long long s_cc = T * cc / Ge;
+          const float* piece = a.partial + (2 * cc + (s_cc < A ? 1 : 0)) * kPartialFloats;
+          merge(__ldcg(piece + kCols * kHeadDim + col), __ldcg(piece + kCols * kHeadDim + kCols + col), piece);
+        }
+        l_lane = l_acc;
       }
       // ---- O^T / l, bf16, to out[token, head, dim]
       const float inv_lane = l_lane > 0.0f ? 1.0f / l_lane : 0.0f;
