@@ -200,7 +200,7 @@ def attention_roofline(torch, w, hbm_peak: float) -> dict:
     qo_bytes = 2 * num_tokens * s.heads * s.head_dim * 2
     algorithmic = kv_bytes + qo_bytes
     achieved = algorithmic / (per_launch_us * 1e-6) / 1e9
-    # DRAM traffic from one ncu capture of the config-2 launch (148.17 MB read + written for 135.32 MB
+    # DRAM traffic from one ncu capture of the config-2 launch (148.27 MB read + written for 135.32 MB
     # algorithmic), scaled to this launch by its algorithmic bytes (traffic grows with the keys)
     traffic = round(algorithmic * CFG2_TRAFFIC_BYTES / CFG2_ALGORITHMIC_BYTES)
     return {"kernel": "specdec::attention::verify_attention_kernel<4>", "bound": "hbm",
