@@ -75,6 +75,7 @@ def test_target_qk_norm_rope_store():
     cos_sin = rope_cache(128, 4096, 1000000.0, DEV)
     positions = torch.randint(0, 4096, (T,), device=DEV, generator=g)
     slots = torch.randperm(4 * 256, device=DEV, generator=g)[:T].to(torch.int32)
+    slots[::7] = -1                     # padding rows: q still computed, k / v not stored
     k_cache = torch.zeros(4, 256, hkv, 128, dtype=torch.bfloat16, device=DEV)
     v_cache = torch.zeros_like(k_cache)
     q = qk_norm_rope_store(qkv, H, hkv, q_norm, k_norm, cos_sin, positions, slots, k_cache, v_cache, 1e-6)
@@ -104,7 +105,8 @@ def test_rmsnorm_and_silu():
     assert np.array_equal(res.float().cpu().numpy(), s)
     close_bf16(out2.float().cpu().numpy(), OC.rmsnorm(x.float().cpu().numpy() + r.float().cpu().numpy(),
                                                       w.float().cpu().numpy(), 1e-6))
-    gu = torch.randn(37, 2 * 1024, device=DEV, generator=g).bfloat16()
-    y = silu_and_mul(gu).float().cpu().numpy()
-    a, b = gu.float().cpu().numpy()[:, :1024], gu.float().cpu().numpy()[:, 1024:]
-    close_bf16(y, OC.bf16(a / (1 + np.exp(-a)) * b))
+    for rows, inter in [(37, 1024), (512, 12288)]:     # the second: several grid-stride rounds per thread
+        gu = torch.randn(rows, 2 * inter, device=DEV, generator=g).bfloat16()
+        y = silu_and_mul(gu).float().cpu().numpy()
+        a, b = gu.float().cpu().numpy()[:, :inter], gu.float().cpu().numpy()[:, inter:]
+        close_bf16(y, OC.bf16(a / (1 + np.exp(-a)) * b))
