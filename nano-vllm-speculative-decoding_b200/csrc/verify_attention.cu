@@ -46,6 +46,7 @@ using namespace sm100;
 
 constexpr int kHeadDim = 128;
 constexpr int kKeysPerTile = 128;
+constexpr int kSubKeys = 32;                              // an item's last tile loads in 32-key sub-boxes
 constexpr int kCols = 32;              // packed query columns (group x positions)
 constexpr int kStages = 3;             // K ring and V ring depth
 constexpr int kThreads = 384;            // warps 0-3: TMA (Q, K), MMA, prologue, TMA (V); 4-11: softmax
@@ -222,7 +223,8 @@ __device__ __forceinline__ long long ceil_div(long long x, long long y) { return
 template <int G>
 __global__ void __launch_bounds__(kThreads, 1)
     verify_attention_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
-                            const __grid_constant__ CUtensorMap vmap, const Args a) {
+                            const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap kmap32,
+                            const __grid_constant__ CUtensorMap vmap32, const Args a) {
   constexpr int QMAX = kCols / G;     // query positions per row this build packs
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -260,6 +262,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tensormap(&qmap);
     prefetch_tensormap(&kmap);
     prefetch_tensormap(&vmap);
+    prefetch_tensormap(&kmap32);
+    prefetch_tensormap(&vmap32);
   }
   if (warp == 2) {
     // ---- this CTA's share: the tile sequence split evenly over min(grid, tiles) CTAs, then the row holding
@@ -326,6 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint64_t* empty = kq ? S.k_empty : S.v_empty;
       unsigned char* ring = kq ? sK : sV;
       const CUtensorMap* map = kq ? &kmap : &vmap;
+      const CUtensorMap* map32 = kq ? &kmap32 : &vmap32;
       Walk<QMAX> wk;
       wk.start(a, S);
       bool ok = true;
@@ -350,9 +355,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], kTileBytes);
-          tma_load_3d(ring + stage * kTileBytes, map, 0, wk.h, slot, &full[stage]);
-          tma_load_3d(ring + stage * kTileBytes + kHalfTileBytes, map, 64, wk.h, slot, &full[stage]);
+          // the item's last tile: only the 32-key sub-boxes holding context keys (the rest of the stage keeps
+          // stale rows, which the softmax masks in S and zeroes in V)
+          const int subs = t == wk.r.nt - 1 ? (wk.r.L - key0 + kSubKeys - 1) / kSubKeys : kKeysPerTile / kSubKeys;
+          unsigned char* dst = ring + stage * kTileBytes;
+          if (subs == kKeysPerTile / kSubKeys) {
+            mbar_arrive_expect_tx(&full[stage], kTileBytes);
+            tma_load_3d(dst, map, 0, wk.h, slot, &full[stage]);
+            tma_load_3d(dst + kHalfTileBytes, map, 64, wk.h, slot, &full[stage]);
+          } else {
+            mbar_arrive_expect_tx(&full[stage], subs * kSubKeys * 256);
+            for (int j = 0; j < subs; ++j) {
+              tma_load_3d(dst + j * kSubKeys * 128, map32, 0, wk.h, slot + j * kSubKeys, &full[stage]);
+              tma_load_3d(dst + kHalfTileBytes + j * kSubKeys * 128, map32, 64, wk.h, slot + j * kSubKeys,
+                          &full[stage]);
+            }
+          }
         }
       }
     }
@@ -704,15 +722,15 @@ static int make_map(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1
 }
 
 template <int G>
-static int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const Args& a, int grid,
-                  cudaStream_t stream) {
+static int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const CUtensorMap& km32,
+                  const CUtensorMap& vm32, const Args& a, int grid, cudaStream_t stream) {
   static bool configured = false;
   if (!configured) {
     SPECDEC_CUDA_TRY(cudaFuncSetAttribute(verify_attention_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           kSmemBytes));
     configured = true;
   }
-  verify_attention_kernel<G><<<grid, kThreads, kSmemBytes, stream>>>(qm, km, vm, a);
+  verify_attention_kernel<G><<<grid, kThreads, kSmemBytes, stream>>>(qm, km, vm, km32, vm32, a);
   SPECDEC_LAUNCH_CHECK();
   return kOk;
 }
@@ -782,7 +800,7 @@ int specdec_paged_attention(const void* q, long long T, long long q_row_stride, 
                     "give cu_seqlens_q/k (varlen) or context_lens and q_per_seq (decode)");
   SPECDEC_CHECK_ARG(cu_seqlens_q || (q_per_seq <= max_seqlen_q && (long long)R * q_per_seq <= T),
                     "decode mode: q_per_seq must fit the batch");
-  CUtensorMap qm, km, vm;
+  CUtensorMap qm, km, vm, km32, vm32;
   const uint64_t row_bytes = (uint64_t)num_kv_heads * head_dim * 2;
   if (int st = make_map(&qm, q, head_dim, num_heads, T, (uint64_t)head_dim * 2, (uint64_t)q_row_stride * 2, G,
                         kCols / G))
@@ -792,6 +810,12 @@ int specdec_paged_attention(const void* q, long long T, long long q_row_stride, 
     return st;
   if (int st = make_map(&vm, v_cache, head_dim, num_kv_heads, num_slots, (uint64_t)head_dim * 2, row_bytes, 1,
                         kKeysPerTile))
+    return st;
+  if (int st = make_map(&km32, k_cache, head_dim, num_kv_heads, num_slots, (uint64_t)head_dim * 2, row_bytes, 1,
+                        kSubKeys))
+    return st;
+  if (int st = make_map(&vm32, v_cache, head_dim, num_kv_heads, num_slots, (uint64_t)head_dim * 2, row_bytes, 1,
+                        kSubKeys))
     return st;
   Args a{};
   a.cu_seqlens_q = cu_seqlens_q;
@@ -821,10 +845,10 @@ int specdec_paged_attention(const void* q, long long T, long long q_row_stride, 
   a.partial = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + counters_bytes(R, num_kv_heads));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (G) {
-    case 1: return launch<1>(qm, km, vm, a, grid, s);
-    case 2: return launch<2>(qm, km, vm, a, grid, s);
-    case 4: return launch<4>(qm, km, vm, a, grid, s);
-    default: return launch<8>(qm, km, vm, a, grid, s);
+    case 1: return launch<1>(qm, km, vm, km32, vm32, a, grid, s);
+    case 2: return launch<2>(qm, km, vm, km32, vm32, a, grid, s);
+    case 4: return launch<4>(qm, km, vm, km32, vm32, a, grid, s);
+    default: return launch<8>(qm, km, vm, km32, vm32, a, grid, s);
   }
 }
 
