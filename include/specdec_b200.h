@@ -112,6 +112,19 @@ int specdec_paged_attention(const void* q, long long T, long long q_row_stride, 
                             int max_seqlen_q, float softmax_scale, int causal, void* out, long long out_row_stride,
                             void* workspace, long long workspace_bytes, int* err, void* stream);
 
+/* specdec_paged_attention with launch flags.  SPECDEC_ATTN_EARLY_LAUNCH: launched as a programmatic dependent of
+ * the preceding kernel in the stream, so its prologue (row metadata scan, barrier and tensor-memory setup) runs
+ * while that kernel finishes; everything else waits for that kernel's completion.  The caller promises that the
+ * preceding kernel does not write cu_seqlens_q / cu_seqlens_k / context_lens / block_tables (q and the caches it
+ * may write).  specdec_paged_attention is this call with flags 0. */
+#define SPECDEC_ATTN_EARLY_LAUNCH 1u
+int specdec_paged_attention_ex(const void* q, long long T, long long q_row_stride, int num_heads, int num_kv_heads,
+                               int head_dim, const void* k_cache, const void* v_cache, long long num_slots,
+                               int block_size, const int* cu_seqlens_q, const int* cu_seqlens_k,
+                               const int* context_lens, int q_per_seq, int R, const int* block_tables, int W,
+                               int max_seqlen_q, float softmax_scale, int causal, void* out, long long out_row_stride,
+                               void* workspace, long long workspace_bytes, int* err, unsigned flags, void* stream);
+
 /* ------------------------------------------------------------------------------------------ kernel 3: Markov rows */
 /* One row step of DFlashDrafter._markov_rows (nanovllm/engine/speculative.py:163-184) for every batch row: with
  * row_logits = logits[:, row] + bias (bias = markov_head(prev), [B, V]; rounded to bf16 when round_bf16):

@@ -65,6 +65,11 @@ __device__ __forceinline__ float load_f32(const T* p) { return to_f32(*p); }
 
 // 16-byte streaming load (read-once data: evict-first in L1/L2 is not wanted for rows re-read by the tail
 // pass, so this is a plain non-coherent global load).
+// Programmatic dependent launch: wait until the grid this one depends on has completed and its writes are
+// visible (returns at once for a grid launched without the dependency), and let dependents start launching.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 __device__ __forceinline__ uint4 ldg16(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
 
 // Unpacks a 16-byte vector of T into floats; returns the number of lanes (4 for f32, 8 for 16-bit types).

@@ -86,6 +86,7 @@ struct NormRopeArgs {
 // grid: (ceil(T * (Hq + Hkv) / 8), layers); 8 warps per CTA, one (token, head) row per warp; V rows are copied by
 // the warp that owns the K row of the same head.
 __global__ void __launch_bounds__(256) norm_rope_store_kernel(const NormRopeArgs a) {
+  griddep_launch_dependents();   // a dependent launched early (verify attention) may start its prologue
   const int lane = threadIdx.x & 31;
   const long long item = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int heads = a.Hq + a.Hkv;

@@ -34,6 +34,7 @@
 // context in its last tile are never read as values: their P is 0 and their V rows are zeroed in shared memory.
 #include "common.cuh"
 #include "sm100.cuh"
+#include "specdec_b200.h"
 
 #include <cudaTypedefs.h>
 #include <math.h>
@@ -315,6 +316,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // An early (programmatic dependent) launch ran the prologue above while the preceding kernel finished; nothing
+  // below reads or writes memory before that kernel's completion (a no-op for an ordinary launch).
+  griddep_wait();
   const uint32_t tmem = S.tmem_base;
   volatile int* abort = &S.abort;
   const long long x_begin = S.x_begin, x_end = S.x_end;
@@ -723,14 +727,24 @@ static int make_map(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1
 
 template <int G>
 static int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const CUtensorMap& km32,
-                  const CUtensorMap& vm32, const Args& a, int grid, cudaStream_t stream) {
+                  const CUtensorMap& vm32, const Args& a, int grid, bool early, cudaStream_t stream) {
   static bool configured = false;
   if (!configured) {
     SPECDEC_CUDA_TRY(cudaFuncSetAttribute(verify_attention_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           kSmemBytes));
     configured = true;
   }
-  verify_attention_kernel<G><<<grid, kThreads, kSmemBytes, stream>>>(qm, km, vm, km32, vm32, a);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = early ? 1 : 0;
+  SPECDEC_CUDA_TRY(cudaLaunchKernelEx(&cfg, verify_attention_kernel<G>, qm, km, vm, km32, vm32, a));
   SPECDEC_LAUNCH_CHECK();
   return kOk;
 }
@@ -775,13 +789,14 @@ long long specdec_attention_workspace_bytes(int R, int num_kv_heads) {
   return attention::workspace_bytes(R, num_kv_heads, info.sm_count);
 }
 
-int specdec_paged_attention(const void* q, long long T, long long q_row_stride, int num_heads, int num_kv_heads,
-                            int head_dim, const void* k_cache, const void* v_cache, long long num_slots,
-                            int block_size, const int* cu_seqlens_q, const int* cu_seqlens_k,
-                            const int* context_lens, int q_per_seq, int R, const int* block_tables, int W,
-                            int max_seqlen_q, float softmax_scale, int causal, void* out, long long out_row_stride,
-                            void* workspace, long long workspace_bytes, int* err, void* stream) {
+int specdec_paged_attention_ex(const void* q, long long T, long long q_row_stride, int num_heads, int num_kv_heads,
+                               int head_dim, const void* k_cache, const void* v_cache, long long num_slots,
+                               int block_size, const int* cu_seqlens_q, const int* cu_seqlens_k,
+                               const int* context_lens, int q_per_seq, int R, const int* block_tables, int W,
+                               int max_seqlen_q, float softmax_scale, int causal, void* out, long long out_row_stride,
+                               void* workspace, long long workspace_bytes, int* err, unsigned flags, void* stream) {
   using namespace attention;
+  SPECDEC_CHECK_ARG((flags & ~(unsigned)SPECDEC_ATTN_EARLY_LAUNCH) == 0, "unknown flags 0x%x", flags);
   SPECDEC_CHECK_ARG(q && k_cache && v_cache && block_tables && out && workspace && err, "null pointer argument");
   SPECDEC_CHECK_ARG((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "workspace must be 256-byte aligned");
   SPECDEC_CHECK_ARG(head_dim == kHeadDim, "head_dim %d: this build implements 128", head_dim);
@@ -844,12 +859,25 @@ int specdec_paged_attention(const void* q, long long T, long long q_row_stride, 
   a.counters = static_cast<int*>(workspace);
   a.partial = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + counters_bytes(R, num_kv_heads));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool early = (flags & SPECDEC_ATTN_EARLY_LAUNCH) != 0;
   switch (G) {
-    case 1: return launch<1>(qm, km, vm, km32, vm32, a, grid, s);
-    case 2: return launch<2>(qm, km, vm, km32, vm32, a, grid, s);
-    case 4: return launch<4>(qm, km, vm, km32, vm32, a, grid, s);
-    default: return launch<8>(qm, km, vm, km32, vm32, a, grid, s);
+    case 1: return launch<1>(qm, km, vm, km32, vm32, a, grid, early, s);
+    case 2: return launch<2>(qm, km, vm, km32, vm32, a, grid, early, s);
+    case 4: return launch<4>(qm, km, vm, km32, vm32, a, grid, early, s);
+    default: return launch<8>(qm, km, vm, km32, vm32, a, grid, early, s);
   }
+}
+
+int specdec_paged_attention(const void* q, long long T, long long q_row_stride, int num_heads, int num_kv_heads,
+                            int head_dim, const void* k_cache, const void* v_cache, long long num_slots,
+                            int block_size, const int* cu_seqlens_q, const int* cu_seqlens_k,
+                            const int* context_lens, int q_per_seq, int R, const int* block_tables, int W,
+                            int max_seqlen_q, float softmax_scale, int causal, void* out, long long out_row_stride,
+                            void* workspace, long long workspace_bytes, int* err, void* stream) {
+  return specdec_paged_attention_ex(q, T, q_row_stride, num_heads, num_kv_heads, head_dim, k_cache, v_cache,
+                                    num_slots, block_size, cu_seqlens_q, cu_seqlens_k, context_lens, q_per_seq, R,
+                                    block_tables, W, max_seqlen_q, softmax_scale, causal, out, out_row_stride,
+                                    workspace, workspace_bytes, err, 0u, stream);
 }
 
 }  // extern "C"

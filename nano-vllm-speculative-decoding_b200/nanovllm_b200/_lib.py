@@ -49,6 +49,10 @@ SIGNATURES = {
                                          _c_int, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_int, _c_void_p, _c_int,
                                          _c_int, _c_float, _c_int, _c_void_p, _c_ll, _c_void_p, _c_ll, _c_void_p,
                                          _c_void_p]),
+    "specdec_paged_attention_ex": (_c_int, [_c_void_p, _c_ll, _c_ll, _c_int, _c_int, _c_int, _c_void_p, _c_void_p,
+                                            _c_ll, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_int, _c_void_p,
+                                            _c_int, _c_int, _c_float, _c_int, _c_void_p, _c_ll, _c_void_p, _c_ll,
+                                            _c_void_p, ctypes.c_uint, _c_void_p]),
     "specdec_attention_workspace_bytes": (_c_ll, [_c_int, _c_int]),
     "specdec_norm_rope_store": (_c_int, [_c_void_p, _c_ll, _c_ll, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_void_p,
                                          _c_ll, _c_void_p, _c_ll, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_ll,

@@ -71,13 +71,18 @@ def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor,
                                            ptr(_err_word(device)), stream_of(device)))
 
 
+EARLY_LAUNCH = 1   # SPECDEC_ATTN_EARLY_LAUNCH
+
+
 def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
                     scale: float, *, cu_seqlens_q: torch.Tensor | None = None,
                     cu_seqlens_k: torch.Tensor | None = None, max_seqlen_q: int | None = None,
                     context_lens: torch.Tensor | None = None, query_len_per_seq: int = 1, causal: bool = True,
-                    out: torch.Tensor | None = None) -> torch.Tensor:
+                    out: torch.Tensor | None = None, early_launch: bool = False) -> torch.Tensor:
     """Attention of q [T, H, D] over the paged caches.  Varlen (cu_seqlens_q/k, the verify forward) or decode
-    (context_lens with query_len_per_seq queries per row).  Returns out [T, H, D] bf16."""
+    (context_lens with query_len_per_seq queries per row).  Returns out [T, H, D] bf16.  early_launch: launch as a
+    programmatic dependent of the preceding kernel (its prologue overlaps that kernel's end); only when that kernel
+    does not write the row metadata (cu_seqlens / context_lens / block_tables)."""
     device = require_cuda(q, k_cache, v_cache, block_tables)
     T, H, D = q.shape
     blocks, block_size, Hkv, Dc = k_cache.shape
@@ -104,10 +109,11 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
         q_per_seq = query_len_per_seq
         max_seqlen_q = query_len_per_seq
     ws = _split_workspace(device, R, Hkv)
-    check(_lib.lib().specdec_paged_attention(
+    check(_lib.lib().specdec_paged_attention_ex(
         ptr(q), T, q.stride(0), H, Hkv, D, ptr(k_cache), ptr(v_cache), blocks * block_size, block_size, ptr(cq),
         ptr(ck), ptr(ctx), q_per_seq, R, ptr(tables), W, int(max_seqlen_q), float(scale), int(causal), ptr(out),
-        out.stride(0), ptr(ws), ws.numel(), ptr(_err_word(device)), stream_of(device)))
+        out.stride(0), ptr(ws), ws.numel(), ptr(_err_word(device)), EARLY_LAUNCH if early_launch else 0,
+        stream_of(device)))
     return out
 
 

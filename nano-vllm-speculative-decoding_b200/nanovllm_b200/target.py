@@ -92,9 +92,10 @@ class Qwen3Target:
             qkv = torch.matmul(x, w["w_qkv"].t())
             q = fused.qk_norm_rope_store(qkv, s.heads, s.kv_heads, w["q_norm"], w["k_norm"], self.cos_sin, positions,
                                          slot_mapping, self.kv_cache[0, layer_id], self.kv_cache[1, layer_id], s.eps)
+            # launched early: its predecessor (the q/k norm, RoPE and K/V store) writes q and the caches only
             o = attention.paged_attention(q, self.kv_cache[0, layer_id], self.kv_cache[1, layer_id], block_tables,
                                           self.scale, cu_seqlens_q=cu_seqlens_q, cu_seqlens_k=cu_seqlens_k,
-                                          max_seqlen_q=max_seqlen_q)
+                                          max_seqlen_q=max_seqlen_q, early_launch=True)
             h = torch.matmul(o.view(T, -1), w["w_o"].t())
             x, residual = fused.rmsnorm(h, w["post_norm"], s.eps, residual=residual)
             h = torch.matmul(fused.silu_and_mul(torch.matmul(x, w["w_gate_up"].t())), w["w_down"].t())

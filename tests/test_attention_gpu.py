@@ -199,3 +199,32 @@ def test_workspace_query(A):
     sms = torch.cuda.get_device_properties(DEV).multi_processor_count
     assert need == (64 * 8 * 4 + 255) // 256 * 256 + 2 * sms * (32 * 128 + 64) * 4
     assert lib.specdec_attention_workspace_bytes(0, 8) == -1
+
+
+def test_early_launch_after_the_qk_store(A):
+    """An early (programmatic dependent) launch right after the kernel that writes q and the new K/V rows reads
+    what that kernel wrote: the same bits as an ordinary launch, and the oracle's values."""
+    from nanovllm_b200.fused import qk_norm_rope_store, rope_cache
+    rng = np.random.default_rng(7)
+    c = paged_case([8] * 16, rng.integers(300, 2000, size=16).tolist(), seed=41)
+    T, H, Hkv = c["q"].shape[0], 32, 8
+    g = torch.Generator(device=DEV).manual_seed(9)
+    qkv = torch.randn(T, (H + 2 * Hkv) * 128, device=DEV, generator=g).bfloat16()
+    q_norm = (1.0 + 0.1 * torch.randn(128, device=DEV, generator=g)).bfloat16()
+    k_norm = (1.0 + 0.1 * torch.randn(128, device=DEV, generator=g)).bfloat16()
+    cos_sin = rope_cache(128, 8192, 1000000.0, DEV)
+    positions = torch.tensor([kl - ql + j for ql, kl in zip(c["q_lens"], c["k_lens"]) for j in range(ql)],
+                             device=DEV)
+    outs, caches = [], []
+    for early in (False, True):
+        kc, vc = c["k_cache"].clone(), c["v_cache"].clone()
+        q = qk_norm_rope_store(qkv, H, Hkv, q_norm, k_norm, cos_sin, positions, c["slots"], kc, vc, 1e-6)
+        outs.append(A.paged_attention(q, kc, vc, c["tables"], c["scale"], cu_seqlens_q=c["cu_q"],
+                                      cu_seqlens_k=c["cu_k"], max_seqlen_q=8, early_launch=early))
+        caches.append((q, kc, vc))
+    torch.cuda.synchronize()
+    assert A.device_error(DEV) == 0
+    assert torch.equal(outs[0], outs[1])
+    q, kc, vc = caches[1]
+    c2 = dict(c, q=q, k_cache=kc, v_cache=vc)
+    np.testing.assert_allclose(outs[1].float().cpu().numpy(), oracle_out(c2), atol=ATOL, rtol=0)
