@@ -95,6 +95,8 @@ struct Smem {
   long long row_tile0;       // sequence index of the first tile of row b_start
   int b_start;               // row holding tile x_begin
   int active;                // CTAs given tiles: min(gridDim.x, total_tiles)
+  int r0[4];                 // row b_start's RowInfo (q_start, ql, L, nt)
+  int slot0;                 // cache slot of the share's first tile
   int last_piece;            // the epilogue's broadcast: this CTA combines the split item
   alignas(16) float red_max[2][32][4];   // [tile parity][column][warp] maxima (read as float4)
   alignas(16) float red_sum[32][4];      // [column][warp] sums (epilogue)
@@ -172,7 +174,7 @@ struct Walk {
   RowInfo r;
   __device__ __forceinline__ void start(const Args& a, const Smem& S) {
     b = S.b_start;
-    r = row_info<QMAX>(a, b, false);
+    r = RowInfo{S.r0[0], S.r0[1], S.r0[2], S.r0[3]};   // found by the prologue
     h = (int)((S.x_begin - S.row_tile0) / r.nt);
     A = S.row_tile0 + (long long)h * r.nt;
   }
@@ -279,14 +281,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const long long Ge = T < (long long)gridDim.x ? T : (long long)gridDim.x;
     const long long c = blockIdx.x;
     long long xb = 0, xe = 0, row0 = 0;
-    int bstart = 0;
+    int bstart = 0, slot0 = 0;
+    RowInfo r0{0, 0, 0, 1};
     if (c < Ge) {
       xb = T * c / Ge;
       xe = T * (c + 1) / Ge;
       long long pre = 0;
       for (int b0 = 0; b0 < a.R; b0 += 32) {
         const int b = b0 + lane;
-        const long long v = b < a.R ? (long long)row_info<QMAX>(a, b, false).nt * a.Hkv : 0;
+        const RowInfo ri = b < a.R ? row_info<QMAX>(a, b, false) : RowInfo{0, 0, 0, 0};
+        const long long v = (long long)ri.nt * a.Hkv;
         long long inc = v;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -299,10 +303,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int src = __ffs(hit) - 1;
           bstart = b0 + src;
           row0 = __shfl_sync(0xffffffffu, first, src);
+          r0.q_start = __shfl_sync(0xffffffffu, ri.q_start, src);
+          r0.ql = __shfl_sync(0xffffffffu, ri.ql, src);
+          r0.L = __shfl_sync(0xffffffffu, ri.L, src);
+          r0.nt = __shfl_sync(0xffffffffu, ri.nt, src);
           break;
         }
         pre += __shfl_sync(0xffffffffu, inc, 31);
       }
+    }
+    if (c < Ge && lane == 0) {       // the share's first tile: its key in the row and its cache slot
+      const long long h = (xb - row0) / r0.nt;
+      const int key0 = (int)(xb - row0 - h * r0.nt) * kKeysPerTile;
+      slot0 = a.block_tables[(long long)bstart * a.W + key0 / a.block_size] * a.block_size + key0 % a.block_size;
+      // the first item's Q and first K / V tile into L2 ahead of the loads (before an early launch's wait too)
+      tma_prefetch_3d(&kmap, 0, (int)h, slot0);
+      tma_prefetch_3d(&kmap, 64, (int)h, slot0);
+      tma_prefetch_3d(&vmap, 0, (int)h, slot0);
+      tma_prefetch_3d(&vmap, 64, (int)h, slot0);
+      tma_prefetch_3d(&qmap, 0, (int)h * G, r0.q_start);
+      tma_prefetch_3d(&qmap, 64, (int)h * G, r0.q_start);
     }
     if (lane == 0) {
       S.total_tiles = T;
@@ -311,6 +331,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       S.x_end = xe;
       S.row_tile0 = row0;
       S.b_start = bstart;
+      S.r0[0] = r0.q_start;
+      S.r0[1] = r0.ql;
+      S.r0[2] = r0.L;
+      S.r0[3] = r0.nt;
+      S.slot0 = slot0;
     }
   }
   tc_fence_before();
@@ -354,7 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int stage = g % kStages;
           const uint32_t use = g / kStages;
           const int key0 = t * kKeysPerTile;
-          const int slot = table[key0 / a.block_size] * a.block_size + key0 % a.block_size;
+          const int slot = g == 0 ? S.slot0 : table[key0 / a.block_size] * a.block_size + key0 % a.block_size;
           if (g >= kStages && !mbar_wait(&empty[stage], (use - 1) & 1, abort, a.err, kErrTimeoutEmpty)) {
             ok = false;
             break;
