@@ -487,6 +487,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int t0 = wk.t0(x_begin), t1 = wk.t1(x_end);
       const uint32_t tmem_o = tmem + lane_off + 64 + (n & 1) * 32 + cb;
       const int min_limit = L - ql;            // smallest causal limit among the valid columns
+      // The item's first piece, when this CTA holds it, reads the item's arrival counter now, while the tiles
+      // stream: the other pieces (processed at the starts of later shares) have usually been published already,
+      // and the epilogue then needs no counter round trip.
+      const long long c_lo = ceil_div((wk.A + 1) * Ge, T) - 1, c_hi = ceil_div((wk.A + wk.r.nt) * Ge, T) - 1;
+      int seen_early = -1;
+      if (threadIdx.x == 128 && c_lo != c_hi && c == c_lo)
+        seen_early = ld_acquire_gpu(a.counters + (long long)wk.b * a.Hkv + wk.h);
       // Running maxima (log2 domain): lane j owns column cb + (j & 15)'s (m_lane) and every thread keeps a copy
       // of its group's 16 (m_all), changed only when some column grows by more than 2^8 (lazy rescaling).  The
       // start value is a large negative finite number, so no -inf arithmetic is needed.  l_part: this thread's
@@ -608,13 +615,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- an item split over CTAs c_lo..c_hi: every piece but the last to arrive is published; the last merges
       // them in CTA order (its own from registers when it holds the first piece and finds every other piece already
       // published; from its published copy otherwise), so the output does not depend on which CTA arrived last
-      const long long A = wk.A, B = wk.A + wk.r.nt;
-      const long long c_lo = ceil_div((A + 1) * Ge, T) - 1, c_hi = ceil_div(B * Ge, T) - 1;
+      const long long A = wk.A;
       if (c_lo != c_hi) {
         int* counter = a.counters + (long long)wk.b * a.Hkv + wk.h;
         if (threadIdx.x == 128) {
           // the first piece arriving last (the usual case: it ends this CTA's share) skips its own publication
-          S.last_piece = (c == c_lo && ld_acquire_gpu(counter) == (int)(c_hi - c_lo)) ? 2 : 0;
+          const int need = (int)(c_hi - c_lo);
+          S.last_piece = (c == c_lo && (seen_early == need || ld_acquire_gpu(counter) == need)) ? 2 : 0;
         }
         named_barrier(3, 256);
         const bool own_in_registers = S.last_piece == 2;
