@@ -151,7 +151,7 @@ def build_workload(torch, device, batch: int, ctx: int, seed: int):
                            lengths=lengths, width=width, shape=shape)
 
 
-CFG2_TRAFFIC_BYTES = 148_266_752       # 143.169792 MB read + 5.096960 MB written, one launch
+CFG2_TRAFFIC_BYTES = 141_530_624       # 136.830976 MB read + 4.699648 MB written, one launch
 CFG2_ALGORITHMIC_BYTES = 135_319_552
 
 
@@ -200,7 +200,7 @@ def attention_roofline(torch, w, hbm_peak: float) -> dict:
     qo_bytes = 2 * num_tokens * s.heads * s.head_dim * 2
     algorithmic = kv_bytes + qo_bytes
     achieved = algorithmic / (per_launch_us * 1e-6) / 1e9
-    # DRAM traffic from one ncu capture of the config-2 launch (148.27 MB read + written for 135.32 MB
+    # DRAM traffic from one ncu capture of the config-2 launch (141.53 MB read + written for 135.32 MB
     # algorithmic), scaled to this launch by its algorithmic bytes (traffic grows with the keys)
     traffic = round(algorithmic * CFG2_TRAFFIC_BYTES / CFG2_ALGORITHMIC_BYTES)
     return {"kernel": "specdec::attention::verify_attention_kernel<4>", "bound": "hbm",

@@ -108,8 +108,10 @@ def test_baseline_config2_verify_attention(A):
     np.testing.assert_allclose(got, want, atol=ATOL, rtol=0)
 
 
-@pytest.mark.parametrize("k_lens", [[1, 2, 8], [127, 128, 129], [255, 256, 257], [383, 512, 640]])
+@pytest.mark.parametrize("k_lens", [[1, 2, 8], [127, 128, 129], [255, 256, 257], [383, 512, 640],
+                                    [31, 32, 33], [159, 160, 161], [191, 192, 193], [223, 224, 225]])
 def test_ragged_rows_and_tile_edges(A, k_lens):
+    """Row ends at every 32-key sub-box edge of a last tile (a partial last tile loads only its sub-boxes)."""
     q_lens = [min(k, q) for k, q in zip(k_lens, [1, 5, 8])]
     c = paged_case(q_lens, k_lens, seed=sum(k_lens))
     out = run_verify(A, c)
