@@ -308,12 +308,23 @@ __device__ void row_range_ms(const T* row, int lo, int hi, float temp, int vec_o
       const int inext = i + NT * 4;
       if (inext < nvec) load_batch(inext, nxt);
       float vm = -INFINITY;
+      if constexpr (sizeof(T) == 2) {
+        // the batch maximum on packed pairs (exact; NaN dropped as fmaxf does), then scaled once: x / T is
+        // monotone in x, so max(x) / T is the maximum of the scaled values
+        using H2 = typename std::conditional<std::is_same<T, __half>::value, __half2, __nv_bfloat162>::type;
+        H2 mx2 = group_max_h2<H2>(cur[0]);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        float f[VE];
-        unpack(cur[u], f);
+        for (int u = 1; u < 4; ++u) mx2 = __hmax2(mx2, group_max_h2<H2>(cur[u]));
+        vm = fmaxf(__low2float(mx2), __high2float(mx2));
+        if (!unit_temp) vm = scale_logit(vm, temp);
+      } else {
 #pragma unroll
-        for (int e = 0; e < VE; ++e) vm = fmaxf(vm, f[e]);
+        for (int u = 0; u < 4; ++u) {
+          float f[VE];
+          unpack(cur[u], f);
+#pragma unroll
+          for (int e = 0; e < VE; ++e) vm = fmaxf(vm, f[e]);
+        }
       }
       if (vm > m) {
         if (m != -INFINITY) s *= exp_sum_term(m - vm);
