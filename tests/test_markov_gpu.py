@@ -214,3 +214,31 @@ def test_persistent_q_buffer_matches_fresh_zeroed_buffers():
         assert torch.equal(d, d_ref)
         assert torch.equal(qbuf.probs, q_ref)
         assert int((qbuf.probs != 0).sum(dim=-1).max()) <= cand
+
+
+@pytest.mark.parametrize("dtype,V", [(torch.float32, 6001), (torch.bfloat16, 6001), (torch.float32, 8000)])
+def test_markov_rows_fp32_and_ragged_vocab(dtype, V):
+    """fp32 logits and bias (no rounding of the biased row, 3-digit radix keys) and rows whose length is not a
+    multiple of 8 (the scalar load path) against the oracle."""
+    from nanovllm_b200.markov import markov_rows, num_candidates
+    from oracle.ctx_store import bf16
+    B, k = 4, 3
+    g = torch.Generator(device=DEV).manual_seed(V)
+    logits = (torch.randn(B, k, V, device=DEV, generator=g) * 2).to(dtype)
+    table = (torch.randn(16, V, device=DEV, generator=g)).to(dtype)
+    head = lambda prev: table[prev % 16]
+    samp = sampling_of([1.0, 0.8, 1.3, 0.6], [50] * B, [1.0, 0.9, 1.0, 0.7])
+    cand = num_candidates(samp.max_top_k, samp.all_top_k, V)
+    noise = torch.empty(B, k, cand, device=DEV).exponential_(generator=g).clamp_min_(1e-10)
+    drafts = torch.empty(B, k, dtype=torch.int64, device=DEV)
+    probs = torch.empty(B, k, V, device=DEV)
+    prev = torch.randint(V, (B,), device=DEV, generator=g)
+    markov_rows(logits, prev, samp, noise, drafts, probs, cand, head)
+    tab = table.float().cpu().numpy()
+    sampling = dict(temps=samp.temperatures.cpu().numpy(), top_k=samp.top_k.cpu().numpy(),
+                    top_p=samp.top_p.cpu().numpy(), max_top_k=samp.max_top_k, has_top_p=samp.has_top_p)
+    want, want_probs = OM.markov_rows(logits.float().cpu().numpy(), prev.cpu().numpy(), lambda p: tab[p % 16],
+                                      sampling, noise.cpu().numpy(), cand,
+                                      round_fn=bf16 if dtype == torch.bfloat16 else (lambda x: x))
+    assert drafts.cpu().numpy().tolist() == want.tolist()
+    np.testing.assert_allclose(probs.cpu().numpy(), want_probs, rtol=1e-5, atol=1e-8)

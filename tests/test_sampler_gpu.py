@@ -267,3 +267,31 @@ def test_inconsistent_lengths_and_drafts_are_reported_not_read(S):
     assert device_status(DEV) == 2
     S.accept_from_logits(logits, q, drafts, samp, lens, None)
     assert device_status(DEV) == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("vocab", [32000, 4099])          # 16-byte vectors / a ragged row (scalar paths)
+@pytest.mark.parametrize("params", [None, ([0.7] * 16, [20] * 16, [0.8] * 16), MIXED_TOPK])
+def test_accept_dtypes_and_vocab_shapes(S, dtype, vocab, params):
+    """Every logits dtype the kernels take, on vectorised and ragged rows, without and with truncation (the
+    packed 16-bit selection, the scalar fallback, the kept-token and full-row tail races)."""
+    batch = 16
+    if params is MIXED_TOPK:
+        params = tuple(p[:batch] for p in MIXED_TOPK)
+    temps, top_k, top_p = params or (None, None, None)
+    logits, q, drafts, lens, samp = synthetic_round(S, batch, 7, vocab, dtype, True, seed=vocab + batch,
+                                                    temps=temps, top_k=top_k, top_p=top_p)
+    gen = torch.Generator(device=DEV).manual_seed(23)
+    u = torch.rand(batch, 7, device=DEV, generator=gen)
+    noise = S.exponential_noise_(torch.empty(batch, vocab, device=DEV), gen)
+    n_accept, tail = S.accept_from_logits(logits, q, drafts, samp, lens, None, draws=(u, noise))
+    lens_np = lens.cpu().numpy()
+    per = lambda t: np.repeat(t.cpu().numpy(), lens_np)
+    p = O.probs_from_logits(logits.float().cpu().numpy(), per(samp.temperatures), per(samp.top_k),
+                            per(samp.top_p), samp.max_top_k, samp.has_top_p)
+    args = (q.cpu().numpy(), drafts.cpu().numpy(), lens_np, u.cpu().numpy(), noise.cpu().numpy())
+    want_n, want_tail = O.accept_random_varlen(p, *args)
+    keep = ~O.near_tie_flags(p, *args)
+    assert keep.sum() >= batch - 1
+    assert np.array_equal(n_accept.cpu().numpy()[keep], want_n[keep])
+    assert np.array_equal(tail.cpu().numpy()[keep], want_tail[keep])
