@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Benchmark of the B200 verify + accept round.
+"""Benchmark of the B200 verify + accept round (benchmark config 3).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--batch 64] [--ctx 1000]
 
@@ -49,7 +49,7 @@ def parse_args():
     p.add_argument("--ctx", type=int, default=1000, help="mean context length (tokens before the verified ones)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--kernel", choices=["attention", "accept", "accept_topk", "markov", "ctx_store"], default=None,
-                   help="time one kernel alone on its BASELINE config (attention: config 2, accept: config 3's "
+                   help="time one kernel alone on its benchmark config (attention: config 2, accept: config 3's "
                         "logits) instead of the round; used for profiling")
     return p.parse_args()
 
@@ -321,7 +321,7 @@ def run_reference(args) -> int:
 
 # ---------------------------------------------------------------------------------------------- one kernel
 def run_kernel(args) -> int:
-    """Times one kernel alone (CUDA events, W warm-up launches, K timed launches) on its BASELINE config:
+    """Times one kernel alone (CUDA events, W warm-up launches, K timed launches) on its benchmark config:
     attention = config 2 (32 rows x 8 queries, contexts U[900, 1100], 32/8 heads, random block permutation);
     accept = config 3's fused accept (64 rows x 8 positions of bf16 logits, temperature 1, in-kernel draws)."""
     import torch

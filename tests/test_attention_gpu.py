@@ -96,7 +96,7 @@ def test_store_kvcache_is_an_exact_copy(A):
 
 
 def test_baseline_config2_verify_attention(A):
-    """32 rows x 8 queries, 32/8 heads, head_dim 128, contexts U[900, 1100], block size 256,
+    """benchmark config 2: 32 rows x 8 queries, 32/8 heads, head_dim 128, contexts U[900, 1100], block size 256,
     random block permutation, stale NaN in unused slots."""
     rng = np.random.default_rng(0)
     k_lens = rng.integers(900, 1101, size=32).tolist()

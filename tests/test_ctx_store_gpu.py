@@ -39,7 +39,7 @@ def test_golden_store_context_kv():
 
 @pytest.mark.parametrize("T,layers", [(288, 5), (7, 1), (512, 5)])
 def test_ctx_store_config4_shape_matches_oracle(T, layers):
-    """BASELINE config 4's draft: 5 layers, hidden 4096, 8 KV heads of 128; kernel given the same projection the
+    """benchmark config 4's draft: 5 layers, hidden 4096, 8 KV heads of 128; kernel given the same projection the
     oracle receives (the GEMM is cuBLAS), so the comparison isolates the kernel."""
     from nanovllm_b200.dflash import store_context_kv
     from nanovllm_b200.fused import rope_cache

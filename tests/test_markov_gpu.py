@@ -64,7 +64,7 @@ class RecordingHead:
 
 @pytest.mark.parametrize("greedy", [False, True])
 def test_config4_markov_rows_match_oracle(greedy):
-    """BASELINE config 4's drafter: B = 64 rows, k = 7, V = 151936, rank 256, bf16, top_k = 128 (192 candidates)."""
+    """benchmark config 4's drafter: B = 64 rows, k = 7, V = 151936, rank 256, bf16, top_k = 128 (192 candidates)."""
     from nanovllm_b200.markov import markov_rows, num_candidates
     B, k, V, r = 64, 7, 151936, 256
     g = torch.Generator(device=DEV).manual_seed(4)

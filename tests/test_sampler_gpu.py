@@ -157,7 +157,7 @@ def synthetic_round(S, batch, k, vocab, dtype, varlen, seed, temps=None, top_k=N
 
 
 @pytest.mark.parametrize("batch,k,dtype,varlen,params", [
-    (8, 7, torch.float32, False, None),
+    (8, 7, torch.float32, False, None),                                     # benchmark config 1
     (64, 7, torch.bfloat16, False, None),                                   # config 3's accept
     (64, 7, torch.bfloat16, True, None),                                    # config 4's varlen lengths
     (16, 7, torch.bfloat16, True, ([0.7] * 16, [20] * 16, [0.8] * 16)),    # protocol sampling
