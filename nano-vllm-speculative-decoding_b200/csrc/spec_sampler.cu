@@ -950,6 +950,19 @@ __device__ __forceinline__ float4 philox_uniform4(unsigned long long seed, unsig
   return _curand_uniform4(curand_Philox4x32_10(ctr, key));
 }
 
+// Race-element filter.  After its first round every CTA holds, per request, a lower bound lb of the request's
+// largest ratio (the best exact ratio any CTA had published by then).  An element with w < lb * E cannot win, and
+// E = -ln(u) is bounded below cheaply: -lg2.approx(u) ln 2 is within ~2e-7 absolute of -ln(u), so for u < 0.999
+// (E > 1e-3) the value shrunk by 1e-3 relative stays below the exact E.  Elements near u = 1 (tiny E, large
+// ratios) and requests without a bound yet are never skipped.
+__device__ __forceinline__ bool race_candidate(float w, float u, float lb) {
+  if (!(lb > 0.0f) || u >= 0.999f) return true;
+  float l2;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(l2) : "f"(u));
+  const float e_lo = -l2 * (0.6931471805599453f * (1.0f - 1e-3f));
+  return !(w < lb * e_lo);
+}
+
 // Accept-tail race.  Work per element: the Philox draw and torch's -log transform (exact), p = e^(f - m) / s as
 // exp_compensated(f - m) * (1/s), the residual, w / E as a fast quotient (p and the quotient within a few 1e-7
 // relative: inside the 1e-6 relative p uncertainty the parity rule allows for the race, where a winner within
@@ -960,12 +973,14 @@ __global__ void __launch_bounds__(kThreads, 4) tail_accept_kernel(Args a) {
   extern __shared__ __align__(16) unsigned char tail_smem[];
   TailDesc* s_td = reinterpret_cast<TailDesc*>(tail_smem);
   unsigned long long* s_best = reinterpret_cast<unsigned long long*>(tail_smem + sizeof(TailDesc) * a.B);
+  float* s_lb = reinterpret_cast<float*>(tail_smem + (sizeof(TailDesc) + sizeof(unsigned long long)) * a.B);
   __shared__ int s_last;
   const volatile int* status = a.status;
   if (status[0] != 0) return;                   // pass 1 rejected its inputs
   if (a.tail_gate && status[1] == 0) return;    // every request raced among its kept tokens
   for (int i = threadIdx.x; i < a.B; i += kThreads) {
     s_best[i] = 0ull;
+    s_lb[i] = 0.0f;                                           // no bound during the first round
     const ReqDesc d = a.desc[i];
     TailDesc t;
     t.m = d.m;
@@ -993,15 +1008,28 @@ __global__ void __launch_bounds__(kThreads, 4) tail_accept_kernel(Args a) {
   TailLoads cur{}, nxt{};
   if (a.e_rounds > 0 && warp0 < N) tail_issue_loads<T>(a, s_td, b, v, li0, S, N, cur);
   for (int n = 0; n < a.e_rounds; ++n) {
-    if (warp0 >= N) break;                                     // warp-uniform
+    if (n == 1) {
+      // the bound exchange after the first round: this CTA's bests out, every CTA's published bests back (one
+      // exchange measured best: later or repeated ones cost more than their tighter bounds save)
+      __syncthreads();
+      for (int i = threadIdx.x; i < a.B; i += kThreads)
+        if (s_best[i]) atomicMax(&a.tail_key[i], s_best[i]);
+      __syncthreads();
+      for (int i = threadIdx.x; i < a.B; i += kThreads) {
+        const unsigned long long kk = __ldcg(&a.tail_key[i]);
+        s_lb[i] = kk ? __uint_as_float(static_cast<unsigned>(kk >> 32) & 0x7fffffffu) : 0.0f;
+      }
+      __syncthreads();
+    }
+    if (warp0 >= N) continue;                                  // warp-uniform (every warp reaches the exchange)
     if (n + 1 < a.e_rounds && warp0 + 4 * S < N) tail_issue_loads<T>(a, s_td, b, v, li0 + 4 * S, S, N, nxt);
-    float ee[4];
+    float uu[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     if (gen) {
       const float4 r4 = direct ? philox_uniform4(a.seed, c0, idx, n) : curand_uniform4(&st);
-      ee[0] = torch_exponential_clamped(r4.x);
-      ee[1] = torch_exponential_clamped(r4.y);
-      ee[2] = torch_exponential_clamped(r4.z);
-      ee[3] = torch_exponential_clamped(r4.w);
+      uu[0] = r4.x;
+      uu[1] = r4.y;
+      uu[2] = r4.z;
+      uu[3] = r4.w;
     }
     unsigned bb = cur.b0, vv = cur.v0;
     if (!a.probs_mode && warp0 + 3 * S + 32 <= N) {
@@ -1013,7 +1041,12 @@ __global__ void __launch_bounds__(kThreads, 4) tail_accept_kernel(Args a) {
         const float f = d.w == 1.0f ? cur.x[ii] : scale_logit(cur.x[ii], d.w);
         const float p = f >= d.z ? exp_compensated(f - d.x) * d.y : 0.0f;
         const float w = qrow ? fmaxf(p - cur.q[ii], 0.0f) : p;
-        const float e = gen ? ee[ii] : a.E[li0 + ii * S];
+        // the whole warp skips elements that provably cannot win (given draws have no u: never skipped)
+        if (!__any_sync(0xffffffffu, !gen || race_candidate(w, uu[ii], s_lb[bb]))) {
+          tail_step(a, bb, vv);
+          continue;
+        }
+        const float e = gen ? torch_exponential_clamped(uu[ii]) : a.E[li0 + ii * S];
         const unsigned bits = __float_as_uint(__fdividef(w, e)) & 0x7fffffffu;
         if (__all_sync(0xffffffffu, vv >= (unsigned)lane)) {
           // 32 consecutive columns vv(lane 0) + lane of one row
@@ -1045,7 +1078,7 @@ __global__ void __launch_bounds__(kThreads, 4) tail_accept_kernel(Args a) {
               p = f >= d.z ? exp_compensated(f - d.x) * d.y : 0.0f;
             }
             const float w = s_td[bb].qrow ? fmaxf(p - cur.q[ii], 0.0f) : p;
-            const float e = gen ? ee[ii] : a.E[li];
+            const float e = gen ? torch_exponential_clamped(uu[ii]) : a.E[li];
             bits = __float_as_uint(__fdividef(w, e)) & 0x7fffffffu;   // w >= 0: clears a -0
           }
           const unsigned b0 = __shfl_sync(0xffffffffu, bb, 0);
@@ -1341,7 +1374,7 @@ static int launch_tail(Args& a, const DeviceInfo& info, bool race, cudaStream_t 
   if (race) {
     race_kernel<<<a.e_grid, kThreads, 0, stream>>>(a);
   } else {
-    const size_t smem = (sizeof(TailDesc) + sizeof(unsigned long long)) * a.B;
+    const size_t smem = (sizeof(TailDesc) + sizeof(unsigned long long) + sizeof(float)) * a.B;
     tail_accept_kernel<T><<<a.e_grid, kThreads, smem, stream>>>(a);
   }
   SPECDEC_LAUNCH_CHECK();
