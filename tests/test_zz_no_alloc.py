@@ -23,13 +23,16 @@ def case(seed, batch, k, dtype, varlen):
     return logits, q, drafts, (lens if varlen else None), temps
 
 
-def call(lib, name, logits, q, drafts, lens, temps, seed, workspace=None):
+def call(lib, name, logits, q, drafts, lens, temps, seed, workspace=None, top_k=None, top_p=None):
     batch, k = drafts.shape
+    max_top_k = 0 if top_k is None else int(top_k.max())
+    has_top_p = 0 if top_p is None else int((top_p < 1).any())
     n_accept = torch.full((batch,), -1, dtype=torch.int64, device=DEV)
     tail = torch.full((batch,), -1, dtype=torch.int64, device=DEV)
     dtype_code = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}[logits.dtype]
     args = [logits.data_ptr(), 0, dtype_code, logits.shape[0], V, q.data_ptr(), drafts.data_ptr(), batch, k,
-            None if lens is None else lens.data_ptr(), temps.data_ptr(), None, None, 0, 0, None, None, seed, 0, 4,
+            None if lens is None else lens.data_ptr(), temps.data_ptr(), None if top_k is None else top_k.data_ptr(),
+            None if top_p is None else top_p.data_ptr(), max_top_k, has_top_p, None, None, seed, 0, 4,
             n_accept.data_ptr(), tail.data_ptr()]
     if workspace is not None:
         args += [workspace.data_ptr(), workspace.numel()]
@@ -50,6 +53,27 @@ def test_no_alloc_accept_matches_the_workspace_entry_point_twice():
         assert st_ref == 0 and st == 0, lib.specdec_last_error()
         assert torch.equal(n, n_ref) and torch.equal(t, t_ref)
         assert (n >= 0).all() and (t >= 0).all()
+
+
+def test_no_alloc_accept_with_truncation_matches_the_workspace_entry_point():
+    """Top-k / top-p rows: the kept-token tail race (every row truncated) and the gated full-row race (rows
+    without top-k mixed in) through the fixed scratch, twice in a row."""
+    from nanovllm_b200 import _lib
+    lib = _lib.load()
+    for i, mixed in enumerate([False, True]):
+        logits, q, drafts, lens, temps = case(10 + i, 32, 7, torch.bfloat16, True)
+        top_k = torch.full((32,), 20, dtype=torch.int64, device=DEV)
+        if mixed:
+            top_k[::3] = 0
+        top_p = torch.where(top_k > 0, 0.8, 1.0).float()
+        workspace = torch.zeros(lib.specdec_sampler_workspace_bytes(logits.shape[0]), dtype=torch.uint8,
+                                device=DEV)
+        ref = call(lib, "specdec_accept", logits, q, drafts, lens, temps, 50 + i, workspace, top_k, top_p)
+        for _ in range(2):
+            got = call(lib, "specdec_accept_noalloc", logits, q, drafts, lens, temps, 50 + i, None, top_k, top_p)
+            torch.cuda.synchronize()
+            assert ref[0] == 0 and got[0] == 0, lib.specdec_last_error()
+            assert torch.equal(got[1], ref[1]) and torch.equal(got[2], ref[2])
 
 
 def test_no_alloc_accept_refuses_more_rows_than_its_scratch_holds():
