@@ -413,9 +413,10 @@ def run_kernel(args) -> int:
     for _ in range(args.warmup):
         fn()
     timing = "events"
-    if args.kernel in ("attention", "ctx_store"):
-        # short launches: K calls captured in one CUDA graph and replayed, so the host's per-call work (tensor
-        # map encoding, Python) does not pace the device
+    if args.kernel in ("attention", "ctx_store", "markov"):
+        # K calls captured in one CUDA graph and replayed, so the host's per-call work (tensor map encoding,
+        # Python) does not pace the device; the reference captures its Markov rows in a graph the same way
+        # (speculative.py:216-231)
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
