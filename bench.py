@@ -48,7 +48,8 @@ def parse_args():
     p.add_argument("--batch", type=int, default=64)
     p.add_argument("--ctx", type=int, default=1000, help="mean context length (tokens before the verified ones)")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--kernel", choices=["attention", "accept", "accept_topk", "markov", "ctx_store"], default=None,
+    p.add_argument("--kernel", choices=["attention", "accept", "accept_topk", "markov", "ctx_store", "after_verify"],
+                   default=None,
                    help="time one kernel alone on its benchmark config (attention: config 2, accept: config 3's "
                         "logits) instead of the round; used for profiling")
     return p.parse_args()
@@ -394,6 +395,31 @@ def run_kernel(args) -> int:
             store_context_kv(features, w, k_norm, cos_sin, positions, slots, cache, 1e-6, kv_out=kv)
         # weights (GEMM) + features + projection write/read + cache writes
         algorithmic = w.numel() * 2 + features.numel() * 2 + 2 * kv.numel() * 2 + T * layers * 2 * hkv * 128 * 2
+    elif args.kernel == "after_verify":
+        # config 4's whole after_verify: context features (fc 20480 -> 4096 + hidden_norm) of T = 288 verified
+        # tokens, then the 5 draft layers' context K/V (W_kv GEMM + k_norm / RoPE / paged store)
+        from nanovllm_b200.dflash import after_verify
+        from nanovllm_b200.fused import rope_cache
+        T, layers, hidden, hkv, bs = 288, 5, 4096, 8, 256
+        gg = torch.Generator(device=device).manual_seed(0)
+        aux = torch.randn(T, 5 * hidden, device=device, generator=gg).bfloat16()
+        w_fc = (torch.randn(hidden, 5 * hidden, device=device, generator=gg) * 0.01).bfloat16()
+        hidden_norm = torch.ones(hidden, device=device).bfloat16()
+        w = (torch.randn(layers * 2 * hkv * 128, hidden, device=device, generator=gg) * 0.02).bfloat16()
+        k_norm = torch.ones(layers, 128, device=device).bfloat16()
+        cos_sin = rope_cache(128, 8192, 1000000.0, device)
+        positions = torch.randint(0, 8192, (T,), device=device, generator=gg)
+        slots = torch.randperm(64 * 16 * bs, device=device, generator=gg)[:T].to(torch.int32)
+        cache = torch.zeros(2, layers, 64 * 16, bs, hkv, 128, dtype=torch.bfloat16, device=device)
+        bufs = {"fc": torch.empty(T, hidden, dtype=torch.bfloat16, device=device),
+                "features": torch.empty(T, hidden, dtype=torch.bfloat16, device=device),
+                "kv": torch.empty(T, layers * 2 * hkv * 128, dtype=torch.bfloat16, device=device)}
+
+        def fn():
+            after_verify(aux, w_fc, hidden_norm, w, k_norm, cos_sin, positions, slots, cache, 1e-6, buffers=bufs)
+        # both weights + aux + fc / features / projection writes and reads + cache writes
+        algorithmic = (w_fc.numel() + w.numel() + aux.numel() + 4 * T * hidden + 2 * bufs["kv"].numel()
+                       + T * layers * 2 * hkv * 128) * 2
     else:
         from nanovllm_b200 import spec_sampler as S
         B = 64
@@ -413,7 +439,7 @@ def run_kernel(args) -> int:
     for _ in range(args.warmup):
         fn()
     timing = "events"
-    if args.kernel in ("attention", "ctx_store", "markov"):
+    if args.kernel in ("attention", "ctx_store", "after_verify", "markov"):
         # K calls captured in one CUDA graph and replayed, so the host's per-call work (tensor map encoding,
         # Python) does not pace the device; the reference captures its Markov rows in a graph the same way
         # (speculative.py:216-231)

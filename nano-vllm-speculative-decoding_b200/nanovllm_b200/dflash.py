@@ -11,6 +11,8 @@ DFlashDrafter.after_verify (nanovllm/engine/speculative.py:326-337) for every ve
 Here the five per-layer projections are one cuBLAS GEMM against the layers' stacked W_kv (a plain library GEMM),
 and every layer's k_norm + RoPE + paged scatter of K and V is a single kernel launch over (token, layer, head)
 rows (specdec_norm_rope_store with no query heads).  Slot -1 rows (padding) are skipped before any load.
+context_features (dflash.py:84-86, hidden_norm(fc(aux))) is the cuBLAS fc GEMM then this library's RMSNorm
+kernel; after_verify chains it with store_context_kv.
 """
 from __future__ import annotations
 
@@ -19,6 +21,30 @@ import torch
 from . import _lib
 from ._lib import check, ptr, require_cuda, stream_of
 from .fused import err_word
+from .fused import rmsnorm as fused_rmsnorm
+
+
+def context_features(aux: torch.Tensor, w_fc: torch.Tensor, norm_weight: torch.Tensor, eps: float, *,
+                     fc_out: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """DFlashDraftModel.context_features (dflash.py:84-86): hidden_norm(fc(aux)).  aux [T, len(aux layers) * H]
+    bf16, w_fc [H, len(aux layers) * H] bf16 (the fc projection is a cuBLAS GEMM), norm_weight [H]; returns the
+    normalised features [T, H] bf16 (the RMSNorm is this library's kernel)."""
+    require_cuda(aux, w_fc, norm_weight)
+    x = torch.matmul(aux, w_fc.t(), out=fc_out)
+    return fused_rmsnorm(x, norm_weight, eps, out=out)
+
+
+def after_verify(aux: torch.Tensor, w_fc: torch.Tensor, norm_weight: torch.Tensor, w_kv_stacked: torch.Tensor,
+                 k_norm: torch.Tensor, cos_sin: torch.Tensor, positions: torch.Tensor, slot_mapping: torch.Tensor,
+                 kv_cache: torch.Tensor, eps: float, *, buffers: dict | None = None) -> None:
+    """DFlashDrafter.after_verify's device work (speculative.py:326-337 -> dflash.py:84-96): the context features
+    of every verified position from the aux layers the verification exported, then every draft layer's context
+    K/V at slot_mapping.  buffers (optional, e.g. for CUDA graph capture): preallocated "fc" [T, H], "features"
+    [T, H] and "kv" [T, L * 2 * Hkv * 128] bf16."""
+    buffers = buffers or {}
+    features = context_features(aux, w_fc, norm_weight, eps, fc_out=buffers.get("fc"), out=buffers.get("features"))
+    store_context_kv(features, w_kv_stacked, k_norm, cos_sin, positions, slot_mapping, kv_cache, eps,
+                     kv_out=buffers.get("kv"))
 
 
 def stacked_kv_weight(layer_kv_weights: list[torch.Tensor]) -> torch.Tensor:

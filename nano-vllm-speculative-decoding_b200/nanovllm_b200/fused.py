@@ -26,13 +26,14 @@ def rope_cache(head_dim: int, max_position: int, base: float, device: torch.devi
     return torch.cat((freqs.cos(), freqs.sin()), dim=-1).contiguous().to(device)
 
 
-def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.Tensor | None = None):
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.Tensor | None = None, *,
+            out: torch.Tensor | None = None):
     """layernorm.py:16-40: without residual returns norm(x); with it returns (norm(x + residual), x + residual)."""
     device = require_cuda(x, weight, residual)
     width = x.shape[-1]
     T = x.numel() // width
     x = x.contiguous()
-    out = torch.empty_like(x)
+    out = torch.empty_like(x) if out is None else out
     res_out = torch.empty_like(x) if residual is not None else None
     check(_lib.lib().specdec_rmsnorm(ptr(x), ptr(None if residual is None else residual.contiguous()), ptr(weight),
                                      ptr(out), ptr(res_out), T, width, float(eps), stream_of(device)))

@@ -110,3 +110,38 @@ def test_rmsnorm_and_silu():
         y = silu_and_mul(gu).float().cpu().numpy()
         a, b = gu.float().cpu().numpy()[:, :inter], gu.float().cpu().numpy()[:, inter:]
         close_bf16(y, OC.bf16(a / (1 + np.exp(-a)) * b))
+
+
+def test_after_verify_context_features_then_store():
+    """after_verify's device work: context_features (fc GEMM + hidden_norm RMSNorm) then store_context_kv, at
+    the draft's shapes (5 aux layers of hidden 4096 -> 4096, 5 draft layers), against the oracle run on the same
+    GEMM outputs (the GEMMs are cuBLAS; the comparison isolates this library's kernels)."""
+    from nanovllm_b200.dflash import after_verify
+    from nanovllm_b200.fused import rope_cache
+    g = torch.Generator(device=DEV).manual_seed(21)
+    T, hidden, layers, hkv, blocks, bs = 96, 4096, 5, 8, 4, 256
+    aux = torch.randn(T, 5 * hidden, device=DEV, generator=g).bfloat16()
+    w_fc = (torch.randn(hidden, 5 * hidden, device=DEV, generator=g) * 0.01).bfloat16()
+    hidden_norm = (1.0 + 0.1 * torch.randn(hidden, device=DEV, generator=g)).bfloat16()
+    w_kv = (torch.randn(layers * 2 * hkv * 128, hidden, device=DEV, generator=g) * 0.02).bfloat16()
+    k_norm = (1.0 + 0.1 * torch.randn(layers, 128, device=DEV, generator=g)).bfloat16()
+    cos_sin = rope_cache(128, 8192, 1000000.0, DEV)
+    positions = torch.randint(0, 8192, (T,), device=DEV, generator=g)
+    slots = torch.randperm(blocks * bs, device=DEV, generator=g)[:T].to(torch.int32)
+    slots[::7] = -1
+    cache = torch.zeros(2, layers, blocks, bs, hkv, 128, dtype=torch.bfloat16, device=DEV)
+    buffers = {"fc": torch.empty(T, hidden, dtype=torch.bfloat16, device=DEV),
+               "features": torch.empty(T, hidden, dtype=torch.bfloat16, device=DEV),
+               "kv": torch.empty(T, layers * 2 * hkv * 128, dtype=torch.bfloat16, device=DEV)}
+    after_verify(aux, w_fc, hidden_norm, w_kv, k_norm, cos_sin, positions, slots, cache, 1e-6, buffers=buffers)
+    fc = buffers["fc"].float().cpu().numpy()
+    want_features = OC.rmsnorm(fc, hidden_norm.float().cpu().numpy(), 1e-6)
+    close_bf16(buffers["features"].float().cpu().numpy(), want_features)
+    want = np.zeros(cache.shape, dtype=np.float32)
+    kv_np = buffers["kv"].float().cpu().numpy()
+    width = 2 * hkv * 128
+    cs = cos_sin.cpu().numpy()
+    for layer in range(layers):
+        OC.norm_rope_store(kv_np[:, layer * width:(layer + 1) * width], hkv, k_norm[layer].float().cpu().numpy(), cs,
+                           positions.cpu().numpy(), slots.cpu().numpy(), want[0, layer], want[1, layer], 1e-6)
+    close_bf16(cache.float().cpu().numpy(), want)
