@@ -163,6 +163,31 @@ int specdec_norm_rope_store(const void* x, long long x_layer_stride, long long x
                             long long cache_layer_stride, long long num_slots, void* q_out, float eps, int* err,
                             void* stream);
 
+/* ------------------------------------------------------------------------------------------ kernel 5: context GEMM */
+/* The draft context path's projections (nanovllm/models/dflash.py:84-96: fc in context_features, the per-layer
+ * W_kv of store_context_kv) on the tensor cores: out[T, O] = x[T, K] . w[O, K]^T, bf16 operands and output (one
+ * rounding of the fp32 sum), row strides in elements (16-byte multiples).  1 <= T <= 288 tokens per call,
+ * O a multiple of 128, K a multiple of 64.  workspace: 256-byte aligned device bytes, zero-filled once before
+ * first use (the kernel leaves its counters zeroed), at least specdec_context_gemm_workspace_bytes(T, O); calls
+ * that share a workspace must not overlap on the GPU.  Waits that run out record a code in *err. */
+long long specdec_context_gemm_workspace_bytes(int T, int O);
+int specdec_context_gemm(const void* x, long long x_row_stride, const void* w, long long w_row_stride, int T, int O,
+                         int K, void* out, long long out_row_stride, void* workspace, long long workspace_bytes,
+                         int* err, void* stream);
+/* DFlashDraftModel.store_context_kv (dflash.py:88-96) fused: the same GEMM against the layers' stacked W_kv
+ * ([layers * 2 * Hkv * 128, K]: per layer its K rows then its V rows) with the projection never leaving the chip:
+ * each 128-row tile is one (layer, K|V, head); K rows get RMSNorm (k_norm [layers, 128], layer stride in
+ * elements) and RoPE at positions[t] (cos_sin [max_position, 128]: cos | sin), and every row is stored at slot
+ * slot_mapping[t] of k_cache / v_cache ([layers][num_slots][Hkv][128], layer stride in elements; slot -1
+ * skipped).  A position or slot out of range is skipped and recorded in *err (4, 3).  Workspace as for
+ * specdec_context_gemm with O = layers * 2 * Hkv * 128. */
+int specdec_context_kv_store(const void* x, long long x_row_stride, const void* w_kv, long long w_row_stride, int T,
+                             int layers, int num_kv_heads, int K, const void* k_norm, long long k_norm_layer_stride,
+                             const float* cos_sin, long long max_position, const long long* positions,
+                             const int* slot_mapping, void* k_cache, void* v_cache, long long cache_layer_stride,
+                             long long num_slots, float eps, void* workspace, long long workspace_bytes, int* err,
+                             void* stream);
+
 /* ------------------------------------------------------------------------------------------ verify forward helpers */
 /* RMSNorm.rms_forward / add_rms_forward (nanovllm/layers/layernorm.py:16-40): rows of `width` bf16 (a multiple of
  * 8, <= 8192).  With residual: s = x + residual, residual_out = s, out = norm(s) * weight; else out = norm(x). */

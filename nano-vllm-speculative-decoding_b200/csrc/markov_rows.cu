@@ -59,11 +59,11 @@ struct Args {
                             // zeroed probs; with it, probs stays zero elsewhere and only these are cleared
 };
 
-// Workspace: tickets and greedy keys (zeroed once, self-cleaning), then the pieces' candidate keys.
-constexpr long long kHeaderAlign = 256;
-__host__ __device__ inline long long ws_head_bytes(int B) {
-  return ((long long)B * (4 + 8) + kHeaderAlign - 1) / kHeaderAlign * kHeaderAlign;
-}
+// Workspace: tickets [kMaxRowsWs] and greedy keys [kMaxRowsWs] (zeroed once, self-cleaning) at fixed offsets, so
+// calls of any batch size share one workspace, then the pieces' candidate keys.
+constexpr long long kMaxRowsWs = 65536;
+constexpr long long kBestOffset = kMaxRowsWs * 4;
+__host__ __device__ inline long long ws_head_bytes(int) { return kMaxRowsWs * (4 + 8); }
 
 __device__ __forceinline__ float load_any(const void* p, int dt, long long i) {
   if (dt == kF32) return reinterpret_cast<const float*>(p)[i];
@@ -517,7 +517,7 @@ int specdec_markov_step(const void* logits, int logits_dtype, const void* bias, 
   a.gchunk = ((V + 7) / 8 + a.P - 1) / a.P;
   char* ws = static_cast<char*>(workspace);
   a.tickets = reinterpret_cast<unsigned*>(ws);
-  a.best = reinterpret_cast<unsigned long long*>(ws + (((long long)B * 4 + 7) / 8 * 8));
+  a.best = reinterpret_cast<unsigned long long*>(ws + kBestOffset);
   a.keys = reinterpret_cast<unsigned long long*>(ws + ws_head_bytes(B));
   markov_step_kernel<<<dim3(a.P, B), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
   SPECDEC_LAUNCH_CHECK();

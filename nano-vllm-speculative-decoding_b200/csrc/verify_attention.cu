@@ -781,11 +781,15 @@ static int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMa
   return kOk;
 }
 
-// Workspace: R * Hkv arrival counters (256-byte padded), then two piece slots per CTA.
+// Workspace: two piece slots per SM (a size fixed per device), then R * Hkv arrival counters (256-byte padded).
+// The counters sit at the same offset for calls of every shape, so a workspace zeroed once stays valid: every
+// call leaves the counters it used at zero, and no call's pieces overlap another call's counters.
+static long long partial_bytes(int sm_count) { return 2LL * sm_count * kPartialFloats * 4; }
 static long long counters_bytes(long long R, int Hkv) { return (R * Hkv * 4 + 255) / 256 * 256; }
-static long long workspace_bytes(long long R, int Hkv, int grid) {
-  return counters_bytes(R, Hkv) + 2LL * grid * kPartialFloats * 4;
+static long long workspace_bytes(long long R, int Hkv, int sm_count) {
+  return partial_bytes(sm_count) + counters_bytes(R, Hkv);
 }
+static_assert((kPartialFloats * 4 * 2) % 256 == 0, "counters stay 256-byte aligned");
 
 }  // namespace attention
 }  // namespace specdec
@@ -885,11 +889,11 @@ int specdec_paged_attention_ex(const void* q, long long T, long long q_row_strid
   if (int st = device_info(&info)) return st;
   const long long max_tiles = (long long)R * num_kv_heads * ((long long)W * block_size / kKeysPerTile);
   const int grid = (int)(max_tiles < info.sm_count ? max_tiles : info.sm_count);
-  const long long need = attention::workspace_bytes(R, num_kv_heads, grid);
+  const long long need = attention::workspace_bytes(R, num_kv_heads, info.sm_count);
   if (workspace_bytes < need)
     return set_error(kWorkspaceTooSmall, "attention workspace of %lld bytes, %lld needed", workspace_bytes, need);
-  a.counters = static_cast<int*>(workspace);
-  a.partial = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + counters_bytes(R, num_kv_heads));
+  a.partial = static_cast<float*>(workspace);
+  a.counters = reinterpret_cast<int*>(static_cast<unsigned char*>(workspace) + partial_bytes(info.sm_count));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool early = (flags & SPECDEC_ATTN_EARLY_LAUNCH) != 0;
   switch (G) {

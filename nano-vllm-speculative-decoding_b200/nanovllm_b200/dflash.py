@@ -8,11 +8,12 @@ DFlashDrafter.after_verify (nanovllm/engine/speculative.py:326-337) for every ve
         k = RoPE(positions, k_norm[layer](k))
         store_kvcache(k, v, kv_cache[0, layer], kv_cache[1, layer], slot_mapping)
 
-Here the five per-layer projections are one cuBLAS GEMM against the layers' stacked W_kv (a plain library GEMM),
-and every layer's k_norm + RoPE + paged scatter of K and V is a single kernel launch over (token, layer, head)
-rows (specdec_norm_rope_store with no query heads).  Slot -1 rows (padding) are skipped before any load.
-context_features (dflash.py:84-86, hidden_norm(fc(aux))) is the cuBLAS fc GEMM then this library's RMSNorm
-kernel; after_verify chains it with store_context_kv.
+store_context_kv projects with one cuBLAS GEMM against the layers' stacked W_kv and then runs every layer's
+k_norm + RoPE + paged scatter of K and V as one kernel over (token, layer, head) rows (specdec_norm_rope_store with
+no query heads); slot -1 rows (padding) are skipped.  context_features (dflash.py:84-86, hidden_norm(fc(aux))) is
+the cuBLAS fc GEMM then this library's RMSNorm; after_verify chains the two.  store_context_kv_fused and
+context_gemm run the same projections on this library's tcgen05 stream-K GEMM (the former with the norm / RoPE /
+store epilogue); both are verified against the oracle but slower than the cuBLAS path on these shapes.
 """
 from __future__ import annotations
 
@@ -24,14 +25,81 @@ from .fused import err_word
 from .fused import rmsnorm as fused_rmsnorm
 
 
+CONTEXT_GEMM_MAX_TOKENS = 288
+
+
+def context_gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """x [T, K] bf16 . w [O, K]^T -> [T, O] bf16 on this library's tcgen05 stream-K kernel (fp32 accumulation,
+    one rounding, deterministic); tokens go through in calls of at most 288.  Measured slower than cuBLAS on the
+    draft's shapes (the split tiles' fp32 pieces dominate), so the production path keeps cuBLAS."""
+    device = require_cuda(x, w, out)
+    if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
+        raise ValueError("the context GEMM takes bf16 operands")
+    T, K = x.shape
+    O = w.shape[0]
+    if x.stride(1) != 1 or w.stride(1) != 1:
+        raise ValueError("rows must be contiguous")
+    if out is None:
+        out = torch.empty(T, O, dtype=torch.bfloat16, device=device)
+    lib = _lib.lib()
+    with torch.cuda.device(device):
+        need = int(lib.specdec_context_gemm_workspace_bytes(min(T, CONTEXT_GEMM_MAX_TOKENS), O))
+    if need < 0:
+        raise _lib.SpecdecError(lib.specdec_last_error().decode())
+    ws = _lib.Workspace.get(device, need, name="context_gemm")
+    for t0 in range(0, T, CONTEXT_GEMM_MAX_TOKENS):
+        n = min(CONTEXT_GEMM_MAX_TOKENS, T - t0)
+        check(lib.specdec_context_gemm(ptr(x[t0:]), x.stride(0), ptr(w), w.stride(0), n, O, K, ptr(out[t0:]),
+                                       out.stride(0), ptr(ws), ws.numel(), ptr(err_word(device)),
+                                       stream_of(device)))
+    return out
+
+
 def context_features(aux: torch.Tensor, w_fc: torch.Tensor, norm_weight: torch.Tensor, eps: float, *,
                      fc_out: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
     """DFlashDraftModel.context_features (dflash.py:84-86): hidden_norm(fc(aux)).  aux [T, len(aux layers) * H]
-    bf16, w_fc [H, len(aux layers) * H] bf16 (the fc projection is a cuBLAS GEMM), norm_weight [H]; returns the
-    normalised features [T, H] bf16 (the RMSNorm is this library's kernel)."""
+    bf16, w_fc [H, len(aux layers) * H] bf16, norm_weight [H]; returns the normalised features [T, H] bf16.  The fc
+    projection is a cuBLAS GEMM (faster here than this library's context_gemm), the RMSNorm this library's kernel."""
     require_cuda(aux, w_fc, norm_weight)
     x = torch.matmul(aux, w_fc.t(), out=fc_out)
     return fused_rmsnorm(x, norm_weight, eps, out=out)
+
+
+def store_context_kv_fused(features: torch.Tensor, w_kv_stacked: torch.Tensor, k_norm: torch.Tensor,
+                           cos_sin: torch.Tensor, positions: torch.Tensor, slot_mapping: torch.Tensor,
+                           kv_cache: torch.Tensor, eps: float) -> None:
+    """store_context_kv (dflash.py:88-96) as one tcgen05 kernel: the stacked W_kv projection with the k_norm,
+    RoPE and paged store in its epilogue (the projection never goes to memory).  Arguments as store_context_kv.
+    Correct, but measured ~9x slower than store_context_kv at T = 288 (its per-16-token epilogue and the split
+    tiles' merges are latency-bound), so the production path keeps store_context_kv."""
+    device = require_cuda(features, w_kv_stacked, k_norm, cos_sin, positions, slot_mapping, kv_cache)
+    T, hidden = features.shape
+    _, layers, blocks, block_size, num_kv_heads, head_dim = kv_cache.shape
+    if head_dim != 128 or k_norm.shape != (layers, 128):
+        raise ValueError("ctx_store expects 128-dim heads and one k_norm row per layer")
+    if w_kv_stacked.shape != (layers * 2 * num_kv_heads * 128, hidden):
+        raise ValueError(f"stacked W_kv of shape {tuple(w_kv_stacked.shape)} does not match the cache")
+    if features.dtype != torch.bfloat16 or w_kv_stacked.dtype != torch.bfloat16:
+        raise ValueError("the fused context store takes bf16 features and weights")
+    features = features.contiguous()
+    k_norm = k_norm.contiguous()
+    positions = positions.to(torch.int64).contiguous()
+    slots = slot_mapping.to(torch.int32).contiguous()
+    k_cache, v_cache = kv_cache[0], kv_cache[1]
+    O = layers * 2 * num_kv_heads * 128
+    lib = _lib.lib()
+    with torch.cuda.device(device):
+        need = int(lib.specdec_context_gemm_workspace_bytes(min(T, CONTEXT_GEMM_MAX_TOKENS), O))
+    if need < 0:
+        raise _lib.SpecdecError(lib.specdec_last_error().decode())
+    ws = _lib.Workspace.get(device, need, name="context_gemm")
+    for t0 in range(0, T, CONTEXT_GEMM_MAX_TOKENS):
+        n = min(CONTEXT_GEMM_MAX_TOKENS, T - t0)
+        check(lib.specdec_context_kv_store(
+            ptr(features[t0:]), features.stride(0), ptr(w_kv_stacked), w_kv_stacked.stride(0), n, layers,
+            num_kv_heads, hidden, ptr(k_norm), k_norm.stride(0), ptr(cos_sin), cos_sin.shape[0], ptr(positions[t0:]),
+            ptr(slots[t0:]), ptr(k_cache), ptr(v_cache), k_cache.stride(0), blocks * block_size, float(eps), ptr(ws),
+            ws.numel(), ptr(err_word(device)), stream_of(device)))
 
 
 def after_verify(aux: torch.Tensor, w_fc: torch.Tensor, norm_weight: torch.Tensor, w_kv_stacked: torch.Tensor,
@@ -39,8 +107,8 @@ def after_verify(aux: torch.Tensor, w_fc: torch.Tensor, norm_weight: torch.Tenso
                  kv_cache: torch.Tensor, eps: float, *, buffers: dict | None = None) -> None:
     """DFlashDrafter.after_verify's device work (speculative.py:326-337 -> dflash.py:84-96): the context features
     of every verified position from the aux layers the verification exported, then every draft layer's context
-    K/V at slot_mapping.  buffers (optional, e.g. for CUDA graph capture): preallocated "fc" [T, H], "features"
-    [T, H] and "kv" [T, L * 2 * Hkv * 128] bf16."""
+    K/V at slot_mapping.  buffers (optional, e.g. for CUDA graph capture): preallocated "fc" and "features" [T, H]
+    and "kv" [T, L * 2 * Hkv * 128] bf16."""
     buffers = buffers or {}
     features = context_features(aux, w_fc, norm_weight, eps, fc_out=buffers.get("fc"), out=buffers.get("features"))
     store_context_kv(features, w_kv_stacked, k_norm, cos_sin, positions, slot_mapping, kv_cache, eps,

@@ -230,3 +230,25 @@ def test_early_launch_after_the_qk_store(A):
     q, kc, vc = caches[1]
     c2 = dict(c, q=q, k_cache=kc, v_cache=vc)
     np.testing.assert_allclose(outs[1].float().cpu().numpy(), oracle_out(c2), atol=ATOL, rtol=0)
+
+
+def test_workspace_shared_by_calls_of_different_shapes(A):
+    """One workspace, zeroed once, serves calls with different row counts: the split-item counters sit at a fixed
+    offset, past the pieces of every call, so a larger call's counters never land on a smaller call's pieces."""
+    rng = np.random.default_rng(11)
+    big = paged_case([8] * 64, rng.integers(800, 1200, size=64).tolist(), seed=61)
+    small = paged_case([8] * 9, rng.integers(2000, 4000, size=9).tolist(), seed=62)
+
+    def attend(c):
+        return A.paged_attention(c["q"], c["k_cache"], c["v_cache"], c["tables"], c["scale"], cu_seqlens_q=c["cu_q"],
+                                 cu_seqlens_k=c["cu_k"], max_seqlen_q=8)
+
+    first_big = run_verify(A, big)                   # zeroes the workspace, stores the new K/V, attends
+    A.store_kvcache(small["k"], small["v"], small["k_cache"], small["v_cache"], small["slots"])
+    for _ in range(2):
+        out_small = attend(small)
+        again_big = attend(big)
+        torch.cuda.synchronize()
+        assert torch.equal(again_big, first_big)
+    assert A.device_error(DEV) == 0
+    np.testing.assert_allclose(out_small.float().cpu().numpy(), oracle_out(small), atol=ATOL, rtol=0)

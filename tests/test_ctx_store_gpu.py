@@ -114,8 +114,8 @@ def test_rmsnorm_and_silu():
 
 def test_after_verify_context_features_then_store():
     """after_verify's device work: context_features (fc GEMM + hidden_norm RMSNorm) then store_context_kv, at
-    the draft's shapes (5 aux layers of hidden 4096 -> 4096, 5 draft layers), against the oracle run on the same
-    GEMM outputs (the GEMMs are cuBLAS; the comparison isolates this library's kernels)."""
+    the draft's shapes (5 aux layers of hidden 4096 -> 4096, 5 draft layers), against the oracle (fp32 products
+    rounded to bf16)."""
     from nanovllm_b200.dflash import after_verify
     from nanovllm_b200.fused import rope_cache
     g = torch.Generator(device=DEV).manual_seed(21)
@@ -135,13 +135,46 @@ def test_after_verify_context_features_then_store():
                "kv": torch.empty(T, layers * 2 * hkv * 128, dtype=torch.bfloat16, device=DEV)}
     after_verify(aux, w_fc, hidden_norm, w_kv, k_norm, cos_sin, positions, slots, cache, 1e-6, buffers=buffers)
     fc = buffers["fc"].float().cpu().numpy()
+    ref_fc = (aux.float() @ w_fc.float().t()).cpu().numpy()
+    assert np.all(np.abs(fc - ref_fc) <= np.abs(ref_fc) * 2 ** -8 + 1e-3 * np.abs(ref_fc).max())
     want_features = OC.rmsnorm(fc, hidden_norm.float().cpu().numpy(), 1e-6)
     close_bf16(buffers["features"].float().cpu().numpy(), want_features)
     want = np.zeros(cache.shape, dtype=np.float32)
+    # the projection against the fp32 product (cuBLAS sums in another order), then the oracle fed the same
+    # projection, so the cache comparison isolates this library's kernels
     kv_np = buffers["kv"].float().cpu().numpy()
+    ref_kv = (buffers["features"].float() @ w_kv.float().t()).cpu().numpy()
+    assert np.all(np.abs(kv_np - ref_kv) <= np.abs(ref_kv) * 2 ** -8 + 1e-3 * np.abs(ref_kv).max())
     width = 2 * hkv * 128
     cs = cos_sin.cpu().numpy()
     for layer in range(layers):
         OC.norm_rope_store(kv_np[:, layer * width:(layer + 1) * width], hkv, k_norm[layer].float().cpu().numpy(), cs,
                            positions.cpu().numpy(), slots.cpu().numpy(), want[0, layer], want[1, layer], 1e-6)
     close_bf16(cache.float().cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("T", [288, 7, 300])
+def test_fused_context_store_matches_the_unfused_path(T):
+    """store_context_kv_fused (one tcgen05 kernel) against store_context_kv (cuBLAS GEMM + norm/RoPE/store kernel):
+    the same cache rows, up to summation-order ulps of the projection; padding slots untouched."""
+    from nanovllm_b200.dflash import store_context_kv, store_context_kv_fused
+    from nanovllm_b200.fused import rope_cache
+    g = torch.Generator(device=DEV).manual_seed(T)
+    hidden, layers, hkv, blocks, bs = 4096, 5, 8, 4, 256
+    features = torch.randn(T, hidden, device=DEV, generator=g).bfloat16()
+    w = (torch.randn(layers * 2 * hkv * 128, hidden, device=DEV, generator=g) * 0.02).bfloat16()
+    k_norm = (1.0 + 0.1 * torch.randn(layers, 128, device=DEV, generator=g)).bfloat16()
+    cos_sin = rope_cache(128, 8192, 1000000.0, DEV)
+    positions = torch.randint(0, 8192, (T,), device=DEV, generator=g)
+    slots = torch.randperm(blocks * bs, device=DEV, generator=g)[:T].to(torch.int32)
+    slots[::5] = -1
+    a = torch.zeros(2, layers, blocks, bs, hkv, 128, dtype=torch.bfloat16, device=DEV)
+    b = torch.zeros_like(a)
+    store_context_kv(features, w, k_norm, cos_sin, positions, slots, a, 1e-6)
+    store_context_kv_fused(features, w, k_norm, cos_sin, positions, slots, b, 1e-6)
+    torch.cuda.synchronize()
+    got, want = b.float().cpu().numpy(), a.float().cpu().numpy()
+    ok = np.abs(got - want) <= ULP * np.maximum(np.abs(want), np.abs(got)) + 1e-6
+    assert ok.mean() >= 0.95
+    np.testing.assert_allclose(got, want, atol=2e-2, rtol=2 ** -6)     # a bf16 step of either projection
+    assert float((a != b).float().mean()) < 0.05

@@ -242,3 +242,30 @@ def test_markov_rows_fp32_and_ragged_vocab(dtype, V):
                                       round_fn=bf16 if dtype == torch.bfloat16 else (lambda x: x))
     assert drafts.cpu().numpy().tolist() == want.tolist()
     np.testing.assert_allclose(probs.cpu().numpy(), want_probs, rtol=1e-5, atol=1e-8)
+
+
+def test_markov_workspace_shared_by_batches_of_different_sizes():
+    """One Markov workspace (zeroed once) serves batches of different sizes: the per-row tickets and greedy keys
+    sit at fixed offsets, so a call never finds another call's candidate keys in its tickets."""
+    from nanovllm_b200.markov import markov_rows, num_candidates
+    k, V = 3, 20000
+    g = torch.Generator(device=DEV).manual_seed(12)
+    table = (torch.randn(16, V, device=DEV, generator=g)).bfloat16()
+    head = lambda prev: table[prev % 16]
+    runs = {}
+    for B in (3, 40, 3, 40):
+        gB = torch.Generator(device=DEV).manual_seed(B)
+        logits = (torch.randn(B, k, V, device=DEV, generator=gB) * 2).bfloat16()
+        samp = sampling_of([1.0] * B, [30] * B, [1.0] * B)
+        cand = num_candidates(samp.max_top_k, samp.all_top_k, V)
+        noise = torch.empty(B, k, cand, device=DEV).exponential_(generator=gB).clamp_min_(1e-10)
+        prev = torch.randint(V, (B,), device=DEV, generator=gB)
+        drafts = torch.empty(B, k, dtype=torch.int64, device=DEV)
+        probs = torch.empty(B, k, V, device=DEV)
+        markov_rows(logits, prev, samp, noise, drafts, probs, cand, head)
+        greedy = torch.empty(B, k, dtype=torch.int64, device=DEV)
+        markov_rows(logits, prev, None, None, greedy, None, 0, head)
+        torch.cuda.synchronize()
+        if B in runs:
+            assert torch.equal(drafts, runs[B][0]) and torch.equal(greedy, runs[B][1])
+        runs[B] = (drafts, greedy)
