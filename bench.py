@@ -48,7 +48,8 @@ def parse_args():
     p.add_argument("--batch", type=int, default=64)
     p.add_argument("--ctx", type=int, default=1000, help="mean context length (tokens before the verified ones)")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--kernel", choices=["attention", "accept", "accept_topk", "markov", "ctx_store", "after_verify"],
+    p.add_argument("--kernel", choices=["attention", "accept", "accept_topk", "accept_greedy", "sample", "markov",
+                                        "ctx_store", "after_verify"],
                    default=None,
                    help="time one kernel alone on its benchmark config (attention: config 2, accept: config 3's "
                         "logits) instead of the round; used for profiling")
@@ -420,6 +421,26 @@ def run_kernel(args) -> int:
         # both weights + aux + fc / features / projection writes and reads + cache writes
         algorithmic = (w_fc.numel() + w.numel() + aux.numel() + 4 * T * hidden + 2 * bufs["kv"].numel()
                        + T * layers * 2 * hkv * 128) * 2
+    elif args.kernel == "accept_greedy":
+        # config 3's greedy accept: 64 requests x 8 verified rows of bf16 logits, argmax prefix match
+        from nanovllm_b200 import spec_sampler as S
+        B = 64
+        logits = (torch.randn(B * 8, V, device=device) * 3).bfloat16()
+        drafts = torch.randint(V, (B, 7), device=device)
+
+        def fn():
+            S.accept_greedy(logits.view(B, 8, V), drafts)
+        algorithmic = logits.numel() * 2                       # the logits once
+    elif args.kernel == "sample":
+        # the exponential race of a [64, V] fp32 distribution with in-kernel Exp(1) draws (spec_sampler.sample)
+        from nanovllm_b200 import spec_sampler as S
+        B = 64
+        w = torch.softmax(torch.randn(B, V, device=device) * 3, -1)
+        gen = torch.Generator(device=device).manual_seed(0)
+
+        def fn():
+            S.sample(w, gen)
+        algorithmic = w.numel() * 4                            # the weights once (the draws are generated)
     else:
         from nanovllm_b200 import spec_sampler as S
         B = 64
