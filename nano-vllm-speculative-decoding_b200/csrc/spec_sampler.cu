@@ -1275,9 +1275,55 @@ __global__ void __launch_bounds__(kThreads) greedy_kernel(Args a) {
   const int hi = min((long long)lo + a.chunk, a.V);
   const T* row = reinterpret_cast<const T*>(a.x) + (long long)t * a.V;
   unsigned long long best = 0ull;
-  for (int v = lo + threadIdx.x; v < hi; v += kThreads) {
-    unsigned long long kk = argmax_key(to_f32(row[v]), (unsigned)v);
-    best = kk > best ? kk : best;
+  bool done = false;
+  if constexpr (sizeof(T) == 2) {
+    if (a.vec_ok) {
+      // 16-byte groups of 8 (lo, hi multiples of 8): the largest 16-bit ordered key of each group by SIMD
+      // halfword maxima (widening to fp32 is exact, so this is the order ordered_key gives the fp32 values), the
+      // first group holding the thread's maximum kept, then the first element of that group with it
+      const uint4* groups = reinterpret_cast<const uint4*>(row);
+      unsigned best16 = 0u;
+      int best_g = -1;
+      auto okey2 = [](unsigned w) {      // two 16-bit ordered keys: negative values inverted, positive ones flagged
+        return w ^ ((((w >> 15) & 0x00010001u) * 0x7fffu) | 0x80008000u);
+      };
+      constexpr int kU = 4;
+      const int ng = hi / 8;
+      for (int g0 = lo / 8 + threadIdx.x; g0 < ng; g0 += kU * kThreads) {
+        uint4 w[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int g = g0 + u * kThreads;
+          w[u] = g < ng ? ldg16(groups + g) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {   // ascending g: a later group replaces the kept one only when larger
+          const int g = g0 + u * kThreads;
+          const unsigned m2 = __vmaxu2(__vmaxu2(okey2(w[u].x), okey2(w[u].y)), __vmaxu2(okey2(w[u].z), okey2(w[u].w)));
+          const unsigned gm = max(m2 & 0xffffu, m2 >> 16);
+          if (g < ng && (gm > best16 || best_g < 0)) { best16 = gm; best_g = g; }
+        }
+      }
+      if (best_g >= 0) {
+        const uint4 w = ldg16(groups + best_g);
+        const unsigned words[4] = {w.x, w.y, w.z, w.w};
+        int e = 7;
+#pragma unroll
+        for (int i = 7; i >= 0; --i) {
+          const unsigned k = (okey2(words[i >> 1]) >> ((i & 1) * 16)) & 0xffffu;
+          if (k == best16) e = i;
+        }
+        const int v = best_g * 8 + e;
+        best = argmax_key(to_f32(row[v]), (unsigned)v);
+      }
+      done = true;
+    }
+  }
+  if (!done) {
+    for (int v = lo + threadIdx.x; v < hi; v += kThreads) {
+      unsigned long long kk = argmax_key(to_f32(row[v]), (unsigned)v);
+      best = kk > best ? kk : best;
+    }
   }
   best = warp_max_u64(best);
   if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = best;
@@ -1529,6 +1575,7 @@ int specdec_accept_greedy(const void* logits, int dtype, long long T, long long 
   Args a{};
   a.x = logits; a.T = T; a.V = V; a.dtype = dtype; a.drafts = drafts; a.B = (int)B; a.k = (int)k;
   a.lens = verified_lens; a.n_accept = n_accept; a.tail = tail;
+  a.vec_ok = aligned16(logits) && ((V * (long long)dtype_bytes(dtype)) % 16 == 0);
   choose_chunks(a, info);
   bind_workspace(a, workspace);
   cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -203,6 +203,32 @@ def test_full_vocab_greedy_matches_oracle(S):
     assert tail.cpu().numpy().tolist() == want_tail.tolist()
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("vocab", [4096, 4099, V_FULL])
+def test_greedy_ties_and_infinities(S, dtype, vocab):
+    """Rows of few distinct values (many tied maxima, the first index wins), rows whose maximum is +inf, rows of
+    -inf only; 16-byte groups when V * size is a multiple of 16, elementwise loads otherwise."""
+    batch, k = 6, 3
+    gen = torch.Generator().manual_seed(vocab)
+    rows = batch * (k + 1)
+    logits = torch.randint(-3, 4, (rows, vocab), generator=gen).to(torch.float32)
+    logits[1, vocab // 2] = float("inf")
+    logits[1, vocab - 1] = float("inf")
+    logits[5] = float("-inf")
+    logits[9, :] = 2.0
+    logits[13, -1] = 7.0
+    logits = logits.to(DEV, dtype)
+    target = logits.float().argmax(-1).view(batch, k + 1)
+    drafts = torch.randint(0, vocab, (batch, k), generator=gen).to(DEV)
+    for b in range(batch):      # agree with the target on a prefix of length b % (k + 1)
+        drafts[b, : b % (k + 1)] = target[b, : b % (k + 1)]
+    n_accept, tail = S.accept_greedy(logits.view(batch, k + 1, vocab), drafts)
+    want_n, want_tail = O.accept_greedy_varlen(logits.float().cpu().numpy(), drafts.cpu().numpy(),
+                                               np.full(batch, k + 1))
+    assert n_accept.cpu().numpy().tolist() == want_n.tolist()
+    assert tail.cpu().numpy().tolist() == want_tail.tolist()
+
+
 def test_fixed_length_entry_points(S):
     batch, k = 8, 7
     logits, q, drafts, lens, samp = synthetic_round(S, batch, k, 4099, torch.float32, False, seed=8)
