@@ -49,7 +49,7 @@ def parse_args():
     p.add_argument("--ctx", type=int, default=1000, help="mean context length (tokens before the verified ones)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--kernel", choices=["attention", "accept", "accept_topk", "accept_greedy", "sample", "markov",
-                                        "ctx_store", "after_verify"],
+                                        "ctx_store", "after_verify", "attention_tp"],
                    default=None,
                    help="time one kernel alone on its benchmark config (attention: config 2, accept: config 3's "
                         "logits) instead of the round; used for profiling")
@@ -483,11 +483,123 @@ def run_kernel(args) -> int:
     return 0
 
 
+def run_attention_tp(args) -> int:
+    """KV-head tensor-parallel verify attention (benchmark config 5's TP mode), one rank per GPU under torchrun:
+    B rows x 8 verify positions (T = 8B), 32 / 8 heads of 128, contexts ~ctx in 256-slot blocks (random block
+    permutation); each of N ranks holds Hkv/N KV heads of every row.  One layer = this rank's K/V store + the
+    paged attention over its heads + the in-place NCCL all-gather of the outputs + the head interleave.  Timed as a
+    CUDA graph of K layers over 4 rotating caches (beyond L2), 3 replays, max over ranks; the local store +
+    attention alone is timed the same way, so the difference is the exchange."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    from nanovllm_b200.context import reset_context, set_context
+    from nanovllm_b200.replicas import barrier, reduce_scalar
+    from nanovllm_b200.tp_attention import TPAttention
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    B, H, Hkv, D, bs, nq = args.batch, 32, 8, 128, 256, K_DRAFTS + 1
+    g = torch.Generator().manual_seed(0)                 # the same rows on every rank
+    ctx = torch.randint(max(args.ctx - 50, 1), args.ctx + 51, (B,), generator=g).tolist()
+    k_lens = [c + nq for c in ctx]
+    nb = [math.ceil(k / bs) for k in k_lens]
+    NB = sum(nb) + 1
+    perm = torch.randperm(NB - 1, generator=g).tolist()
+    tables = torch.full((B, max(nb)), NB - 1, dtype=torch.int32)
+    used = 0
+    for r, n in enumerate(nb):
+        tables[r, :n] = torch.tensor(perm[used:used + n])
+        used += n
+    slots = [int(tables[r, p // bs]) * bs + p % bs for r in range(B) for p in range(ctx[r], k_lens[r])]
+    m = TPAttention(H, D, D ** -0.5, Hkv)
+    Hl, Hkl, T = H // m.world, Hkv // m.world, B * nq
+    copies = 4
+    caches = []
+    for _ in range(copies):
+        pair = []
+        for _kv in range(2):
+            c = torch.empty(NB, bs, Hkl, D, dtype=torch.bfloat16, device=device)
+            c.normal_()
+            pair.append(c)
+        caches.append(pair)
+    q = torch.randn(T, Hl, D, device=device).bfloat16()
+    k_new = torch.randn(T, Hkl, D, device=device).bfloat16()
+    v_new = torch.randn(T, Hkl, D, device=device).bfloat16()
+    out = torch.empty(T, H, D, dtype=torch.bfloat16, device=device)
+    cu_q = torch.arange(0, T + 1, nq, dtype=torch.int32, device=device)
+    cu_k = torch.tensor([0] + torch.tensor(k_lens).cumsum(0).tolist(), dtype=torch.int32, device=device)
+    set_context(True, cu_q, cu_k, nq, max(k_lens), torch.tensor(slots, dtype=torch.int32, device=device), None,
+                tables.to(device))
+    state = {"i": 0}
+
+    def bind():
+        m.k_cache, m.v_cache = caches[state["i"] % copies]
+        state["i"] += 1
+
+    def layer():
+        bind()
+        m(q, k_new, v_new, out=out)
+
+    def local_only():
+        bind()
+        m.local(q, k_new, v_new, out=m.gather_buffer(T, device)[m.rank])
+
+    for _ in range(max(args.warmup, 3)):
+        layer()
+        local_only()
+    barrier()
+    steps = args.steps
+    graphs = {}
+    for name, fn in (("tp", layer), ("local", local_only)):
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+            for _ in range(steps):
+                fn()
+        graphs[name] = graph
+    barrier()
+    times = {}
+    with ClockSampler(local_rank) as clocks:
+        for name in ("tp", "local", "tp", "local"):
+            graphs[name].replay()
+            barrier()
+            times[name] = reduce_scalar(time_events(torch, graphs[name].replay, 3) / steps, "max")
+    barrier()
+    reset_context()
+    graphs.clear()                                       # graphs holding NCCL calls go before the group
+    keys = sum(k_lens)
+    local_bytes = keys * Hkl * D * 2 * 2 + 2 * T * Hl * D * 2 + 2 * T * Hkl * D * 2   # K/V + q, out + stores
+    pk = peaks()
+    achieved = local_bytes / (times["local"] * 1e-6) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "kernel": "attention_tp", "n_gpus": world, "rows": B, "verify_positions": nq, "ctx_mean": args.ctx,
+            "heads": H, "kv_heads_per_gpu": Hkl, "us_per_layer": round(times["tp"], 2),
+            "local_attention_us": round(times["local"], 2),
+            "exchange_us": round(times["tp"] - times["local"], 2),
+            "per_gpu_algorithmic_bytes": local_bytes, "local_achieved_GBps": round(achieved, 1),
+            "peak_GBps": pk["hbm_gbs"], "local_frac": round(achieved / pk["hbm_gbs"], 4), "peak_source": pk["source"],
+            "nvlink_bytes_in_per_gpu": 2 * T * H * D * (world - 1) // world,
+            "timing": f"CUDA graph of {steps} layers over {copies} rotating caches, 3 replays, max over ranks",
+            "clocks": clocks.summary()}), flush=True)
+    del caches
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 # ---------------------------------------------------------------------------------------------- our arm
 def main() -> int:
     args = parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.kernel == "attention_tp":
+        return run_attention_tp(args)
     if args.kernel is not None:
         return run_kernel(args)
     import torch

@@ -94,6 +94,10 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
     R, W = tables.shape
     if out is None:
         out = torch.empty(T, H, D, dtype=torch.bfloat16, device=device)
+    elif (out.shape != (T, H, D) or out.dtype != torch.bfloat16 or out.device != device or out.stride(2) != 1
+          or out.stride(1) != D):
+        raise ValueError(f"out must be a bf16 [{T}, {H}, {D}] tensor on {device} with dense heads "
+                         f"(got {out.dtype} {tuple(out.shape)} strides {out.stride()})")
     if cu_seqlens_q is not None:
         cq = cu_seqlens_q.to(torch.int32).contiguous()
         ck = cu_seqlens_k.to(torch.int32).contiguous()
@@ -128,7 +132,10 @@ class Attention(nn.Module):
         self.num_kv_heads = num_kv_heads
         self.k_cache = self.v_cache = torch.tensor([])
 
-    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor | None = None
+                ) -> torch.Tensor:
+        """The reference's forward(q, k, v); out optionally names the [T, H, D] bf16 tensor to write (rows may be
+        strided), which the tensor-parallel mode uses to write straight into its all-gather buffer."""
         context = get_context()
         k_cache, v_cache = self.k_cache, self.v_cache
         if k_cache.numel() and v_cache.numel():
@@ -139,7 +146,7 @@ class Attention(nn.Module):
                 raise NotImplementedError("prefill without a block table is outside the B200 verify/accept path")
             return paged_attention(q, k_cache, v_cache, context.block_tables, self.scale,
                                    cu_seqlens_q=context.cu_seqlens_q, cu_seqlens_k=context.cu_seqlens_k,
-                                   max_seqlen_q=context.max_seqlen_q, causal=True)
+                                   max_seqlen_q=context.max_seqlen_q, causal=True, out=out)
         return paged_attention(q, k_cache, v_cache, context.block_tables, self.scale,
                                context_lens=context.context_lens, query_len_per_seq=context.query_len_per_seq,
-                               causal=context.causal)
+                               causal=context.causal, out=out)
