@@ -487,9 +487,10 @@ def run_attention_tp(args) -> int:
     """KV-head tensor-parallel verify attention (benchmark config 5's TP mode), one rank per GPU under torchrun:
     B rows x 8 verify positions (T = 8B), 32 / 8 heads of 128, contexts ~ctx in 256-slot blocks (random block
     permutation); each of N ranks holds Hkv/N KV heads of every row.  One layer = this rank's K/V store + the
-    paged attention over its heads + the in-place NCCL all-gather of the outputs + the head interleave.  Timed as a
-    CUDA graph of K layers over 4 rotating caches (beyond L2), 3 replays, max over ranks; the local store +
-    attention alone is timed the same way, so the difference is the exchange."""
+    paged attention over its heads + the in-place NCCL all-gather of the outputs + the head interleave; with N > 1
+    also the peer-store exchange (the kernel stores every tile into all ranks' symmetric output buffers, then one
+    bounded cross-GPU barrier).  Timed as a CUDA graph of K layers over 4 rotating caches (beyond L2), 3 replays,
+    max over ranks; the local store + attention alone is timed the same way, so the difference is the exchange."""
     import datetime
     import torch
     import torch.distributed as dist
@@ -516,8 +517,12 @@ def run_attention_tp(args) -> int:
         tables[r, :n] = torch.tensor(perm[used:used + n])
         used += n
     slots = [int(tables[r, p // bs]) * bs + p % bs for r in range(B) for p in range(ctx[r], k_lens[r])]
+    T = B * nq
     m = TPAttention(H, D, D ** -0.5, Hkv)
-    Hl, Hkl, T = H // m.world, Hkv // m.world, B * nq
+    modules = {"tp": m}
+    if m.world > 1:        # the fused exchange: stores into the peers' symmetric buffers + bounded barrier
+        modules["tp_peer"] = TPAttention(H, D, D ** -0.5, Hkv, exchange="peer", max_tokens=T, device=device)
+    Hl, Hkl = H // m.world, Hkv // m.world
     copies = 4
     caches = []
     for _ in range(copies):
@@ -530,32 +535,35 @@ def run_attention_tp(args) -> int:
     q = torch.randn(T, Hl, D, device=device).bfloat16()
     k_new = torch.randn(T, Hkl, D, device=device).bfloat16()
     v_new = torch.randn(T, Hkl, D, device=device).bfloat16()
-    out = torch.empty(T, H, D, dtype=torch.bfloat16, device=device)
     cu_q = torch.arange(0, T + 1, nq, dtype=torch.int32, device=device)
     cu_k = torch.tensor([0] + torch.tensor(k_lens).cumsum(0).tolist(), dtype=torch.int32, device=device)
     set_context(True, cu_q, cu_k, nq, max(k_lens), torch.tensor(slots, dtype=torch.int32, device=device), None,
                 tables.to(device))
     state = {"i": 0}
 
-    def bind():
-        m.k_cache, m.v_cache = caches[state["i"] % copies]
+    def bind(module):
+        module.k_cache, module.v_cache = caches[state["i"] % copies]
         state["i"] += 1
 
-    def layer():
-        bind()
-        m(q, k_new, v_new, out=out)
+    def layer_fn(module):
+        def layer():
+            bind(module)
+            module(q, k_new, v_new)
+        return layer
 
     def local_only():
-        bind()
+        bind(m)
         m.local(q, k_new, v_new, out=m.gather_buffer(T, device)[m.rank])
 
+    fns = {name: layer_fn(module) for name, module in modules.items()}
+    fns["local"] = local_only
     for _ in range(max(args.warmup, 3)):
-        layer()
-        local_only()
+        for fn in fns.values():
+            fn()
     barrier()
     steps = args.steps
     graphs = {}
-    for name, fn in (("tp", layer), ("local", local_only)):
+    for name, fn in fns.items():
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, capture_error_mode="thread_local"):
             for _ in range(steps):
@@ -564,11 +572,12 @@ def run_attention_tp(args) -> int:
     barrier()
     times = {}
     with ClockSampler(local_rank) as clocks:
-        for name in ("tp", "local", "tp", "local"):
+        for name in list(fns) * 2:                       # each timed twice; the second timing is kept
             graphs[name].replay()
             barrier()
             times[name] = reduce_scalar(time_events(torch, graphs[name].replay, 3) / steps, "max")
     barrier()
+    peer_status = modules["tp_peer"].peer_error() if "tp_peer" in modules else 0
     reset_context()
     graphs.clear()                                       # graphs holding NCCL calls go before the group
     keys = sum(k_lens)
@@ -581,6 +590,9 @@ def run_attention_tp(args) -> int:
             "heads": H, "kv_heads_per_gpu": Hkl, "us_per_layer": round(times["tp"], 2),
             "local_attention_us": round(times["local"], 2),
             "exchange_us": round(times["tp"] - times["local"], 2),
+            "peer_store_us_per_layer": round(times["tp_peer"], 2) if "tp_peer" in times else None,
+            "peer_store_exchange_us": round(times["tp_peer"] - times["local"], 2) if "tp_peer" in times else None,
+            "peer_barrier_status": peer_status,
             "per_gpu_algorithmic_bytes": local_bytes, "local_achieved_GBps": round(achieved, 1),
             "peak_GBps": pk["hbm_gbs"], "local_frac": round(achieved / pk["hbm_gbs"], 4), "peak_source": pk["source"],
             "nvlink_bytes_in_per_gpu": 2 * T * H * D * (world - 1) // world,

@@ -125,6 +125,34 @@ int specdec_paged_attention_ex(const void* q, long long T, long long q_row_strid
                                int max_seqlen_q, float softmax_scale, int causal, void* out, long long out_row_stride,
                                void* workspace, long long workspace_bytes, int* err, unsigned flags, void* stream);
 
+/* specdec_paged_attention_ex writing its output to num_outs (1 .. 8) destinations with the same offsets and row
+ * stride: outs is a HOST array of device addresses, each a [T, H, 128] bf16 output (this GPU's memory, or a peer
+ * GPU's memory mapped into this process).  For the KV-head tensor-parallel verify attention with peer stores:
+ * under the reference's head split (nanovllm/models/qwen3.py:29-35, nanovllm/layers/linear.py:92) rank r attends
+ * with its H/N heads and passes every rank's [T, H_total, 128] output at head offset r*H/N (out_row_stride =
+ * H_total * 128), so each finished tile crosses NVLink as it is stored and no all-gather follows; the caller
+ * orders the peers' reads after a cross-GPU barrier.  Replaces Attention.forward (attention.py:59-77) followed by
+ * the gather of the heads. */
+int specdec_paged_attention_multi(const void* q, long long T, long long q_row_stride, int num_heads,
+                                  int num_kv_heads, int head_dim, const void* k_cache, const void* v_cache,
+                                  long long num_slots, int block_size, const int* cu_seqlens_q,
+                                  const int* cu_seqlens_k, const int* context_lens, int q_per_seq, int R,
+                                  const int* block_tables, int W, int max_seqlen_q, float softmax_scale, int causal,
+                                  void* const* outs, int num_outs, long long out_row_stride, void* workspace,
+                                  long long workspace_bytes, int* err, unsigned flags, void* stream);
+
+/* Cross-GPU barrier of the peer-store tensor-parallel verify attention (the step that replaces the all-gather of
+ * the heads after Attention.forward, nanovllm/layers/attention.py:59-77, under the head split of
+ * nanovllm/models/qwen3.py:29-35).  flags: HOST array of `world` device addresses, flags[t] = rank t's array of 8
+ * uint32 arrival words (peer memory mapped into this process; all zero before the first barrier of a group);
+ * epoch: this rank's uint32 counter in device memory (zero at first, advanced by the kernel, so a captured
+ * launch replays correctly).  One block signals every rank (system-scope release after a system fence) and
+ * waits for every rank's signal of the same epoch; a wait past timeout_ns sets *err = 21 and returns.  Every
+ * rank must call it the same number of times, each on its own GPU: barriers of several ranks never share one
+ * GPU (nothing makes separate launches run concurrently). */
+int specdec_peer_barrier(void* const* flags, int world, int rank, unsigned* epoch, long long timeout_ns, int* err,
+                         void* stream);
+
 /* ------------------------------------------------------------------------------------------ kernel 3: Markov rows */
 /* One row step of DFlashDrafter._markov_rows (nanovllm/engine/speculative.py:163-184) for every batch row: with
  * row_logits = logits[:, row] + bias (bias = markov_head(prev), [B, V]; rounded to bf16 when round_bf16):

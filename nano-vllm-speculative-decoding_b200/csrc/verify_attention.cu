@@ -64,6 +64,15 @@ constexpr int kErrTimeoutQ = 11, kErrTimeoutK = 12, kErrTimeoutV = 13, kErrTimeo
 // One piece of a split item: O^T columns (unnormalised, relative to the piece's running maxima) then the maxima m
 // and the sums l of the 32 columns.
 constexpr int kPartialFloats = kCols * kHeadDim + 2 * kCols;
+constexpr int kMaxOuts = 8;            // output destinations of one launch (one per rank of an 8-GPU node)
+
+// Destinations beyond Args::out, written with the same offsets by the kPeers instantiation only (the peer-store
+// tensor-parallel mode: every peer's [T, H, D] output, mapped into this process, this rank's head offset folded
+// into the base).  A separate parameter, so the single-output kernel's code and Args are untouched.
+struct PeerOuts {
+  __nv_bfloat16* out[kMaxOuts - 1];
+  int n;                     // 0 .. kMaxOuts - 1
+};
 constexpr float kNegBig = -1.0e30f;    // start value of the running maxima (finite: no -inf arithmetic)
 
 struct Args {
@@ -78,7 +87,7 @@ struct Args {
   float scale_log2;          // softmax_scale * log2(e)
   int causal;
   __nv_bfloat16* out;        // [T, H, D]
-  long long out_row_stride;  // elements between tokens of out
+  long long out_row_stride;  // elements between tokens of out (and of every PeerOuts destination)
   int* counters;             // [R * Hkv] arrivals at split items; zero between launches (the last arrival resets)
   float* partial;            // [2 * gridDim.x][kPartialFloats]: slot 2c = CTA c's first item, 2c + 1 its last
   int* err;                  // global error word (0 = ok)
@@ -223,11 +232,12 @@ struct Cursor {
 
 __device__ __forceinline__ long long ceil_div(long long x, long long y) { return (x + y - 1) / y; }
 
-template <int G>
+template <int G, bool kPeers>
 __global__ void __launch_bounds__(kThreads, 1)
     verify_attention_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                             const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap kmap32,
-                            const __grid_constant__ CUtensorMap vmap32, const Args a) {
+                            const __grid_constant__ CUtensorMap vmap32, const Args a,
+                            const __grid_constant__ PeerOuts peers) {
   constexpr int QMAX = kCols / G;     // query positions per row this build packs
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -684,10 +694,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < 16; ++j) {
         const int p = (cb + j) / G, gq = (cb + j) % G;
         const float inv = __shfl_sync(0xffffffffu, inv_lane, j);
-        if (p < ql)
-          a.out[(long long)(wk.r.q_start + p) * a.out_row_stride + (long long)(wk.h * G + gq) * kHeadDim + d] =
-              __float2bfloat16_rn(o[j] * inv);
+        if (p < ql) {
+          const long long off =
+              (long long)(wk.r.q_start + p) * a.out_row_stride + (long long)(wk.h * G + gq) * kHeadDim + d;
+          const __nv_bfloat16 value = __float2bfloat16_rn(o[j] * inv);
+          a.out[off] = value;
+          if constexpr (kPeers) {
+#pragma unroll
+            for (int t = 0; t < kMaxOuts - 1; ++t)   // unrolled: static parameter reads
+              if (t < peers.n) peers.out[t][off] = value;
+          }
+        }
       }
+      // peer stores ordered (system scope) before anything this thread does later, the barrier's signal included
+      if constexpr (kPeers) __threadfence_system();
     }
   }
   tc_fence_before();
@@ -757,12 +777,13 @@ static int make_map(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1
   return kOk;
 }
 
-template <int G>
+template <int G, bool kPeers>
 static int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const CUtensorMap& km32,
-                  const CUtensorMap& vm32, const Args& a, int grid, bool early, cudaStream_t stream) {
+                  const CUtensorMap& vm32, const Args& a, const PeerOuts& peers, int grid, bool early,
+                  cudaStream_t stream) {
   static bool configured = false;
   if (!configured) {
-    SPECDEC_CUDA_TRY(cudaFuncSetAttribute(verify_attention_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    SPECDEC_CUDA_TRY(cudaFuncSetAttribute(verify_attention_kernel<G, kPeers>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           kSmemBytes));
     configured = true;
   }
@@ -776,7 +797,7 @@ static int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMa
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = early ? 1 : 0;
-  SPECDEC_CUDA_TRY(cudaLaunchKernelEx(&cfg, verify_attention_kernel<G>, qm, km, vm, km32, vm32, a));
+  SPECDEC_CUDA_TRY(cudaLaunchKernelEx(&cfg, verify_attention_kernel<G, kPeers>, qm, km, vm, km32, vm32, a, peers));
   SPECDEC_LAUNCH_CHECK();
   return kOk;
 }
@@ -825,15 +846,19 @@ long long specdec_attention_workspace_bytes(int R, int num_kv_heads) {
   return attention::workspace_bytes(R, num_kv_heads, info.sm_count);
 }
 
-int specdec_paged_attention_ex(const void* q, long long T, long long q_row_stride, int num_heads, int num_kv_heads,
-                               int head_dim, const void* k_cache, const void* v_cache, long long num_slots,
-                               int block_size, const int* cu_seqlens_q, const int* cu_seqlens_k,
-                               const int* context_lens, int q_per_seq, int R, const int* block_tables, int W,
-                               int max_seqlen_q, float softmax_scale, int causal, void* out, long long out_row_stride,
-                               void* workspace, long long workspace_bytes, int* err, unsigned flags, void* stream) {
+int specdec_paged_attention_multi(const void* q, long long T, long long q_row_stride, int num_heads,
+                                  int num_kv_heads, int head_dim, const void* k_cache, const void* v_cache,
+                                  long long num_slots, int block_size, const int* cu_seqlens_q,
+                                  const int* cu_seqlens_k, const int* context_lens, int q_per_seq, int R,
+                                  const int* block_tables, int W, int max_seqlen_q, float softmax_scale, int causal,
+                                  void* const* outs, int num_outs, long long out_row_stride, void* workspace,
+                                  long long workspace_bytes, int* err, unsigned flags, void* stream) {
   using namespace attention;
   SPECDEC_CHECK_ARG((flags & ~(unsigned)SPECDEC_ATTN_EARLY_LAUNCH) == 0, "unknown flags 0x%x", flags);
-  SPECDEC_CHECK_ARG(q && k_cache && v_cache && block_tables && out && workspace && err, "null pointer argument");
+  SPECDEC_CHECK_ARG(outs && num_outs >= 1 && num_outs <= kMaxOuts, "num_outs %d: 1 .. %d destinations", num_outs,
+                    kMaxOuts);
+  for (int t = 0; t < num_outs; ++t) SPECDEC_CHECK_ARG(outs[t], "null output destination %d", t);
+  SPECDEC_CHECK_ARG(q && k_cache && v_cache && block_tables && workspace && err, "null pointer argument");
   SPECDEC_CHECK_ARG((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "workspace must be 256-byte aligned");
   SPECDEC_CHECK_ARG(head_dim == kHeadDim, "head_dim %d: this build implements 128", head_dim);
   SPECDEC_CHECK_ARG(num_kv_heads >= 1 && num_heads % num_kv_heads == 0, "heads %d not a multiple of kv heads %d",
@@ -880,8 +905,11 @@ int specdec_paged_attention_ex(const void* q, long long T, long long q_row_strid
   a.Hkv = num_kv_heads;
   a.scale_log2 = softmax_scale * 1.4426950408889634f;
   a.causal = causal;
-  a.out = static_cast<__nv_bfloat16*>(out);
+  a.out = static_cast<__nv_bfloat16*>(outs[0]);
   a.out_row_stride = out_row_stride;
+  PeerOuts peers{};
+  for (int t = 1; t < num_outs; ++t) peers.out[t - 1] = static_cast<__nv_bfloat16*>(outs[t]);
+  peers.n = num_outs - 1;
   a.err = err;
   a.R = R;
   // One CTA per SM, fewer when every row's table holds fewer tiles in total.
@@ -896,12 +924,34 @@ int specdec_paged_attention_ex(const void* q, long long T, long long q_row_strid
   a.counters = reinterpret_cast<int*>(static_cast<unsigned char*>(workspace) + partial_bytes(info.sm_count));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool early = (flags & SPECDEC_ATTN_EARLY_LAUNCH) != 0;
-  switch (G) {
-    case 1: return launch<1>(qm, km, vm, km32, vm32, a, grid, early, s);
-    case 2: return launch<2>(qm, km, vm, km32, vm32, a, grid, early, s);
-    case 4: return launch<4>(qm, km, vm, km32, vm32, a, grid, early, s);
-    default: return launch<8>(qm, km, vm, km32, vm32, a, grid, early, s);
+  if (peers.n > 0) {
+    switch (G) {
+      case 1: return launch<1, true>(qm, km, vm, km32, vm32, a, peers, grid, early, s);
+      case 2: return launch<2, true>(qm, km, vm, km32, vm32, a, peers, grid, early, s);
+      case 4: return launch<4, true>(qm, km, vm, km32, vm32, a, peers, grid, early, s);
+      default: return launch<8, true>(qm, km, vm, km32, vm32, a, peers, grid, early, s);
+    }
   }
+  switch (G) {
+    case 1: return launch<1, false>(qm, km, vm, km32, vm32, a, peers, grid, early, s);
+    case 2: return launch<2, false>(qm, km, vm, km32, vm32, a, peers, grid, early, s);
+    case 4: return launch<4, false>(qm, km, vm, km32, vm32, a, peers, grid, early, s);
+    default: return launch<8, false>(qm, km, vm, km32, vm32, a, peers, grid, early, s);
+  }
+}
+
+int specdec_paged_attention_ex(const void* q, long long T, long long q_row_stride, int num_heads, int num_kv_heads,
+                               int head_dim, const void* k_cache, const void* v_cache, long long num_slots,
+                               int block_size, const int* cu_seqlens_q, const int* cu_seqlens_k,
+                               const int* context_lens, int q_per_seq, int R, const int* block_tables, int W,
+                               int max_seqlen_q, float softmax_scale, int causal, void* out, long long out_row_stride,
+                               void* workspace, long long workspace_bytes, int* err, unsigned flags, void* stream) {
+  void* const outs[1] = {out};
+  return specdec_paged_attention_multi(q, T, q_row_stride, num_heads, num_kv_heads, head_dim, k_cache, v_cache,
+                                       num_slots, block_size, cu_seqlens_q, cu_seqlens_k, context_lens, q_per_seq, R,
+                                       block_tables, W, max_seqlen_q, softmax_scale, causal,
+                                       out ? outs : nullptr, 1, out_row_stride, workspace, workspace_bytes, err,
+                                       flags, stream);
 }
 
 int specdec_paged_attention(const void* q, long long T, long long q_row_stride, int num_heads, int num_kv_heads,

@@ -53,7 +53,12 @@ SIGNATURES = {
                                             _c_ll, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_int, _c_void_p,
                                             _c_int, _c_int, _c_float, _c_int, _c_void_p, _c_ll, _c_void_p, _c_ll,
                                             _c_void_p, ctypes.c_uint, _c_void_p]),
+    "specdec_paged_attention_multi": (_c_int, [_c_void_p, _c_ll, _c_ll, _c_int, _c_int, _c_int, _c_void_p,
+                                               _c_void_p, _c_ll, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_int,
+                                               _c_int, _c_void_p, _c_int, _c_int, _c_float, _c_int, _c_void_p,
+                                               _c_int, _c_ll, _c_void_p, _c_ll, _c_void_p, ctypes.c_uint, _c_void_p]),
     "specdec_attention_workspace_bytes": (_c_ll, [_c_int, _c_int]),
+    "specdec_peer_barrier": (_c_int, [_c_void_p, _c_int, _c_int, _c_void_p, _c_ll, _c_void_p, _c_void_p]),
     "specdec_norm_rope_store": (_c_int, [_c_void_p, _c_ll, _c_ll, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_void_p,
                                          _c_ll, _c_void_p, _c_ll, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_ll,
                                          _c_ll, _c_void_p, _c_float, _c_void_p, _c_void_p]),

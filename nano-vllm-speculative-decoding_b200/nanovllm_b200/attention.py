@@ -15,6 +15,8 @@ block_size a multiple of 128; rows of at most 32 / (H / Hkv) queries (8 for Qwen
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 from torch import nn
 
@@ -74,6 +76,31 @@ def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor,
 EARLY_LAUNCH = 1   # SPECDEC_ATTN_EARLY_LAUNCH
 
 
+def _row_metadata(block_tables, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, context_lens, query_len_per_seq):
+    tables = block_tables.to(torch.int32).contiguous()
+    if cu_seqlens_q is not None:
+        if max_seqlen_q is None:
+            raise ValueError("varlen attention needs max_seqlen_q")
+        cq = cu_seqlens_q.to(torch.int32).contiguous()
+        ck = cu_seqlens_k.to(torch.int32).contiguous()
+        return tables, cq, ck, None, cq.numel() - 1, 0, int(max_seqlen_q)
+    ctx = context_lens.to(torch.int32).contiguous()
+    return tables, None, None, ctx, ctx.numel(), query_len_per_seq, query_len_per_seq
+
+
+def _output(out: torch.Tensor | None, shape, device: torch.device) -> torch.Tensor:
+    """out itself after checking it is a bf16 [T, H, D] tensor on `device` with dense heads (rows may be strided),
+    or a new one."""
+    T, H, D = shape
+    if out is None:
+        return torch.empty(T, H, D, dtype=torch.bfloat16, device=device)
+    if (out.shape != (T, H, D) or out.dtype != torch.bfloat16 or out.device != device or out.stride(2) != 1
+            or out.stride(1) != D):
+        raise ValueError(f"out must be a bf16 [{T}, {H}, {D}] tensor on {device} with dense heads "
+                         f"(got {out.dtype} {tuple(out.shape)} strides {out.stride()})")
+    return out
+
+
 def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
                     scale: float, *, cu_seqlens_q: torch.Tensor | None = None,
                     cu_seqlens_k: torch.Tensor | None = None, max_seqlen_q: int | None = None,
@@ -84,41 +111,47 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
     programmatic dependent of the preceding kernel (its prologue overlaps that kernel's end); only when that kernel
     does not write the row metadata (cu_seqlens / context_lens / block_tables)."""
     device = require_cuda(q, k_cache, v_cache, block_tables)
+    out = _output(out, q.shape, device)
+    paged_attention_to(q, k_cache, v_cache, block_tables, scale, [out.data_ptr()], out.stride(0),
+                       cu_seqlens_q=cu_seqlens_q, cu_seqlens_k=cu_seqlens_k, max_seqlen_q=max_seqlen_q,
+                       context_lens=context_lens, query_len_per_seq=query_len_per_seq, causal=causal,
+                       early_launch=early_launch)
+    return out
+
+
+def paged_attention_to(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
+                       scale: float, out_ptrs: list[int], out_row_stride: int, *,
+                       cu_seqlens_q: torch.Tensor | None = None, cu_seqlens_k: torch.Tensor | None = None,
+                       max_seqlen_q: int | None = None, context_lens: torch.Tensor | None = None,
+                       query_len_per_seq: int = 1, causal: bool = True, early_launch: bool = False) -> None:
+    """paged_attention writing its [T, H, D] bf16 output to every device address in out_ptrs (1 to 8; this GPU's
+    memory or a peer's mapped into this process), all with row stride out_row_stride elements.  The caller owns
+    the destinations' extent: each must hold T rows of out_row_stride elements from its address."""
+    device = require_cuda(q, k_cache, v_cache, block_tables)
     T, H, D = q.shape
     blocks, block_size, Hkv, Dc = k_cache.shape
     if Dc != D or v_cache.shape != k_cache.shape:
         raise ValueError("q, k_cache and v_cache disagree on head_dim or shape")
+    if not 1 <= len(out_ptrs) <= 8 or out_row_stride < H * D:
+        raise ValueError(f"{len(out_ptrs)} destinations with row stride {out_row_stride}: 1 to 8, stride >= H * D")
     if q.stride(-1) != 1 or q.stride(1) != D:
         q = q.contiguous()
-    tables = block_tables.to(torch.int32).contiguous()
-    R, W = tables.shape
-    if out is None:
-        out = torch.empty(T, H, D, dtype=torch.bfloat16, device=device)
-    elif (out.shape != (T, H, D) or out.dtype != torch.bfloat16 or out.device != device or out.stride(2) != 1
-          or out.stride(1) != D):
-        raise ValueError(f"out must be a bf16 [{T}, {H}, {D}] tensor on {device} with dense heads "
-                         f"(got {out.dtype} {tuple(out.shape)} strides {out.stride()})")
-    if cu_seqlens_q is not None:
-        cq = cu_seqlens_q.to(torch.int32).contiguous()
-        ck = cu_seqlens_k.to(torch.int32).contiguous()
-        ctx = None
-        if max_seqlen_q is None:
-            raise ValueError("varlen attention needs max_seqlen_q")
-        R = cq.numel() - 1
-        q_per_seq = 0
-    else:
-        cq = ck = None
-        ctx = context_lens.to(torch.int32).contiguous()
-        R = ctx.numel()
-        q_per_seq = query_len_per_seq
-        max_seqlen_q = query_len_per_seq
+    tables, cq, ck, ctx, R, q_per_seq, max_q = _row_metadata(block_tables, cu_seqlens_q, cu_seqlens_k, max_seqlen_q,
+                                                              context_lens, query_len_per_seq)
+    W = tables.shape[1]
     ws = _split_workspace(device, R, Hkv)
-    check(_lib.lib().specdec_paged_attention_ex(
+    flags = EARLY_LAUNCH if early_launch else 0
+    if len(out_ptrs) == 1:
+        check(_lib.lib().specdec_paged_attention_ex(
+            ptr(q), T, q.stride(0), H, Hkv, D, ptr(k_cache), ptr(v_cache), blocks * block_size, block_size, ptr(cq),
+            ptr(ck), ptr(ctx), q_per_seq, R, ptr(tables), W, max_q, float(scale), int(causal), out_ptrs[0],
+            out_row_stride, ptr(ws), ws.numel(), ptr(_err_word(device)), flags, stream_of(device)))
+        return
+    outs = (ctypes.c_void_p * len(out_ptrs))(*out_ptrs)
+    check(_lib.lib().specdec_paged_attention_multi(
         ptr(q), T, q.stride(0), H, Hkv, D, ptr(k_cache), ptr(v_cache), blocks * block_size, block_size, ptr(cq),
-        ptr(ck), ptr(ctx), q_per_seq, R, ptr(tables), W, int(max_seqlen_q), float(scale), int(causal), ptr(out),
-        out.stride(0), ptr(ws), ws.numel(), ptr(_err_word(device)), EARLY_LAUNCH if early_launch else 0,
-        stream_of(device)))
-    return out
+        ptr(ck), ptr(ctx), q_per_seq, R, ptr(tables), W, max_q, float(scale), int(causal), outs, len(out_ptrs),
+        out_row_stride, ptr(ws), ws.numel(), ptr(_err_word(device)), flags, stream_of(device)))
 
 
 class Attention(nn.Module):
@@ -135,7 +168,16 @@ class Attention(nn.Module):
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor | None = None
                 ) -> torch.Tensor:
         """The reference's forward(q, k, v); out optionally names the [T, H, D] bf16 tensor to write (rows may be
-        strided), which the tensor-parallel mode uses to write straight into its all-gather buffer."""
+        strided)."""
+        q = q.view(-1, self.num_heads, self.head_dim)
+        out = _output(out, q.shape, q.device)
+        self.forward_to(q, k, v, [out.data_ptr()], out.stride(0))
+        return out
+
+    def forward_to(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out_ptrs: list[int],
+                   out_row_stride: int) -> None:
+        """forward writing the output to every address in out_ptrs (see paged_attention_to): the store of k / v
+        into this layer's caches at the context's slot_mapping, then the paged branch the context selects."""
         context = get_context()
         k_cache, v_cache = self.k_cache, self.v_cache
         if k_cache.numel() and v_cache.numel():
@@ -144,9 +186,10 @@ class Attention(nn.Module):
         if context.is_prefill:
             if context.block_tables is None:
                 raise NotImplementedError("prefill without a block table is outside the B200 verify/accept path")
-            return paged_attention(q, k_cache, v_cache, context.block_tables, self.scale,
-                                   cu_seqlens_q=context.cu_seqlens_q, cu_seqlens_k=context.cu_seqlens_k,
-                                   max_seqlen_q=context.max_seqlen_q, causal=True, out=out)
-        return paged_attention(q, k_cache, v_cache, context.block_tables, self.scale,
+            paged_attention_to(q, k_cache, v_cache, context.block_tables, self.scale, out_ptrs, out_row_stride,
+                               cu_seqlens_q=context.cu_seqlens_q, cu_seqlens_k=context.cu_seqlens_k,
+                               max_seqlen_q=context.max_seqlen_q, causal=True)
+        else:
+            paged_attention_to(q, k_cache, v_cache, context.block_tables, self.scale, out_ptrs, out_row_stride,
                                context_lens=context.context_lens, query_len_per_seq=context.query_len_per_seq,
-                               causal=context.causal, out=out)
+                               causal=context.causal)

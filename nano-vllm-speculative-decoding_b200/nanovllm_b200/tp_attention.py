@@ -16,13 +16,25 @@ This mode instead gathers the attention outputs, for a forward whose other layer
     2. all_gather_into_tensor in place (NCCL over NVLink / NVSwitch; 2*T*H*D*(N-1)/N bytes in per GPU);
     3. one copy interleaves the chunks into [T, H, D] (head index r*H/N + j).
 Only the outputs cross GPUs: the KV cache, the dominant bytes, stays local.
+
+exchange="peer" fuses the gather into the kernel: every rank's [T, H, D] output lives in symmetric memory
+(torch.distributed._symmetric_memory: one allocation per rank, mapped into every rank's process), and the
+attention kernel stores each finished tile at this rank's head offset into all N outputs (specdec_paged_
+attention_multi; the peers' copies cross NVLink as plain stores while later tiles still compute).  One bounded
+cross-GPU barrier kernel (specdec_peer_barrier) then orders every rank's reads after all peers' stores.  No NCCL
+call and no interleave copy; the outputs alternate between two slots, so one barrier per call suffices (a rank
+writes slot s again only after every peer passed the barrier that follows its use of slot s).
 """
 from __future__ import annotations
+
+import ctypes
 
 import torch
 import torch.distributed as dist
 from torch import nn
 
+from . import _lib
+from ._lib import check, stream_of
 from .attention import Attention
 
 
@@ -57,10 +69,14 @@ class TPAttention(nn.Module):
     in a graph need that graph released before the process group is destroyed."""
 
     def __init__(self, num_heads: int, head_dim: int, scale: float, num_kv_heads: int,
-                 group: dist.ProcessGroup | None = None, *, world: int | None = None, rank: int | None = None):
+                 group: dist.ProcessGroup | None = None, *, world: int | None = None, rank: int | None = None,
+                 exchange: str = "nccl", max_tokens: int = 0, device: torch.device | None = None,
+                 barrier_timeout_s: float = 5.0):
         """world / rank default to the process group's; giving them without a group builds one rank's module
         for ranks emulated in one process (its local() and gather_buffer() work, all_gather() needs the
-        group)."""
+        group).  exchange "nccl" (all-gather) or "peer" (stores into the peers' symmetric buffers + barrier);
+        "peer" is collective at construction (every rank builds its module together) and needs max_tokens (the
+        largest T of any call) and the rank's CUDA device."""
         super().__init__()
         self.group = group
         if world is None:
@@ -72,6 +88,57 @@ class TPAttention(nn.Module):
         self.num_heads, self.head_dim = num_heads, head_dim
         self.local = Attention(num_heads // self.world, head_dim, scale, num_kv_heads // self.world)
         self._buffer = torch.empty(0)
+        if exchange not in ("nccl", "peer"):
+            raise ValueError(f"exchange {exchange!r}: 'nccl' or 'peer'")
+        self.exchange = exchange
+        if exchange == "peer":
+            self._setup_peer(max_tokens, device, barrier_timeout_s)
+
+    # ------------------------------------------------------------------------------------ peer-store exchange
+    _FLAG_BYTES = 256       # 8 uint32 arrival words (one per rank), padded
+
+    def _setup_peer(self, max_tokens: int, device: torch.device | None, timeout_s: float) -> None:
+        import torch.distributed._symmetric_memory as symm_mem
+        if max_tokens < 1 or device is None or device.type != "cuda":
+            raise ValueError("exchange='peer' needs max_tokens >= 1 and the rank's CUDA device")
+        if not dist.is_initialized() or self.world > 8:
+            raise ValueError("exchange='peer' needs an initialised process group of at most 8 ranks")
+        H, D = self.num_heads, self.head_dim
+        self.max_tokens = max_tokens
+        self._slot_bytes = max_tokens * H * D * 2
+        nbytes = 2 * self._slot_bytes + self._FLAG_BYTES
+        storage = symm_mem.empty(nbytes, dtype=torch.uint8, device=device)
+        handle = symm_mem.rendezvous(storage, self.group if self.group is not None else dist.group.WORLD)
+        self._symm, self._handle = storage, handle
+        ptrs = [int(p) for p in handle.buffer_ptrs]
+        delta = storage.data_ptr() - ptrs[self.rank]          # 0 unless the tensor sits inside its allocation
+        self._peer_ptrs = [p + delta for p in ptrs]
+        self._slots = [storage[i * self._slot_bytes:(i + 1) * self._slot_bytes].view(torch.bfloat16)
+                       .view(max_tokens, H, D) for i in range(2)]
+        storage[2 * self._slot_bytes:].zero_()                      # this rank's arrival words
+        self._epoch = torch.zeros(1, dtype=torch.int32, device=device)
+        self._err = torch.zeros(1, dtype=torch.int32, device=device)
+        self._flag_ptrs = (ctypes.c_void_p * self.world)(*[p + 2 * self._slot_bytes for p in self._peer_ptrs])
+        self._timeout_ns = int(timeout_s * 1e9)
+        self._calls = 0
+        torch.cuda.synchronize(device)
+        dist.barrier(group=self.group)                              # every rank's words are zero before use
+
+    def peer_error(self) -> int:
+        """0, or 21 when a barrier wait gave up (a peer never arrived within the timeout); synchronises."""
+        return int(self._err.item())
+
+    def _forward_peer(self, q, k, v, T: int) -> torch.Tensor:
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens: this module's symmetric buffers hold {self.max_tokens}")
+        slot = self._calls % 2
+        self._calls += 1
+        H, D, Hl = self.num_heads, self.head_dim, self.num_heads // self.world
+        offset = slot * self._slot_bytes + self.rank * Hl * D * 2      # this rank's heads in every rank's slot
+        self.local.forward_to(q, k, v, [p + offset for p in self._peer_ptrs], H * D)
+        check(_lib.lib().specdec_peer_barrier(self._flag_ptrs, self.world, self.rank, self._epoch.data_ptr(),
+                                              self._timeout_ns, self._err.data_ptr(), stream_of(q.device)))
+        return self._slots[slot][:T]
 
     @property
     def k_cache(self) -> torch.Tensor:
@@ -106,7 +173,12 @@ class TPAttention(nn.Module):
 
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor | None = None
                 ) -> torch.Tensor:
+        """[T, H, D] attention output of all heads.  With exchange="peer" and no `out`, a view of this rank's
+        symmetric slot, valid until the call after next (slots alternate)."""
         T = q.numel() // ((self.num_heads // self.world) * self.head_dim)
+        if self.exchange == "peer":
+            result = self._forward_peer(q, k, v, T)
+            return result if out is None else out.copy_(result)
         gathered = self.gather_buffer(T, q.device)
         self.local(q, k, v, out=gathered[self.rank])
         return interleave_heads(self.all_gather(gathered), out)

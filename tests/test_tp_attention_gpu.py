@@ -66,7 +66,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _nccl_worker(rank, world, port, out):
+def _nccl_worker(rank, world, port, out, exchange):
     import torch.distributed as dist
     from test_tp_attention import _case
     from nanovllm_b200.context import set_context
@@ -81,7 +81,7 @@ def _nccl_worker(rank, world, port, out):
     try:
         q, k_cache, v_cache, tables, starts, q_lens, k_lens, scale = _case(seed=3)
         T, H, D = q.shape
-        m = TPAttention(H, D, scale, k_cache.shape[2])
+        m = TPAttention(H, D, scale, k_cache.shape[2], exchange=exchange, max_tokens=T, device=dev)
         qs, ks = m.q_heads, m.kv_heads
         on = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev).bfloat16()   # noqa: E731
         m.k_cache, m.v_cache = on(k_cache[:, :, ks]), on(v_cache[:, :, ks])
@@ -91,26 +91,94 @@ def _nccl_worker(rank, world, port, out):
         set_context(True, cu_q, cu_k, int(q_lens.max()), int(k_lens.max()), slots, None,
                     torch.from_numpy(tables).to(dev))
         kv_new = torch.zeros(T, ks.stop - ks.start, D, dtype=torch.bfloat16, device=dev)
-        got = m(on(q[:, qs]).reshape(T, -1), kv_new, kv_new)
-        for _ in range(3):                                                  # repeated calls reuse the buffer
+        got = m(on(q[:, qs]).reshape(T, -1), kv_new, kv_new).clone()
+        for _ in range(3):                                                  # repeated calls reuse the buffers
             again = m(on(q[:, qs]).reshape(T, -1), kv_new, kv_new)
         torch.cuda.synchronize()
-        out[rank] = (got.float().cpu().numpy(), bool(torch.equal(got, again)))
+        status = m.peer_error() if exchange == "peer" else 0
+        out[rank] = (got.float().cpu().numpy(), bool(torch.equal(got, again)), status)
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.timeout(300)
+@pytest.mark.parametrize("exchange", ["nccl", "peer"])
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_two_nccl_ranks_all_gather_the_heads():
+def test_two_ranks_gather_the_heads(exchange):
     from oracle import attention as OA
     from test_tp_attention import _case
     world, port = 2, _free_port()
     manager = mp.get_context("spawn").Manager()
     out = manager.dict()
-    mp.start_processes(_nccl_worker, args=(world, port, out), nprocs=world, join=True, start_method="spawn")
+    mp.start_processes(_nccl_worker, args=(world, port, out, exchange), nprocs=world, join=True,
+                       start_method="spawn")
     q, k_cache, v_cache, tables, starts, q_lens, k_lens, scale = _case(seed=3)
     want = OA.paged_attention(q, k_cache, v_cache, tables, starts, q_lens, k_lens, scale)
+    assert out[0][2] == 0 and out[1][2] == 0
     assert np.array_equal(out[0][0], out[1][0]) and out[0][1] and out[1][1]
     np.testing.assert_allclose(out[0][0], want, atol=ATOL, rtol=0)
+
+
+def test_multi_destination_outputs_match_the_single_output_bit_for_bit():
+    """specdec_paged_attention_multi with three destinations (each at a head offset of a wider output, as the
+    peer-store mode writes every rank's buffer) stores exactly the single-output result in each."""
+    from nanovllm_b200 import attention as A
+    c = paged_case([8, 8, 3, 1], [700, 129, 1000, 40], seed=21, pad_rows=1)
+    T, H, D = c["q"].shape
+    A.reset_device_error(DEV)
+    A.store_kvcache(c["k"], c["v"], c["k_cache"], c["v_cache"], c["slots"])
+    single = A.paged_attention(c["q"], c["k_cache"], c["v_cache"], c["tables"], c["scale"], cu_seqlens_q=c["cu_q"],
+                               cu_seqlens_k=c["cu_k"], max_seqlen_q=8)
+    wide = [torch.full((T, 3 * H, D), float("nan"), dtype=torch.bfloat16, device=DEV) for _ in range(3)]
+    ptrs = [w.data_ptr() + (i * H * D) * 2 for i, w in enumerate(wide)]   # destination i at head offset i*H
+    A.paged_attention_to(c["q"], c["k_cache"], c["v_cache"], c["tables"], c["scale"], ptrs, 3 * H * D,
+                         cu_seqlens_q=c["cu_q"], cu_seqlens_k=c["cu_k"], max_seqlen_q=8)
+    torch.cuda.synchronize()
+    assert A.device_error(DEV) == 0
+    for i, w in enumerate(wide):
+        got = w[:, i * H:(i + 1) * H]
+        assert torch.equal(got.view(torch.int16), single.view(torch.int16))
+        rest = torch.cat([w[:, :i * H], w[:, (i + 1) * H:]], dim=1)
+        assert torch.isnan(rest.float()).all()          # nothing written outside the destination's heads
+
+
+def _barrier(flags, world, rank, epoch, timeout_ns, err):
+    import ctypes
+    from nanovllm_b200 import _lib
+    from nanovllm_b200._lib import check, stream_of
+    arr = (ctypes.c_void_p * world)(*[f.data_ptr() for f in flags])
+    check(_lib.lib().specdec_peer_barrier(arr, world, rank, epoch.data_ptr(), timeout_ns, err.data_ptr(),
+                                          stream_of(DEV)))
+
+
+def test_peer_barrier_passes_when_every_rank_has_arrived():
+    """One rank's barrier on one GPU: alone (world 1), and in a world of 2 whose peer already signalled the
+    epoch (its word pre-set, as the peer's own barrier would have stored it).  No second waiting kernel runs."""
+    epoch = torch.zeros(1, dtype=torch.int32, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    mine = torch.zeros(8, dtype=torch.int32, device=DEV)
+    _barrier([mine], 1, 0, epoch, 10**9, err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0 and int(epoch.item()) == 1 and int(mine[0].item()) == 1
+    epoch.zero_()
+    mine.zero_()
+    peer = torch.zeros(8, dtype=torch.int32, device=DEV)
+    mine[1] = 1                              # rank 1 has arrived at epoch 1
+    _barrier([mine, peer], 2, 0, epoch, 10**9, err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0 and int(epoch.item()) == 1
+    assert peer.tolist()[:2] == [1, 0]       # rank 0 signalled rank 1 at epoch 1
+
+
+def test_peer_barrier_wait_is_bounded_and_reports_a_status():
+    """A peer that never arrives (its word is never set): the wait gives up after its 50 ms limit, records 21
+    and returns; the context stays usable."""
+    epoch = torch.zeros(1, dtype=torch.int32, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    mine = torch.zeros(8, dtype=torch.int32, device=DEV)
+    peer = torch.zeros(8, dtype=torch.int32, device=DEV)
+    _barrier([mine, peer], 2, 0, epoch, 50_000_000, err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 21
+    assert float(torch.ones(4, device=DEV).sum().item()) == 4.0
