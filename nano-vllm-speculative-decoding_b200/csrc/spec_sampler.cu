@@ -35,6 +35,7 @@ namespace sampler {
 constexpr int kThreads = 256;        // stats / tail / greedy CTAs
 constexpr int kTopkThreads = 512;    // one CTA per truncating row
 constexpr int kStatsCtasPerSm = 4;   // stats_kernel residency its launch bounds guarantee (<= 64 registers)
+constexpr int kGreedyCtasPerSm = 8;  // greedy_kernel residency its launch bounds guarantee (<= 32 registers)
 constexpr int kMaxRequests = 1024;   // B cap (shared-memory tables are sized by it)
 constexpr int kMaxRows = 16384;      // T cap (fixed-offset greedy key table)
 constexpr int kMaxChunks = 64;       // chunks per row in pass 1
@@ -1260,7 +1261,7 @@ __global__ void __launch_bounds__(kThreads) tail_kept_kernel(Args a) {
 // ---------------------------------------------------------------------------------------- greedy
 // grid (C, T): per-chunk argmax folded into a per-row 64-bit key; the request's last CTA decides.
 template <typename T>
-__global__ void __launch_bounds__(kThreads) greedy_kernel(Args a) {
+__global__ void __launch_bounds__(kThreads, kGreedyCtasPerSm) greedy_kernel(Args a) {
   __shared__ int s_start[kMaxRequests + 1];
   __shared__ unsigned long long s_red[kThreads / 32];
   __shared__ int s_last;
@@ -1378,10 +1379,10 @@ static unsigned long long torch_rng_increment(long long numel, const DeviceInfo&
   return (unsigned long long)(((numel - 1) / (kRngBlock * grid * 4) + 1) * 4);
 }
 
-static void choose_chunks(Args& a, const DeviceInfo& info) {
-  // (row, chunk) CTAs of 256 threads, kStatsCtasPerSm resident per SM: as many chunks per row as fit one wave
-  // (a second, partial wave would run at a fraction of the occupancy), at least one
-  const long long slots = (long long)info.sm_count * kStatsCtasPerSm;
+static void choose_chunks(Args& a, const DeviceInfo& info, int ctas_per_sm = kStatsCtasPerSm) {
+  // (row, chunk) CTAs of 256 threads, ctas_per_sm resident per SM (the kernel's launch bounds): as many chunks
+  // per row as fit one wave (a second, partial wave would run at a fraction of the occupancy), at least one
+  const long long slots = (long long)info.sm_count * ctas_per_sm;
   long long C = slots / a.T;
   long long cmax = (a.V + 2047) / 2048;
   if (C > cmax) C = cmax;
@@ -1576,7 +1577,7 @@ int specdec_accept_greedy(const void* logits, int dtype, long long T, long long 
   a.x = logits; a.T = T; a.V = V; a.dtype = dtype; a.drafts = drafts; a.B = (int)B; a.k = (int)k;
   a.lens = verified_lens; a.n_accept = n_accept; a.tail = tail;
   a.vec_ok = aligned16(logits) && ((V * (long long)dtype_bytes(dtype)) % 16 == 0);
-  choose_chunks(a, info);
+  choose_chunks(a, info, kGreedyCtasPerSm);
   bind_workspace(a, workspace);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   SPECDEC_CUDA_TRY(cudaMemsetAsync(a.status, 0, sizeof(int), s));
