@@ -396,8 +396,10 @@ __device__ int select_by_thread_max_x16(int ngroups, int C, LoadPacked load, uns
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) {
       const H2 m2 = group_max_h2<H2>(w[u]);
-      if (fmaxf(__low2float(m2), __high2float(m2)) >= bound) {   // rare: a candidate in this group
-        const int g = g0 + u * NT;
+      const int g = g0 + u * NT;
+      // rare: a candidate in this group (padding groups past the range hold -inf, which a -inf bound, fewer than
+      // C finite thread maxima, would otherwise admit)
+      if (g < ngroups && fmaxf(__low2float(m2), __high2float(m2)) >= bound) {
         float x[8];
         Packed16<H2>::unpack(w[u], x);
 #pragma unroll
