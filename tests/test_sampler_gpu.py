@@ -321,3 +321,40 @@ def test_accept_dtypes_and_vocab_shapes(S, dtype, vocab, params):
     assert keep.sum() >= batch - 1
     assert np.array_equal(n_accept.cpu().numpy()[keep], want_n[keep])
     assert np.array_equal(tail.cpu().numpy()[keep], want_tail[keep])
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_truncation_with_fewer_finite_logits_than_top_k(S, dtype):
+    """Masked vocabularies: odd rows keep only 12 finite logits (the rest -inf) under top_k = 20, so the
+    selection bound is -inf (fewer than top_k finite thread maxima) and every element, -inf ones included, ties
+    into the kept set; probabilities stay zero off the finite entries and the accept matches the oracle."""
+    batch, k, vocab = 16, 7, 32000
+    temps, top_k, top_p = [0.7] * batch, [20] * batch, [0.8] * batch
+    logits, q, drafts, lens, samp = synthetic_round(S, batch, k, vocab, dtype, True, seed=77, temps=temps,
+                                                    top_k=top_k, top_p=top_p)
+    starts = (torch.cumsum(lens, 0) - lens).tolist()
+    gen_mask = torch.Generator(device=DEV).manual_seed(5)
+    for b in range(1, batch, 2):
+        for r in range(starts[b], starts[b] + int(lens[b])):
+            keep = torch.randperm(vocab, device=DEV, generator=gen_mask)[:12]
+            row = torch.full((vocab,), float("-inf"), device=DEV, dtype=dtype)
+            row[keep] = logits[r, keep]
+            logits[r] = row
+    gen = torch.Generator(device=DEV).manual_seed(29)
+    u = torch.rand(batch, k, device=DEV, generator=gen)
+    noise = S.exponential_noise_(torch.empty(batch, vocab, device=DEV), gen)
+    n_accept, tail = S.accept_from_logits(logits, q, drafts, samp, lens, None, draws=(u, noise))
+    lens_np = lens.cpu().numpy()
+    per = lambda t: np.repeat(t.cpu().numpy(), lens_np)
+    p = O.probs_from_logits(logits.float().cpu().numpy(), per(samp.temperatures), per(samp.top_k),
+                            per(samp.top_p), samp.max_top_k, samp.has_top_p)
+    args = (q.cpu().numpy(), drafts.cpu().numpy(), lens_np, u.cpu().numpy(), noise.cpu().numpy())
+    want_n, want_tail = O.accept_random_varlen(p, *args)
+    keep = ~O.near_tie_flags(p, *args)
+    assert keep.sum() >= batch - 1
+    assert np.array_equal(n_accept.cpu().numpy()[keep], want_n[keep])
+    assert np.array_equal(tail.cpu().numpy()[keep], want_tail[keep])
+    assert (tail.cpu().numpy() < vocab).all()
+    p_gpu = S.probs_from_logits(logits, S.sampling_per_token(samp, lens, int(lens_np.sum()))).cpu().numpy()
+    assert np.array_equal(p_gpu > 0, p > 0)
+    np.testing.assert_allclose(p_gpu, p, rtol=RTOL, atol=1e-9)
