@@ -71,6 +71,8 @@ int specdec_peer_barrier(void* const* flags, int world, int rank, unsigned* epoc
   using namespace specdec;
   using namespace specdec::peer;
   SPECDEC_CHECK_ARG(flags && epoch && err, "null pointer argument");
+  SPECDEC_CHECK_ARG((reinterpret_cast<uintptr_t>(epoch) & 3) == 0 && (reinterpret_cast<uintptr_t>(err) & 3) == 0,
+                    "epoch and err must be 4-byte aligned");
   SPECDEC_CHECK_ARG(world >= 1 && world <= kMaxRanks && rank >= 0 && rank < world, "rank %d of world %d (1 .. %d)",
                     rank, world, kMaxRanks);
   SPECDEC_CHECK_ARG(timeout_ns > 0, "timeout_ns must be positive");

@@ -857,7 +857,9 @@ int specdec_paged_attention_multi(const void* q, long long T, long long q_row_st
   SPECDEC_CHECK_ARG((flags & ~(unsigned)SPECDEC_ATTN_EARLY_LAUNCH) == 0, "unknown flags 0x%x", flags);
   SPECDEC_CHECK_ARG(outs && num_outs >= 1 && num_outs <= kMaxOuts, "num_outs %d: 1 .. %d destinations", num_outs,
                     kMaxOuts);
-  for (int t = 0; t < num_outs; ++t) SPECDEC_CHECK_ARG(outs[t], "null output destination %d", t);
+  for (int t = 0; t < num_outs; ++t)
+    SPECDEC_CHECK_ARG(outs[t] && (reinterpret_cast<uintptr_t>(outs[t]) & 1) == 0,
+                      "output destination %d null or not 2-byte aligned", t);
   SPECDEC_CHECK_ARG(q && k_cache && v_cache && block_tables && workspace && err, "null pointer argument");
   SPECDEC_CHECK_ARG((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "workspace must be 256-byte aligned");
   SPECDEC_CHECK_ARG(head_dim == kHeadDim, "head_dim %d: this build implements 128", head_dim);

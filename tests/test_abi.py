@@ -35,3 +35,30 @@ def test_host_queries_run_without_a_gpu(lib):
     assert lib.specdec_version() >= 1
     assert lib.specdec_sampler_workspace_bytes(512) > 0
     assert lib.specdec_last_error() is not None
+
+
+def _attention_multi(lib, outs, num_outs):
+    """specdec_paged_attention_multi with plausible (never dereferenced) addresses: only the host validation
+    runs, so a call must be rejected before any CUDA call."""
+    import ctypes
+    fake = 1 << 20
+    arr = (ctypes.c_void_p * max(len(outs), 1))(*(outs or [0]))
+    return lib.specdec_paged_attention_multi(fake, 8, 4096, 32, 8, 128, fake, fake, 256, 256, fake, fake, None, 0,
+                                             1, fake, 1, 8, 0.088, 1, arr, num_outs, 4096, fake, 1 << 24, fake, 0,
+                                             None)
+
+
+@pytest.mark.parametrize("outs,num_outs", [([1 << 20], 0), ([1 << 20] * 9, 9), ([(1 << 20) + 1], 1),
+                                           ([1 << 20, 0], 2)])
+def test_multi_destination_attention_rejects_bad_destinations_on_the_host(lib, outs, num_outs):
+    assert _attention_multi(lib, outs, num_outs) == 1            # kInvalidArgument, nothing launched
+    assert b"destination" in lib.specdec_last_error()
+
+
+@pytest.mark.parametrize("world,rank,timeout_ns,flag_off,epoch_off", [
+    (9, 0, 10**9, 0, 0), (2, 2, 10**9, 0, 0), (2, 0, 0, 0, 0), (2, 0, 10**9, 2, 0), (2, 0, 10**9, 0, 2)])
+def test_peer_barrier_rejects_bad_arguments_on_the_host(lib, world, rank, timeout_ns, flag_off, epoch_off):
+    import ctypes
+    fake = 1 << 20
+    flags = (ctypes.c_void_p * 8)(*[fake + flag_off] * 8)
+    assert lib.specdec_peer_barrier(flags, world, rank, fake + epoch_off, timeout_ns, fake, None) == 1
