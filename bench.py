@@ -703,8 +703,9 @@ def main() -> int:
             "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "cfg3: verify+accept round, random-init Qwen3-8B target, B=64 rows x 8 verify "
-                                   "positions, ctx ~1000 (U[ctx-50, ctx+50]), temperature 1, in-kernel draws",
+            "config": {"workload": f"cfg3: verify+accept round, random-init Qwen3-8B target, B={batch} rows x 8 "
+                                   f"verify positions, ctx ~{args.ctx} (U[ctx-50, ctx+50]), temperature 1, "
+                                   f"in-kernel draws",
                        "model": "Qwen3-8B architecture (random init)", "global_batch": batch * world,
                        "seq_len": args.ctx, "parallelism": f"dp{world} (row-sharded replicas)",
                        "l2": "no flush: weights 16.4 GB + KV > L2 every step"},
