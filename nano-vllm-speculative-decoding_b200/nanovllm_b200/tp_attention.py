@@ -66,7 +66,11 @@ class TPAttention(nn.Module):
     [T, Hkv/N, D]; k_cache / v_cache are this rank's [blocks, block_size, Hkv/N, D] caches (set like the
     reference's Attention.k_cache).  Returns [T, H, D] bf16, identical on every rank.  The gather buffer is
     persistent (grown to the largest T seen), so a captured CUDA graph keeps valid pointers; NCCL calls captured
-    in a graph need that graph released before the process group is destroyed."""
+    in a graph need that graph released before the process group is destroyed.  With exchange="peer" each module
+    owns one symmetric allocation (2 x max_tokens x H x D bf16 plus its arrival words) made by a collective
+    rendezvous, so a model keeps one module and binds each layer's caches before that layer's call: the layers'
+    calls are sequential on one stream, so the two alternating slots and the one barrier per call stay correct
+    across layers."""
 
     def __init__(self, num_heads: int, head_dim: int, scale: float, num_kv_heads: int,
                  group: dist.ProcessGroup | None = None, *, world: int | None = None, rank: int | None = None,
