@@ -196,7 +196,10 @@ def attention_roofline(torch, w, hbm_peak: float) -> dict:
     with torch.cuda.graph(graph):
         all_layers()
     graph.replay()
-    per_launch_us = time_events(torch, graph.replay, 5) / s.layers
+    # five timings of 5 replays each; the median, so that one disturbed timing (seen as +10 us per launch now
+    # and then) does not stand for the kernel
+    samples = [time_events(torch, graph.replay, 5) / s.layers for _ in range(5)]
+    per_launch_us = statistics.median(samples)
     keys = sum(n + K_DRAFTS for n in w.lengths)       # row r verifies positions len-1 .. len+6
     kv_bytes = keys * s.kv_heads * s.head_dim * 2 * 2
     qo_bytes = 2 * num_tokens * s.heads * s.head_dim * 2
@@ -210,6 +213,8 @@ def attention_roofline(torch, w, hbm_peak: float) -> dict:
             "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
             "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of config 2, scaled by keys",
             "algorithmic_bytes_per_launch": algorithmic, "us_per_launch": round(per_launch_us, 2),
+            "us_per_launch_samples": [round(x, 2) for x in samples],
+            "timing": "median of 5 timings of 5 graph replays of the 36 layers' launches",
             "launches_per_step": s.layers}
 
 
@@ -218,7 +223,8 @@ def accept_timing(torch, w) -> dict:
     num_tokens = w.q.shape[0] * (K_DRAFTS + 1)
     logits = w.target.graphs[num_tokens][1]["logits"]
     gen = torch.Generator(device=logits.device).manual_seed(3)
-    us = time_events(torch, lambda: S.accept_from_logits(logits, w.q, w.drafts, w.sampling, None, gen), 20)
+    us = statistics.median(time_events(torch, lambda: S.accept_from_logits(logits, w.q, w.drafts, w.sampling, None,
+                                                                            gen), 20) for _ in range(3))
     batch = w.q.shape[0]
     algorithmic = logits.numel() * 2 + batch * V * (4 + 2)    # logits once + q and logits of the tail rows
     return {"us": round(us, 2), "algorithmic_bytes": algorithmic,
