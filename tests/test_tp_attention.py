@@ -97,3 +97,28 @@ def test_all_gather_over_two_gloo_ranks_matches_full_attention():
     want = OA.paged_attention(q, k_cache, v_cache, tables, starts, q_lens, k_lens, scale)
     assert np.array_equal(out[0], out[1])
     np.testing.assert_allclose(out[0], want, atol=2e-2, rtol=0)
+
+
+def test_module_validates_its_exchange_on_the_host():
+    with pytest.raises(ValueError):
+        TPAttention(32, 128, 0.088, 8, exchange="allreduce")
+    with pytest.raises(ValueError):          # the peer exchange needs a process group (and a CUDA device)
+        TPAttention(32, 128, 0.088, 8, exchange="peer", max_tokens=512, device=torch.device("cuda", 0))
+    with pytest.raises(ValueError):
+        TPAttention(32, 128, 0.088, 8, exchange="peer", max_tokens=0, device=torch.device("cuda", 0))
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_emulated_rank_modules_hold_their_heads_and_one_growing_buffer(world):
+    for rank in range(world):
+        m = TPAttention(32, 128, 0.088, 8, world=world, rank=rank)
+        assert (m.world, m.rank) == (world, rank)
+        assert (m.local.num_heads, m.local.num_kv_heads) == (32 // world, 8 // world)
+        assert m.q_heads == slice(rank * 32 // world, (rank + 1) * 32 // world)
+        big = m.gather_buffer(64, torch.device("cpu"))
+        assert big.shape == (world, 64, 32 // world, 128) and big.dtype == torch.bfloat16
+        small = m.gather_buffer(16, torch.device("cpu"))
+        assert small.shape == (world, 16, 32 // world, 128)
+        assert small.data_ptr() == big.data_ptr()        # smaller calls reuse the persistent storage
+        m.k_cache = torch.zeros(2, 256, 8 // world, 128)
+        assert m.local.k_cache is m.k_cache
