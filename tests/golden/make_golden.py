@@ -319,6 +319,48 @@ def markov_cases(reference: Path) -> dict[str, np.ndarray]:
     return out
 
 
+def masked_cases(ss) -> dict[str, np.ndarray]:
+    """Masked vocabularies: rows whose finite logits are fewer than their top_k (the rest -inf), through
+    probs_from_logits and the fused accept, with the draws recorded as in logits_cases."""
+    out: dict[str, np.ndarray] = {}
+    rng = np.random.default_rng(33)
+    configs = [
+        # name, batch, k, vocab, dtype, temps, top_k, top_p, finite logits per masked row
+        ("few_finite_bf16_v640", 6, 7, 640, torch.bfloat16, [0.7] * 6, [20] * 6, [0.8] * 6, 12),
+        ("few_finite_fp32_v640", 5, 4, 640, torch.float32, [1.0, 0.7, 0.9, 1.0, 0.5], [20, 3, 64, 0, 7],
+         [1.0, 0.8, 0.9, 1.0, 0.6], 5),
+    ]
+    for name, batch, k, vocab, dtype, temps, top_k, top_p, n_finite in configs:
+        g = torch.Generator().manual_seed(zlib.crc32(name.encode()) % 100000)
+        lens = torch.from_numpy(random_lens(rng, batch, k))
+        total = int(lens.sum())
+        logits = torch.randn(total, vocab, generator=g) * 3
+        starts = (torch.cumsum(lens, 0) - lens).tolist()
+        for b in range(1, batch, 2):                       # odd requests: every verified row masked
+            for r in range(starts[b], starts[b] + int(lens[b])):
+                keep = torch.randperm(vocab, generator=g)[:n_finite]
+                row = torch.full((vocab,), float("-inf"))
+                row[keep] = logits[r, keep]
+                logits[r] = row
+        logits = logits.to(dtype)
+        samp = sampling(ss, temps, top_k, top_p)
+        per_token = ss.sampling_per_token(samp, lens, total)
+        p = ss.probs_from_logits(logits, per_token)
+        q = ss.probs_from_logits(torch.randn(batch, k, vocab, generator=g) * 3, samp)
+        drafts = ss.sample(q, g)
+        u, noise, clone = draws(g, batch, k, vocab)
+        n_accept, tail = ss.accept_random_varlen(p, q, drafts, lens, g)
+        assert torch.equal(g.get_state(), clone.get_state()), name
+        prefix = f"masked/{name}/"
+        for key, value in dict(logits=logits.float(), p=p, q=q, drafts=drafts, lens=lens, u=u, noise=noise,
+                               n_accept=n_accept, tail=tail, temperature=samp.temperatures, top_k=samp.top_k,
+                               top_p=samp.top_p).items():
+            out[prefix + key] = value.numpy()
+        out[prefix + "max_top_k"] = np.array(samp.max_top_k)
+        out[prefix + "has_top_p"] = np.array(samp.has_top_p)
+    return out
+
+
 def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__)
     default_ref = os.environ.get("SPECDEC_REFERENCE", str(HERE.parents[2] / "reference"))
@@ -332,6 +374,9 @@ def main() -> int:
     fixtures.update(greedy_cases(ss))
     np.savez_compressed(HERE / "sampler.npz", **fixtures)
     print(f"wrote {len(fixtures)} arrays to {HERE / 'sampler.npz'}")
+    masked = masked_cases(ss)
+    np.savez_compressed(HERE / "sampler_masked.npz", **masked)
+    print(f"wrote {len(masked)} arrays to {HERE / 'sampler_masked.npz'}")
     markov = markov_cases(Path(args.reference))
     np.savez_compressed(HERE / "markov.npz", **markov)
     print(f"wrote {len(markov)} arrays to {HERE / 'markov.npz'}")

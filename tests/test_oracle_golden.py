@@ -84,3 +84,25 @@ def test_near_tie_flags_catch_an_exact_tie():
     u = np.array([[1.0]], dtype=np.float32)            # u * q_d == p_d: the accept test is on the knife edge
     noise = np.ones((1, 2), dtype=np.float32)
     assert O.near_tie_flags(p, q, drafts, np.array([2]), u, noise).tolist() == [True]
+
+
+MASKED = np.load(Path(__file__).parent / "golden" / "sampler_masked.npz")
+
+
+@pytest.mark.parametrize("name", sorted({key.split("/")[1] for key in MASKED.files}))
+def test_masked_vocabulary_accept_matches_reference(name):
+    """Rows with fewer finite logits than top_k (the rest -inf): probabilities, the kept set and the accept
+    against the reference's own outputs (the kernel is held to the oracle on such rows by the GPU tests)."""
+    prefix = f"masked/{name}/"
+    c = {key[len(prefix):]: MASKED[key] for key in MASKED.files if key.startswith(prefix)}
+    lens = c["lens"]
+    per_token = lambda v: np.repeat(v, lens)   # noqa: E731  (sampling_per_token, spec_sampler.py:44-52)
+    p = O.probs_from_logits(c["logits"], per_token(c["temperature"]), per_token(c["top_k"]),
+                            per_token(c["top_p"]), int(c["max_top_k"]), bool(c["has_top_p"]))
+    assert np.array_equal(p > 0, c["p"] > 0)
+    np.testing.assert_allclose(p, c["p"], rtol=1e-5, atol=1e-7)
+    n_accept, tail = O.accept_random_varlen(p, c["q"], c["drafts"], lens, c["u"], c["noise"])
+    keep = ~O.near_tie_flags(c["p"], c["q"], c["drafts"], lens, c["u"], c["noise"])
+    assert keep.sum() >= len(lens) - 1
+    assert np.array_equal(n_accept[keep], c["n_accept"][keep])
+    assert np.array_equal(tail[keep], c["tail"][keep])
