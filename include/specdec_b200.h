@@ -147,7 +147,9 @@ int specdec_paged_attention_multi(const void* q, long long T, long long q_row_st
  * uint32 arrival words (peer memory mapped into this process; all zero before the first barrier of a group);
  * epoch: this rank's uint32 counter in device memory (zero at first, advanced by the kernel, so a captured
  * launch replays correctly).  One block signals every rank (system-scope release after a system fence) and
- * waits for every rank's signal of the same epoch; a wait past timeout_ns sets *err = 21 and returns.  Every
+ * waits for every rank's signal of the same epoch; a wait past timeout_ns sets *err = 21 and returns (this rank's
+ * epoch has still advanced, so the group's epochs may now disagree: treat 21 as fatal for the group and zero
+ * every flag array and epoch, with no barrier in flight, before using it again).  Every
  * rank must call it the same number of times, each on its own GPU: barriers of several ranks never share one
  * GPU (nothing makes separate launches run concurrently). */
 int specdec_peer_barrier(void* const* flags, int world, int rank, unsigned* epoch, long long timeout_ns, int* err,

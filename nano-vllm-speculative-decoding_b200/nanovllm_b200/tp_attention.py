@@ -129,7 +129,9 @@ class TPAttention(nn.Module):
         dist.barrier(group=self.group)                              # every rank's words are zero before use
 
     def peer_error(self) -> int:
-        """0, or 21 when a barrier wait gave up (a peer never arrived within the timeout); synchronises."""
+        """0, or 21 when a barrier wait gave up (a peer never arrived within the timeout); synchronises.  After 21
+        the ranks' barrier epochs may disagree: the module is unusable and a new one (a new rendezvous) replaces
+        it."""
         return int(self._err.item())
 
     def _forward_peer(self, q, k, v, T: int) -> torch.Tensor:
