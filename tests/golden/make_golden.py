@@ -361,6 +361,32 @@ def masked_cases(ss) -> dict[str, np.ndarray]:
     return out
 
 
+def greedy_edge_cases(ss) -> dict[str, np.ndarray]:
+    """Greedy accept on rows of few distinct values (many tied maxima: the first index wins), rows whose maximum
+    is +inf (twice), a row of -inf only and a constant row, in fp32 and bf16."""
+    out: dict[str, np.ndarray] = {}
+    batch, k, vocab = 6, 3, 4099
+    for dtype in (torch.float32, torch.bfloat16):
+        g = torch.Generator().manual_seed(vocab)
+        rows = batch * (k + 1)
+        logits = torch.randint(-3, 4, (rows, vocab), generator=g).to(torch.float32)
+        logits[1, vocab // 2] = float("inf")
+        logits[1, vocab - 1] = float("inf")
+        logits[5] = float("-inf")
+        logits[9, :] = 2.0
+        logits[13, -1] = 7.0
+        logits = logits.to(dtype)
+        target = logits.float().argmax(-1).view(batch, k + 1)
+        drafts = torch.randint(0, vocab, (batch, k), generator=g)
+        for b in range(batch):      # agree with the target on a prefix of length b % (k + 1)
+            drafts[b, : b % (k + 1)] = target[b, : b % (k + 1)]
+        n_accept, tail = ss.accept_greedy(logits.view(batch, k + 1, vocab), drafts)
+        prefix = f"greedy_edge/{str(dtype).replace('torch.', '')}/"
+        for key, value in dict(logits=logits.float(), drafts=drafts, n_accept=n_accept, tail=tail).items():
+            out[prefix + key] = value.numpy()
+    return out
+
+
 def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__)
     default_ref = os.environ.get("SPECDEC_REFERENCE", str(HERE.parents[2] / "reference"))
@@ -374,9 +400,9 @@ def main() -> int:
     fixtures.update(greedy_cases(ss))
     np.savez_compressed(HERE / "sampler.npz", **fixtures)
     print(f"wrote {len(fixtures)} arrays to {HERE / 'sampler.npz'}")
-    masked = masked_cases(ss)
-    np.savez_compressed(HERE / "sampler_masked.npz", **masked)
-    print(f"wrote {len(masked)} arrays to {HERE / 'sampler_masked.npz'}")
+    edges = {**masked_cases(ss), **greedy_edge_cases(ss)}
+    np.savez_compressed(HERE / "sampler_edges.npz", **edges)
+    print(f"wrote {len(edges)} arrays to {HERE / 'sampler_edges.npz'}")
     markov = markov_cases(Path(args.reference))
     np.savez_compressed(HERE / "markov.npz", **markov)
     print(f"wrote {len(markov)} arrays to {HERE / 'markov.npz'}")

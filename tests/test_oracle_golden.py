@@ -86,15 +86,19 @@ def test_near_tie_flags_catch_an_exact_tie():
     assert O.near_tie_flags(p, q, drafts, np.array([2]), u, noise).tolist() == [True]
 
 
-MASKED = np.load(Path(__file__).parent / "golden" / "sampler_masked.npz")
+EDGES = np.load(Path(__file__).parent / "golden" / "sampler_edges.npz")
 
 
-@pytest.mark.parametrize("name", sorted({key.split("/")[1] for key in MASKED.files}))
+def edge_cases(kind):
+    return sorted({key.split("/")[1] for key in EDGES.files if key.startswith(kind + "/")})
+
+
+@pytest.mark.parametrize("name", edge_cases("masked"))
 def test_masked_vocabulary_accept_matches_reference(name):
     """Rows with fewer finite logits than top_k (the rest -inf): probabilities, the kept set and the accept
     against the reference's own outputs (the kernel is held to the oracle on such rows by the GPU tests)."""
     prefix = f"masked/{name}/"
-    c = {key[len(prefix):]: MASKED[key] for key in MASKED.files if key.startswith(prefix)}
+    c = {key[len(prefix):]: EDGES[key] for key in EDGES.files if key.startswith(prefix)}
     lens = c["lens"]
     per_token = lambda v: np.repeat(v, lens)   # noqa: E731  (sampling_per_token, spec_sampler.py:44-52)
     p = O.probs_from_logits(c["logits"], per_token(c["temperature"]), per_token(c["top_k"]),
@@ -106,3 +110,14 @@ def test_masked_vocabulary_accept_matches_reference(name):
     assert keep.sum() >= len(lens) - 1
     assert np.array_equal(n_accept[keep], c["n_accept"][keep])
     assert np.array_equal(tail[keep], c["tail"][keep])
+
+
+@pytest.mark.parametrize("name", edge_cases("greedy_edge"))
+def test_greedy_ties_and_infinities_match_reference(name):
+    """Tied maxima (first index), +inf maxima, an all -inf row and a constant row, as the reference decides
+    them (the kernel is held to the oracle on the same construction by the GPU tests)."""
+    prefix = f"greedy_edge/{name}/"
+    c = {key[len(prefix):]: EDGES[key] for key in EDGES.files if key.startswith(prefix)}
+    batch, k = c["drafts"].shape
+    n_accept, tail = O.accept_greedy_varlen(c["logits"], c["drafts"], np.full(batch, k + 1))
+    assert np.array_equal(n_accept, c["n_accept"]) and np.array_equal(tail, c["tail"])
