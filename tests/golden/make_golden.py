@@ -387,6 +387,64 @@ def greedy_edge_cases(ss) -> dict[str, np.ndarray]:
     return out
 
 
+def attention_cases(reference: Path) -> dict[str, np.ndarray]:
+    """The reference's paged-attention stand-in (tests/fake_paged_attention.py: store_kvcache, then SDPA over the
+    keys gathered through the block table) in its decode layout: query_len_per_seq queries per row, causal
+    (queries at the end of the context, the verify rule) and non-causal (the DFlash draft block), fp32 math on
+    values exact in fp16 (stored as fp16 to keep the fixture small), GQA group 4, shuffled block tables, a padding
+    token at slot -1; of the updated caches only the rows at the stored slots are kept."""
+    sys.path.insert(0, str(reference / "tests"))
+    import fake_paged_attention as fpa
+    from nanovllm.utils.context import reset_context, set_context
+    out: dict[str, np.ndarray] = {}
+    H, Hkv, D, bs = 4, 1, 128, 256
+    for name, q_per_seq, causal, context_lens in [("verify_causal", 8, True, [300, 129, 600, 8, 257]),
+                                                   ("draft_block", 7, False, [7, 260, 40, 390])]:
+        g = torch.Generator().manual_seed(zlib.crc32(name.encode()) % 100000)
+        R = len(context_lens)
+        nblk = [-(-n // bs) for n in context_lens]
+        num_blocks = sum(nblk) + 2
+        perm = torch.randperm(num_blocks, generator=g)
+        tables = torch.full((R, max(nblk)), num_blocks - 1, dtype=torch.int32)
+        used = 0
+        for r, n in enumerate(nblk):
+            tables[r, :n] = perm[used:used + n].to(torch.int32)
+            used += n
+        exact = lambda *shape: torch.randn(*shape, generator=g).half().float()   # noqa: E731
+        k_cache = exact(num_blocks, bs, Hkv, D)
+        v_cache = exact(num_blocks, bs, Hkv, D)
+        T = R * q_per_seq
+        q = exact(T, H, D)
+        k = exact(T, Hkv, D)
+        v = exact(T, Hkv, D)
+        slots = []
+        for r, n in enumerate(context_lens):          # the row's last q_per_seq positions are its new tokens
+            for j in range(q_per_seq):
+                pos = n - q_per_seq + j
+                slots.append(int(tables[r, pos // bs]) * bs + pos % bs if pos >= 0 else -1)
+        slots[1] = -1                                   # a padding token: not stored
+        cache_in = (k_cache.clone(), v_cache.clone())
+        layer = SimpleNamespace(k_cache=k_cache, v_cache=v_cache, num_heads=H, num_kv_heads=Hkv, head_dim=D,
+                                scale=D ** -0.5)
+        set_context(False, slot_mapping=torch.tensor(slots), context_lens=torch.tensor(context_lens),
+                    block_tables=tables, query_len_per_seq=q_per_seq, causal=causal)
+        try:
+            o = fpa.attention_forward(layer, q, k, v)
+        finally:
+            reset_context()
+        prefix = f"attention/{name}/"
+        stored = torch.tensor([x for x in slots if x >= 0])
+        for key, value in dict(q=q.half(), k=k.half(), v=v.half(), k_cache_in=cache_in[0].half(),
+                               v_cache_in=cache_in[1].half(), tables=tables, slots=torch.tensor(slots),
+                               context_lens=torch.tensor(context_lens), out=o,
+                               k_stored=k_cache.view(-1, Hkv, D)[stored].half(),
+                               v_stored=v_cache.view(-1, Hkv, D)[stored].half()).items():
+            out[prefix + key] = value.numpy()
+        out[prefix + "q_per_seq"] = np.array(q_per_seq)
+        out[prefix + "causal"] = np.array(causal)
+    return out
+
+
 def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__)
     default_ref = os.environ.get("SPECDEC_REFERENCE", str(HERE.parents[2] / "reference"))
@@ -406,6 +464,9 @@ def main() -> int:
     markov = markov_cases(Path(args.reference))
     np.savez_compressed(HERE / "markov.npz", **markov)
     print(f"wrote {len(markov)} arrays to {HERE / 'markov.npz'}")
+    attn = attention_cases(Path(args.reference))
+    np.savez_compressed(HERE / "attention.npz", **attn)
+    print(f"wrote {len(attn)} arrays to {HERE / 'attention.npz'}")
     ctx = ctx_store_cases(Path(args.reference))
     np.savez_compressed(HERE / "ctx_store.npz", **ctx)
     print(f"wrote {len(ctx)} arrays to {HERE / 'ctx_store.npz'}")
