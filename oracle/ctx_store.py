@@ -4,6 +4,7 @@ DFlashDraftModel.store_context_kv   nanovllm/models/dflash.py:88-96
 RMSNorm.rms_forward                 nanovllm/layers/layernorm.py:16-26  (fp32 stats; cast to bf16, times weight)
 apply_rotary_emb / RotaryEmbedding   nanovllm/layers/rotary_embedding.py:6-27
 store_kvcache                       nanovllm/layers/attention.py:33-40
+SiluAndMul                          nanovllm/layers/activation.py:8-11  (compiled: fp32 math, one bf16 rounding)
 bf16 arithmetic is emulated with round-to-nearest-even on the fp32 bit patterns.
 """
 from __future__ import annotations
@@ -24,6 +25,15 @@ def rope_cache(head_dim: int, max_position: int, base: float) -> np.ndarray:
     t = np.arange(max_position, dtype=np.float32)
     freqs = np.outer(t, inv_freq).astype(np.float32)
     return np.concatenate([np.cos(freqs), np.sin(freqs)], axis=-1).astype(np.float32)
+
+
+def silu_and_mul(gate_up: np.ndarray) -> np.ndarray:
+    """activation.py:8-11: silu(x) * y over the two halves of the last dim, in fp32, rounded once to bf16 (the
+    reference's torch.compile'd forward fuses the two ops; its eager body rounds after each, within one bf16 ulp
+    of this)."""
+    gate_up = gate_up.astype(np.float32)
+    a, b = np.split(gate_up, 2, axis=-1)
+    return bf16(a / (np.float32(1.0) + np.exp(-a)) * b)
 
 
 def rmsnorm(x: np.ndarray, weight: np.ndarray, eps: float) -> np.ndarray:

@@ -445,6 +445,28 @@ def attention_cases(reference: Path) -> dict[str, np.ndarray]:
     return out
 
 
+def forward_helper_cases() -> dict[str, np.ndarray]:
+    """The verify forward's RMSNorm (plain and with residual, nanovllm/layers/layernorm.py) and SiluAndMul
+    (nanovllm/layers/activation.py), the reference's modules on bf16 CPU tensors (their eager bodies: this script
+    disables torch.compile)."""
+    from nanovllm.layers.activation import SiluAndMul
+    from nanovllm.layers.layernorm import RMSNorm
+    g = torch.Generator().manual_seed(17)
+    rows, hidden, inter = 16, 4096, 1024
+    x = torch.randn(rows, hidden, generator=g).bfloat16()
+    residual = torch.randn(rows, hidden, generator=g).bfloat16()
+    norm = RMSNorm(hidden, 1e-6)
+    norm.weight.data = (1.0 + 0.1 * torch.randn(hidden, generator=g)).bfloat16()
+    gate_up = (torch.randn(rows, 2 * inter, generator=g) * 2).bfloat16()
+    with torch.no_grad():
+        y = norm(x)
+        y_res, res_out = norm(x, residual)
+        act = SiluAndMul()(gate_up)
+    out = dict(x=x, residual=residual, weight=norm.weight.data, y=y, y_res=y_res, res_out=res_out,
+               gate_up=gate_up, act=act)
+    return {"forward/" + key: value.float().numpy() for key, value in out.items()} | {"forward/eps": np.array(1e-6)}
+
+
 def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__)
     default_ref = os.environ.get("SPECDEC_REFERENCE", str(HERE.parents[2] / "reference"))
@@ -467,6 +489,9 @@ def main() -> int:
     attn = attention_cases(Path(args.reference))
     np.savez_compressed(HERE / "attention.npz", **attn)
     print(f"wrote {len(attn)} arrays to {HERE / 'attention.npz'}")
+    fwd = forward_helper_cases()
+    np.savez_compressed(HERE / "forward.npz", **fwd)
+    print(f"wrote {len(fwd)} arrays to {HERE / 'forward.npz'}")
     ctx = ctx_store_cases(Path(args.reference))
     np.savez_compressed(HERE / "ctx_store.npz", **ctx)
     print(f"wrote {len(ctx)} arrays to {HERE / 'ctx_store.npz'}")

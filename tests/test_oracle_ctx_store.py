@@ -56,3 +56,23 @@ def test_q_norm_rope_matches_reference():
     ok = within_one_bf16_ulp(got, G["ctx/q_out"])
     assert ok.mean() > 0.999
     np.testing.assert_allclose(got, G["ctx/q_out"], atol=2e-2, rtol=0)
+
+
+F = np.load(Path(__file__).parent / "golden" / "forward.npz")
+
+
+def test_rmsnorm_matches_reference():
+    """layernorm.py rms_forward / add_rms_forward: the residual sum bit-exact, the normed rows within one bf16 ulp
+    (fp32 rsqrt of the variance may differ in its last bits)."""
+    x, r, w, eps = F["forward/x"], F["forward/residual"], F["forward/weight"], float(F["forward/eps"])
+    got = OC.rmsnorm(x, w, eps)
+    assert within_one_bf16_ulp(got, F["forward/y"]).all()
+    s = OC.bf16(x + r)
+    assert np.array_equal(s, F["forward/res_out"])
+    assert within_one_bf16_ulp(OC.rmsnorm(x + r, w, eps), F["forward/y_res"]).all()
+
+
+def test_silu_and_mul_matches_reference():
+    got = OC.silu_and_mul(F["forward/gate_up"])
+    ok = within_one_bf16_ulp(got, F["forward/act"])
+    assert ok.all(), f"{(~ok).sum()} entries beyond one bf16 ulp"
