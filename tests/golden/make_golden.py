@@ -467,6 +467,58 @@ def forward_helper_cases() -> dict[str, np.ndarray]:
     return {"forward/" + key: value.float().numpy() for key, value in out.items()} | {"forward/eps": np.array(1e-6)}
 
 
+class _Seq:
+    """The Sequence fields verify_varlen_metadata reads: len(seq), last_token, target_kv.block_table."""
+
+    def __init__(self, length: int, last_token: int, block_table: list[int]):
+        self.length, self.last_token = length, last_token
+        self.target_kv = SimpleNamespace(block_table=block_table)
+
+    def __len__(self) -> int:
+        return self.length
+
+
+def metadata_cases() -> dict[str, np.ndarray]:
+    """nanovllm/engine/batch_metadata.py verify_varlen_metadata on random batches: ragged block tables, fixed and
+    variable verified lengths, padding rows and empty row slots.  Ragged inputs are stored padded with -1."""
+    from nanovllm.engine.batch_metadata import verify_varlen_metadata
+    import random
+    out: dict[str, np.ndarray] = {}
+    for case in range(12):
+        rng = random.Random(1000 + case)
+        k, block_size, width, pad = 7, 256, 8, 999
+        n = rng.randint(1, 10)
+        lengths, tokens, tables, lens = [], [], [], []
+        next_block = 0
+        for _ in range(n):
+            length = rng.randint(1, 1500)
+            ln = rng.randint(1, k + 1) if case % 2 else k + 1
+            blocks = -(-(length - 1 + ln) // block_size)
+            lengths.append(length)
+            tokens.append(rng.randint(0, 150000))
+            tables.append(list(range(next_block, next_block + blocks)))
+            next_block += blocks
+            lens.append(ln)
+        num_rows = n + rng.randint(0, 3)
+        num_tokens = sum(lens) + rng.randint(0, (num_rows - n) * (k + 1))
+        seqs = [_Seq(a, b, c) for a, b, c in zip(lengths, tokens, tables)]
+        m = verify_varlen_metadata(seqs, lens, k, block_size, num_rows, num_tokens, pad, width)
+        prefix = f"meta/{case:02d}/"
+        padded = np.full((n, width), -1, dtype=np.int64)
+        for r, t in enumerate(tables):
+            padded[r, :len(t)] = t
+        params = dict(lengths=lengths, last_tokens=tokens, verified_lens=lens,
+                      scalars=[k, block_size, num_rows, num_tokens, pad, width])
+        for key, value in params.items():
+            out[prefix + key] = np.array(value, dtype=np.int64)
+        out[prefix + "tables"] = padded
+        for key in ("input_ids", "positions", "slot_mapping", "cu_seqlens_q", "cu_seqlens_k", "draft_index",
+                    "draft_source"):
+            out[prefix + key] = np.array(getattr(m, key), dtype=np.int64)
+        out[prefix + "block_tables"] = np.array(m.block_tables, dtype=np.int64)
+    return out
+
+
 def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__)
     default_ref = os.environ.get("SPECDEC_REFERENCE", str(HERE.parents[2] / "reference"))
@@ -489,6 +541,9 @@ def main() -> int:
     attn = attention_cases(Path(args.reference))
     np.savez_compressed(HERE / "attention.npz", **attn)
     print(f"wrote {len(attn)} arrays to {HERE / 'attention.npz'}")
+    meta = metadata_cases()
+    np.savez_compressed(HERE / "metadata.npz", **meta)
+    print(f"wrote {len(meta)} arrays to {HERE / 'metadata.npz'}")
     fwd = forward_helper_cases()
     np.savez_compressed(HERE / "forward.npz", **fwd)
     print(f"wrote {len(fwd)} arrays to {HERE / 'forward.npz'}")

@@ -52,3 +52,21 @@ def test_packed_metadata_rejects_overfull_padding():
     n64, n32 = packed_sizes(2, 20, 4)
     with pytest.raises(AssertionError):
         pack_verify_metadata(rows, [8], 7, 256, 2, 20, 9, 4, np.zeros(n64, np.int64), np.zeros(n32, np.int32))
+
+
+META = np.load(__import__("pathlib").Path(__file__).parent / "golden" / "metadata.npz")
+
+
+@pytest.mark.parametrize("case", sorted({key.split("/")[1] for key in META.files}))
+def test_list_builder_matches_the_reference(case):
+    """The list builder against the reference's verify_varlen_metadata run on the same batches
+    (tests/golden/make_golden.py): every list, padding rows and empty row slots included."""
+    c = {key.split("/")[2]: META[key] for key in META.files if key.startswith(f"meta/{case}/")}
+    k, bs, num_rows, num_tokens, pad, width = (int(x) for x in c["scalars"])
+    rows = [RowState(length=int(n), last_token=int(t), block_table=[int(b) for b in table if b >= 0])
+            for n, t, table in zip(c["lengths"], c["last_tokens"], c["tables"])]
+    m = verify_varlen_metadata(rows, [int(x) for x in c["verified_lens"]], k, bs, num_rows, num_tokens, pad, width)
+    for key in ("input_ids", "positions", "slot_mapping", "cu_seqlens_q", "cu_seqlens_k", "draft_index",
+                "draft_source"):
+        assert getattr(m, key) == c[key].tolist(), key
+    assert m.block_tables == c["block_tables"].tolist()
