@@ -121,3 +121,25 @@ def test_greedy_ties_and_infinities_match_reference(name):
     batch, k = c["drafts"].shape
     n_accept, tail = O.accept_greedy_varlen(c["logits"], c["drafts"], np.full(batch, k + 1))
     assert np.array_equal(n_accept, c["n_accept"]) and np.array_equal(tail, c["tail"])
+
+
+@pytest.mark.parametrize("name", cases("logits"))
+def test_host_sampling_tensors_match_reference(name):
+    """sampling_tensors / sampling_per_token (the host bookkeeping feeding the kernels) give the reference's
+    per-row tensors and host flags for the same per-request parameters, on CPU."""
+    import torch
+    from types import SimpleNamespace
+    from nanovllm_b200 import spec_sampler as S
+    c = case("logits", name)
+    seqs = [SimpleNamespace(temperature=float(t), top_k=int(k), top_p=float(p))
+            for t, k, p in zip(c["temperature"], c["top_k"], c["top_p"])]
+    samp = S.sampling_tensors(seqs, torch.device("cpu"))
+    assert np.array_equal(samp.temperatures.numpy(), c["temperature"])
+    assert np.array_equal(samp.top_k.numpy(), c["top_k"]) and np.array_equal(samp.top_p.numpy(), c["top_p"])
+    assert (samp.max_top_k, samp.has_top_p) == (int(c["max_top_k"]), bool(c["has_top_p"]))
+    lens = torch.from_numpy(c["lens"])
+    per = S.sampling_per_token(samp, lens, int(lens.sum()))
+    assert np.array_equal(per.top_k.numpy(), np.repeat(c["top_k"], c["lens"]))
+    assert np.array_equal(per.temperatures.numpy(), np.repeat(c["temperature"], c["lens"]))
+    with pytest.raises(ValueError):                     # the reference rejects mixed greedy and random rows
+        S.sampling_tensors(seqs + [SimpleNamespace(temperature=0.0, top_k=0, top_p=1.0)], torch.device("cpu"))
