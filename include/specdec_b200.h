@@ -24,17 +24,21 @@ extern "C" {
 #endif
 
 /* ------------------------------------------------------------------------------------------ library */
+/* Library plumbing, no counterpart in the reference (its Python raises): the calling thread's message for the
+ * last non-zero status, the ABI version. */
 const char* specdec_last_error(void);
 int specdec_version(void);
 /* 1 when the current CUDA device is compute capability 10.0 (the only target of this build). */
 int specdec_device_supported(void);
 
 /* ------------------------------------------------------------------------------------------ kernel 1: sampler */
-/* Workspace bytes for the sampler entry points over `rows` rows of logits / probabilities. */
+/* Workspace bytes for the sampler entry points over `rows` rows of logits / probabilities (no counterpart in the
+ * reference: torch allocates its temporaries). */
 size_t specdec_sampler_workspace_bytes(long long rows);
 
 /* Philox offset increment torch's CUDA generator consumes for one torch.rand / exponential_ draw of `numel`
- * floats on the current device (ATen's calc_execution_policy); callers advance their generator by it. */
+ * floats on the current device (ATen's calc_execution_policy); callers advance their generator by it, so it ends
+ * where the reference's draws (nanovllm/layers/spec_sampler.py:141,149) leave it. */
 unsigned long long specdec_philox_increment(long long numel);
 
 /* probs_from_logits (nanovllm/layers/spec_sampler.py:65-69, truncate_logits :72-96).
@@ -112,7 +116,8 @@ int specdec_paged_attention(const void* q, long long T, long long q_row_stride, 
                             int max_seqlen_q, float softmax_scale, int causal, void* out, long long out_row_stride,
                             void* workspace, long long workspace_bytes, int* err, void* stream);
 
-/* specdec_paged_attention with launch flags.  SPECDEC_ATTN_EARLY_LAUNCH: launched as a programmatic dependent of
+/* specdec_paged_attention (Attention.forward, nanovllm/layers/attention.py:59-77) with launch flags.
+ * SPECDEC_ATTN_EARLY_LAUNCH: launched as a programmatic dependent of
  * the preceding kernel in the stream, so its prologue (row metadata scan, barrier and tensor-memory setup) runs
  * while that kernel finishes; everything else waits for that kernel's completion.  The caller promises that the
  * preceding kernel does not write cu_seqlens_q / cu_seqlens_k / context_lens / block_tables (q and the caches it
