@@ -319,6 +319,67 @@ def markov_cases(reference: Path) -> dict[str, np.ndarray]:
     return out
 
 
+def markov_bf16_cases(reference: Path) -> dict[str, np.ndarray]:
+    """_markov_rows on the production dtypes: bf16 logits and a bf16 head output, summed in bf16 (the fp32 sum
+    rounded once).  Greedy rows use random values (a tied maximum takes its first index on both sides).  torch.topk
+    leaves the order of equal values open and that order assigns the candidates' noise, so the candidate rows are
+    built tie-free: each row's logits are a permutation of a grid 2^-3 apart and the head's products stay below
+    2^-5, so sums round to bf16 (in the binades where the grid is the bf16 spacing) without two ever meeting."""
+    from nanovllm.engine.speculative import DFlashDrafter, num_candidates
+    from nanovllm.layers import spec_sampler as ss
+    out: dict[str, np.ndarray] = {}
+    configs = [
+        # name, B, k, V, temps (None = greedy), top_k, top_p
+        ("greedy_bf16_v4096", 4, 7, 4096, None, [0] * 4, [1.0] * 4),
+        ("candidates_bf16_v512", 4, 7, 512, [1.0, 0.7, 0.9, 1.2], [8, 3, 20, 5], [1.0, 0.8, 0.9, 1.0]),
+    ]
+    for name, batch, k, vocab, temps, top_k, top_p in configs:
+        g = torch.Generator().manual_seed(zlib.crc32(name.encode()) % 100000)
+        if temps is None:
+            logits = (torch.randn(batch, k, vocab, generator=g) * 4).bfloat16()
+            bias_a = torch.randn(vocab, generator=g).bfloat16()
+            bias_c = torch.randn(vocab, generator=g).bfloat16()
+        else:
+            grid = (torch.arange(vocab) - vocab // 2).float() * 0.125           # exact in bf16 (|x| < 32)
+            logits = torch.stack([grid[torch.randperm(vocab, generator=g)] for _ in range(batch * k)])
+            logits = logits.view(batch, k, vocab).bfloat16()
+            signs = lambda: torch.randint(0, 2, (vocab,), generator=g).float() * 2 - 1   # noqa: E731
+            bias_a = (signs() * 0.125).bfloat16()                                  # |a| = 2^-3
+            bias_c = (signs() * torch.randint(1, 4, (vocab,), generator=g).float() * 0.0625).bfloat16()  # < 2^-2
+        prev = torch.randint(vocab, (batch,), generator=g)
+        drafter = object.__new__(DFlashDrafter)
+        drafter.model = SimpleNamespace(markov_head=lambda p, a=bias_a, c=bias_c: a[p][:, None] * c[None, :])
+        drafts = torch.empty(batch, k, dtype=torch.int64)
+        samp = noise = probs = None
+        cand = 0
+        if temps is None:
+            drafter._markov_rows(logits, prev.clone(), None, None, drafts, None, 0)
+        else:
+            samp = sampling(ss, temps, top_k, top_p)
+            cand = num_candidates(samp.max_top_k, samp.all_top_k, vocab)
+            noise = ss.exponential_noise_(torch.empty(batch, k, cand), g)
+            probs = torch.empty(batch, k, vocab)
+            drafter._markov_rows(logits, prev.clone(), samp, noise, drafts, probs, cand)
+            p_row = prev                               # tie-free check on the rows the reference drew
+            for row in range(k):
+                values = (logits[:, row] + drafter.model.markov_head(p_row)).float()
+                top = values.sort(dim=-1, descending=True).values[:, :cand + 1]
+                assert not bool((top[:, 1:] == top[:, :-1]).any()), name
+                p_row = drafts[:, row]
+        prefix = f"markov_bf16/{name}/"
+        for key, value in dict(logits=logits.float(), bias_a=bias_a.float(), bias_c=bias_c.float(), prev=prev,
+                               drafts=drafts).items():
+            out[prefix + key] = value.numpy()
+        out[prefix + "candidates"] = np.array(cand)
+        if samp is not None:
+            for key, value in dict(temperature=samp.temperatures, top_k=samp.top_k, top_p=samp.top_p,
+                                   noise=noise, probs=probs).items():
+                out[prefix + key] = value.numpy()
+            out[prefix + "max_top_k"] = np.array(samp.max_top_k)
+            out[prefix + "has_top_p"] = np.array(samp.has_top_p)
+    return out
+
+
 def masked_cases(ss) -> dict[str, np.ndarray]:
     """Masked vocabularies: rows whose finite logits are fewer than their top_k (the rest -inf), through
     probs_from_logits and the fused accept, with the draws recorded as in logits_cases."""
@@ -538,6 +599,9 @@ def main() -> int:
     markov = markov_cases(Path(args.reference))
     np.savez_compressed(HERE / "markov.npz", **markov)
     print(f"wrote {len(markov)} arrays to {HERE / 'markov.npz'}")
+    markov16 = markov_bf16_cases(Path(args.reference))
+    np.savez_compressed(HERE / "markov_bf16.npz", **markov16)
+    print(f"wrote {len(markov16)} arrays to {HERE / 'markov_bf16.npz'}")
     attn = attention_cases(Path(args.reference))
     np.savez_compressed(HERE / "attention.npz", **attn)
     print(f"wrote {len(attn)} arrays to {HERE / 'attention.npz'}")
