@@ -142,15 +142,20 @@ def require_cuda(*tensors: torch.Tensor | None) -> torch.device:
 
 class Workspace:
     """A zero-initialised device byte buffer per (device, name), grown on demand.  The library keeps its tickets
-    and argmax keys self-cleaning at fixed offsets, so the buffer is zeroed once per allocation only."""
+    and argmax keys self-cleaning at fixed offsets, so the buffer is zeroed once per allocation only.  A grown
+    buffer's predecessor is kept alive: a CUDA graph captured with the old address keeps replaying into valid
+    memory (its own, since later calls outside the graph use the new buffer)."""
 
     _buffers: dict[tuple[int, str], torch.Tensor] = {}
+    _retired: list[torch.Tensor] = []
 
     @classmethod
     def get(cls, device: torch.device, nbytes: int, name: str = "sampler") -> torch.Tensor:
         key = (device.index if device.index is not None else torch.cuda.current_device(), name)
         buf = cls._buffers.get(key)
         if buf is None or buf.numel() < nbytes:
+            if buf is not None:
+                cls._retired.append(buf)
             size = max(nbytes, 1 << 20)
             buf = torch.zeros(size, dtype=torch.uint8, device=device)
             cls._buffers[key] = buf

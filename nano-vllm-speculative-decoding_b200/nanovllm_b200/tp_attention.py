@@ -92,6 +92,7 @@ class TPAttention(nn.Module):
         self.num_heads, self.head_dim = num_heads, head_dim
         self.local = Attention(num_heads // self.world, head_dim, scale, num_kv_heads // self.world)
         self._buffer = torch.empty(0)
+        self._retired: list[torch.Tensor] = []
         if exchange not in ("nccl", "peer"):
             raise ValueError(f"exchange {exchange!r}: 'nccl' or 'peer'")
         self.exchange = exchange
@@ -167,6 +168,8 @@ class TPAttention(nn.Module):
         Hl, D = self.num_heads // self.world, self.head_dim
         need = self.world * T * Hl * D
         if self._buffer.numel() < need or self._buffer.device != device:
+            if self._buffer.numel():
+                self._retired.append(self._buffer)       # a captured graph may still address it
             self._buffer = torch.empty(need, dtype=torch.bfloat16, device=device)
         return self._buffer[:need].view(self.world, T, Hl, D)
 

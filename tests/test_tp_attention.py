@@ -122,3 +122,19 @@ def test_emulated_rank_modules_hold_their_heads_and_one_growing_buffer(world):
         assert small.data_ptr() == big.data_ptr()        # smaller calls reuse the persistent storage
         m.k_cache = torch.zeros(2, 256, 8 // world, 128)
         assert m.local.k_cache is m.k_cache
+
+
+def test_grown_buffers_keep_their_predecessors_alive():
+    """A CUDA graph captured before a buffer grows keeps addressing the old storage: growth retires, never
+    frees, the previous buffer (the gather buffer here, the library workspaces alike)."""
+    from nanovllm_b200._lib import Workspace
+    m = TPAttention(32, 128, 0.088, 8, world=2, rank=0)
+    small = m.gather_buffer(8, torch.device("cpu"))
+    big = m.gather_buffer(64, torch.device("cpu"))
+    assert big.data_ptr() != small.data_ptr()
+    assert any(t.data_ptr() == small.data_ptr() for t in m._retired)
+    dev = torch.device("cpu", 0)
+    first = Workspace.get(dev, 16, name="growth-test")
+    grown = Workspace.get(dev, (2 << 20), name="growth-test")
+    assert grown.numel() >= (2 << 20) and not grown.any()
+    assert any(t.data_ptr() == first.data_ptr() for t in Workspace._retired)
