@@ -16,19 +16,23 @@ int set_error(int code, const char* fmt, ...) {
 }
 
 int device_info(DeviceInfo* out) {
-  static DeviceInfo cache[64];
-  static bool valid[64] = {false};
+  static DeviceInfo cache[kMaxDevices];
+  static std::atomic<bool> valid[kMaxDevices];
+  static std::mutex mu;
   int dev = 0;
   SPECDEC_CUDA_TRY(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= 64) return set_error(kInvalidArgument, "device ordinal %d out of range", dev);
-  if (!valid[dev]) {
-    DeviceInfo info;
-    SPECDEC_CUDA_TRY(cudaDeviceGetAttribute(&info.sm_count, cudaDevAttrMultiProcessorCount, dev));
-    SPECDEC_CUDA_TRY(cudaDeviceGetAttribute(&info.max_threads_per_sm, cudaDevAttrMaxThreadsPerMultiProcessor, dev));
-    SPECDEC_CUDA_TRY(cudaDeviceGetAttribute(&info.cc_major, cudaDevAttrComputeCapabilityMajor, dev));
-    SPECDEC_CUDA_TRY(cudaDeviceGetAttribute(&info.cc_minor, cudaDevAttrComputeCapabilityMinor, dev));
-    cache[dev] = info;
-    valid[dev] = true;
+  if (dev < 0 || dev >= kMaxDevices) return set_error(kInvalidArgument, "device ordinal %d out of range", dev);
+  if (!valid[dev].load(std::memory_order_acquire)) {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!valid[dev].load(std::memory_order_relaxed)) {
+      DeviceInfo info;
+      SPECDEC_CUDA_TRY(cudaDeviceGetAttribute(&info.sm_count, cudaDevAttrMultiProcessorCount, dev));
+      SPECDEC_CUDA_TRY(cudaDeviceGetAttribute(&info.max_threads_per_sm, cudaDevAttrMaxThreadsPerMultiProcessor, dev));
+      SPECDEC_CUDA_TRY(cudaDeviceGetAttribute(&info.cc_major, cudaDevAttrComputeCapabilityMajor, dev));
+      SPECDEC_CUDA_TRY(cudaDeviceGetAttribute(&info.cc_minor, cudaDevAttrComputeCapabilityMinor, dev));
+      cache[dev] = info;
+      valid[dev].store(true, std::memory_order_release);
+    }
   }
   *out = cache[dev];
   return kOk;

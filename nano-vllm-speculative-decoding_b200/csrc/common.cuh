@@ -12,6 +12,9 @@
 #include <stdio.h>
 #include <stdarg.h>
 
+#include <atomic>
+#include <mutex>
+
 namespace specdec {
 
 // ------------------------------------------------------------------------------------------- status codes
@@ -416,12 +419,33 @@ __device__ int select_by_thread_max_x16(int ngroups, int C, LoadPacked load, uns
   return finish_thread_max_selection<NT>(C, buf, cap, s_count, top);
 }
 
-// Device properties the library needs (cached per device on first use).
+// Device properties the library needs (cached per device on first use; thread-safe).
 struct DeviceInfo {
   int sm_count;
   int max_threads_per_sm;
   int cc_major, cc_minor;
 };
 int device_info(DeviceInfo* out);
+
+constexpr int kMaxDevices = 64;
+
+// Raises a kernel's dynamic shared-memory limit to `bytes` on the current device, once per device and kernel.
+// The attribute belongs to the device that was current when it was set, so a process driving several GPUs needs
+// it on each; host threads launching at once serialise on the first call per device only.
+template <auto kKernel>
+int ensure_dynamic_smem(int bytes) {
+  static std::atomic<bool> done[kMaxDevices];
+  static std::mutex mu;
+  int dev = 0;
+  SPECDEC_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return set_error(kInvalidArgument, "device ordinal %d out of range", dev);
+  if (done[dev].load(std::memory_order_acquire)) return kOk;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!done[dev].load(std::memory_order_relaxed)) {
+    SPECDEC_CUDA_TRY(cudaFuncSetAttribute(kKernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done[dev].store(true, std::memory_order_release);
+  }
+  return kOk;
+}
 
 }  // namespace specdec

@@ -321,15 +321,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------------------- host side
+// The driver's tensor-map encoder (one entry point for every device), looked up on first use; the initialisation
+// of a function-local static is thread-safe.
 static PFN_cuTensorMapEncodeTiled_v12000 encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
+  static const PFN_cuTensorMapEncodeTiled_v12000 fn = []() -> PFN_cuTensorMapEncodeTiled_v12000 {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
+      return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    return nullptr;
+  }();
   return fn;
 }
 
@@ -394,12 +396,7 @@ static int launch(Args a, const void* x, long long x_row_stride, const void* w, 
   CUtensorMap wm, xm;
   if (int st = make_map_2d(&wm, w, a.K, a.O, w_row_stride, kTileM)) return st;
   if (int st = make_map_2d(&xm, x, a.K, a.T, x_row_stride, a.tn)) return st;
-  static bool configured = false;
-  if (!configured) {
-    SPECDEC_CUDA_TRY(cudaFuncSetAttribute(context_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          kSmemBytes));
-    configured = true;
-  }
+  if (int st = ensure_dynamic_smem<context_gemm_kernel>(kSmemBytes)) return st;
   context_gemm_kernel<<<grid, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(wm, xm, a);
   SPECDEC_LAUNCH_CHECK();
   return kOk;

@@ -1498,12 +1498,17 @@ int specdec_probs(const void* logits, int dtype, long long R, long long V, long 
   });
 }
 
-int specdec_accept(const void* x, int x_is_probs, int dtype, long long T, long long V, const float* q,
-                   const long long* drafts, long long B, long long k, const long long* verified_lens,
-                   const float* temperature, const long long* top_k, const float* top_p, int max_top_k,
-                   int has_top_p, const float* u, const float* E, unsigned long long seed,
-                   unsigned long long offset_u, unsigned long long offset_E, long long* n_accept,
-                   long long* tail, void* workspace, size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace specdec {
+namespace sampler {
+
+// The host-side checks of specdec_accept's arguments (everything but the workspace), shared with the
+// no-allocation entry point, which must reject a call before it touches its shared scratch.
+static int check_accept_args(const void* x, int x_is_probs, int dtype, long long T, long long V, const float* q,
+                             const long long* drafts, long long B, long long k, const long long* verified_lens,
+                             const float* temperature, const long long* top_k, const float* top_p, int max_top_k,
+                             int has_top_p, const long long* n_accept, const long long* tail) {
   SPECDEC_CHECK_ARG(x && q && drafts && n_accept && tail, "x, q, drafts, n_accept and tail must be non-null");
   SPECDEC_CHECK_ARG(dtype_ok(dtype), "dtype code %d is not f32/bf16/f16", dtype);
   SPECDEC_CHECK_ARG(!x_is_probs || dtype == kF32, "probabilities must be fp32");
@@ -1521,6 +1526,23 @@ int specdec_accept(const void* x, int x_is_probs, int dtype, long long T, long l
       return set_error(kUnsupported, "top_k %d above this build's cap %d", max_top_k, kMaxTopK);
   }
   SPECDEC_CHECK_ARG(!has_top_p || top_p != nullptr, "top_p required when has_top_p");
+  return kOk;
+}
+
+}  // namespace sampler
+}  // namespace specdec
+
+extern "C" {
+
+int specdec_accept(const void* x, int x_is_probs, int dtype, long long T, long long V, const float* q,
+                   const long long* drafts, long long B, long long k, const long long* verified_lens,
+                   const float* temperature, const long long* top_k, const float* top_p, int max_top_k,
+                   int has_top_p, const float* u, const float* E, unsigned long long seed,
+                   unsigned long long offset_u, unsigned long long offset_E, long long* n_accept,
+                   long long* tail, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int st = check_accept_args(x, x_is_probs, dtype, T, V, q, drafts, B, k, verified_lens, temperature, top_k,
+                                 top_p, max_top_k, has_top_p, n_accept, tail))
+    return st;
   if (workspace_bytes < layout(T).total)
     return set_error(kWorkspaceTooSmall, "workspace %zu < %zu bytes", workspace_bytes, layout(T).total);
   DeviceInfo info;
@@ -1622,22 +1644,30 @@ constexpr size_t kNoAllocHeaderBytes = layout(1).rows;                     // st
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
 
-// The array's device address, looked up once per device with that device current.  In host code the array's
-// name is only a host-side stand-in, so kernels always receive this looked-up address.
+// The array's device address, looked up once per device with that device current (the first call on a device
+// does this set-up, so it should come before any stream capture).  In host code the array's name is only a
+// host-side stand-in, so kernels always receive this looked-up address.  Host threads calling at once serialise
+// on the first lookup per device only.  A cudaDeviceReset ends the context that owns the array: the cached
+// address is then stale, and this entry point must not be called again in that process.
 static int noalloc_scratch(void** out) {
-  static void* addr[64] = {nullptr};
+  static std::atomic<void*> addr[kMaxDevices];
+  static std::mutex mu;
   int dev = 0;
   SPECDEC_CUDA_TRY(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= 64) return set_error(kInvalidArgument, "device ordinal %d out of range", dev);
-  if (addr[dev] == nullptr) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess)
-      return set_error(kCudaError, "cudaGetSymbolAddress of the no-allocation scratch failed: %s",
-                       cudaGetErrorString(e));
-    addr[dev] = p;
+  if (dev < 0 || dev >= kMaxDevices) return set_error(kInvalidArgument, "device ordinal %d out of range", dev);
+  void* p = addr[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    std::lock_guard<std::mutex> lock(mu);
+    p = addr[dev].load(std::memory_order_relaxed);
+    if (p == nullptr) {
+      const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+      if (e != cudaSuccess)
+        return set_error(kCudaError, "cudaGetSymbolAddress of the no-allocation scratch failed: %s",
+                         cudaGetErrorString(e));
+      addr[dev].store(p, std::memory_order_release);
+    }
   }
-  *out = addr[dev];
+  *out = p;
   return kOk;
 }
 
@@ -1657,6 +1687,10 @@ extern "C" int specdec_accept_noalloc(const void* x, int x_is_probs, int dtype, 
                      "specdec_accept_noalloc takes at most %lld verified rows (got %lld): its fixed scratch holds "
                      "%zu bytes; use specdec_accept with a caller workspace for more",
                      kNoAllocMaxRows, T, kNoAllocBytes);
+  // A call the host rejects leaves the shared array alone (another call's work may be using it).
+  if (int st = check_accept_args(x, x_is_probs, dtype, T, V, q, drafts, B, k, verified_lens, temperature, top_k,
+                                 top_p, max_top_k, has_top_p, n_accept, tail))
+    return st;
   void* scratch = nullptr;
   if (int st = noalloc_scratch(&scratch)) return st;
   // The array keeps the previous call's contents: clear the tickets and keys that must start at zero (a call

@@ -746,15 +746,17 @@ __global__ void __launch_bounds__(256) store_kv_kernel(const __nv_bfloat16* key,
 }
 
 // ---------------------------------------------------------------------------------------- host side
+// The driver's tensor-map encoder (one entry point for every device), looked up on first use; the initialisation
+// of a function-local static is thread-safe.
 static PFN_cuTensorMapEncodeTiled_v12000 encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
+  static const PFN_cuTensorMapEncodeTiled_v12000 fn = []() -> PFN_cuTensorMapEncodeTiled_v12000 {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
+      return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    return nullptr;
+  }();
   return fn;
 }
 
@@ -781,12 +783,7 @@ template <int G, bool kPeers>
 static int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const CUtensorMap& km32,
                   const CUtensorMap& vm32, const Args& a, const PeerOuts& peers, int grid, bool early,
                   cudaStream_t stream) {
-  static bool configured = false;
-  if (!configured) {
-    SPECDEC_CUDA_TRY(cudaFuncSetAttribute(verify_attention_kernel<G, kPeers>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          kSmemBytes));
-    configured = true;
-  }
+  if (int st = ensure_dynamic_smem<verify_attention_kernel<G, kPeers>>(kSmemBytes)) return st;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3(kThreads);

@@ -1,13 +1,14 @@
-"""Host-side verification metadata (nanovllm/engine/batch_metadata.py:140-181): as plain lists
-(verify_varlen_metadata, the reference's shape) and packed into two arrays (pack_verify_metadata, what a round
-copies to the device).
+"""Host-side verification metadata (nanovllm/engine/batch_metadata.py:140-181), built with array operations
+straight into the two packed arrays a round copies to the device (pack_verify_metadata), plus where each
+verified draft goes among the round's input ids (draft_placement).  The values are those of the reference's
+verify_varlen_metadata; tests/golden/metadata.npz holds that function's output on random batches.
 
 A row needs only what the reference reads from a Sequence: its length (len(seq)), its last token and its
 block table (seq.target_kv.block_table).  PAD_SLOT rows store nothing; padding rows read the pad block.
 """
 from __future__ import annotations
 
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 
 PAD_SLOT = -1
 
@@ -23,53 +24,6 @@ class RowState:
 def slot_of(block_table: list[int], block_size: int, position: int) -> int:
     """batch_metadata.py:14-15."""
     return block_table[position // block_size] * block_size + position % block_size
-
-
-@dataclass
-class VerifyMetadata:
-    input_ids: list[int] = field(default_factory=list)      # draft positions hold 0, filled on device
-    positions: list[int] = field(default_factory=list)
-    slot_mapping: list[int] = field(default_factory=list)
-    cu_seqlens_q: list[int] = field(default_factory=lambda: [0])
-    cu_seqlens_k: list[int] = field(default_factory=lambda: [0])
-    block_tables: list[list[int]] = field(default_factory=list)
-    draft_index: list[int] = field(default_factory=list)    # where each verified draft goes in input_ids
-    draft_source: list[int] = field(default_factory=list)   # and where it is in the drafts [B, k], flattened
-
-
-def verify_varlen_metadata(rows: list[RowState], verified_lens: list[int], num_drafts: int, block_size: int,
-                           num_rows: int, num_tokens: int, pad_block_id: int, width: int) -> VerifyMetadata:
-    """batch_metadata.py:149-181: row r verifies its last token and its first verified_lens[r] - 1 drafts at
-    positions len-1 onward; the tokens left of num_tokens fill padding rows (<= k + 1 tokens each, positions 0
-    onward of the pad block); the row slots left of num_rows are empty."""
-    query_len = num_drafts + 1
-    m = VerifyMetadata()
-    for r, (row, length) in enumerate(zip(rows, verified_lens)):
-        table = row.block_table
-        start = row.length - 1
-        assert 1 <= length <= query_len
-        assert len(table) <= width and len(table) * block_size >= start + length
-        first = len(m.input_ids)
-        m.input_ids.extend([row.last_token] + [0] * (length - 1))
-        m.positions.extend(range(start, start + length))
-        m.slot_mapping.extend(slot_of(table, block_size, p) for p in range(start, start + length))
-        m.draft_index.extend(range(first + 1, first + length))
-        m.draft_source.extend(range(r * num_drafts, r * num_drafts + length - 1))
-        m.cu_seqlens_q.append(m.cu_seqlens_q[-1] + length)
-        m.cu_seqlens_k.append(m.cu_seqlens_k[-1] + start + length)
-        m.block_tables.append(table + [pad_block_id] * (width - len(table)))
-    left = num_tokens - len(m.input_ids)
-    for _ in range(num_rows - len(rows)):
-        length = min(left, query_len)
-        left -= length
-        m.input_ids.extend([0] * length)
-        m.positions.extend(range(length))
-        m.slot_mapping.extend([PAD_SLOT] * length)
-        m.cu_seqlens_q.append(m.cu_seqlens_q[-1] + length)
-        m.cu_seqlens_k.append(m.cu_seqlens_k[-1] + length)
-        m.block_tables.append([pad_block_id] * width)
-    assert left == 0, "the padding rows cannot hold the tokens left"
-    return m
 
 
 # ---------------------------------------------------------------------------------------------- packed arrays
@@ -137,3 +91,22 @@ def pack_verify_metadata(rows: list[RowState], verified_lens: list[int], num_dra
     v["cu_seqlens_q"][1:] = np.cumsum(all_q)
     v["cu_seqlens_k"][0] = 0
     v["cu_seqlens_k"][1:] = np.cumsum(all_k)
+
+
+def draft_placement(verified_lens, num_drafts: int):
+    """Where a round's verified drafts go: row r's drafts 0 .. verified_lens[r] - 2 sit right after its last token
+    in the flat input ids.  Returns (index into the input ids, index into the flattened drafts [B, k]), both int64
+    numpy arrays in row order (the draft_index / draft_source lists of batch_metadata.py:135-136, 167-168)."""
+    import numpy as np
+    lens = np.asarray(verified_lens, dtype=np.int64)
+    n = lens.shape[0]
+    first = np.zeros(n, dtype=np.int64)
+    if n:
+        np.cumsum(lens[:-1], out=first[1:])
+    drafts_per_row = lens - 1
+    row_of = np.repeat(np.arange(n, dtype=np.int64), drafts_per_row)
+    row_start = np.zeros(n, dtype=np.int64)
+    if n:
+        np.cumsum(drafts_per_row[:-1], out=row_start[1:])
+    j = np.arange(row_of.shape[0], dtype=np.int64) - row_start[row_of]
+    return first[row_of] + 1 + j, row_of * num_drafts + j

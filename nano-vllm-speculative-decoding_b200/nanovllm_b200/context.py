@@ -17,8 +17,8 @@ class Context:
     slot_mapping: torch.Tensor | None = None
     context_lens: torch.Tensor | None = None
     block_tables: torch.Tensor | None = None
-    query_len_per_seq: int = 1    # decode queries per sequence; a DFlash draft block passes its block size
-    causal: bool = True           # a DFlash draft block attends to its whole block: False
+    query_len_per_seq: int = 1    # query rows per sequence in the decode branch (k for a draft block)
+    causal: bool = True           # False lets every query row see every key of its block (the draft block)
 
 
 _CONTEXT = Context()

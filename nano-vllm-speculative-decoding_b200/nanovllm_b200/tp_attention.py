@@ -183,7 +183,8 @@ class TPAttention(nn.Module):
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor | None = None
                 ) -> torch.Tensor:
         """[T, H, D] attention output of all heads.  With exchange="peer" and no `out`, a view of this rank's
-        symmetric slot, valid until the call after next (slots alternate)."""
+        symmetric slot, valid only until this module's next call: a peer that has passed that call's barrier
+        may already be storing the call after it into the same slot.  Copy it, or pass `out`, to keep it longer."""
         T = q.numel() // ((self.num_heads // self.world) * self.head_dim)
         if self.exchange == "peer":
             result = self._forward_peer(q, k, v, T)

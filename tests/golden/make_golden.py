@@ -545,23 +545,28 @@ def metadata_cases() -> dict[str, np.ndarray]:
     from nanovllm.engine.batch_metadata import verify_varlen_metadata
     import random
     out: dict[str, np.ndarray] = {}
-    for case in range(12):
+    for case in range(24):
         rng = random.Random(1000 + case)
         k, block_size, width, pad = 7, 256, 8, 999
-        n = rng.randint(1, 10)
+        # cases 12-23: no rows at all (12, 13), every row verifying its last token only (14, 15), and row slots
+        # left empty after the padding rows' tokens (every other case from 16)
+        n = 0 if case in (12, 13) else rng.randint(1, 10)
         lengths, tokens, tables, lens = [], [], [], []
         next_block = 0
         for _ in range(n):
             length = rng.randint(1, 1500)
-            ln = rng.randint(1, k + 1) if case % 2 else k + 1
+            ln = 1 if case in (14, 15) else rng.randint(1, k + 1) if case % 2 else k + 1
             blocks = -(-(length - 1 + ln) // block_size)
             lengths.append(length)
             tokens.append(rng.randint(0, 150000))
             tables.append(list(range(next_block, next_block + blocks)))
             next_block += blocks
             lens.append(ln)
-        num_rows = n + rng.randint(0, 3)
-        num_tokens = sum(lens) + rng.randint(0, (num_rows - n) * (k + 1))
+        num_rows = n + rng.randint(1 if case >= 12 else 0, 3)
+        extra = rng.randint(0, (num_rows - n) * (k + 1))
+        if case >= 16 and case % 2 == 0:
+            extra = rng.randint(0, (num_rows - n - 1) * (k + 1))   # at least one row slot stays empty
+        num_tokens = sum(lens) + extra
         seqs = [_Seq(a, b, c) for a, b, c in zip(lengths, tokens, tables)]
         m = verify_varlen_metadata(seqs, lens, k, block_size, num_rows, num_tokens, pad, width)
         prefix = f"meta/{case:02d}/"
@@ -584,7 +589,14 @@ def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__)
     default_ref = os.environ.get("SPECDEC_REFERENCE", str(HERE.parents[2] / "reference"))
     parser.add_argument("--reference", default=default_ref)
+    parser.add_argument("--only", choices=["metadata"], default=None, help="write only this fixture file")
     args = parser.parse_args()
+    if args.only == "metadata":
+        import_reference(Path(args.reference))
+        meta = metadata_cases()
+        np.savez_compressed(HERE / "metadata.npz", **meta)
+        print(f"wrote {len(meta)} arrays to {HERE / 'metadata.npz'}")
+        return 0
     ss = import_reference(Path(args.reference))
     fixtures = {}
     fixtures.update(accept_cases(ss))

@@ -84,3 +84,27 @@ def test_no_alloc_accept_refuses_more_rows_than_its_scratch_holds():
     assert st == 3
     assert b"at most 1024 verified rows" in lib.specdec_last_error()
     assert (n == -1).all()                      # nothing was launched
+
+
+def test_no_alloc_accept_allocates_no_device_memory():
+    """The entry point's contract: after a first call on the device (which looks up the array's address), a call
+    leaves the device's free memory exactly where it was, and a call the host rejects launches nothing."""
+    from nanovllm_b200 import _lib
+    lib = _lib.load()
+    logits, q, drafts, lens, temps = case(4, 48, 7, torch.bfloat16, True)
+    assert call(lib, "specdec_accept_noalloc", logits, q, drafts, lens, temps, 11)[0] == 0
+    n_accept = torch.full((48,), -1, dtype=torch.int64, device=DEV)
+    tail = torch.full((48,), -1, dtype=torch.int64, device=DEV)
+    torch.cuda.synchronize()
+    free_before, _ = torch.cuda.mem_get_info(DEV)
+    stream = torch.cuda.current_stream().cuda_stream
+    args = [logits.data_ptr(), 0, 1, logits.shape[0], V, q.data_ptr(), drafts.data_ptr(), 48, 7, lens.data_ptr(),
+            temps.data_ptr(), None, None, 0, 0, None, None, 12, 0, 4, n_accept.data_ptr(), tail.data_ptr(), stream]
+    assert lib.specdec_accept_noalloc(*args) == 0
+    rejected = list(args)
+    rejected[2] = 9                                       # an unknown dtype code
+    assert lib.specdec_accept_noalloc(*rejected) == 1
+    torch.cuda.synchronize()
+    free_after, _ = torch.cuda.mem_get_info(DEV)
+    assert free_after == free_before
+    assert (n_accept >= 0).all() and (tail >= 0).all()
