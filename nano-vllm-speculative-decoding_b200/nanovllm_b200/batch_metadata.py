@@ -110,3 +110,49 @@ def draft_placement(verified_lens, num_drafts: int):
         np.cumsum(drafts_per_row[:-1], out=row_start[1:])
     j = np.arange(row_of.shape[0], dtype=np.int64) - row_start[row_of]
     return first[row_of] + 1 + j, row_of * num_drafts + j
+
+
+# ---------------------------------------------------------------------------------------------- draft blocks
+def draft_packed_sizes(num_rows: int, query_len: int, width: int) -> tuple[int, int]:
+    """Elements of the int64 part (input_ids | positions) and the int32 part (slot_mapping | context_lens |
+    block_tables) of a draft block forward's metadata, in that order."""
+    t = num_rows * query_len
+    return 2 * t, t + num_rows + num_rows * width
+
+
+def draft_packed_views(buf64, buf32, num_rows: int, query_len: int, width: int) -> dict:
+    t, r = num_rows * query_len, num_rows
+    return dict(input_ids=buf64[:t], positions=buf64[t:2 * t], slot_mapping=buf32[:t], context_lens=buf32[t:t + r],
+                block_tables=buf32[t + r:t + r + r * width].reshape(r, width))
+
+
+def pack_draft_block_metadata(rows: list[RowState], block_size: int, query_len: int, mask_token_id: int,
+                              num_rows: int, pad_block_id: int, width: int, buf64, buf32) -> None:
+    """The values of the reference's draft_block_metadata (batch_metadata.py:99-117) written into the packed
+    numpy buffers: row r's block is its last token (the anchor, position len-1) then query_len - 1 mask tokens at
+    the following positions, stored at their block-table slots, reading len-1 + query_len keys; padding rows are
+    query_len mask tokens at positions 0 onward that store nothing and read the pad block."""
+    import numpy as np
+    v = draft_packed_views(buf64, buf32, num_rows, query_len, width)
+    n = len(rows)
+    assert n <= num_rows
+    ids, positions, slots = (v[key].reshape(num_rows, query_len) for key in ("input_ids", "positions",
+                                                                           "slot_mapping"))
+    tables = v["block_tables"]
+    tables.fill(pad_block_id)
+    ids.fill(mask_token_id)
+    positions[:] = np.arange(query_len, dtype=np.int64)
+    slots.fill(PAD_SLOT)
+    v["context_lens"].fill(query_len)
+    if not n:
+        return
+    anchors = np.fromiter((row.length - 1 for row in rows), dtype=np.int64, count=n)
+    for i, row in enumerate(rows):
+        table = row.block_table
+        assert len(table) <= width and len(table) * block_size >= anchors[i] + query_len
+        tables[i, :len(table)] = table
+    ids[:n, 0] = np.fromiter((row.last_token for row in rows), dtype=np.int64, count=n)
+    pos = anchors[:, None] + np.arange(query_len, dtype=np.int64)[None, :]
+    positions[:n] = pos
+    slots[:n] = tables[np.arange(n)[:, None], pos // block_size].astype(np.int64) * block_size + pos % block_size
+    v["context_lens"][:n] = anchors + query_len

@@ -142,3 +142,90 @@ def store_context_kv(features: torch.Tensor, w_kv_stacked: torch.Tensor, k_norm:
         ptr(kv), width, kv.stride(0), T, layers, 0, num_kv_heads, None, ptr(k_norm.contiguous()), 128,
         ptr(cos_sin), cos_sin.shape[0], ptr(positions), ptr(slot_mapping.to(torch.int32)), ptr(k_cache),
         ptr(v_cache), k_cache.stride(0), num_slots, None, float(eps), ptr(err_word(device)), stream_of(device)))
+
+
+class DFlashDraftModel:
+    """DFlashDraftModel (nanovllm/models/dflash.py:55-115) with random-initialised weights (no checkpoints here):
+    embed_tokens, Qwen3 decoder layers, the final norm and LM head, the context projection fc + hidden_norm, and
+    DSpark's Markov head (markov_w1 / markov_w2 of rank markov_rank; 0 = DFlash, no head).  Its paged KV cache
+    [2, layers, blocks + 1, block_size, Hkv, 128] shares the target's block ids and pad block
+    (speculative.py:80-91).
+
+    forward runs a draft block: every row's anchor and mask tokens through the layers, each layer storing the
+    block's K/V at slot_mapping and attending, non-causally, to the context below the anchor and the whole block
+    (the decode branch of the paged attention with query_len_per_seq = block length, causal off)."""
+
+    def __init__(self, shape, aux_layer_ids: tuple[int, ...], device: torch.device, num_blocks: int,
+                 block_size: int = 256, markov_rank: int = 256, mask_token_id: int = 151669, seed: int = 1,
+                 init_scale: float = 0.02, markov_scale: float = 0.1):
+        from .target import random_layer_weights
+        self.shape = s = shape
+        self.device = device
+        self.aux_layer_ids = tuple(aux_layer_ids)
+        self.aux_width = len(self.aux_layer_ids) * s.hidden
+        self.mask_token_id = mask_token_id
+        self.block_size = block_size
+        g = torch.Generator(device=device).manual_seed(seed)
+        bf = torch.bfloat16
+
+        def rand(*dims, scale=init_scale):
+            return (torch.randn(*dims, device=device, generator=g, dtype=torch.float32) * scale).to(bf)
+
+        def norm_weight(n):
+            return (1.0 + 0.05 * torch.randn(n, device=device, generator=g)).to(bf)
+
+        self.embed = rand(s.vocab, s.hidden)
+        self.layers = [random_layer_weights(s, rand, norm_weight) for _ in range(s.layers)]
+        self.final_norm = norm_weight(s.hidden)
+        self.lm_head = rand(s.vocab, s.hidden)
+        self.w_fc = rand(s.hidden, self.aux_width, scale=init_scale / 2)
+        self.hidden_norm = norm_weight(s.hidden)
+        q_rows = s.heads * s.head_dim
+        # each layer's W_k | W_v rows (qkv_proj.weight[q_size:], dflash.py:92), stacked for one projection GEMM
+        self.w_kv = stacked_kv_weight([w["w_qkv"][q_rows:] for w in self.layers])
+        self.k_norm = torch.stack([w["k_norm"] for w in self.layers]).contiguous()
+        self.markov_head = None
+        if markov_rank:
+            from .markov import MarkovHeadWeights
+            self.markov_head = MarkovHeadWeights(rand(s.vocab, markov_rank, scale=markov_scale),
+                                                 rand(s.vocab, markov_rank, scale=markov_scale))
+        self.kv_cache = torch.zeros(2, s.layers, num_blocks + 1, block_size, s.kv_heads, s.head_dim, dtype=bf,
+                                    device=device)
+        from .fused import rope_cache
+        self.cos_sin = rope_cache(s.head_dim, s.max_position, s.rope_theta, device)
+        self.scale = s.head_dim ** -0.5
+
+    def forward(self, input_ids: torch.Tensor, positions: torch.Tensor, slot_mapping: torch.Tensor,
+                context_lens: torch.Tensor, block_tables: torch.Tensor, query_len: int) -> torch.Tensor:
+        """dflash.py:98-105 over block rows, sequence-major ([B * query_len]): hidden states after the final norm."""
+        from . import attention
+        from .target import decoder_layer
+        s = self.shape
+
+        def attend(q, layer_id):
+            return attention.paged_attention(q, self.kv_cache[0, layer_id], self.kv_cache[1, layer_id], block_tables,
+                                             self.scale, context_lens=context_lens, query_len_per_seq=query_len,
+                                             causal=False, early_launch=True)
+
+        h = torch.nn.functional.embedding(input_ids, self.embed)
+        residual = None
+        for layer_id, w in enumerate(self.layers):
+            h, residual = decoder_layer(s, w, layer_id, h, residual, positions, slot_mapping, self.kv_cache,
+                                        self.cos_sin, attend)
+        h, _ = fused_rmsnorm(h, self.final_norm, s.eps, residual=residual)
+        return h
+
+    def compute_logits(self, hidden: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """dflash.py:107-108: [rows, vocab] bf16 over every row."""
+        return torch.matmul(hidden, self.lm_head.t(), out=out)
+
+    def context_features(self, aux: torch.Tensor, *, fc_out: torch.Tensor | None = None,
+                         out: torch.Tensor | None = None) -> torch.Tensor:
+        """dflash.py:84-86: hidden_norm(fc(aux))."""
+        return context_features(aux, self.w_fc, self.hidden_norm, self.shape.eps, fc_out=fc_out, out=out)
+
+    def store_context_kv(self, features: torch.Tensor, positions: torch.Tensor, slot_mapping: torch.Tensor, *,
+                         kv_out: torch.Tensor | None = None) -> None:
+        """dflash.py:88-96: every layer's context K/V of the features at slot_mapping (slot -1 skipped)."""
+        store_context_kv(features, self.w_kv, self.k_norm, self.cos_sin, positions, slot_mapping, self.kv_cache,
+                         self.shape.eps, kv_out=kv_out)

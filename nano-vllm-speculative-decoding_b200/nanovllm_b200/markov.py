@@ -64,6 +64,12 @@ class MarkovQBuffer:
         self.ids = torch.full((batch, k, candidates), -1, dtype=torch.int32, device=device)
         self.candidates = candidates
 
+    def rows(self, batch: int) -> "MarkovQBuffer":
+        """The same buffer's first `batch` rows (views), for a smaller padded batch."""
+        view = object.__new__(MarkovQBuffer)
+        view.probs, view.ids, view.candidates = self.probs[:batch], self.ids[:batch], self.candidates
+        return view
+
 
 def markov_rows(logits: torch.Tensor, prev: torch.Tensor, sampling, noise: torch.Tensor | None,
                 drafts: torch.Tensor, draft_probs: torch.Tensor | None, candidates: int, markov_head) -> None:
@@ -80,7 +86,7 @@ def markov_rows(logits: torch.Tensor, prev: torch.Tensor, sampling, noise: torch
     greedy = draft_probs is None
     if not greedy and candidates and qbuf is None:
         draft_probs.zero_()                     # q is zero outside each row's candidates (speculative.py:171)
-    prev_buf = prev.to(torch.int64).clone()
+    prev_buf = prev.to(torch.int64).clone(memory_format=torch.contiguous_format)   # the kernel writes it
     weights = markov_head if isinstance(markov_head, MarkovHeadWeights) else None
     e_buf = None
     if weights is not None:

@@ -34,15 +34,17 @@ def paged_attention(q, k_cache, v_cache, block_tables, q_starts, q_lens, k_lens,
             continue
         positions = np.arange(kl)
         slots = block_tables[r, positions // block_size].astype(np.int64) * block_size + positions % block_size
-        keys = np.repeat(keys_all[slots], group, axis=1)        # [L, H, D]
-        values = np.repeat(values_all[slots], group, axis=1)
-        queries = q[qs:qs + ql]                                  # [n, H, D]
-        scores = np.einsum("nhd,lhd->hnl", queries, keys) * np.float32(scale)
+        keys = keys_all[slots].transpose(1, 2, 0)                 # [Hkv, D, L]
+        values = values_all[slots].transpose(1, 0, 2)             # [Hkv, L, D]
+        # query head h reads KV head h // group: per KV head, its group's queries as (g, n) rows
+        queries = q[qs:qs + ql].reshape(ql, Hkv, group, D).transpose(1, 2, 0, 3).reshape(Hkv, group * ql, D)
+        scores = np.matmul(queries, keys) * np.float32(scale)     # [Hkv, G n, L]
         if causal:
             allowed = positions[None, :] <= (kl - ql + np.arange(ql))[:, None]
-            scores = np.where(allowed[None], scores, -np.inf)
+            scores = np.where(np.tile(allowed, (group, 1))[None], scores, -np.inf)
         scores = scores - scores.max(axis=-1, keepdims=True)
         weights = np.exp(scores)
         weights /= weights.sum(axis=-1, keepdims=True)
-        out[qs:qs + ql] = np.einsum("hnl,lhd->nhd", weights, values)
+        o = np.matmul(weights, values)                            # [Hkv, G n, D]
+        out[qs:qs + ql] = o.reshape(Hkv, group, ql, D).transpose(2, 0, 1, 3).reshape(ql, H, D)
     return out

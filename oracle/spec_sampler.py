@@ -123,19 +123,20 @@ def accept_greedy(target_logits: np.ndarray, drafts: np.ndarray):
 
 
 # ------------------------------------------------------------------------------------------ parity flags
-def near_tie_flags(p: np.ndarray, q: np.ndarray, drafts: np.ndarray, verified_lens: np.ndarray, u: np.ndarray,
-                   noise: np.ndarray, eps: float = 1e-6) -> np.ndarray:
-    """Requests [B] whose outcome may legitimately differ between two correct fp32 implementations whose p
-    agree to `eps` relative: an accept draw with |u q_d - p_d| <= eps * max(p_d, u q_d), or a tail race whose
-    winner is within the p uncertainty of another candidate.  The bit-exact comparisons skip these rows; tests
-    count them."""
+def near_tie_kinds(p: np.ndarray, q: np.ndarray, drafts: np.ndarray, verified_lens: np.ndarray, u: np.ndarray,
+                   noise: np.ndarray, eps: float = 1e-6) -> tuple[np.ndarray, np.ndarray]:
+    """Requests [B] whose outcome may legitimately differ between two correct fp32 implementations whose p agree
+    to `eps` relative, by kind: (accept, race).  accept: an accept draw with |u q_d - p_d| <= eps * max(p_d, u q_d)
+    (the exemption the parity rule states).  race: the tail race's winner is within the p uncertainty of another
+    candidate (two softmaxes summing in different orders disagree in the last bits of p, so such a race may pick
+    either).  Tests compare the other requests bit for bit and count each kind."""
     batch_size, num_drafts = drafts.shape
     starts, positions, verified = verified_positions(verified_lens, num_drafts)
     p_draft = p[positions, drafts].astype(np.float64)
     q_draft = np.take_along_axis(q, drafts[..., None], axis=-1)[..., 0].astype(np.float64)
     uq = u.astype(np.float64) * q_draft
     close = (np.abs(uq - p_draft) <= eps * np.maximum(p_draft, uq)) & verified
-    flags = close.any(axis=-1)
+    accept_flags = close.any(axis=-1)
     n_accept, _ = accept_random_varlen(p, q, drafts, verified_lens, u, noise)
     rows = np.arange(batch_size)
     p_next = p[starts + n_accept].astype(np.float64)
@@ -149,5 +150,12 @@ def near_tie_flags(p: np.ndarray, q: np.ndarray, drafts: np.ndarray, verified_le
     lower = ratio[rows, win] - slack[rows, win]
     upper = ratio + slack
     upper[rows, win] = -np.inf
-    flags |= upper.max(axis=-1) >= lower
-    return flags
+    race_flags = (upper.max(axis=-1) >= lower) & ~accept_flags
+    return accept_flags, race_flags
+
+
+def near_tie_flags(p: np.ndarray, q: np.ndarray, drafts: np.ndarray, verified_lens: np.ndarray, u: np.ndarray,
+                   noise: np.ndarray, eps: float = 1e-6) -> np.ndarray:
+    """Requests [B] flagged by either kind of near_tie_kinds."""
+    accept_flags, race_flags = near_tie_kinds(p, q, drafts, verified_lens, u, noise, eps)
+    return accept_flags | race_flags

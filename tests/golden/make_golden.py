@@ -585,15 +585,122 @@ def metadata_cases() -> dict[str, np.ndarray]:
     return out
 
 
+def draft_block_cases() -> dict[str, np.ndarray]:
+    """nanovllm/engine/batch_metadata.py draft_block_metadata on random batches (ragged block tables, padded batch
+    sizes, no rows); ragged inputs stored padded with -1."""
+    from nanovllm.engine.batch_metadata import draft_block_metadata
+    import random
+    out: dict[str, np.ndarray] = {}
+    for case in range(12):
+        rng = random.Random(2000 + case)
+        k, block_size, width, pad, mask = 7, 256, 8, 999, 151669
+        n = 0 if case == 0 else rng.randint(1, 10)
+        lengths, tokens, tables = [], [], []
+        next_block = 0
+        for _ in range(n):
+            length = rng.randint(1, 1500)
+            blocks = -(-(length - 1 + k) // block_size)
+            lengths.append(length)
+            tokens.append(rng.randint(0, 150000))
+            tables.append(list(range(next_block, next_block + blocks)))
+            next_block += blocks
+        padded_rows = n + rng.randint(0 if n else 1, 4)
+        seqs = [_Seq(a, b, c) for a, b, c in zip(lengths, tokens, tables)]
+        m = draft_block_metadata(seqs, block_size, k, mask, padded_rows, pad, width)
+        prefix = f"draft/{case:02d}/"
+        padded = np.full((n, width), -1, dtype=np.int64)
+        for r, t in enumerate(tables):
+            padded[r, :len(t)] = t
+        out[prefix + "lengths"] = np.array(lengths, dtype=np.int64)
+        out[prefix + "last_tokens"] = np.array(tokens, dtype=np.int64)
+        out[prefix + "scalars"] = np.array([k, block_size, mask, padded_rows, pad, width], dtype=np.int64)
+        out[prefix + "tables"] = padded
+        for key in ("input_ids", "positions", "slot_mapping", "context_lens"):
+            out[prefix + key] = np.array(getattr(m, key), dtype=np.int64)
+        out[prefix + "block_tables"] = np.array(m.block_tables, dtype=np.int64)
+    return out
+
+
+def qwen3_forward_cases(reference: Path) -> dict[str, np.ndarray]:
+    """The reference's Qwen3ForCausalLM (nanovllm/models/qwen3.py) on CPU bf16 over the inputs of
+    tests/golden/qwen3_case.py: the verify layout (8 tokens at the end of each row's context, causal) through the
+    reference's paged-attention stand-in (tests/fake_paged_attention.py, whose decode branch with 8 queries per
+    row applies the verify rule), the aux layers' outputs exported (qwen3.py:186-190), all logits.  The fixture
+    holds the outputs, the stored K/V rows and checksums of the inputs (regenerated from seeds by the tests)."""
+    import torch.distributed as dist
+    from transformers import Qwen3Config
+    sys.path.insert(0, str(reference / "tests"))
+    sys.path.insert(0, str(HERE))
+    import fake_paged_attention as fpa
+    import qwen3_case as Q
+    from nanovllm.layers import attention as attention_module
+    from nanovllm.models.qwen3 import Qwen3ForCausalLM
+    from nanovllm.utils.context import reset_context, set_context
+    if not dist.is_initialized():
+        dist.init_process_group("gloo", init_method="tcp://127.0.0.1:29517", world_size=1, rank=0)
+    case = Q.inputs()
+    config = Qwen3Config(vocab_size=Q.VOCAB, hidden_size=Q.HIDDEN, intermediate_size=Q.FFN,
+                         num_hidden_layers=Q.LAYERS, num_attention_heads=Q.HEADS, num_key_value_heads=Q.KV_HEADS,
+                         head_dim=Q.HEAD_DIM, max_position_embeddings=Q.MAX_POSITION, rms_norm_eps=Q.EPS,
+                         rope_theta=Q.ROPE_THETA, attention_bias=False, tie_word_embeddings=False,
+                         hidden_act="silu")
+    default = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        model = Qwen3ForCausalLM(config)
+    finally:
+        torch.set_default_dtype(default)
+    m = model.model
+    m.embed_tokens.weight.data.copy_(case["embed"])
+    m.norm.weight.data.copy_(case["final_norm"])
+    model.lm_head.weight.data.copy_(case["lm_head"])
+    for layer, w, (k_cache, v_cache) in zip(m.layers, case["layers"], case["caches"]):
+        attn = layer.self_attn
+        for module, key in ((attn.qkv_proj, "w_qkv"), (attn.o_proj, "w_o"), (attn.q_norm, "q_norm"),
+                            (attn.k_norm, "k_norm"), (layer.mlp.gate_up_proj, "w_gate_up"),
+                            (layer.mlp.down_proj, "w_down"), (layer.input_layernorm, "in_norm"),
+                            (layer.post_attention_layernorm, "post_norm")):
+            module.weight.data.copy_(w[key])
+        attn.attn.k_cache, attn.attn.v_cache = k_cache.clone(), v_cache.clone()
+    m.aux_layer_ids = Q.AUX_LAYER_IDS
+    T = case["input_ids"].shape[0]
+    original = attention_module.Attention.forward
+    attention_module.Attention.forward = fpa.attention_forward
+    set_context(False, slot_mapping=case["slot_mapping"], context_lens=case["key_lens"],
+                block_tables=case["tables"], query_len_per_seq=Q.QUERY_LEN, causal=True)
+    try:
+        with torch.inference_mode():
+            aux = torch.zeros(T, len(Q.AUX_LAYER_IDS) * Q.HIDDEN, dtype=torch.bfloat16)
+            hidden = model(case["input_ids"], case["positions"], aux)
+            logits = model.compute_logits(hidden, all_logits=True)
+    finally:
+        attention_module.Attention.forward = original
+        reset_context()
+    slots = case["slot_mapping"].long()
+    out = {"qwen3/hidden": hidden.float().numpy(), "qwen3/aux": aux.float().numpy(),
+           "qwen3/logits": logits.float().numpy(), "qwen3/checksums": np.array(Q.checksums(case))}
+    for i, layer in enumerate(m.layers):
+        cache_k, cache_v = layer.self_attn.attn.k_cache, layer.self_attn.attn.v_cache
+        out[f"qwen3/k_stored{i}"] = cache_k.view(-1, Q.KV_HEADS, Q.HEAD_DIM)[slots].float().numpy()
+        out[f"qwen3/v_stored{i}"] = cache_v.view(-1, Q.KV_HEADS, Q.HEAD_DIM)[slots].float().numpy()
+    return out
+
+
 def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__)
     default_ref = os.environ.get("SPECDEC_REFERENCE", str(HERE.parents[2] / "reference"))
     parser.add_argument("--reference", default=default_ref)
-    parser.add_argument("--only", choices=["metadata"], default=None, help="write only this fixture file")
+    parser.add_argument("--only", choices=["metadata", "qwen3"], default=None, help="write only this fixture file")
     args = parser.parse_args()
+    if args.only == "qwen3":
+        import_reference(Path(args.reference))
+        fx = qwen3_forward_cases(Path(args.reference))
+        np.savez_compressed(HERE / "qwen3.npz", **fx)
+        print(f"wrote {len(fx)} arrays to {HERE / 'qwen3.npz'}")
+        return 0
     if args.only == "metadata":
         import_reference(Path(args.reference))
-        meta = metadata_cases()
+        meta = metadata_cases() | draft_block_cases()
         np.savez_compressed(HERE / "metadata.npz", **meta)
         print(f"wrote {len(meta)} arrays to {HERE / 'metadata.npz'}")
         return 0
@@ -617,7 +724,7 @@ def main() -> int:
     attn = attention_cases(Path(args.reference))
     np.savez_compressed(HERE / "attention.npz", **attn)
     print(f"wrote {len(attn)} arrays to {HERE / 'attention.npz'}")
-    meta = metadata_cases()
+    meta = metadata_cases() | draft_block_cases()
     np.savez_compressed(HERE / "metadata.npz", **meta)
     print(f"wrote {len(meta)} arrays to {HERE / 'metadata.npz'}")
     fwd = forward_helper_cases()
@@ -626,6 +733,9 @@ def main() -> int:
     ctx = ctx_store_cases(Path(args.reference))
     np.savez_compressed(HERE / "ctx_store.npz", **ctx)
     print(f"wrote {len(ctx)} arrays to {HERE / 'ctx_store.npz'}")
+    fx = qwen3_forward_cases(Path(args.reference))
+    np.savez_compressed(HERE / "qwen3.npz", **fx)
+    print(f"wrote {len(fx)} arrays to {HERE / 'qwen3.npz'}")
     return 0
 
 

@@ -7,11 +7,13 @@ from pathlib import Path
 import numpy as np
 import pytest
 
-from nanovllm_b200.batch_metadata import (PAD_SLOT, RowState, draft_placement, pack_verify_metadata, packed_sizes,
-                                          packed_views)
+from nanovllm_b200.batch_metadata import (PAD_SLOT, RowState, draft_packed_sizes, draft_packed_views,
+                                          draft_placement, pack_draft_block_metadata, pack_verify_metadata,
+                                          packed_sizes, packed_views)
 
 META = np.load(Path(__file__).parent / "golden" / "metadata.npz")
-CASES = sorted({key.split("/")[1] for key in META.files})
+CASES = sorted({key.split("/")[1] for key in META.files if key.startswith("meta/")})
+DRAFT_CASES = sorted({key.split("/")[1] for key in META.files if key.startswith("draft/")})
 
 
 def golden_case(case):
@@ -118,3 +120,21 @@ def test_packed_metadata_rejects_overfull_padding():
     n64, n32 = packed_sizes(2, 20, 4)
     with pytest.raises(AssertionError):
         pack_verify_metadata(rows, [8], 7, 256, 2, 20, 9, 4, np.zeros(n64, np.int64), np.zeros(n32, np.int32))
+
+
+@pytest.mark.parametrize("case", DRAFT_CASES)
+def test_draft_block_metadata_matches_the_reference(case):
+    """The draft block forward's packed metadata against the reference's draft_block_metadata (batch_metadata.py:
+    99-117): anchors and mask tokens, positions, slots, context lengths and block tables, padding rows included."""
+    c = {key.split("/")[2]: META[key] for key in META.files if key.startswith(f"draft/{case}/")}
+    k, bs, mask, num_rows, pad, width = (int(x) for x in c["scalars"])
+    rows = [RowState(length=int(n), last_token=int(t), block_table=[int(b) for b in table if b >= 0])
+            for n, t, table in zip(c["lengths"], c["last_tokens"], c["tables"])]
+    n64, n32 = draft_packed_sizes(num_rows, k, width)
+    buf64 = np.full(n64, -7, dtype=np.int64)
+    buf32 = np.full(n32, -7, dtype=np.int32)
+    pack_draft_block_metadata(rows, bs, k, mask, num_rows, pad, width, buf64, buf32)
+    v = draft_packed_views(buf64, buf32, num_rows, k, width)
+    for key in ("input_ids", "positions", "slot_mapping", "context_lens"):
+        assert v[key].tolist() == c[key].tolist(), key
+    assert v["block_tables"].tolist() == c["block_tables"].tolist()
