@@ -48,6 +48,8 @@ def parse_args():
     p.add_argument("--batch", type=int, default=64)
     p.add_argument("--ctx", type=int, default=1000, help="mean context length (tokens before the verified ones)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-extra", action="store_true",
+                   help="skip the extra workloads (4k round, 16k attention, config-4 round; TP layer under torchrun)")
     p.add_argument("--kernel", choices=["attention", "accept", "accept_topk", "accept_greedy", "sample", "markov",
                                         "ctx_store", "after_verify", "attention_tp"],
                    default=None,
@@ -231,98 +233,388 @@ def accept_timing(torch, w) -> dict:
             "GBps": round(algorithmic / (us * 1e-6) / 1e9, 1)}
 
 
+# ---------------------------------------------------------------------------------------------- more workloads
+def weight_bytes(model) -> int:
+    """Bytes of the matrices a forward reads once (every layer's weights and the LM head; the embedding is only
+    gathered)."""
+    total = model.lm_head.numel() * 2 + model.final_norm.numel() * 2
+    for w in model.layers:
+        total += sum(t.numel() * t.element_size() for t in w.values())
+    return total
+
+
+def round_bytes(w, num_tokens: int) -> dict:
+    """Algorithmic HBM bytes of one config-3-shaped round: the target's weights, every row's K/V read once per
+    layer (context + verified positions) and the new K/V stored, the logits written by the LM head and read by
+    the sampler, and the tail rows (q and logits) the race reads again."""
+    s = w.shape
+    per_key = s.kv_heads * s.head_dim * 2 * 2                       # K and V, bf16, one layer
+    keys = sum(n + K_DRAFTS for n in w.lengths)                     # row r reads len - 1 + 8 keys
+    batch = len(w.lengths)
+    out = {"weights": weight_bytes(w.target), "kv": s.layers * (keys + num_tokens) * per_key,
+           "logits": 2 * num_tokens * V * 2 + batch * V * (4 + 2)}
+    out["total"] = sum(out.values())
+    return out
+
+
+def round_timing(torch, device, ctx: int, steps: int, warmup: int, hbm_peak: float) -> dict:
+    """The verify + accept round of config 3's shape at another context length (the north-star target: ~4k),
+    device-timed over `steps` rounds after `warmup`; bytes and the roofline time at the measured copy peak."""
+    w = build_workload(torch, device, 64, ctx, seed=4321)
+    rnd = w.round
+    gen = torch.Generator(device=device).manual_seed(5)
+    num_tokens = rnd.load(w.rows)
+    for _ in range(warmup):
+        rnd.verify_and_accept(num_tokens, 64, w.drafts, w.q, w.sampling, gen)
+    accepted = torch.zeros((), dtype=torch.int64, device=device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record()
+    for _ in range(steps):
+        n_accept, _ = rnd.verify_and_accept(num_tokens, 64, w.drafts, w.q, w.sampling, gen)
+        accepted += n_accept.sum() + 64
+    end.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / steps
+    nbytes = round_bytes(w, num_tokens)
+    floor_ms = nbytes["total"] / (hbm_peak * 1e9) * 1e3
+    out = {"workload": f"config-3 round at contexts ~{ctx} (U[ctx-50, ctx+50]), B=64 x 8, temperature 1",
+           "ms_per_round": round(ms, 3), "accepted_tok_s": round(float(accepted.item()) / steps / (ms / 1e3), 1),
+           "algorithmic_bytes": nbytes, "hbm_roofline_ms": round(floor_ms, 3),
+           "x_roofline": round(ms / floor_ms, 3), "frac": round(floor_ms / ms, 4), "steps": steps}
+    w.target.close()
+    del w, rnd
+    torch.cuda.empty_cache()
+    return out
+
+
+def attention_long_timing(torch, device, ctx: int, steps: int, hbm_peak: float) -> dict:
+    """One layer's verify attention for 64 rows x 8 queries at contexts ~ctx (config 5's 16k case), as a CUDA
+    graph of `steps` launches over 3 rotating caches (each beyond L2)."""
+    from nanovllm_b200 import attention
+    R, H, Hkv, D, bs = 64, 32, 8, 128, 256
+    g = torch.Generator().manual_seed(16)
+    k_lens = [n + 8 for n in torch.randint(ctx - 50, ctx + 51, (R,), generator=g).tolist()]
+    nb = [math.ceil(k / bs) for k in k_lens]
+    NB = sum(nb) + 1
+    perm = torch.randperm(NB - 1, generator=g).tolist()
+    tables = torch.full((R, max(nb)), NB - 1, dtype=torch.int32)
+    used = 0
+    for r, n in enumerate(nb):
+        tables[r, :n] = torch.tensor(perm[used:used + n])
+        used += n
+    copies = 3
+    caches = []
+    for _ in range(copies):
+        kc = torch.empty(NB, bs, Hkv, D, dtype=torch.bfloat16, device=device).normal_()
+        vc = torch.empty(NB, bs, Hkv, D, dtype=torch.bfloat16, device=device).normal_()
+        caches.append((kc, vc))
+    q = torch.randn(R * 8, H, D, device=device).bfloat16()
+    out = torch.empty_like(q)
+    cu_q = torch.arange(0, 8 * R + 1, 8, dtype=torch.int32, device=device)
+    cu_k = torch.tensor([0] + torch.tensor(k_lens).cumsum(0).tolist(), dtype=torch.int32, device=device)
+    tables = tables.to(device)
+
+    def launch(i):
+        kc, vc = caches[i % copies]
+        attention.paged_attention(q, kc, vc, tables, D ** -0.5, cu_seqlens_q=cu_q, cu_seqlens_k=cu_k,
+                                  max_seqlen_q=8, out=out)
+
+    for i in range(copies):
+        launch(i)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(steps):
+            launch(i)
+    graph.replay()
+    us = time_events(torch, graph.replay, 3) / steps
+    algorithmic = sum(k_lens) * Hkv * D * 2 * 2 + 2 * R * 8 * H * D * 2
+    achieved = algorithmic / (us * 1e-6) / 1e9
+    del caches, graph
+    torch.cuda.empty_cache()
+    return {"workload": f"verify attention, 64 rows x 8 queries, contexts ~{ctx}, 32/8 heads of 128",
+            "us_per_launch": round(us, 2), "algorithmic_bytes": algorithmic, "achieved_GBps": round(achieved, 1),
+            "frac": round(achieved / hbm_peak, 4), "timing": f"CUDA graph of {steps} launches over {copies} caches"}
+
+
+def dspark_timing(torch, device, steps: int, warmup: int, hbm_peak: float) -> dict:
+    """Benchmark config 4: the variable-length DSpark round end to end through SpeculativeDecoder.run_round
+    (propose: the 5-layer draft's block forward + 7 Markov rows at top_k 128; verify at the lengths' token
+    bucket with the aux export and after_verify inside the graph; the fused accept; the one D2H copy).  B = 64
+    rows at contexts ~3000, verified lengths uniform on {1..8} (mean 4.5): four seeded length sets, cycled."""
+    from types import SimpleNamespace
+    from nanovllm_b200 import spec_sampler as S
+    from nanovllm_b200.batch_metadata import RowState
+    from nanovllm_b200.dflash import DFlashDraftModel
+    from nanovllm_b200.speculative import DFlashDrafter, SpeculativeDecoder
+    from nanovllm_b200.target import Qwen3Shape, Qwen3Target
+    B, ctx, bs = 64, 3000, 256
+    g = torch.Generator().manual_seed(3000)
+    lengths = torch.randint(ctx - 50, ctx + 51, (B,), generator=g).tolist()
+    lens_sets = [torch.randint(1, K_DRAFTS + 2, (B,), generator=g).tolist() for _ in range(4)]
+    blocks = [math.ceil((n + K_DRAFTS) / bs) for n in lengths]
+    num_blocks = sum(blocks) + 4
+    width = max(blocks)
+    perm = torch.randperm(num_blocks, generator=g).tolist()
+    shape = Qwen3Shape()
+    target = Qwen3Target(shape, device, num_blocks, bs, seed=30)
+    model = DFlashDraftModel(Qwen3Shape(layers=5), shape.aux_layer_ids, device, num_blocks, bs, markov_rank=256,
+                             seed=31)
+    for cache in (target.kv_cache, model.kv_cache):
+        for layer in range(cache.shape[1]):
+            cache[:, layer, :num_blocks].normal_()
+    rows, used = [], 0
+    for n, nb in zip(lengths, blocks):
+        rows.append(RowState(length=n, last_token=int(torch.randint(V, (1,), generator=g)),
+                             block_table=perm[used:used + nb]))
+        used += nb
+    drafter = DFlashDrafter(model, K_DRAFTS, [B], width, target.pad_block_id)
+    buckets = sorted({-(-sum(lens) // (K_DRAFTS + 1)) * (K_DRAFTS + 1) for lens in lens_sets})
+    dec = SpeculativeDecoder(target, drafter, K_DRAFTS, width, token_counts=buckets)
+    sampling = S.sampling_tensors([SimpleNamespace(temperature=1.0, top_k=128, top_p=1.0)] * B, device)
+    gen = torch.Generator(device=device).manual_seed(6)
+    for i in range(max(warmup, 2)):
+        dec.run_round(rows, sampling, gen, verified_lens=lens_sets[i % 4])
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    tokens = verified = 0
+    torch.cuda.synchronize()
+    start.record()
+    for i in range(steps):
+        out = dec.run_round(rows, sampling, gen, verified_lens=lens_sets[i % 4])
+        tokens += sum(len(r) for r in out)
+        verified += sum(lens_sets[i % 4])
+    end.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / steps
+    # the propose alone (block graph + sampling graph), device-timed
+    start.record()
+    for _ in range(steps):
+        drafter.propose(rows, sampling, gen)
+    end.record()
+    torch.cuda.synchronize()
+    propose_ms = start.elapsed_time(end) / steps
+    # algorithmic bytes of a round at the mean verified length
+    T = verified / steps
+    per_key = shape.kv_heads * 128 * 2 * 2
+    ctx_keys = sum(n - 1 for n in lengths)
+    markov_w2 = model.markov_head.w2.numel() * 2
+    nbytes = {
+        "target_weights": weight_bytes(target),
+        "target_kv": round(shape.layers * (ctx_keys + 2 * T) * per_key),
+        "target_logits": round(2 * T * V * 2 + B * V * (4 + 2)),
+        "aux_and_context": round(model.w_fc.numel() * 2 + model.w_kv.numel() * 2 + 2 * T * len(shape.aux_layer_ids)
+                                 * shape.hidden * 2 + T * model.shape.layers * per_key),
+        "draft_weights": weight_bytes(model),
+        "draft_kv": (model.shape.layers * (ctx_keys + 2 * B * K_DRAFTS) * per_key),
+        "draft_logits_and_markov": B * K_DRAFTS * V * 2 + K_DRAFTS * (markov_w2 + B * V * 2),
+    }
+    nbytes["total"] = sum(nbytes.values())
+    floor_ms = nbytes["total"] / (hbm_peak * 1e9) * 1e3
+    dec.close()
+    del dec, drafter, model, target
+    torch.cuda.empty_cache()
+    return {"workload": "config 4: variable-length DSpark round, B=64, contexts ~3000, verified lengths U{1..8} "
+                        "(4 seeded sets, graph buckets " + ",".join(map(str, buckets)) + "), 5-layer draft + "
+                        "rank-256 Markov head, top_k 128, 36-layer target, temperature 1",
+            "ms_per_round": round(ms, 3), "accepted_tok_s": round(tokens / steps / (ms / 1e3), 1),
+            "tokens_per_round": round(tokens / steps, 2), "mean_verified_tokens": round(T, 1),
+            "propose_ms": round(propose_ms, 3), "algorithmic_bytes": nbytes, "hbm_roofline_ms": round(floor_ms, 3),
+            "x_roofline": round(ms / floor_ms, 3), "frac": round(floor_ms / ms, 4), "steps": steps,
+            "timing": "CUDA events around run_round (host metadata, H2D, graphs, accept, D2H) per round"}
+
+
 # ---------------------------------------------------------------------------------------------- CPU side
-def cpu_round_sample(rows_sample: int, layers_sample: int, ctx: int, threads: int):
-    """The reference's algorithm for the path on CPU (numpy oracle): paged attention of `rows_sample` rows over
-    `layers_sample` layers and the sampler (probs_from_logits + accept_random) of the same rows; returns the
-    seconds it took and the work it covered."""
+class CpuRound:
+    """The reference's algorithm for a config-3 round on the host cores, as the numpy oracle restates it: one
+    step is 1/36 of a round - one Qwen3-8B decoder layer over all 64 rows x 8 verified tokens (oracle/forward.py:
+    RMSNorms, the qkv / o / gate_up / down GEMMs on all BLAS threads, q/k norm + RoPE, the paged K/V store and
+    oracle/attention.py's paged attention over ~ctx keys per row, split over threads), 1/36 of the LM head's
+    vocabulary for the 512 tokens, and the sampler (probs_from_logits + accept_random at temperature 1) of two
+    requests (64 / 32 of them per round).  A round = 36 x (layer + LM-head share) + 32 x (two requests' accept)."""
+
+    LAYERS, BATCH = 36, 64
+
+    def __init__(self, ctx: int, threads: int, seed: int = 0):
+        import numpy as np
+        from oracle import ctx_store as OC
+        from oracle import spec_sampler as OS
+        self.np, self.threads = np, threads
+        rng = np.random.default_rng(seed)
+        H, Hkv, D, hidden, inter, bs = 32, 8, 128, 4096, 12288, 256
+
+        pool = rng.standard_normal(1 << 22, dtype=np.float32)
+
+        def rand(*shape, scale=0.02):
+            """fp32 N(0, scale^2) values tiled from a 4M-value pool (drawing 200M values one by one takes
+            seconds; the timing depends on the shapes, not on the values being independent)."""
+            x = np.resize(pool, shape)
+            x *= np.float32(scale)
+            return x
+
+        def norm(n):
+            return OC.bf16(1.0 + 0.05 * rng.standard_normal(n, dtype=np.float32))
+
+        self.w = dict(w_qkv=rand((H + 2 * Hkv) * D, hidden), w_o=rand(hidden, H * D), w_gate_up=rand(2 * inter, hidden),
+                      w_down=rand(hidden, inter), in_norm=norm(hidden), post_norm=norm(hidden), q_norm=norm(D),
+                      k_norm=norm(D))
+        B = self.BATCH
+        lengths = rng.integers(ctx - 50, ctx + 51, B) if ctx > 100 else np.full(B, ctx)
+        blocks = -(-(lengths + K_DRAFTS) // bs)
+        num_blocks = int(blocks.sum()) + 1
+        perm = rng.permutation(num_blocks - 1)
+        self.tables = np.full((B, int(blocks.max())), num_blocks - 1, dtype=np.int64)
+        used = 0
+        for r, nb in enumerate(blocks):
+            self.tables[r, :nb] = perm[used:used + nb]
+            used += nb
+        self.k_cache = rand(num_blocks, bs, Hkv, D, scale=1.0)
+        self.v_cache = rand(num_blocks, bs, Hkv, D, scale=1.0)
+        self.v_cache = np.roll(self.v_cache, 12345)
+        self.positions = (lengths[:, None] - 1 + np.arange(K_DRAFTS + 1)[None, :]).reshape(-1)
+        rows = np.repeat(np.arange(B), K_DRAFTS + 1)
+        self.slots = self.tables[rows, self.positions // bs] * bs + self.positions % bs
+        self.q_starts = np.arange(B) * (K_DRAFTS + 1)
+        self.q_lens = np.full(B, K_DRAFTS + 1)
+        self.k_lens = lengths + K_DRAFTS
+        self.h = rand(B * (K_DRAFTS + 1), hidden, scale=1.0)
+        self.residual = rand(B * (K_DRAFTS + 1), hidden, scale=1.0)
+        self.cos_sin = OC.rope_cache(D, 40960, 1000000.0)
+        self.lm_share = rand(-(-V // self.LAYERS), hidden)
+        # two requests' sampler inputs: logits ~ N(0, 1.65^2) (a scale at which the acceptance, ~1.7 tokens per
+        # row, is the GPU round's on its random-init target), q = softmax of N(0, 1) draft logits, drafts raced
+        # from q
+        self.logits = (rng.standard_normal((2 * (K_DRAFTS + 1), V), dtype=np.float32) * np.float32(1.65))
+        self.q = OS.softmax(rng.standard_normal((2, K_DRAFTS, V), dtype=np.float32))
+        self.drafts = OS.race(self.q, OS.clamp_noise(rng.exponential(size=(2, K_DRAFTS, V)).astype(np.float32)))
+        self.rng = rng
+        self.heads, self.kv_heads = H, Hkv
+
+    def _attend(self, pool):
+        from oracle import attention as OA
+        np = self.np
+
+        def attend(q, k_cache, v_cache, tables, q_starts, q_lens, k_lens, scale, causal):
+            chunks = np.array_split(np.arange(len(q_lens)), self.threads)
+
+            def part(rows):
+                return OA.paged_attention(q, k_cache, v_cache, tables[rows], np.asarray(q_starts)[rows],
+                                          np.asarray(q_lens)[rows], np.asarray(k_lens)[rows], scale, causal)
+            return sum(pool.map(part, [c for c in chunks if len(c)]))
+        return attend
+
+    def step(self, pool) -> dict:
+        import time as _time
+        from threadpoolctl import threadpool_limits
+        from oracle import forward as OF
+        from oracle import spec_sampler as OS
+        np = self.np
+        t0 = _time.perf_counter()
+        attend = self._attend(pool)
+
+        def single_thread_attend(*args):
+            with threadpool_limits(1):               # the row split supplies the parallelism
+                return attend(*args)
+        h, _ = OF.decoder_layer(self.w, self.h, self.residual, self.positions, self.slots, self.k_cache,
+                                self.v_cache, self.tables, self.q_starts, self.q_lens, self.k_lens, self.cos_sin,
+                                self.heads, self.kv_heads, 1e-6, True, single_thread_attend)
+        t1 = _time.perf_counter()
+        OF.linear(h, self.lm_share)
+        t2 = _time.perf_counter()
+        p = OS.probs_from_logits(self.logits, np.ones(self.logits.shape[0], np.float32))
+        u = self.rng.random((2, K_DRAFTS), dtype=np.float32)
+        noise = OS.clamp_noise(self.rng.exponential(size=(2, V)).astype(np.float32))
+        n_accept, _tail = OS.accept_random(p.reshape(2, K_DRAFTS + 1, V), self.q, self.drafts, u, noise)
+        t3 = _time.perf_counter()
+        return {"layer_s": t1 - t0, "lm_s": t2 - t1, "accept_s": t3 - t2, "tokens": float(n_accept.sum() + 2)}
+
+    def round_seconds(self, st: dict) -> float:
+        return self.LAYERS * (st["layer_s"] + st["lm_s"]) + (self.BATCH // 2) * st["accept_s"]
+
+
+def cpu_arm(ctx: int, steps: int, warmup: int) -> dict:
+    """Runs CpuRound on every host core: `warmup` untimed steps, then `steps` timed ones; returns the accepted
+    tokens per second of a whole round (from the median step), the measured step time and the work covered."""
+    import concurrent.futures as cf
+    threads = os.cpu_count() or 1
+    t_setup = time.perf_counter()
+    cpu = CpuRound(ctx, threads)
+    setup_s = time.perf_counter() - t_setup
+    with cf.ThreadPoolExecutor(max_workers=threads) as pool:
+        for _ in range(warmup):
+            cpu.step(pool)
+        stats = [cpu.step(pool) for _ in range(steps)]
+    rounds = sorted(cpu.round_seconds(st) for st in stats)
+    round_s = rounds[len(rounds) // 2]
+    tokens_per_row = sum(st["tokens"] for st in stats) / (2 * len(stats))
+    tokens = CpuRound.BATCH * tokens_per_row
+    step_s = [st["layer_s"] + st["lm_s"] + st["accept_s"] for st in stats]
+    return {"value": tokens / round_s, "round_s": round_s, "tokens_per_round": tokens, "cores": threads,
+            "step_ms": 1e3 * statistics.mean(step_s), "steps": len(stats), "setup_s": setup_s,
+            "layer_s": statistics.median(st["layer_s"] for st in stats),
+            "lm_share_s": statistics.median(st["lm_s"] for st in stats),
+            "accept2_s": statistics.median(st["accept_s"] for st in stats),
+            "sample": (f"per step: one Qwen3-8B decoder layer (GEMMs included) over 64 rows x 8 tokens at contexts "
+                       f"~{ctx}, 1/36 of the LM head's vocabulary for those 512 tokens, and the sampler of 2 "
+                       f"requests, numpy oracle on {threads} threads; a round = 36 x (layer + LM-head share) + "
+                       f"32 x (2 requests' sampler), from the median of {len(stats)} timed steps")}
+
+
+def parity_sample(torch, w, requests: int = 16) -> dict:
+    """The GPU round's fused accept on its own logits against the oracle on the same inputs and draws, for the
+    first `requests` requests: mismatching requests, and near-tie requests by kind (accept-draw ties are the
+    parity rule's exemption; race ties are reported separately)."""
     import numpy as np
-    from oracle import attention as OA
+    from nanovllm_b200 import spec_sampler as S
     from oracle import spec_sampler as OS
-    rng = np.random.default_rng(0)
-    H, Hkv, D, bs = 32, 8, 128, 256
-    nb = math.ceil((ctx + 8) / bs)
-    k_cache = rng.standard_normal((rows_sample * nb, bs, Hkv, D), dtype=np.float32)
-    v_cache = rng.standard_normal((rows_sample * nb, bs, Hkv, D), dtype=np.float32)
-    tables = np.arange(rows_sample * nb).reshape(rows_sample, nb)
-    q = rng.standard_normal((rows_sample * 8, H, D), dtype=np.float32)
-    starts = np.arange(rows_sample) * 8
-    logits = (rng.standard_normal((rows_sample * 8, V), dtype=np.float32) * 3).astype(np.float32)
-    qd = OS.softmax(rng.standard_normal((rows_sample, 7, V), dtype=np.float32))
-    drafts = rng.integers(0, V, (rows_sample, 7))
-    u = rng.random((rows_sample, 7), dtype=np.float32)
-    noise = OS.clamp_noise(rng.exponential(size=(rows_sample, V)).astype(np.float32))
-    t0 = time.perf_counter()
-    for _ in range(layers_sample):
-        OA.paged_attention(q, k_cache, v_cache, tables, starts, [8] * rows_sample, [ctx + 8] * rows_sample, D ** -0.5)
-    t1 = time.perf_counter()
-    p = OS.probs_from_logits(logits, np.ones(rows_sample * 8, np.float32))
-    n_accept, _tail = OS.accept_random(p.reshape(rows_sample, 8, V), qd, drafts, u, noise)
-    t2 = time.perf_counter()
-    return {"attn_s": t1 - t0, "accept_s": t2 - t1, "rows": rows_sample, "layers": layers_sample,
-            "tokens_per_row": float(n_accept.mean() + 1)}
-
-
-def cpu_round_seconds(sample: dict, batch: int, layers: int) -> float:
-    per_row_layer = sample["attn_s"] / (sample["rows"] * sample["layers"])
-    per_row_accept = sample["accept_s"] / sample["rows"]
-    return batch * layers * per_row_layer + batch * per_row_accept
-
-
-def _cpu_task(ctx: int) -> dict:
-    """One reference-arm task in a worker process: four rows through two layers' attention plus their sampler."""
-    from threadpoolctl import threadpool_limits
-    with threadpool_limits(1):
-        return cpu_round_sample(4, 2, ctx, 1)
-
-
-def _cpu_warm(ctx: int) -> None:
-    _cpu_task(ctx)               # first-call costs (imports, page faults) stay out of the timed tasks
+    rnd = w.round
+    num_tokens = rnd.load(w.rows)
+    batch = len(w.rows)
+    gen = torch.Generator(device=w.target.device).manual_seed(77)
+    replay = torch.Generator(device=w.target.device)
+    replay.set_state(gen.get_state())
+    n_accept, tail = rnd.verify_and_accept(num_tokens, batch, w.drafts, w.q, w.sampling, gen)
+    u = torch.rand(batch, K_DRAFTS, device=w.target.device, generator=replay)
+    noise = S.exponential_noise_(torch.empty(batch, V, device=w.target.device), replay)
+    sel = slice(0, requests)
+    logits = rnd.logits(num_tokens)[:requests * (K_DRAFTS + 1)].float().cpu().numpy()
+    q = w.q[sel].cpu().numpy()
+    drafts = w.drafts[sel].cpu().numpy()
+    lens = np.full(requests, K_DRAFTS + 1)
+    u_np, e_np = u[sel].cpu().numpy(), noise[sel].cpu().numpy()
+    p = OS.probs_from_logits(logits, np.ones(logits.shape[0], np.float32))
+    want_n, want_tail = OS.accept_random_varlen(p, q, drafts, lens, u_np, e_np)
+    accept_flags, race_flags = OS.near_tie_kinds(p, q, drafts, lens, u_np, e_np)
+    got_n, got_tail = n_accept[sel].cpu().numpy(), tail[sel].cpu().numpy()
+    differ = (got_n != want_n) | (got_tail != want_tail)
+    return {"requests": requests, "mismatches": int(differ.sum()),
+            "mismatches_not_flagged": int((differ & ~(accept_flags | race_flags)).sum()),
+            "accept_draw_near_ties": int(accept_flags.sum()), "race_near_ties": int(race_flags.sum()),
+            "rule": "bit-exact n_accept and tail except accept draws with |u q_d - p_d| <= 1e-6 max(p_d, u q_d)"}
 
 
 def run_reference(args) -> int:
-    """--impl reference: the reference's algorithm for the path (numpy oracle) on every host core, rank 0 only.
-    A process pool (one single-threaded worker per core, spawned, each warmed up once) runs each step as one task
-    per worker: four rows through two layers' paged attention plus those rows' sampler.  The whole job of the
-    config (batch x n_gpus rows, 36 layers) is costed from the step's per-task times and the pool's measured
-    parallelism; the host has the same cores whatever the GPU count, so the whole-job time grows with the rows.
-    Steps beyond 10 are not run (the median of 10 bounded samples already settles)."""
+    """--impl reference: the reference's algorithm for the round on the host cores (CpuRound, the numpy oracle;
+    the reference itself is Python over ATen and does not travel to the GPU box), rank 0 only: W untimed steps,
+    K timed steps, each step 1/36 of a config-3 round (GEMMs included); value = accepted tokens / s of a whole
+    round from the median step."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    import concurrent.futures as cf
-    import multiprocessing as mp
-    workers = os.cpu_count() or 1
-    os.environ.setdefault("OMP_NUM_THREADS", "1")
-    rows = args.batch * args.gpus
-    values, round_times, par, tasks = [], [], [], 0
-    with cf.ProcessPoolExecutor(max_workers=workers, mp_context=mp.get_context("spawn"), initializer=_cpu_warm,
-                                initargs=(args.ctx,)) as pool:
-        for _ in range(max(1, min(args.steps, 10))):
-            t0 = time.perf_counter()
-            results = list(pool.map(_cpu_task, [args.ctx] * workers))
-            wall = time.perf_counter() - t0
-            tasks += len(results)
-            attn = statistics.mean(r["attn_s"] / (r["rows"] * r["layers"]) for r in results)   # per row, layer
-            accept = statistics.mean(r["accept_s"] / r["rows"] for r in results)               # per row
-            parallelism = sum(r["attn_s"] + r["accept_s"] for r in results) / wall
-            round_s = rows * (36 * attn + accept) / parallelism
-            tokens = rows * statistics.mean(r["tokens_per_row"] for r in results)
-            values.append(tokens / round_s)
-            round_times.append(round_s)
-            par.append(parallelism)
-    value = statistics.median(values)
-    line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(statistics.median(round_times) * 1e3, 1),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": {"workload": "cfg3 round path on CPU (numpy oracle)", "global_batch": rows,
-                                             "seq_len": args.ctx, "parallelism": f"cpu x{workers} processes"},
-            "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": workers, "kind": "port",
-                             "sample": f"{tasks} tasks of 4 rows x 2 layers of paged attention at ctx {args.ctx} + "
-                                       f"those rows' sampler on {workers} single-threaded processes (median "
-                                       f"parallelism {statistics.median(par):.1f}), costed to {rows} rows x 36 "
-                                       f"layers; GEMMs excluded"},
-            "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    res = cpu_arm(args.ctx, args.steps, args.warmup)
+    line = {"impl": "reference", "metric": METRIC, "value": round(res["value"], 4), "unit": "tok/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(res["step_ms"], 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "cfg3 round on the host cores (numpy oracle: Qwen3 layers with their GEMMs, "
+                                   "paged attention, LM head, sampler); a step is 1/36 of a round",
+                       "global_batch": 64, "seq_len": args.ctx, "parallelism": f"cpu x{res['cores']} threads"},
+            "cpu_baseline": {"value": round(res["value"], 4), "unit": "tok/s", "cores": res["cores"], "kind": "port",
+                             "sample": res["sample"]},
+            "e2e": {"value": round(res["value"], 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "extra": {"round_s": round(res["round_s"], 3), "tokens_per_round": round(res["tokens_per_round"], 2),
+                      "layer_s": round(res["layer_s"], 4), "lm_share_s": round(res["lm_share_s"], 4),
+                      "accept_2_requests_s": round(res["accept2_s"], 4), "setup_s": round(res["setup_s"], 1),
+                      "scaling_to_round": "36 x (layer + LM-head share) + 32 x (2 requests' sampler)"}}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -500,9 +792,6 @@ def run_attention_tp(args) -> int:
     import datetime
     import torch
     import torch.distributed as dist
-    from nanovllm_b200.context import reset_context, set_context
-    from nanovllm_b200.replicas import barrier, reduce_scalar
-    from nanovllm_b200.tp_attention import TPAttention
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -510,10 +799,27 @@ def run_attention_tp(args) -> int:
     device = torch.device("cuda", local_rank)
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
-    B, H, Hkv, D, bs, nq = args.batch, 32, 8, 128, 256, K_DRAFTS + 1
+    out = attention_tp_timing(torch, device, world, rank, local_rank, args.batch, args.ctx, args.steps,
+                              args.warmup)
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def attention_tp_timing(torch, device, world: int, rank: int, local_rank: int, batch: int, ctx: int, steps: int,
+                        warmup: int) -> dict:
+    """The KV-head tensor-parallel layer timing of run_attention_tp inside an initialised process group (or
+    none for one GPU); every rank returns the same max-over-ranks figures."""
+    from nanovllm_b200.context import reset_context, set_context
+    from nanovllm_b200.replicas import barrier, reduce_scalar
+    from nanovllm_b200.tp_attention import TPAttention
+    B, H, Hkv, D, bs, nq = batch, 32, 8, 128, 256, K_DRAFTS + 1
     g = torch.Generator().manual_seed(0)                 # the same rows on every rank
-    ctx = torch.randint(max(args.ctx - 50, 1), args.ctx + 51, (B,), generator=g).tolist()
-    k_lens = [c + nq for c in ctx]
+    ctx_lens = torch.randint(max(ctx - 50, 1), ctx + 51, (B,), generator=g).tolist()
+    k_lens = [c + nq for c in ctx_lens]
     nb = [math.ceil(k / bs) for k in k_lens]
     NB = sum(nb) + 1
     perm = torch.randperm(NB - 1, generator=g).tolist()
@@ -522,7 +828,7 @@ def run_attention_tp(args) -> int:
     for r, n in enumerate(nb):
         tables[r, :n] = torch.tensor(perm[used:used + n])
         used += n
-    slots = [int(tables[r, p // bs]) * bs + p % bs for r in range(B) for p in range(ctx[r], k_lens[r])]
+    slots = [int(tables[r, p // bs]) * bs + p % bs for r in range(B) for p in range(ctx_lens[r], k_lens[r])]
     T = B * nq
     m = TPAttention(H, D, D ** -0.5, Hkv)
     modules = {"tp": m}
@@ -563,11 +869,10 @@ def run_attention_tp(args) -> int:
 
     fns = {name: layer_fn(module) for name, module in modules.items()}
     fns["local"] = local_only
-    for _ in range(max(args.warmup, 3)):
+    for _ in range(max(warmup, 3)):
         for fn in fns.values():
             fn()
     barrier()
-    steps = args.steps
     graphs = {}
     for name, fn in fns.items():
         graph = torch.cuda.CUDAGraph()
@@ -590,25 +895,27 @@ def run_attention_tp(args) -> int:
     local_bytes = keys * Hkl * D * 2 * 2 + 2 * T * Hl * D * 2 + 2 * T * Hkl * D * 2   # K/V + q, out + stores
     pk = peaks()
     achieved = local_bytes / (times["local"] * 1e-6) / 1e9
-    if rank == 0:
-        print(json.dumps({
-            "kernel": "attention_tp", "n_gpus": world, "rows": B, "verify_positions": nq, "ctx_mean": args.ctx,
-            "heads": H, "kv_heads_per_gpu": Hkl, "us_per_layer": round(times["tp"], 2),
-            "local_attention_us": round(times["local"], 2),
-            "exchange_us": round(times["tp"] - times["local"], 2),
-            "peer_store_us_per_layer": round(times["tp_peer"], 2) if "tp_peer" in times else None,
-            "peer_store_exchange_us": round(times["tp_peer"] - times["local"], 2) if "tp_peer" in times else None,
-            "peer_barrier_status": peer_status,
-            "per_gpu_algorithmic_bytes": local_bytes, "local_achieved_GBps": round(achieved, 1),
-            "peak_GBps": pk["hbm_gbs"], "local_frac": round(achieved / pk["hbm_gbs"], 4), "peak_source": pk["source"],
-            "nvlink_bytes_in_per_gpu": 2 * T * H * D * (world - 1) // world,
-            "timing": f"CUDA graph of {steps} layers over {copies} rotating caches, 3 replays, max over ranks",
-            "clocks": clocks.summary()}), flush=True)
+    nvlink_in = 2 * T * H * D * (world - 1) // world
+    # roofline of the fused layer: the slower of its local HBM bytes and its NVLink bytes in (measured 770 GB/s
+    # per direction per GPU)
+    floor_us = max(local_bytes / (pk["hbm_gbs"] * 1e9), nvlink_in / 770e9) * 1e6
+    out = {
+        "kernel": "attention_tp", "n_gpus": world, "rows": B, "verify_positions": nq, "ctx_mean": ctx,
+        "heads": H, "kv_heads_per_gpu": Hkl, "us_per_layer": round(times["tp"], 2),
+        "local_attention_us": round(times["local"], 2),
+        "exchange_us": round(times["tp"] - times["local"], 2),
+        "peer_store_us_per_layer": round(times["tp_peer"], 2) if "tp_peer" in times else None,
+        "peer_store_exchange_us": round(times["tp_peer"] - times["local"], 2) if "tp_peer" in times else None,
+        "peer_barrier_status": peer_status,
+        "per_gpu_algorithmic_bytes": local_bytes, "local_achieved_GBps": round(achieved, 1),
+        "peak_GBps": pk["hbm_gbs"], "local_frac": round(achieved / pk["hbm_gbs"], 4), "peak_source": pk["source"],
+        "nvlink_bytes_in_per_gpu": nvlink_in, "layer_roofline_us": round(floor_us, 2),
+        "frac_nccl_layer": round(floor_us / times["tp"], 4),
+        "frac_peer_layer": round(floor_us / times["tp_peer"], 4) if "tp_peer" in times else None,
+        "timing": f"CUDA graph of {steps} layers over {copies} rotating caches, 3 replays, max over ranks",
+        "clocks": clocks.summary()}
     del caches
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    return 0
+    return out
 
 
 # ---------------------------------------------------------------------------------------------- our arm
@@ -692,19 +999,35 @@ def main() -> int:
                                                         # silu; final norm; sampler stats + tail
     h2d = (num_tokens * (8 + 8 + 4) + 2 * (batch + 1) * 4 + batch * w.width * 4)
     d2h = batch * (K_DRAFTS + 2) * 8
-    line = None
+    round_nbytes = round_bytes(w, num_tokens)
+    extra = {"round_us": round(ms_per_step * 1e3, 1),
+             "verified_tok_s": round(batch * (K_DRAFTS + 1) * world / (ms_per_step / 1e3), 1),
+             "tokens_per_round_per_row": round(total_accepted / args.steps / world / batch, 4),
+             "round_algorithmic_bytes": round_nbytes,
+             "round_hbm_roofline_ms": round(round_nbytes["total"] / (pk["hbm_gbs"] * 1e9) * 1e3, 3),
+             "accept_kernel": accept}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        # the CPU leg: the oracle as the timed CPU baseline (a bounded sample of the round on every host core),
+        # and as the checker of this round's fused accept on a sample of its requests
+        extra["parity_sample"] = parity_sample(torch, w)
+        res = cpu_arm(args.ctx, 3, 1)
+        cpu = {"value": round(res["value"], 4), "unit": "tok/s", "cores": res["cores"], "kind": "port",
+               "sample": res["sample"], "round_s": round(res["round_s"], 3)}
+    w.target.close()
+    del w, rnd
+    torch.cuda.empty_cache()
+    if not args.no_extra:
+        if world == 1:
+            # the north-star target (the round at ~4k contexts), config 5's 16k attention and config 4's round
+            extra["north_star_round_4k"] = round_timing(torch, device, 4096, 10, 3, pk["hbm_gbs"])
+            extra["attention_16k"] = attention_long_timing(torch, device, 16384, 10, pk["hbm_gbs"])
+            extra["dspark_round_cfg4"] = dspark_timing(torch, device, 20, 3, pk["hbm_gbs"])
+        else:
+            # config 5's KV-head tensor-parallel attention layer (the collective on the path), ~4k contexts
+            extra["attention_tp_4k"] = attention_tp_timing(torch, device, world, rank, local_rank, batch, 4096, 20,
+                                                           3)
     if rank == 0:
-        cpu = None
-        if world == 1 and not args.no_cpu_baseline:
-            from threadpoolctl import threadpool_limits
-            with threadpool_limits(1):                    # the reported core count is the one used
-                sample = cpu_round_sample(8, 16, args.ctx, 1)
-            cpu_round_s = cpu_round_seconds(sample, batch, w.shape.layers)
-            tokens_per_round = total_accepted / args.steps / world
-            cpu = {"value": round(tokens_per_round / cpu_round_s, 3), "unit": "tok/s", "cores": 1, "kind": "port",
-                   "sample": f"numpy oracle: paged attention of {sample['rows']} rows x {sample['layers']} layers at ctx {args.ctx} "
-                             f"({sample['attn_s']:.2f} s) + sampler of the same rows ({sample['accept_s']:.2f} s), "
-                             f"scaled to {batch} rows x {w.shape.layers} layers; GEMMs excluded"}
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
@@ -721,14 +1044,9 @@ def main() -> int:
             "cpu_baseline": cpu,
             "clocks": clocks.summary(),
             "gpu_launches": launches_per_step * args.steps,
-            "extra": {"round_us": round(ms_per_step * 1e3, 1),
-                      "verified_tok_s": round(batch * (K_DRAFTS + 1) * world / (ms_per_step / 1e3), 1),
-                      "tokens_per_round_per_row": round(total_accepted / args.steps / world / batch, 4),
-                      "accept_kernel": accept},
+            "extra": extra,
         }
         print(json.dumps(line), flush=True)
-    w.target.close()
-    del w
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()

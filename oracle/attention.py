@@ -21,12 +21,12 @@ def paged_attention(q, k_cache, v_cache, block_tables, q_starts, q_lens, k_lens,
     """q [T, H, D]; k_cache / v_cache [blocks, block_size, Hkv, D]; per row r: queries q[q_starts[r] :
     q_starts[r] + q_lens[r]], keys 0 .. k_lens[r]-1 through block_tables[r].  Returns out [T, H, D] fp32 (rows
     not covered stay 0)."""
-    q = q.astype(np.float32)
+    q = np.asarray(q, dtype=np.float32)
     T, H, D = q.shape
     block_size, Hkv = k_cache.shape[1], k_cache.shape[2]
     group = H // Hkv
-    keys_all = k_cache.reshape(-1, Hkv, D).astype(np.float32)
-    values_all = v_cache.reshape(-1, Hkv, D).astype(np.float32)
+    keys_all = np.asarray(k_cache, dtype=np.float32).reshape(-1, Hkv, D)       # no copy when already fp32
+    values_all = np.asarray(v_cache, dtype=np.float32).reshape(-1, Hkv, D)
     out = np.zeros((T, H, D), dtype=np.float32)
     for r in range(len(q_lens)):
         ql, kl, qs = int(q_lens[r]), int(k_lens[r]), int(q_starts[r])
