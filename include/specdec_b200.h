@@ -123,6 +123,11 @@ int specdec_paged_attention(const void* q, long long T, long long q_row_stride, 
  * preceding kernel does not write cu_seqlens_q / cu_seqlens_k / context_lens / block_tables (q and the caches it
  * may write).  specdec_paged_attention is this call with flags 0. */
 #define SPECDEC_ATTN_EARLY_LAUNCH 1u
+/* Bits 8..15 of flags: at most this many CTAs (persistent, one per SM; 0 = one per SM of the device), so the
+ * kernel can share the GPU with work on another stream that runs on the remaining SMs.
+ * SPECDEC_ATTN_MAX_CTAS(n) builds the field. */
+#define SPECDEC_ATTN_CTAS_SHIFT 8u
+#define SPECDEC_ATTN_MAX_CTAS(n) (((unsigned)(n) & 0xffu) << SPECDEC_ATTN_CTAS_SHIFT)
 int specdec_paged_attention_ex(const void* q, long long T, long long q_row_stride, int num_heads, int num_kv_heads,
                                int head_dim, const void* k_cache, const void* v_cache, long long num_slots,
                                int block_size, const int* cu_seqlens_q, const int* cu_seqlens_k,

@@ -851,7 +851,8 @@ int specdec_paged_attention_multi(const void* q, long long T, long long q_row_st
                                   void* const* outs, int num_outs, long long out_row_stride, void* workspace,
                                   long long workspace_bytes, int* err, unsigned flags, void* stream) {
   using namespace attention;
-  SPECDEC_CHECK_ARG((flags & ~(unsigned)SPECDEC_ATTN_EARLY_LAUNCH) == 0, "unknown flags 0x%x", flags);
+  SPECDEC_CHECK_ARG((flags & ~((unsigned)SPECDEC_ATTN_EARLY_LAUNCH | SPECDEC_ATTN_MAX_CTAS(0xff))) == 0,
+                    "unknown flags 0x%x", flags);
   SPECDEC_CHECK_ARG(outs && num_outs >= 1 && num_outs <= kMaxOuts, "num_outs %d: 1 .. %d destinations", num_outs,
                     kMaxOuts);
   for (int t = 0; t < num_outs; ++t)
@@ -915,7 +916,9 @@ int specdec_paged_attention_multi(const void* q, long long T, long long q_row_st
   DeviceInfo info;
   if (int st = device_info(&info)) return st;
   const long long max_tiles = (long long)R * num_kv_heads * ((long long)W * block_size / kKeysPerTile);
-  const int grid = (int)(max_tiles < info.sm_count ? max_tiles : info.sm_count);
+  const int cap = (int)((flags >> SPECDEC_ATTN_CTAS_SHIFT) & 0xffu);
+  const int ctas = cap > 0 && cap < info.sm_count ? cap : info.sm_count;
+  const int grid = (int)(max_tiles < ctas ? max_tiles : ctas);
   const long long need = attention::workspace_bytes(R, num_kv_heads, info.sm_count);
   if (workspace_bytes < need)
     return set_error(kWorkspaceTooSmall, "attention workspace of %lld bytes, %lld needed", workspace_bytes, need);

@@ -48,12 +48,12 @@ def reset_device_error(device: torch.device) -> None:
 _SPLIT_MIN_BYTES = 8 << 20
 
 
-def _split_workspace(device: torch.device, R: int, Hkv: int) -> torch.Tensor:
+def _split_workspace(device: torch.device, R: int, Hkv: int, name: str = "attention_split") -> torch.Tensor:
     with torch.cuda.device(device):
         need = int(_lib.lib().specdec_attention_workspace_bytes(R, Hkv))
     if need < 0:
         raise _lib.SpecdecError(_lib.lib().specdec_last_error().decode())
-    return Workspace.get(device, max(need, _SPLIT_MIN_BYTES), name="attention_split")
+    return Workspace.get(device, max(need, _SPLIT_MIN_BYTES), name=name)
 
 
 def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
@@ -74,6 +74,7 @@ def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor,
 
 
 EARLY_LAUNCH = 1   # SPECDEC_ATTN_EARLY_LAUNCH
+CTAS_SHIFT = 8     # SPECDEC_ATTN_CTAS_SHIFT: bits 8..15 of the flags cap the persistent grid
 
 
 def _row_metadata(block_tables, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, context_lens, query_len_per_seq):
@@ -105,17 +106,20 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
                     scale: float, *, cu_seqlens_q: torch.Tensor | None = None,
                     cu_seqlens_k: torch.Tensor | None = None, max_seqlen_q: int | None = None,
                     context_lens: torch.Tensor | None = None, query_len_per_seq: int = 1, causal: bool = True,
-                    out: torch.Tensor | None = None, early_launch: bool = False) -> torch.Tensor:
+                    out: torch.Tensor | None = None, early_launch: bool = False, max_ctas: int = 0,
+                    workspace: str = "attention_split") -> torch.Tensor:
     """Attention of q [T, H, D] over the paged caches.  Varlen (cu_seqlens_q/k, the verify forward) or decode
     (context_lens with query_len_per_seq queries per row).  Returns out [T, H, D] bf16.  early_launch: launch as a
     programmatic dependent of the preceding kernel (its prologue overlaps that kernel's end); only when that kernel
-    does not write the row metadata (cu_seqlens / context_lens / block_tables)."""
+    does not write the row metadata (cu_seqlens / context_lens / block_tables).  max_ctas (1..255, 0 = one per SM):
+    cap the persistent grid, leaving SMs to work on another stream.  workspace: the name of the split-item
+    workspace; launches that may run at the same time on different streams need different names."""
     device = require_cuda(q, k_cache, v_cache, block_tables)
     out = _output(out, q.shape, device)
     paged_attention_to(q, k_cache, v_cache, block_tables, scale, [out.data_ptr()], out.stride(0),
                        cu_seqlens_q=cu_seqlens_q, cu_seqlens_k=cu_seqlens_k, max_seqlen_q=max_seqlen_q,
                        context_lens=context_lens, query_len_per_seq=query_len_per_seq, causal=causal,
-                       early_launch=early_launch)
+                       early_launch=early_launch, max_ctas=max_ctas, workspace=workspace)
     return out
 
 
@@ -123,7 +127,8 @@ def paged_attention_to(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Te
                        scale: float, out_ptrs: list[int], out_row_stride: int, *,
                        cu_seqlens_q: torch.Tensor | None = None, cu_seqlens_k: torch.Tensor | None = None,
                        max_seqlen_q: int | None = None, context_lens: torch.Tensor | None = None,
-                       query_len_per_seq: int = 1, causal: bool = True, early_launch: bool = False) -> None:
+                       query_len_per_seq: int = 1, causal: bool = True, early_launch: bool = False,
+                       max_ctas: int = 0, workspace: str = "attention_split") -> None:
     """paged_attention writing its [T, H, D] bf16 output to every device address in out_ptrs (1 to 8; this GPU's
     memory or a peer's mapped into this process), all with row stride out_row_stride elements.  The caller owns
     the destinations' extent: each must hold T rows of out_row_stride elements from its address."""
@@ -139,8 +144,10 @@ def paged_attention_to(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Te
     tables, cq, ck, ctx, R, q_per_seq, max_q = _row_metadata(block_tables, cu_seqlens_q, cu_seqlens_k, max_seqlen_q,
                                                               context_lens, query_len_per_seq)
     W = tables.shape[1]
-    ws = _split_workspace(device, R, Hkv)
-    flags = EARLY_LAUNCH if early_launch else 0
+    if not 0 <= max_ctas <= 255:
+        raise ValueError(f"max_ctas {max_ctas}: 0 (one CTA per SM) to 255")
+    ws = _split_workspace(device, R, Hkv, workspace)
+    flags = (EARLY_LAUNCH if early_launch else 0) | (max_ctas << CTAS_SHIFT)
     if len(out_ptrs) == 1:
         check(_lib.lib().specdec_paged_attention_ex(
             ptr(q), T, q.stride(0), H, Hkv, D, ptr(k_cache), ptr(v_cache), blocks * block_size, block_size, ptr(cq),
