@@ -51,7 +51,7 @@ def parse_args():
     p.add_argument("--no-extra", action="store_true",
                    help="skip the extra workloads (4k round, 16k attention, config-4 round; TP layer under torchrun)")
     p.add_argument("--kernel", choices=["attention", "accept", "accept_topk", "accept_greedy", "sample", "markov",
-                                        "ctx_store", "after_verify", "attention_tp"],
+                                        "markov_fused", "ctx_store", "after_verify", "attention_tp", "overlap"],
                    default=None,
                    help="time one kernel alone on its benchmark config (attention: config 2, accept: config 3's "
                         "logits) instead of the round; used for profiling")
@@ -655,7 +655,7 @@ def run_kernel(args) -> int:
             attention.paged_attention(q, kc, vc, tables, D ** -0.5, cu_seqlens_q=cu_q, cu_seqlens_k=cu_k,
                                       max_seqlen_q=8)
         algorithmic = sum(k_lens) * Hkv * D * 2 * 2 + 2 * R * 8 * H * D * 2
-    elif args.kernel == "markov":
+    elif args.kernel in ("markov", "markov_fused"):
         # config 4's drafter: 64 rows x 7 in-block steps, V = 151936, rank-256 Markov head, top_k 128 (192 candidates)
         from nanovllm_b200 import spec_sampler as S
         from nanovllm_b200.markov import MarkovHeadWeights, MarkovQBuffer, markov_rows, num_candidates
@@ -671,8 +671,10 @@ def run_kernel(args) -> int:
         drafts = torch.empty(B, k, dtype=torch.int64, device=device)
         qbuf = MarkovQBuffer(B, k, V, cand, device)     # persistent q: only the last call's candidates cleared
 
+        fused = args.kernel == "markov_fused"      # the bias GEMM from specdec_markov_bias (logits added in it)
+
         def fn():
-            markov_rows(logits, prev, samp, noise, drafts, qbuf, cand, head)
+            markov_rows(logits, prev, samp, noise, drafts, qbuf, cand, head, fused_bias=fused)
         # per step: W2 (77.8 MB) + the row's logits (19.4 MB); q is scattered (C values per row), not zero-filled
         algorithmic = k * (V * r * 2 + B * V * 2)
     elif args.kernel == "ctx_store":
@@ -758,7 +760,7 @@ def run_kernel(args) -> int:
     for _ in range(args.warmup):
         fn()
     timing = "events"
-    if args.kernel in ("attention", "ctx_store", "after_verify", "markov"):
+    if args.kernel in ("attention", "ctx_store", "after_verify", "markov", "markov_fused"):
         # K calls captured in one CUDA graph and replayed, so the host's per-call work (tensor map encoding,
         # Python) does not pace the device; the reference captures its Markov rows in a graph the same way
         # (speculative.py:216-231)
@@ -778,6 +780,90 @@ def run_kernel(args) -> int:
                       "algorithmic_bytes": algorithmic,
                       "achieved_GBps": round(achieved, 1), "peak_GBps": pk["hbm_gbs"],
                       "frac": round(achieved / pk["hbm_gbs"], 4), "peak_source": pk["source"]}), flush=True)
+    return 0
+
+
+def run_overlap(args) -> int:
+    """--kernel overlap: whether half a round's work can overlap the other half's at ~4k contexts on one B200.
+    Half the batch (32 rows x 8 queries, contexts ~ctx) of one layer's verify attention (HBM-bound) with its grid
+    capped at n CTAs, one layer's four GEMMs for the other half (256 tokens: qkv, o, gate_up, down; compute-bound)
+    through cuBLASLt with n SMs carved out, each alone and both at once on two streams; also the attention alone
+    at every cap.  The two-micro-batch overlap is worth building only if 'both' beats the sum of the two alone."""
+    import torch
+    from nanovllm_b200 import attention
+    device = torch.device("cuda", 0)
+    R, H, Hkv, D, bs, ctx = 32, 32, 8, 128, 256, max(args.ctx, 4096)
+    g = torch.Generator().manual_seed(0)
+    k_lens = [n + 8 for n in torch.randint(ctx - 50, ctx + 51, (R,), generator=g).tolist()]
+    nb = [math.ceil(k / bs) for k in k_lens]
+    NB = sum(nb) + 1
+    perm = torch.randperm(NB - 1, generator=g).tolist()
+    tables = torch.full((R, max(nb)), NB - 1, dtype=torch.int32)
+    used = 0
+    for r, n in enumerate(nb):
+        tables[r, :n] = torch.tensor(perm[used:used + n])
+        used += n
+    copies = 6
+    caches = [(torch.empty(NB, bs, Hkv, D, dtype=torch.bfloat16, device=device).normal_(),
+               torch.empty(NB, bs, Hkv, D, dtype=torch.bfloat16, device=device).normal_()) for _ in range(copies)]
+    q = torch.randn(R * 8, H, D, device=device).bfloat16()
+    out = torch.empty_like(q)
+    cu_q = torch.arange(0, 8 * R + 1, 8, dtype=torch.int32, device=device)
+    cu_k = torch.tensor([0] + torch.tensor(k_lens).cumsum(0).tolist(), dtype=torch.int32, device=device)
+    tables = tables.to(device)
+    kv_bytes = sum(k_lens) * Hkv * D * 4
+    state = {"i": 0}
+
+    def attn(ctas, ws="attention_split"):
+        state["i"] += 1
+        kc, vc = caches[state["i"] % copies]
+        attention.paged_attention(q, kc, vc, tables, D ** -0.5, cu_seqlens_q=cu_q, cu_seqlens_k=cu_k,
+                                  max_seqlen_q=8, out=out, max_ctas=ctas, workspace=ws)
+
+    T = 256
+    x = torch.randn(T, 4096, device=device).bfloat16()
+    xi = torch.randn(T, 12288, device=device).bfloat16()
+    ws = [torch.randn(n, 4096, device=device).bfloat16() for n in (6144, 4096, 24576)]
+    wd = torch.randn(4096, 12288, device=device).bfloat16()
+
+    def gemms():
+        for w in ws:
+            torch.matmul(x, w.t())
+        torch.matmul(xi, wd.t())
+
+    def timed(fn, iters=10):
+        for _ in range(3):                      # warm-up: workspaces, cuBLAS handles and heuristics
+            fn()
+        return time_events(torch, fn, iters)
+
+    res = {"kernel": "overlap", "rows": R, "ctx": ctx, "gemm_tokens": T}
+    for c in (0, 120, 100, 74, 48):
+        us = timed(lambda c=c: attn(c), 12)
+        res[f"attention_ctas{c or 148}_us"] = round(us, 1)
+        res[f"attention_ctas{c or 148}_TBps"] = round(kv_bytes / us / 1e6, 2)
+    res["gemms_us"] = round(timed(gemms), 1)
+    torch.backends.cuda.preferred_blas_library("cublaslt")
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    for carve in (48, 74):
+        torch._C._set_sm_carveout_experimental(carve)
+        res[f"gemms_carveout{carve}_us"] = round(timed(gemms), 1)
+        torch._C._set_sm_carveout_experimental(0)
+
+        def both(carve=carve):
+            cur = torch.cuda.current_stream()
+            s1.wait_stream(cur)
+            s2.wait_stream(cur)
+            with torch.cuda.stream(s1):
+                torch._C._set_sm_carveout_experimental(carve)
+                gemms()
+                torch._C._set_sm_carveout_experimental(0)
+            with torch.cuda.stream(s2):
+                attn(carve, "attention_split_b")
+            cur.wait_stream(s1)
+            cur.wait_stream(s2)
+        res[f"both_{carve}_us"] = round(timed(both), 1)
+    res["sum_alone_us"] = round(res["gemms_us"] + res["attention_ctas148_us"], 1)
+    print(json.dumps(res), flush=True)
     return 0
 
 
@@ -925,6 +1011,8 @@ def main() -> int:
         return run_reference(args)
     if args.kernel == "attention_tp":
         return run_attention_tp(args)
+    if args.kernel == "overlap":
+        return run_overlap(args)
     if args.kernel is not None:
         return run_kernel(args)
     import torch

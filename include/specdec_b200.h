@@ -178,7 +178,8 @@ int specdec_peer_barrier(void* const* flags, int world, int rank, unsigned* epoc
  * overlap on the GPU.  last_ids (int32 [B, k, candidates], or null): with it, probs is a persistent buffer that
  * is zero except where this row scattered q on the previous call, listed in last_ids (-1 = none; all -1 and a
  * zeroed probs at first use); those entries are cleared and the new ids recorded, so the caller need not zero
- * the [B, k, V] probs (the reference's speculative.py:170-171 zero-fill) every call. */
+ * the [B, k, V] probs (the reference's speculative.py:170-171 zero-fill) every call.  bias null: logits is this
+ * step's already biased rows, [B, V] (as specdec_markov_bias writes them), and round_bf16 applies to nothing. */
 long long specdec_markov_workspace_bytes(int B, int V, int candidates, int greedy);
 int specdec_markov_step(const void* logits, int logits_dtype, const void* bias, int bias_dtype, int B, int k, int V,
                         int row, int candidates, int greedy, int round_bf16, const float* temperature,
@@ -214,6 +215,17 @@ long long specdec_context_gemm_workspace_bytes(int T, int O);
 int specdec_context_gemm(const void* x, long long x_row_stride, const void* w, long long w_row_stride, int T, int O,
                          int K, void* out, long long out_row_stride, void* workspace, long long workspace_bytes,
                          int* err, void* stream);
+/* DSpark's biased row (nanovllm/engine/speculative.py:173 with MarkovHead, nanovllm/models/dflash.py:39-41):
+ * out[b, v] = bf16(bf16(sum_r e[b, r] * w2[v, r]) + logits[b, v]) for b < B, the rank-`rank` Markov bias of the
+ * previous tokens' embeddings e [B, rank] (markov_w1 rows) against markov_w2 [V, rank], added to this step's logits
+ * rows in the same tensor-core GEMM's epilogue, so the bias never reaches memory; the biased rows go straight to
+ * specdec_markov_step with a null bias.  bf16 throughout, row strides in elements (16-byte multiples for e and
+ * w2); B <= 288, V a multiple of 128, rank a multiple of 64.  Workspace as for specdec_context_gemm with
+ * T = B, O = V. */
+int specdec_markov_bias(const void* w2, long long w2_row_stride, const void* e, long long e_row_stride, int B, int V,
+                        int rank, const void* logits, long long logits_row_stride, void* out,
+                        long long out_row_stride, void* workspace, long long workspace_bytes, int* err,
+                        void* stream);
 /* DFlashDraftModel.store_context_kv (dflash.py:88-96) fused: the same GEMM against the layers' stacked W_kv
  * ([layers * 2 * Hkv * 128, K]: per layer its K rows then its V rows) with the projection never leaving the chip:
  * each 128-row tile is one (layer, K|V, head); K rows get RMSNorm (k_norm [layers, 128], layer stride in

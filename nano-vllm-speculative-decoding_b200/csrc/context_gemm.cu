@@ -40,10 +40,14 @@ constexpr int kStageBytes = kABytes + kMaxBBytes;            // 52 KB
 constexpr int kErrTimeout = 16;
 
 struct Args {
-  int mode;                    // 0: out = the product; 1: draft context K/V (tiles = (layer, K|V, head) of 128)
+  int mode;                    // 0: out = the product; 1: draft context K/V (tiles = (layer, K|V, head) of 128);
+                               // 2: DSpark's biased row, out = bf16(bf16(product) + logits)
   int T, O, K;                 // tokens, output features, reduction length
   int n_sub, tn;               // UMMAs per k step and their width: n_sub * tn >= T, tn % 16 == 0, tn <= 256
   int kblocks;                 // K / 64
+  int whole_tiles;             // 1: every CTA takes whole tiles (more tiles than CTAs), no split tiles
+  int nbuf;                    // accumulators in tensor memory: 2 (MMAs of the next tile overlap this tile's
+                               // epilogue) when whole tiles of <= 128 columns, else 1
   __nv_bfloat16* out;          // [T, O] (row stride out_stride)
   long long out_stride;
   int* counters;               // [O / 128] arrivals at split tiles (zero between launches)
@@ -61,11 +65,15 @@ struct Args {
   __nv_bfloat16* v_cache;
   long long cache_layer_stride, num_slots;
   float eps;
+  // mode 2 (the Markov bias): token t's logits row (token = batch row, output feature = vocabulary entry)
+  const __nv_bfloat16* logits; // [T] rows of O values, row stride logits_stride
+  long long logits_stride;
+  int vec2;                    // mode 2 with T <= 64 and 16-byte aligned rows: the shared-memory epilogue
 };
 
 struct Smem {
   uint64_t full[kStages], empty[kStages];
-  uint64_t acc_full, acc_empty;
+  uint64_t acc_full[2], acc_empty[2];
   uint32_t tmem_base;
   int abort;
   int last;
@@ -75,6 +83,8 @@ struct Smem {
 
 constexpr int kSmemBytes = kStages * kStageBytes + (int)sizeof(Smem) + 1024;
 static_assert(kSmemBytes <= 232448, "shared memory above the sm_100 per-CTA limit");
+// mode 2's transposed tile fits in stage 0 past the operands of a <= 64-column call
+static_assert(kABytes + 64 * kBlockK * 2 + 64 * (kTileM + 8) * 2 <= kStageBytes, "mode 2 tile buffer");
 
 __device__ __forceinline__ long long ceil_div_ll(long long x, long long y) { return (x + y - 1) / y; }
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
@@ -107,6 +117,20 @@ __device__ __forceinline__ void emit16(const Args& a, Smem& S, int m, int c0, in
 #pragma unroll
     for (int j = 0; j < 16; ++j)
       if (c0 + j < a.T) a.out[(long long)(c0 + j) * a.out_stride + o] = __float2bfloat16_rn(v[j]);
+    return;
+  }
+  if (a.mode == 2) {
+    // speculative.py:173: logits[:, row] + markov_head(prev), the head's F.linear output rounded to bf16, then
+    // the bf16 sum (the exact fp32 sum of two bf16 values, rounded once)
+    const int o = m * kTileM + row;
+    float l[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      l[j] = c0 + j < a.T ? __bfloat162float(a.logits[(long long)(c0 + j) * a.logits_stride + o]) : 0.0f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (c0 + j < a.T)
+        a.out[(long long)(c0 + j) * a.out_stride + o] = __float2bfloat16_rn(bf16_round(v[j]) + l[j]);
     return;
   }
   const int layer = m / (2 * a.Hkv), kv = (m / a.Hkv) & 1, head = m % a.Hkv;
@@ -161,6 +185,89 @@ __device__ __forceinline__ void emit16(const Args& a, Smem& S, int m, int c0, in
   }
 }
 
+// Mode 2, a whole tile: this thread's vocabulary entry o of the tile for every batch row.  The logits of the first
+// 64 rows were loaded (raw bf16) before the accumulator was ready, so the epilogue does not wait on them.
+constexpr int kPrefetchCols = 64;
+__device__ __forceinline__ void prefetch_logits(const Args& a, int m, int row, unsigned short (&pre)[kPrefetchCols]) {
+  const unsigned short* lg = reinterpret_cast<const unsigned short*>(a.logits) + m * kTileM + row;
+#pragma unroll
+  for (int j = 0; j < kPrefetchCols; ++j) pre[j] = j < a.T ? __ldg(lg + (long long)j * a.logits_stride) : 0;
+}
+
+__device__ __forceinline__ void biased_tile(const Args& a, uint32_t acc, int m, int row, int ncols,
+                                            const unsigned short (&pre)[kPrefetchCols]) {
+  const int o = m * kTileM + row;
+#pragma unroll
+  for (int c0 = 0; c0 < kPrefetchCols; c0 += 16) {
+    if (c0 < ncols) {
+      float v[16];
+      tmem_ld_32x32b_x16(acc + c0, v);
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (c0 + j < a.T)
+          a.out[(long long)(c0 + j) * a.out_stride + o] =
+              __float2bfloat16_rn(bf16_round(v[j]) + __uint_as_float((unsigned)pre[c0 + j] << 16));
+    }
+  }
+  for (int c0 = kPrefetchCols; c0 < ncols; c0 += 16) {         // rows past the prefetched ones (B > 64)
+    float v[16];
+    tmem_ld_32x32b_x16(acc + c0, v);
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (c0 + j < a.T)
+        a.out[(long long)(c0 + j) * a.out_stride + o] = __float2bfloat16_rn(
+            bf16_round(v[j]) + __bfloat162float(a.logits[(long long)(c0 + j) * a.logits_stride + o]));
+  }
+}
+
+// Mode 2, a whole tile of <= 64 batch rows through shared memory: the accumulator's columns (one vocabulary entry
+// per thread, one batch row per column) rounded to bf16 and stored transposed into tb [row][128 entries], then
+// every thread adds 16-byte vectors of the logits rows (loaded before the accumulator was ready) and writes 16-byte
+// vectors of the biased rows.  tb lies in stage 0's bytes past the operands of a <= 64-column call, which TMA never
+// writes.
+constexpr int kTbStride = kTileM + 8;          // bf16 per transposed row (padding against bank conflicts)
+constexpr int kVecPerThread = kPrefetchCols * (kTileM / 8) / 128;   // 8 vectors of 8 entries per epilogue thread
+__device__ __forceinline__ void prefetch_logits_vec(const Args& a, int m, int tid, uint4 (&pre)[kVecPerThread]) {
+#pragma unroll
+  for (int i = 0; i < kVecPerThread; ++i) {
+    const int id = tid + 128 * i, b = id >> 4, v0 = (id & 15) * 8;
+    pre[i] = b < a.T ? ldg16(a.logits + (long long)b * a.logits_stride + m * kTileM + v0) : make_uint4(0, 0, 0, 0);
+  }
+}
+
+__device__ __forceinline__ void biased_tile_vec(const Args& a, uint32_t acc, int m, int row, int tid, int ncols,
+                                                __nv_bfloat16* tb, const uint4 (&pre)[kVecPerThread]) {
+  for (int c0 = 0; c0 < ncols; c0 += 16) {
+    float v[16];
+    tmem_ld_32x32b_x16(acc + c0, v);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) tb[(c0 + j) * kTbStride + row] = __float2bfloat16_rn(v[j]);   // the bf16 bias
+  }
+  named_barrier(3, 128);
+#pragma unroll
+  for (int i = 0; i < kVecPerThread; ++i) {
+    const int id = tid + 128 * i, b = id >> 4, v0 = (id & 15) * 8;
+    if (b < a.T) {
+      const uint4 bias = *reinterpret_cast<const uint4*>(tb + b * kTbStride + v0);
+      const uint4 l = pre[i];
+      uint4 r;
+      const unsigned* bp = reinterpret_cast<const unsigned*>(&bias);
+      const unsigned* lp = reinterpret_cast<const unsigned*>(&l);
+      unsigned* rp = reinterpret_cast<unsigned*>(&r);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {      // bf16 pairs: the exact sum of two bf16 values, rounded once
+        __nv_bfloat162 x, y;
+        memcpy(&x, &lp[e], 4);
+        memcpy(&y, &bp[e], 4);
+        const __nv_bfloat162 z = __hadd2(x, y);
+        memcpy(&rp[e], &z, 4);
+      }
+      *reinterpret_cast<uint4*>(a.out + (long long)b * a.out_stride + m * kTileM + v0) = r;
+    }
+  }
+  named_barrier(3, 128);                 // tb is rewritten by the next tile
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     context_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                         const Args a) {
@@ -169,21 +276,33 @@ __global__ void __launch_bounds__(kThreads, 1)
   Smem& S = *reinterpret_cast<Smem*>(base + kStages * kStageBytes);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ncols = a.n_sub * a.tn;
-  const int tmem_cols = ncols > 256 ? 512 : 256;
+  const int tmem_cols = ncols * a.nbuf > 256 ? 512 : 256;
 
-  // ---- this CTA's share of the (tile, k block) units
-  const long long U = (long long)(a.O / kTileM) * a.kblocks;
-  const long long Ge = U < (long long)gridDim.x ? U : (long long)gridDim.x;
+  // ---- this CTA's share of the (tile, k block) units: stream-K over units, or (more tiles than CTAs) whole
+  // tiles, tiles * c / G .. tiles * (c + 1) / G
+  const long long tiles = a.O / kTileM;
+  const long long U = tiles * a.kblocks;
   const long long c = blockIdx.x;
-  const long long xb = c < Ge ? U * c / Ge : 0, xe = c < Ge ? U * (c + 1) / Ge : 0;
+  long long Ge, xb, xe;
+  if (a.whole_tiles) {
+    Ge = tiles < (long long)gridDim.x ? tiles : (long long)gridDim.x;
+    xb = c < Ge ? tiles * c / Ge * a.kblocks : 0;
+    xe = c < Ge ? tiles * (c + 1) / Ge * a.kblocks : 0;
+  } else {
+    Ge = U < (long long)gridDim.x ? U : (long long)gridDim.x;
+    xb = c < Ge ? U * c / Ge : 0;
+    xe = c < Ge ? U * (c + 1) / Ge : 0;
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&S.full[s], 1);
       mbar_init(&S.empty[s], 1);
     }
-    mbar_init(&S.acc_full, 1);
-    mbar_init(&S.acc_empty, 4);     // one elected arrival per epilogue warp
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&S.acc_full[i], 1);
+      mbar_init(&S.acc_empty[i], 4);     // one elected arrival per epilogue warp
+    }
     S.abort = 0;
     fence_barrier_init();
     prefetch_tensormap(&wmap);
@@ -223,8 +342,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       while (ok && x < xe) {
         const int m = (int)(x / a.kblocks);
         const long long end = (long long)(m + 1) * a.kblocks < xe ? (long long)(m + 1) * a.kblocks : xe;
-        if (piece > 0 && !mbar_wait(&S.acc_empty, (piece - 1) & 1, abort, a.err, kErrTimeout)) break;
+        const int buf = piece % a.nbuf;
+        if (piece >= a.nbuf && !mbar_wait(&S.acc_empty[buf], ((piece / a.nbuf) - 1) & 1, abort, a.err, kErrTimeout))
+          break;
         tc_fence_after();
+        const uint32_t acc = tmem + (uint32_t)(buf * ncols);
         for (bool first = true; x < end; ++x, ++g, first = false) {
           const int stage = g % kStages;
           if (!mbar_wait(&S.full[stage], (g / kStages) & 1, abort, a.err, kErrTimeout)) { ok = false; break; }
@@ -235,13 +357,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t adesc = smem_desc(st + kk * 32, 16, 1024, kSwizzle128B);
             for (int h = 0; h < a.n_sub; ++h) {
               const uint64_t bdesc = smem_desc(st + kABytes + h * a.tn * 128 + kk * 32, 16, 1024, kSwizzle128B);
-              mma_bf16_ss(tmem + h * a.tn, adesc, bdesc, idesc, (first && kk == 0) ? 0u : 1u);
+              mma_bf16_ss(acc + h * a.tn, adesc, bdesc, idesc, (first && kk == 0) ? 0u : 1u);
             }
           }
           mma_commit(&S.empty[stage]);
         }
         if (!ok) break;
-        mma_commit(&S.acc_full);
+        mma_commit(&S.acc_full[buf]);
         ++piece;
       }
     } else if (warp >= 4) {
@@ -257,30 +379,46 @@ __global__ void __launch_bounds__(kThreads, 1)
         const long long end = B < xe ? B : xe;
         x = end;
         const long long c_lo = ceil_div_ll((A + 1) * Ge, U) - 1, c_hi = ceil_div_ll(B * Ge, U) - 1;
-        if (!mbar_wait(&S.acc_full, piece & 1, abort, a.err, kErrTimeout)) break;
+        const int buf = piece % a.nbuf;
+        const bool biased = a.mode == 2 && a.whole_tiles;
+        unsigned short pre[kPrefetchCols];
+        uint4 prev[kVecPerThread];
+        if (biased && a.vec2) prefetch_logits_vec(a, m, row, prev);   // independent of the MMAs: loaded meanwhile
+        else if (biased) prefetch_logits(a, m, row, pre);
+        if (!mbar_wait(&S.acc_full[buf], (piece / a.nbuf) & 1, abort, a.err, kErrTimeout)) break;
         tc_fence_after();
-        if (c_lo == c_hi) {
+        const uint32_t acc = tmem + lane_off + (uint32_t)(buf * ncols);
+        if (biased) {
+          if (a.vec2)
+            biased_tile_vec(a, acc, m, row, row, ncols,
+                            reinterpret_cast<__nv_bfloat16*>(base + kABytes + kPrefetchCols * kBlockK * 2), prev);
+          else
+            biased_tile(a, acc, m, row, ncols, pre);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&S.acc_empty[buf]);
+        } else if (a.whole_tiles || c_lo == c_hi) {
           // the whole tile here: rows straight from the accumulator
           for (int c0 = 0; c0 < ncols; c0 += 16) {
             float v[16];
-            tmem_ld_32x32b_x16(tmem + lane_off + c0, v);
+            tmem_ld_32x32b_x16(acc + c0, v);
             emit16(a, S, m, c0, row, w, lane, v);
           }
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&S.acc_empty);
+          if (lane == 0) mbar_arrive(&S.acc_empty[buf]);
         } else {
           // a piece: published (fp32), then the last CTA to arrive sums the pieces in CTA order
           float* mine = a.partial + (2LL * c + (xb < A ? 1 : 0)) * (long long)ncols * kTileM;
           for (int c0 = 0; c0 < ncols; c0 += 16) {
             float v[16];
-            tmem_ld_32x32b_x16(tmem + lane_off + c0, v);
+            tmem_ld_32x32b_x16(acc + c0, v);
 #pragma unroll
             for (int j = 0; j < 16; ++j) __stcg(mine + (long long)(c0 + j) * kTileM + row, v[j]);
           }
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&S.acc_empty);        // the MMAs may refill the accumulator now
+          if (lane == 0) mbar_arrive(&S.acc_empty[buf]);   // the MMAs may refill the accumulator now
           __threadfence();
           named_barrier(1, 128);
           if (threadIdx.x == 128) {
@@ -384,12 +522,14 @@ static int launch(Args a, const void* x, long long x_row_stride, const void* w, 
   if (int st = device_info(&info)) return st;
   const long long units = (long long)(a.O / kTileM) * (a.K / kBlockK);
   const int grid = (int)(units < info.sm_count ? units : info.sm_count);
+  a.whole_tiles = a.O / kTileM >= grid ? 1 : 0;
   const long long need = workspace_bytes(a.T, a.O, info.sm_count);
   if (workspace_bytes_given < need)
     return set_error(kWorkspaceTooSmall, "context GEMM workspace of %lld bytes, %lld needed",
                      workspace_bytes_given, need);
   columns(a.T, &a.n_sub, &a.tn);
   a.kblocks = a.K / kBlockK;
+  a.nbuf = a.whole_tiles && a.n_sub * a.tn <= 128 ? 2 : 1;
   a.counters = static_cast<int*>(workspace);
   a.partial = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + counters_bytes(a.O));
   a.err = err;
@@ -427,6 +567,26 @@ int specdec_context_gemm(const void* x, long long x_row_stride, const void* w, l
   a.out = static_cast<__nv_bfloat16*>(out);
   a.out_stride = out_row_stride;
   return gemm::launch(a, x, x_row_stride, w, w_row_stride, workspace, workspace_bytes, err, stream);
+}
+
+int specdec_markov_bias(const void* w2, long long w2_row_stride, const void* e, long long e_row_stride, int B, int V,
+                        int rank, const void* logits, long long logits_row_stride, void* out,
+                        long long out_row_stride, void* workspace, long long workspace_bytes, int* err,
+                        void* stream) {
+  SPECDEC_CHECK_ARG(logits && out, "null pointer argument");
+  SPECDEC_CHECK_ARG(logits_row_stride >= V && out_row_stride >= V, "row strides below V");
+  gemm::Args a{};
+  a.mode = 2;
+  a.T = B;
+  a.O = V;
+  a.K = rank;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.out_stride = out_row_stride;
+  a.logits = static_cast<const __nv_bfloat16*>(logits);
+  a.logits_stride = logits_row_stride;
+  a.vec2 = B <= gemm::kPrefetchCols && ((reinterpret_cast<uintptr_t>(logits) | reinterpret_cast<uintptr_t>(out)) & 15) == 0 &&
+           logits_row_stride % 8 == 0 && out_row_stride % 8 == 0 && V % 8 == 0;
+  return gemm::launch(a, e, e_row_stride, w2, w2_row_stride, workspace, workspace_bytes, err, stream);
 }
 
 int specdec_context_kv_store(const void* x, long long x_row_stride, const void* w_kv, long long w_row_stride, int T,

@@ -31,9 +31,9 @@ constexpr int kMaxCand = 1024;
 constexpr int kSelCap = 4096;          // elements the thread-maxima bound may admit before the radix fallback
 
 struct Args {
-  const void* logits;       // [B, k, V] (dtype ldt)
+  const void* logits;       // [B, k, V] (dtype ldt); with no bias, this step's biased rows [B, V]
   int ldt;
-  const void* bias;         // [B, V] (dtype bdt) this step's Markov bias
+  const void* bias;         // [B, V] (dtype bdt) this step's Markov bias, or null (logits arrive biased)
   int bdt;
   int B, k, V, j, C, greedy, round_bf16;
   const float* temperature; // [B]
@@ -72,7 +72,8 @@ __device__ __forceinline__ float load_any(const void* p, int dt, long long i) {
 }
 
 __device__ __forceinline__ float row_value(const Args& a, long long lrow, long long brow, int v) {
-  float x = load_any(a.logits, a.ldt, lrow + v) + load_any(a.bias, a.bdt, brow + v);
+  float x = load_any(a.logits, a.ldt, lrow + v);
+  if (a.bias) x += load_any(a.bias, a.bdt, brow + v);
   if (a.round_bf16) x = __bfloat162float(__float2bfloat16_rn(x));
   return x;
 }
@@ -85,9 +86,14 @@ __device__ __forceinline__ int load_group(const Args& a, long long lrow, long lo
   if (a.vec && n == 8) {
     float l8[8], b8[8];
     unpack16_bf16(ldg16(reinterpret_cast<const __nv_bfloat16*>(a.logits) + lrow + v0), l8);
-    unpack16_bf16(ldg16(reinterpret_cast<const __nv_bfloat16*>(a.bias) + brow + v0), b8);
+    if (a.bias) {
+      unpack16_bf16(ldg16(reinterpret_cast<const __nv_bfloat16*>(a.bias) + brow + v0), b8);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) x[e] = __bfloat162float(__float2bfloat16_rn(l8[e] + b8[e]));
+      for (int e = 0; e < 8; ++e) x[e] = __bfloat162float(__float2bfloat16_rn(l8[e] + b8[e]));
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[e] = l8[e];
+    }
   } else {
 #pragma unroll
     for (int e = 0; e < 8; ++e) x[e] = e < n ? row_value(a, lrow, brow, v0 + e) : -INFINITY;
@@ -151,7 +157,8 @@ __global__ void __launch_bounds__(kThreads, 2) markov_step_kernel(const Args a) 
 
   const int piece = blockIdx.x, b = blockIdx.y;
   const int V = a.V;
-  const long long lrow = ((long long)b * a.k + a.j) * V;
+  const long long qrow = ((long long)b * a.k + a.j) * V;           // row (b, j) of q [B, k, V]
+  const long long lrow = a.bias ? qrow : (long long)b * V;          // the logits' row: [B, k, V] or biased [B, V]
   const long long brow = (long long)b * V;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int C = a.C;
@@ -194,10 +201,16 @@ __global__ void __launch_bounds__(kThreads, 2) markov_step_kernel(const Args a) 
         // is what torch's bf16 add gives (its fp32 sum of two bf16 values is exact, or off only far below half
         // a bf16 ulp of the larger term).
         const uint4* lg = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.logits) + lrow) + g_lo;
-        const uint4* bg = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.bias) + brow) + g_lo;
-        fast = select_by_thread_max_x16<kThreads, 4, __nv_bfloat162>(
-            ngroups, C, [&](int g) { return bf16x8_add(__ldg(lg + g), __ldg(bg + g)); }, sel, kSelCap, &s_sel,
-            &top);
+        if (a.bias) {
+          const uint4* bg =
+              reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.bias) + brow) + g_lo;
+          fast = select_by_thread_max_x16<kThreads, 4, __nv_bfloat162>(
+              ngroups, C, [&](int g) { return bf16x8_add(__ldg(lg + g), __ldg(bg + g)); }, sel, kSelCap, &s_sel,
+              &top);
+        } else {                      // the row arrives biased (specdec_markov_bias wrote it)
+          fast = select_by_thread_max_x16<kThreads, 4, __nv_bfloat162>(
+              ngroups, C, [&](int g) { return __ldg(lg + g); }, sel, kSelCap, &s_sel, &top);
+        }
       } else {
         fast = select_by_thread_max<kThreads, 1>(ngroups, C, load, sel, kSelCap, &s_sel, &top);
       }
@@ -414,7 +427,7 @@ __global__ void __launch_bounds__(kThreads, 2) markov_step_kernel(const Args a) 
     if (last) {
       for (int i = threadIdx.x; i < C; i += kThreads) {
         const int old = last[i];
-        if (old >= 0 && old < V) a.probs[lrow + old] = 0.0f;
+        if (old >= 0 && old < V) a.probs[qrow + old] = 0.0f;
       }
       __syncthreads();
     }
@@ -422,7 +435,7 @@ __global__ void __launch_bounds__(kThreads, 2) markov_step_kernel(const Args a) 
     for (int i = threadIdx.x; i < C; i += kThreads) {
       const float p = __fdiv_rn(cprob[i], z);
       const int id = (int)(0xffffffffu - (unsigned)(cand[i] & 0xffffffffull));
-      a.probs[lrow + id] = p;
+      a.probs[qrow + id] = p;
       if (last) last[i] = id;
       float ratio = __fdiv_rn(p, noise[i]);
       if (ratio == 0.0f) ratio = 0.0f;
@@ -483,9 +496,9 @@ int specdec_markov_step(const void* logits, int logits_dtype, const void* bias, 
                         int rank, void* e_next, int* last_ids, void* workspace, long long workspace_bytes, int* err,
                         void* stream) {
   using namespace markov;
-  SPECDEC_CHECK_ARG(logits && bias && drafts && prev_out && err && workspace, "null pointer argument");
+  SPECDEC_CHECK_ARG(logits && drafts && prev_out && err && workspace, "null pointer argument");
   SPECDEC_CHECK_ARG((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "workspace must be 256-byte aligned");
-  SPECDEC_CHECK_ARG(dtype_ok(logits_dtype) && dtype_ok(bias_dtype), "unknown dtype code");
+  SPECDEC_CHECK_ARG(dtype_ok(logits_dtype) && (!bias || dtype_ok(bias_dtype)), "unknown dtype code");
   SPECDEC_CHECK_ARG(B >= 1 && B <= 65535 && k >= 1 && V >= 1 && row >= 0 && row < k, "bad sizes");
   SPECDEC_CHECK_ARG(!w1 || (e_next && rank >= 1), "w1 needs e_next and rank");
   if (!greedy) {
@@ -505,7 +518,7 @@ int specdec_markov_step(const void* logits, int logits_dtype, const void* bias, 
   a.w1 = static_cast<const __nv_bfloat16*>(w1); a.rank = rank; a.e_next = static_cast<__nv_bfloat16*>(e_next);
   a.err = err;
   a.last_ids = greedy ? nullptr : last_ids;
-  a.vec = logits_dtype == kBF16 && bias_dtype == kBF16 && V % 8 == 0 &&
+  a.vec = logits_dtype == kBF16 && (!bias || bias_dtype == kBF16) && V % 8 == 0 &&
           ((reinterpret_cast<uintptr_t>(logits) | reinterpret_cast<uintptr_t>(bias)) & 15) == 0;
   DeviceInfo info;
   if (int st = device_info(&info)) return st;

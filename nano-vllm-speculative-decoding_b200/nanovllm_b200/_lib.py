@@ -73,6 +73,8 @@ SIGNATURES = {
     "specdec_context_gemm_workspace_bytes": (_c_ll, [_c_int, _c_int]),
     "specdec_context_gemm": (_c_int, [_c_void_p, _c_ll, _c_void_p, _c_ll, _c_int, _c_int, _c_int, _c_void_p, _c_ll,
                                       _c_void_p, _c_ll, _c_void_p, _c_void_p]),
+    "specdec_markov_bias": (_c_int, [_c_void_p, _c_ll, _c_void_p, _c_ll, _c_int, _c_int, _c_int, _c_void_p, _c_ll,
+                                     _c_void_p, _c_ll, _c_void_p, _c_ll, _c_void_p, _c_void_p]),
     "specdec_context_kv_store": (_c_int, [_c_void_p, _c_ll, _c_void_p, _c_ll, _c_int, _c_int, _c_int, _c_int,
                                           _c_void_p, _c_ll, _c_void_p, _c_ll, _c_void_p, _c_void_p, _c_void_p,
                                           _c_void_p, _c_ll, _c_ll, _c_float, _c_void_p, _c_ll, _c_void_p,

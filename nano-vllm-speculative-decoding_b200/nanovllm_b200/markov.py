@@ -6,7 +6,9 @@ mirrors DFlashDrafter._markov_rows (nanovllm/engine/speculative.py:163-184) with
 k sequential steps, each `bias = markov_head(prev)` (for MarkovHeadWeights a cuBLAS GEMM of the W1 rows the
 previous step's kernel gathered against W2) followed by ONE kernel launch that, for every batch row at once,
 adds the bias, selects the top `candidates` logits (ties by ascending token id), applies the row's temperature /
-top-k / top-p over them, races them against that row's noise and scatters q.  Greedy batches take the argmax.
+top-k / top-p over them, races them against that row's noise, scatters q and gathers the next W1 rows.  With
+fused_bias=True the bias GEMM is this library's tcgen05 kernel with the logits added in its epilogue
+(specdec_markov_bias), and the selection reads the biased rows; verified, slower than cuBLAS here.  Greedy batches take the argmax.
 Rows drawn over the whole vocabulary (candidates == 0: some row does not truncate) use the sampler's
 probs_from_logits + race kernels.  drafts [B, k] and draft_probs [B, k, V] are written in place, as in the
 reference; noise [B, k, candidates or V] is drawn by the caller before row 0 (speculative.py:156-159).
@@ -43,6 +45,44 @@ class MarkovHeadWeights:
         return torch.matmul(self.embed(prev), self.w2.t())
 
 
+def fused_bias_eligible(logits: torch.Tensor, weights) -> bool:
+    """Whether a step's bias can come from specdec_markov_bias: a MarkovHeadWeights head and bf16 logits, the
+    vocabulary a multiple of 128, the rank a multiple of 64 and at most 288 rows (the tensor-core GEMM's shape)."""
+    if not isinstance(weights, MarkovHeadWeights):
+        return False
+    batch, _, vocab = logits.shape
+    rank = weights.w2.shape[1]
+    return (logits.dtype == torch.bfloat16 and weights.w1.dtype == torch.bfloat16 and weights.w2.dtype ==
+            torch.bfloat16 and vocab % 128 == 0 and rank % 64 == 0 and batch <= 288 and weights.w2.stride(1) == 1
+            and (weights.w2.stride(0) * 2) % 16 == 0)
+
+
+def _bias_workspace(device: torch.device, batch: int, vocab: int) -> torch.Tensor:
+    lib = _lib.lib()
+    with torch.cuda.device(device):
+        need = int(lib.specdec_context_gemm_workspace_bytes(batch, vocab))
+    if need < 0:
+        raise _lib.SpecdecError(lib.specdec_last_error().decode())
+    return Workspace.get(device, need, name="markov_bias")
+
+
+def markov_bias(w2: torch.Tensor, e: torch.Tensor, row_logits: torch.Tensor, out: torch.Tensor,
+                workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """speculative.py:173 with MarkovHead (dflash.py:39-41): out [B, V] = bf16(bf16(e . w2^T) + row_logits), the
+    bias GEMM on the tensor cores with the logits added in its epilogue.  e [B, rank] (the markov_w1 rows of the
+    previous tokens), w2 [V, rank], row_logits [B, V] (rows may be strided), all bf16."""
+    device = require_cuda(w2, e, row_logits, out)
+    batch, rank = e.shape
+    vocab = w2.shape[0]
+    if row_logits.stride(1) != 1 or out.stride(1) != 1 or e.stride(1) != 1:
+        raise ValueError("the Markov bias GEMM needs unit-stride rows")
+    ws = workspace if workspace is not None else _bias_workspace(device, batch, vocab)
+    check(_lib.lib().specdec_markov_bias(ptr(w2), w2.stride(0), ptr(e), e.stride(0), batch, vocab, rank,
+                                         ptr(row_logits), row_logits.stride(0), ptr(out), out.stride(0), ptr(ws),
+                                         ws.numel(), ptr(err_word(device)), stream_of(device)))
+    return out
+
+
 def _round_flag(logits: torch.Tensor, bias: torch.Tensor) -> int:
     if logits.dtype == torch.bfloat16 and bias.dtype == torch.bfloat16:
         return 1
@@ -72,9 +112,13 @@ class MarkovQBuffer:
 
 
 def markov_rows(logits: torch.Tensor, prev: torch.Tensor, sampling, noise: torch.Tensor | None,
-                drafts: torch.Tensor, draft_probs: torch.Tensor | None, candidates: int, markov_head) -> None:
+                drafts: torch.Tensor, draft_probs: torch.Tensor | None, candidates: int, markov_head, *,
+                fused_bias: bool = False) -> None:
     """speculative.py:163-184: draw the k rows left to right into drafts (and q into draft_probs unless greedy);
-    prev holds the anchors.  logits [B, k, V]; markov_head(prev [B]) -> bias [B, V]."""
+    prev holds the anchors.  logits [B, k, V]; markov_head(prev [B]) -> bias [B, V].  fused_bias (MarkovHeadWeights,
+    bf16, shapes as fused_bias_eligible): each step's bias from specdec_markov_bias with the logits added in the
+    GEMM's epilogue; verified, but measured slower than the cuBLAS bias GEMM at config 4 (31 vs 17 us per step), so
+    off by default."""
     device = require_cuda(logits, prev, drafts)
     batch, k, vocab = logits.shape
     logits = logits.contiguous()
@@ -108,7 +152,22 @@ def markov_rows(logits: torch.Tensor, prev: torch.Tensor, sampling, noise: torch
         if need < 0:
             raise _lib.SpecdecError(lib.specdec_last_error().decode())
         ws = Workspace.get(device, need, name="markov")    # zeroed once; the kernel keeps its counters zeroed
+    fused = fused_bias and (greedy or candidates) and fused_bias_eligible(logits, weights)
+    if fused:
+        # the bias GEMM with the logits added in its epilogue (one tcgen05 kernel per row), then the selection
+        # reads the biased rows: the [B, V] bias is never written
+        biased = torch.empty(batch, vocab, dtype=torch.bfloat16, device=device)
+        gemm_ws = _bias_workspace(device, batch, vocab)
     for row in range(k):
+        if fused:
+            markov_bias(weights.w2, e_buf, logits[:, row], biased, gemm_ws)
+            check(lib.specdec_markov_step(
+                ptr(biased), DTYPE_CODES[torch.bfloat16], None, 0, batch, k, vocab, row, candidates, int(greedy), 1,
+                ptr(temps), ptr(top_k), ptr(top_p), max_top_k, has_top_p, ptr(noise),
+                0 if noise is None else noise.shape[-1], ptr(drafts), ptr(draft_probs), ptr(prev_buf), ptr(weights.w1),
+                weights.w1.shape[1], ptr(e_buf), ptr(None if qbuf is None else qbuf.ids), ptr(ws), ws.numel(),
+                ptr(err_word(device)), stream))
+            continue
         bias = torch.matmul(e_buf, weights.w2.t()) if weights is not None else markov_head(prev_buf)
         bias = bias.contiguous()
         if greedy or candidates:

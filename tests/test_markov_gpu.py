@@ -269,3 +269,96 @@ def test_markov_workspace_shared_by_batches_of_different_sizes():
         if B in runs:
             assert torch.equal(drafts, runs[B][0]) and torch.equal(greedy, runs[B][1])
         runs[B] = (drafts, greedy)
+
+
+# ---------------------------------------------------------------------------------------------- fused bias GEMM
+def test_markov_bias_gemm_against_the_fp32_product():
+    """specdec_markov_bias: bf16(bf16(e . W2^T) + logits) on the tensor cores, at config 4's shape (64 rows, rank
+    256, V = 151936) and a ragged one (37 rows: a partial column tile), against the fp32 product: the bias within
+    one bf16 rounding plus summation order, then one rounding of the sum."""
+    from nanovllm_b200.markov import markov_bias
+    for B, V in [(64, 151936), (37, 1280)]:
+        g = torch.Generator(device=DEV).manual_seed(B)
+        r = 256
+        w2 = (torch.randn(V, r, device=DEV, generator=g) * 0.1).bfloat16()
+        e = (torch.randn(B, r, device=DEV, generator=g) * 0.1).bfloat16()
+        logits = (torch.randn(B, 3, V, device=DEV, generator=g) * 2).bfloat16()
+        out = torch.full((B, V), float("nan"), dtype=torch.bfloat16, device=DEV)
+        markov_bias(w2, e, logits[:, 1], out)
+        bias = e.float() @ w2.float().t()
+        want = logits[:, 1].float() + bias
+        got = out.float()
+        assert torch.isfinite(got).all()
+        tol = bias.abs() * 2 ** -8 + want.abs() * 2 ** -8 + 1e-3 * bias.abs().max()
+        assert bool(((got - want).abs() <= tol).all())
+
+
+def fused_case(B, k, V, r, seed):
+    from nanovllm_b200.markov import MarkovHeadWeights
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    logits = (torch.randn(B, k, V, device=DEV, generator=g) * 2).bfloat16()
+    head = MarkovHeadWeights((torch.randn(V, r, device=DEV, generator=g) * 0.1).bfloat16(),
+                             (torch.randn(V, r, device=DEV, generator=g) * 0.1).bfloat16())
+    prev = torch.randint(V, (B,), device=DEV, generator=g)
+    return g, logits, head, prev
+
+
+@pytest.mark.parametrize("greedy", [False, True])
+def test_fused_bias_rows_match_oracle(greedy):
+    """Config 4's drafter through the fused-bias path (MarkovHeadWeights, bf16, fused_bias=True): each step's biased
+    rows recomputed with the same kernel from the drafted tokens, and oracle/markov.py run on them (bias 0): drafts
+    bit-exact (at most one row diverging after a near-tie race), q within 1e-5."""
+    from nanovllm_b200.markov import fused_bias_eligible, markov_bias, markov_rows, num_candidates
+    from oracle.ctx_store import bf16
+    B, k, V, r = 64, 7, 151936, 256
+    g, logits, head, prev = fused_case(B, k, V, r, 44)
+    assert fused_bias_eligible(logits, head)
+    drafts = torch.empty(B, k, dtype=torch.int64, device=DEV)
+    if greedy:
+        samp, cand, noise, probs = None, 0, None, None
+    else:
+        samp = sampling_of([1.0] * (B // 2) + [0.7] * (B // 2), [128] * B, [1.0] * (B // 2) + [0.9] * (B // 2))
+        cand = num_candidates(samp.max_top_k, samp.all_top_k, V)
+        noise = torch.empty(B, k, cand, device=DEV).exponential_(generator=g).clamp_min_(1e-10)
+        probs = torch.empty(B, k, V, device=DEV)
+    markov_rows(logits, prev, samp, noise, drafts, probs, cand, head, fused_bias=True)
+    prevs = [prev] + [drafts[:, j] for j in range(k - 1)]
+    biased = torch.empty(B, k, V, dtype=torch.bfloat16, device=DEV)
+    for j, p in enumerate(prevs):
+        markov_bias(head.w2, head.w1[p].contiguous(), logits[:, j], biased[:, j])
+    zero = np.zeros((B, V), np.float32)
+    sampling = None if greedy else dict(temps=samp.temperatures.cpu().numpy(), top_k=samp.top_k.cpu().numpy(),
+                                        top_p=samp.top_p.cpu().numpy(), max_top_k=samp.max_top_k,
+                                        has_top_p=samp.has_top_p)
+    want, want_probs = OM.markov_rows(biased.float().cpu().numpy(), prev.cpu().numpy(), lambda _p: zero, sampling,
+                                      None if noise is None else noise.cpu().numpy(), cand, round_fn=bf16)
+    got = drafts.cpu().numpy()
+    mismatched = (got != want).any(axis=1)
+    assert mismatched.sum() <= 1, f"{mismatched.sum()} rows diverge"
+    if not greedy:
+        same = ~mismatched
+        np.testing.assert_allclose(probs.cpu().numpy()[same], want_probs[same], rtol=1e-5, atol=1e-8)
+
+
+def test_fused_and_unfused_bias_agree_where_the_bias_rounds_alike():
+    """The fused path against the path that adds a given bias in the selection kernel, fed the fused kernel's own
+    biased rows as logits with a zero bias: identical drafts and q (the selection is the same code either way)."""
+    from nanovllm_b200.markov import MarkovQBuffer, markov_bias, markov_rows, num_candidates
+    B, k, V, r = 16, 4, 12800, 64
+    g, logits, head, prev = fused_case(B, k, V, r, 45)
+    samp = sampling_of([0.9] * B, [20] * B, [0.95] * B)
+    cand = num_candidates(samp.max_top_k, samp.all_top_k, V)
+    noise = torch.empty(B, k, cand, device=DEV).exponential_(generator=g).clamp_min_(1e-10)
+    d1 = torch.empty(B, k, dtype=torch.int64, device=DEV)
+    q1 = MarkovQBuffer(B, k, V, cand, DEV)
+    markov_rows(logits, prev, samp, noise, d1, q1, cand, head, fused_bias=True)
+    prevs = [prev] + [d1[:, j] for j in range(k - 1)]
+    biased = torch.empty(B, k, V, dtype=torch.bfloat16, device=DEV)
+    for j, p in enumerate(prevs):
+        markov_bias(head.w2, head.w1[p].contiguous(), logits[:, j], biased[:, j])
+    zero = torch.zeros(B, V, dtype=torch.bfloat16, device=DEV)
+    d2 = torch.empty(B, k, dtype=torch.int64, device=DEV)
+    q2 = torch.empty(B, k, V, device=DEV)
+    markov_rows(biased, prev, samp, noise, d2, q2, cand, lambda _p: zero)
+    assert torch.equal(d1, d2)
+    assert torch.equal(q1.probs, q2)
