@@ -131,9 +131,11 @@ __global__ void __launch_bounds__(256) norm_rope_store_kernel(const NormRopeArgs
 // ---------------------------------------------------------------------------------------- RMSNorm (+ residual)
 // One CTA per token row of `width` bf16 (width % 8 == 0, <= 8192).  With residual: s = x + residual (fp32),
 // residual_out = bf16(s), out = norm(s); without: out = norm(x).
-__global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* x, const __nv_bfloat16* residual,
-                                                      const __nv_bfloat16* weight, __nv_bfloat16* out,
-                                                      __nv_bfloat16* residual_out, int width, float eps) {
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* __restrict__ x,
+                                                      const __nv_bfloat16* __restrict__ residual,
+                                                      const __nv_bfloat16* __restrict__ weight,
+                                                      __nv_bfloat16* __restrict__ out,
+                                                      __nv_bfloat16* __restrict__ residual_out, int width, float eps) {
   constexpr int kMaxVec = 4;   // 4 x 8 elements per thread: width <= 256 * 32 = 8192
   __shared__ float red[8];
   const long long t = blockIdx.x;
@@ -148,16 +150,26 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* x, co
     const int i = threadIdx.x + u * 256;
     if (i < nvec) wraw[u] = wv[i];
   }
+  // every load of the row is issued before the first residual store (the stores would otherwise order them)
+  uint4 xraw[kMaxVec], rraw[kMaxVec];
+#pragma unroll
+  for (int u = 0; u < kMaxVec; ++u) {
+    const int i = threadIdx.x + u * 256;
+    if (i < nvec) {
+      xraw[u] = xv[i];
+      if (rv) rraw[u] = rv[i];
+    }
+  }
   float ss = 0.0f;
 #pragma unroll
   for (int u = 0; u < kMaxVec; ++u) {
     const int i = threadIdx.x + u * 256;
     if (i < nvec) {
       float a[8];
-      unpack16_bf16(xv[i], a);
+      unpack16_bf16(xraw[u], a);
       if (rv) {
         float r[8];
-        unpack16_bf16(rv[i], r);
+        unpack16_bf16(rraw[u], r);
 #pragma unroll
         for (int e = 0; e < 8; ++e) a[e] += r[e];
         uint4 packed;
