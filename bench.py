@@ -51,7 +51,8 @@ def parse_args():
     p.add_argument("--no-extra", action="store_true",
                    help="skip the extra workloads (4k round, 16k attention, config-4 round; TP layer under torchrun)")
     p.add_argument("--kernel", choices=["attention", "accept", "accept_topk", "accept_greedy", "sample", "markov",
-                                        "markov_fused", "ctx_store", "after_verify", "attention_tp", "overlap"],
+                                        "markov_fused", "ctx_store", "after_verify", "attention_tp", "overlap",
+                                        "attention_draft", "round_cfg4"],
                    default=None,
                    help="time one kernel alone on its benchmark config (attention: config 2, accept: config 3's "
                         "logits) instead of the round; used for profiling")
@@ -628,7 +629,36 @@ def run_kernel(args) -> int:
     from types import SimpleNamespace
     device = torch.device("cuda", 0)
     g = torch.Generator().manual_seed(0)
-    if args.kernel == "attention":
+    if args.kernel == "attention_draft":
+        # config 4's draft block attention (the DFlash / DSpark propose forward, attention.py:71-76): 64 rows x 7
+        # queries (anchor + 6 mask tokens), non-causal over the context below the anchor plus the block, contexts
+        # ~3000, 32 / 8 heads of 128, decode layout (context_lens, query_len_per_seq = 7)
+        from nanovllm_b200 import attention
+        R, H, Hkv, D, bs, nq = 64, 32, 8, 128, 256, 7
+        ctx_lens = [n + nq for n in torch.randint(2950, 3051, (R,), generator=g).tolist()]
+        nb = [math.ceil(k / bs) for k in ctx_lens]
+        NB = sum(nb) + 1
+        perm = torch.randperm(NB - 1, generator=g).tolist()
+        tables = torch.full((R, max(nb)), NB - 1, dtype=torch.int32)
+        used = 0
+        for r, n in enumerate(nb):
+            tables[r, :n] = torch.tensor(perm[used:used + n])
+            used += n
+        copies = 4
+        caches = [(torch.randn(NB, bs, Hkv, D, device=device).bfloat16(),
+                   torch.randn(NB, bs, Hkv, D, device=device).bfloat16()) for _ in range(copies)]
+        q = torch.randn(R * nq, H, D, device=device).bfloat16()
+        ctx = torch.tensor(ctx_lens, dtype=torch.int32, device=device)
+        tables = tables.to(device)
+        state = {"i": 0}
+
+        def fn():
+            kc, vc = caches[state["i"] % copies]
+            state["i"] += 1
+            attention.paged_attention(q, kc, vc, tables, D ** -0.5, context_lens=ctx, query_len_per_seq=nq,
+                                      causal=False)
+        algorithmic = sum(ctx_lens) * Hkv * D * 2 * 2 + 2 * R * nq * H * D * 2
+    elif args.kernel == "attention":
         from nanovllm_b200 import attention
         R, H, Hkv, D, bs = 32, 32, 8, 128, 256
         k_lens = torch.randint(900, 1101, (R,), generator=g).tolist()
@@ -760,7 +790,7 @@ def run_kernel(args) -> int:
     for _ in range(args.warmup):
         fn()
     timing = "events"
-    if args.kernel in ("attention", "ctx_store", "after_verify", "markov", "markov_fused"):
+    if args.kernel in ("attention", "attention_draft", "ctx_store", "after_verify", "markov", "markov_fused"):
         # K calls captured in one CUDA graph and replayed, so the host's per-call work (tensor map encoding,
         # Python) does not pace the device; the reference captures its Markov rows in a graph the same way
         # (speculative.py:216-231)
@@ -1013,6 +1043,12 @@ def main() -> int:
         return run_attention_tp(args)
     if args.kernel == "overlap":
         return run_overlap(args)
+    if args.kernel == "round_cfg4":
+        import torch
+        pk = peaks()
+        print(json.dumps(dspark_timing(torch, torch.device("cuda", 0), args.steps, args.warmup, pk["hbm_gbs"])),
+              flush=True)
+        return 0
     if args.kernel is not None:
         return run_kernel(args)
     import torch
