@@ -199,8 +199,8 @@ class DFlashDrafter:
     DSpark's Markov rows drawing them left to right (kernel 3).  The block forward replays one graph per padded
     batch size (speculative.py:296-324); the logits and the k rows replay a sampling graph per padded batch size
     and sampling key, captured when the key first appears, for the first MAX_SAMPLING_KEYS keys
-    (speculative.py:211-266); the noise of all k rows is drawn outside the graphs, before row 0, from the round's
-    generator.  q lives in a persistent buffer per key whose previous candidates are cleared by the kernel
+    (speculative.py:211-266); a key past those runs the same body without a graph; the noise of all k rows is
+    drawn outside the graphs, before row 0, from the round's generator.  q lives in a persistent buffer per key whose previous candidates are cleared by the kernel
     (MarkovQBuffer) instead of zero-filling [B, k, V] every round.  after_verify_graph is what a verification
     graph runs after its logits (speculative.py:326-337)."""
 
@@ -288,15 +288,21 @@ class DFlashDrafter:
         markov_rows(logits, prev, sampling, self.noise[key][:b], drafts, self._q_buffer(key, b), candidates,
                     model.markov_head)
 
-    def _capture_sampling_graphs(self, key) -> None:
+    def _key_buffers(self, key) -> None:
+        """A random key's noise [max batch, k, candidates or V] (finite padding rows) and q buffer
+        (speculative.py:268-275)."""
+        if key is None or key in self.noise:
+            return
         bmax, k, vocab = self.batch_sizes[-1], self.num_drafts, self.model.shape.vocab
         device = self.model.device
-        if key is not None:
-            max_top_k, _, all_top_k = key
-            candidates = num_candidates(max_top_k, all_top_k, vocab)
-            self.noise[key] = torch.ones(bmax, k, candidates or vocab, dtype=torch.float32, device=device)
-            self.q[key] = (MarkovQBuffer(bmax, k, vocab, candidates, device) if candidates else
-                           torch.zeros(bmax, k, vocab, dtype=torch.float32, device=device))
+        max_top_k, _, all_top_k = key
+        candidates = num_candidates(max_top_k, all_top_k, vocab)
+        self.noise[key] = torch.ones(bmax, k, candidates or vocab, dtype=torch.float32, device=device)
+        self.q[key] = (MarkovQBuffer(bmax, k, vocab, candidates, device) if candidates else
+                       torch.zeros(bmax, k, vocab, dtype=torch.float32, device=device))
+
+    def _capture_sampling_graphs(self, key) -> None:
+        self._key_buffers(key)
         graphs: dict = {}
         for b in reversed(self.batch_sizes):
             self._capture(graphs, b, lambda b=b: self._sampling_forward(b, key))
@@ -317,16 +323,21 @@ class DFlashDrafter:
             raise NotImplementedError("this drafter samples DSpark's Markov rows; a DFlash draft has no Markov head")
         self.graphs[padded].replay()
         key = sampling_graph_key(sampling)
-        if key not in self.sampling_graphs:
-            if len(self.sampling_graphs) >= MAX_SAMPLING_KEYS:
-                raise NotImplementedError(f"more than {MAX_SAMPLING_KEYS} sampling keys")
+        eager = key not in self.sampling_graphs and len(self.sampling_graphs) >= MAX_SAMPLING_KEYS
+        if eager:
+            self._key_buffers(key)          # a key past the first MAX_SAMPLING_KEYS samples without a graph
+        elif key not in self.sampling_graphs:
             self._capture_sampling_graphs(key)
         if key is not None:                       # speculative.py:225-238; padding rows keep earlier values
             self.temperatures[:batch].copy_(sampling.temperatures)
             self.top_k[:batch].copy_(sampling.top_k)
             self.top_p[:batch].copy_(sampling.top_p)
             spec_sampler.exponential_noise_(self.noise[key][:batch], generator)
-        self.sampling_graphs[key][padded].replay()
+        if eager:
+            self._sampling_forward(padded, key)
+            self.stats["eager_proposals"] += 1
+        else:
+            self.sampling_graphs[key][padded].replay()
         self.stats["proposals"] += 1
         if key is None:
             return self.drafts[:batch], None

@@ -160,3 +160,23 @@ def test_whole_vocabulary_rows_and_rounds_in_a_row(small):
     params = [(1.0, 0, 1.0), (0.9, 30, 1.0), (1.0, 0, 0.8), (1.1, 5, 1.0), (1.0, 0, 1.0)]
     for i, lens in enumerate([[2, 8, 5, 1, 7], [8, 8, 1, 1, 4], [3, 3, 3, 3, 3]]):
         check_round(small, sampling_of(params), lens, seed=100 + i)
+
+
+def test_keys_past_the_graph_limit_sample_eagerly_and_alike(small, monkeypatch):
+    """A drafter that may capture no sampling graph (MAX_SAMPLING_KEYS = 0) runs the graphs' body eagerly
+    (speculative.py:41-43): the same drafts, q and generator offset as the captured graph, bit for bit."""
+    from nanovllm_b200 import speculative
+    from nanovllm_b200.speculative import DFlashDrafter, sampling_graph_key
+    params = [(1.0, 20, 1.0), (0.8, 20, 0.9), (1.2, 20, 1.0), (0.7, 20, 0.95), (1.0, 20, 1.0)]
+    sampling = sampling_of(params)
+    g1 = torch.Generator(device=DEV).manual_seed(55)
+    d1, q1 = small.drafter.propose(small.rows, sampling, g1)
+    d1, q1 = d1.clone(), q1.clone()
+    monkeypatch.setattr(speculative, "MAX_SAMPLING_KEYS", 0)
+    eager = DFlashDrafter(small.model, K, [8], small.drafter.max_num_blocks, small.drafter.pad_block_id)
+    g2 = torch.Generator(device=DEV).manual_seed(55)
+    d2, q2 = eager.propose(small.rows, sampling, g2)
+    assert eager.stats["eager_proposals"] == 1 and not eager.sampling_graphs
+    assert sampling_graph_key(sampling) in eager.noise
+    assert torch.equal(d1, d2) and torch.equal(q1, q2)
+    assert g1.get_offset() == g2.get_offset()
