@@ -150,7 +150,8 @@ def build_workload(torch, device, batch: int, ctx: int, seed: int):
     draft_logits = torch.randn(batch, K_DRAFTS, V, device=device, generator=dgen)
     sampling = S.sampling_tensors([SimpleNamespace(temperature=1.0, top_k=0, top_p=1.0)] * batch, device)
     q = S.probs_from_logits(draft_logits, sampling)                   # temperature-1 random-logit drafter
-    drafts = S.sample(q, dgen)
+    # the drafter's samples, 128 requests (896 race rows) per call: the race takes at most 1024 rows a call
+    drafts = torch.cat([S.sample(q[i:i + 128], dgen) for i in range(0, batch, 128)])
     del draft_logits
     return SimpleNamespace(target=target, round=rnd, rows=rows, q=q, drafts=drafts, sampling=sampling,
                            lengths=lengths, width=width, shape=shape)
@@ -287,6 +288,39 @@ def round_timing(torch, device, ctx: int, steps: int, warmup: int, hbm_peak: flo
     del w, rnd
     torch.cuda.empty_cache()
     return out
+
+
+def strong_scaling_timing(torch, device, world: int, rank: int, total_rows: int, ctx: int, steps: int,
+                          warmup: int) -> dict:
+    """Config 5's batch split: total_rows requests of the config-3 shape divided evenly over the world's GPUs (512 /
+    N rows per GPU, one replica each), device-timed rounds, max time over ranks, tokens summed over ranks: the
+    strong-scaling counterpart of the headline (which keeps 64 rows per GPU)."""
+    from nanovllm_b200.replicas import barrier, reduce_scalar, shard_rows
+    rows = len(shard_rows(total_rows, world, rank))
+    w = build_workload(torch, device, rows, ctx, seed=777 + rank)
+    rnd = w.round
+    gen = torch.Generator(device=device).manual_seed(8 + rank)
+    num_tokens = rnd.load(w.rows)
+    for _ in range(warmup):
+        rnd.verify_and_accept(num_tokens, rows, w.drafts, w.q, w.sampling, gen)
+    accepted = torch.zeros((), dtype=torch.int64, device=device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    start.record()
+    for _ in range(steps):
+        n_accept, _ = rnd.verify_and_accept(num_tokens, rows, w.drafts, w.q, w.sampling, gen)
+        accepted += n_accept.sum() + rows
+    end.record()
+    barrier()
+    ms = reduce_scalar(start.elapsed_time(end) / steps, "max")
+    tokens = reduce_scalar(float(accepted.item()), "sum")
+    w.target.close()
+    del w, rnd
+    torch.cuda.empty_cache()
+    return {"workload": f"config 5: {total_rows} requests of the config-3 shape split over {world} GPU(s) "
+                        f"({total_rows // world} rows each), contexts ~{ctx}",
+            "rows_per_gpu": rows, "ms_per_round": round(ms, 3),
+            "accepted_tok_s": round(tokens / steps / (ms / 1e3), 1), "steps": steps, "scaling": "strong"}
 
 
 def attention_long_timing(torch, device, ctx: int, steps: int, hbm_peak: float) -> dict:
@@ -1142,6 +1176,7 @@ def main() -> int:
     del w, rnd
     torch.cuda.empty_cache()
     if not args.no_extra:
+        extra["cfg5_strong_512"] = strong_scaling_timing(torch, device, world, rank, 512, args.ctx, 5, 3)
         if world == 1:
             # the north-star target (the round at ~4k contexts), config 5's 16k attention and config 4's round
             extra["north_star_round_4k"] = round_timing(torch, device, 4096, 10, 3, pk["hbm_gbs"])
