@@ -222,17 +222,57 @@ def attention_roofline(torch, w, hbm_peak: float) -> dict:
             "launches_per_step": s.layers}
 
 
+def accept_call(torch, logits, q, drafts, sampling, seed: int = 3):
+    """One fused accept (specdec_accept on logits, draws in-kernel at a fixed Philox offset, workspace with room
+    for the noise codes) as a closure over fixed buffers, so that calls can be captured in a CUDA graph: the
+    in-kernel draws make every call the same work whatever the offset."""
+    from nanovllm_b200 import _lib
+    lib = _lib.lib()
+    batch, k = drafts.shape
+    rows, vocab = logits.shape
+    ws = torch.zeros(lib.specdec_accept_workspace_bytes(rows, batch, vocab), dtype=torch.uint8,
+                     device=logits.device)
+    n_accept = torch.empty(batch, dtype=torch.int64, device=logits.device)
+    tail = torch.empty(batch, dtype=torch.int64, device=logits.device)
+    top_k = sampling.top_k.contiguous() if sampling.max_top_k > 0 else None
+    top_p = sampling.top_p.contiguous() if sampling.has_top_p else None
+    temps = sampling.temperatures.contiguous()
+    dtype_code = _lib.DTYPE_CODES[logits.dtype]
+
+    def fn():
+        _lib.check(lib.specdec_accept(logits.data_ptr(), 0, dtype_code, rows, vocab, q.data_ptr(),
+                                      drafts.data_ptr(), batch, k, None, temps.data_ptr(), _lib.ptr(top_k),
+                                      _lib.ptr(top_p), sampling.max_top_k, int(sampling.has_top_p), None, None,
+                                      seed, 0, 4 * ((batch * k + 1023) // 1024 + 1), n_accept.data_ptr(),
+                                      tail.data_ptr(), ws.data_ptr(), ws.numel(),
+                                      torch.cuda.current_stream().cuda_stream))
+    fn.keep = (ws, n_accept, tail, top_k, top_p, temps)
+    return fn
+
+
+def graph_timing(torch, fn, calls: int, replays: int = 3) -> float:
+    """Device time per call of `calls` calls of fn captured in one CUDA graph (median of `replays` replays)."""
+    torch.cuda.synchronize()
+    fn()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(calls):
+            fn()
+    graph.replay()
+    us = statistics.median(time_events(torch, graph.replay, 1) for _ in range(replays)) / calls
+    del graph
+    return us
+
+
 def accept_timing(torch, w) -> dict:
-    from nanovllm_b200 import spec_sampler as S
     num_tokens = w.q.shape[0] * (K_DRAFTS + 1)
     logits = w.target.graphs[num_tokens][1]["logits"]
-    gen = torch.Generator(device=logits.device).manual_seed(3)
-    us = statistics.median(time_events(torch, lambda: S.accept_from_logits(logits, w.q, w.drafts, w.sampling, None,
-                                                                            gen), 20) for _ in range(3))
+    fn = accept_call(torch, logits, w.q, w.drafts, w.sampling)
+    us = graph_timing(torch, fn, 20)
     batch = w.q.shape[0]
     algorithmic = logits.numel() * 2 + batch * V * (4 + 2)    # logits once + q and logits of the tail rows
     return {"us": round(us, 2), "algorithmic_bytes": algorithmic,
-            "GBps": round(algorithmic / (us * 1e-6) / 1e9, 1)}
+            "GBps": round(algorithmic / (us * 1e-6) / 1e9, 1), "timing": "CUDA graph of 20 calls, 3 replays"}
 
 
 # ---------------------------------------------------------------------------------------------- more workloads
@@ -814,17 +854,15 @@ def run_kernel(args) -> int:
         params = (0.7, 20, 0.8) if args.kernel == "accept_topk" else (1.0, 0, 1.0)   # protocol sampling
         samp = S.sampling_tensors([SimpleNamespace(temperature=params[0], top_k=params[1], top_p=params[2])] * B,
                                   device)
-        gen = torch.Generator(device=device).manual_seed(0)
-
-        def fn():
-            S.accept_from_logits(logits, q, drafts, samp, None, gen)
+        fn = accept_call(torch, logits, q, drafts, samp)
         # logits once, plus the tail rows' q and logits for the full-row race (a truncating batch races only its
         # rows' kept tokens: a few KB)
         algorithmic = logits.numel() * 2 + (B * V * (4 + 2) if args.kernel == "accept" else 0)
     for _ in range(args.warmup):
         fn()
     timing = "events"
-    if args.kernel in ("attention", "attention_draft", "ctx_store", "after_verify", "markov", "markov_fused"):
+    if args.kernel in ("attention", "attention_draft", "ctx_store", "after_verify", "markov", "markov_fused",
+                       "accept", "accept_topk"):
         # K calls captured in one CUDA graph and replayed, so the host's per-call work (tensor map encoding,
         # Python) does not pace the device; the reference captures its Markov rows in a graph the same way
         # (speculative.py:216-231)

@@ -35,6 +35,13 @@ int specdec_device_supported(void);
 /* Workspace bytes for the sampler entry points over `rows` rows of logits / probabilities (no counterpart in the
  * reference: torch allocates its temporaries). */
 size_t specdec_sampler_workspace_bytes(long long rows);
+/* Workspace bytes with which specdec_accept over T rows, B requests and vocabulary V races the tail over noise
+ * codes: specdec_sampler_workspace_bytes(T) plus 2 bytes per element of the [B, V] noise.  A call whose E is NULL,
+ * whose offset_E is a multiple of 4 (torch's always are) and whose rows do not truncate (max_top_k = 0) then
+ * draws the noise once into 16-bit codes that bound each E from both sides, streams the tail rows against them
+ * and regenerates exactly only the elements that can still win; the tokens are the ones the smaller workspace
+ * gives.  Returns 0 for non-positive sizes. */
+size_t specdec_accept_workspace_bytes(long long rows, long long B, long long V);
 
 /* Philox offset increment torch's CUDA generator consumes for one torch.rand / exponential_ draw of `numel`
  * floats on the current device (ATen's calc_execution_policy); callers advance their generator by it, so it ends
@@ -75,6 +82,14 @@ int specdec_accept_greedy(const void* logits, int dtype, long long T, long long 
 int specdec_race(const float* weights, long long R, long long V, const float* E, unsigned long long seed,
                  unsigned long long offset_E, long long* out, void* workspace, size_t workspace_bytes,
                  void* stream);
+
+/* Plumbing for tests of the in-kernel draws (no counterpart in the reference): torch's exponential_ draw of numel
+ * floats at (seed, offset), offset a multiple of 4, clamped at 1e-10 as nanovllm/layers/spec_sampler.py:101 does,
+ * written either as the floats themselves (values [numel]) or as the 16-bit codes the accept's tail race reads
+ * (codes [numel]; value i lies in [lo, hi), the floats whose bits are codes[i] << 16 and (codes[i] + 1) << 16).
+ * Exactly one of codes and values is non-null. */
+int specdec_exponential_codes(unsigned long long seed, unsigned long long offset, long long numel,
+                              unsigned short* codes, float* values, void* stream);
 
 /* specdec_accept without a workspace, for callers that cannot allocate device memory: a plugin whose host owns
  * the device memory budget and forbids cudaMalloc from extensions, or a latency-critical caller that may not

@@ -126,6 +126,8 @@ struct Args {
   ReqDesc* desc;
   int* kept_n;              // [T] tokens a truncated row keeps (ids in kept_ids), or -1: not recorded
   int* kept_ids;            // [T][kKeptCap]
+  unsigned short* codes;    // [B, V] 16-bit codes of the tail noise (noise_codes_kernel), or null
+  int codes_vec;            // tail rows, q rows and code rows are 16-byte aligned with V % 8 == 0
 };
 
 // ---------------------------------------------------------------------------------------- small helpers
@@ -137,10 +139,12 @@ __device__ __forceinline__ float scale_logit(float x, float temp) {
 // torch.rand's transform of a curand_uniform4 lane: (0, 1] with 1 mapped to 0.
 __device__ __forceinline__ float torch_uniform(float r) { return r == 1.0f ? 0.0f : r; }
 
-// torch's CUDA exponential_(lambda = 1) transform of a curand_uniform4 lane, then clamp_min(1e-10).
+// torch's CUDA exponential_(lambda = 1) transform of a curand_uniform4 lane, then clamp_min(1e-10).  ATen takes the
+// logarithm with the fast __logf intrinsic on the device (at::log in ATen/NumericUtils.h), so this does too: the
+// accurate logf differs by up to ~5e-8 near r = 1, where the smallest draws (the likeliest race winners) sit.
 __device__ __forceinline__ float torch_exponential_clamped(float r) {
   const float eps_half = 5.9604644775390625e-08f;  // numeric_limits<float>::epsilon() / 2
-  float lg = (r >= 1.0f - eps_half) ? -eps_half : logf(r);
+  float lg = (r >= 1.0f - eps_half) ? -eps_half : __logf(r);
   float e = -1.0f * lg;
   const float floor_v = 1e-10f;
   return e < floor_v ? floor_v : e;
@@ -909,6 +913,20 @@ __device__ __forceinline__ float exp_compensated(float y) {
   return p * fmaf(err, 0.6931471805599453f, 1.0f);
 }
 
+// The race weight of one element of a request's tail row: p (given, or e^(f - m) / s of the scaled logit with
+// truncated entries at 0), minus q where the tail is a residual, floored at 0.  Both tail kernels call this one
+// function so that their weights are the same floats.
+__device__ __forceinline__ float tail_weight(float x, float q, const TailDesc& d, bool probs_mode, bool residual) {
+  float p;
+  if (probs_mode) {
+    p = x;
+  } else {
+    const float f = d.temp == 1.0f ? x : scale_logit(x, d.temp);
+    p = f >= d.thr ? exp_compensated(f - d.m) * d.inv_s : 0.0f;
+  }
+  return residual ? fmaxf(p - q, 0.0f) : p;
+}
+
 // One round's four elements (lane ii = grid-stride step ii of the round): loaded x and q values and where the
 // round starts.  Element indices stay below 2^32 (B * V < 2^31 and S < 2^21), so they are 32-bit.
 struct TailLoads {
@@ -953,9 +971,9 @@ __device__ __forceinline__ float4 philox_uniform4(unsigned long long seed, unsig
 
 // Race-element filter.  After its first round every CTA holds, per request, a lower bound lb of the request's
 // largest ratio (the best exact ratio any CTA had published by then).  An element with w < lb * E cannot win, and
-// E = -ln(u) is bounded below cheaply: -lg2.approx(u) ln 2 is within ~2e-7 absolute of -ln(u), so for u < 0.999
-// (E > 1e-3) the value shrunk by 1e-3 relative stays below the exact E.  Elements near u = 1 (tiny E, large
-// ratios) and requests without a bound yet are never skipped.
+// E = -__logf(u) is bounded below cheaply: -lg2.approx(u) ln 2 and __logf(u) are both within ~4e-7 absolute of
+// ln(u), so for u < 0.999 (E > 1e-3) the value shrunk by 1e-3 relative stays below E.  Elements near u = 1 (tiny
+// E, large ratios) and requests without a bound yet are never skipped.
 __device__ __forceinline__ bool race_candidate(float w, float u, float lb) {
   if (!(lb > 0.0f) || u >= 0.999f) return true;
   float l2;
@@ -1037,11 +1055,8 @@ __global__ void __launch_bounds__(kThreads, 4) tail_accept_kernel(Args a) {
       // full round: every element in range for the whole warp; selects instead of branches
 #pragma unroll
       for (int ii = 0; ii < 4; ++ii) {
-        const float4 d = *reinterpret_cast<const float4*>(&s_td[bb]);   // m, inv_s, thr, temp
-        const float* qrow = s_td[bb].qrow;
-        const float f = d.w == 1.0f ? cur.x[ii] : scale_logit(cur.x[ii], d.w);
-        const float p = f >= d.z ? exp_compensated(f - d.x) * d.y : 0.0f;
-        const float w = qrow ? fmaxf(p - cur.q[ii], 0.0f) : p;
+        const TailDesc& d = s_td[bb];
+        const float w = tail_weight(cur.x[ii], cur.q[ii], d, false, d.qrow != nullptr);
         // the whole warp skips elements that provably cannot win (given draws have no u: never skipped)
         if (!__any_sync(0xffffffffu, !gen || race_candidate(w, uu[ii], s_lb[bb]))) {
           tail_step(a, bb, vv);
@@ -1070,15 +1085,8 @@ __global__ void __launch_bounds__(kThreads, 4) tail_accept_kernel(Args a) {
           const bool act = li < N;
           unsigned bits = 0u;
           if (act) {
-            const float4 d = *reinterpret_cast<const float4*>(&s_td[bb]);   // m, inv_s, thr, temp
-            float p;
-            if (a.probs_mode) {
-              p = cur.x[ii];
-            } else {
-              const float f = d.w == 1.0f ? cur.x[ii] : scale_logit(cur.x[ii], d.w);
-              p = f >= d.z ? exp_compensated(f - d.x) * d.y : 0.0f;
-            }
-            const float w = s_td[bb].qrow ? fmaxf(p - cur.q[ii], 0.0f) : p;
+            const TailDesc& d = s_td[bb];
+            const float w = tail_weight(cur.x[ii], cur.q[ii], d, a.probs_mode, d.qrow != nullptr);
             const float e = gen ? torch_exponential_clamped(uu[ii]) : a.E[li];
             bits = __float_as_uint(__fdividef(w, e)) & 0x7fffffffu;   // w >= 0: clears a -0
           }
@@ -1118,6 +1126,216 @@ __global__ void __launch_bounds__(kThreads, 4) tail_accept_kernel(Args a) {
   __threadfence();
   for (int i = threadIdx.x; i < a.B; i += kThreads) {
     unsigned long long kk = atomicExch(&a.tail_key[i], 0ull);
+    a.tail[i] = (long long)argmax_key_index(kk);
+  }
+  if (threadIdx.x == 0) atomicExch(a.tail_ticket, 0u);
+}
+
+// ---------------------------------------------------------------------------------------- pass 2 over noise codes
+// The accept tail race when the workspace holds 2 bytes per element of the [B, V] noise
+// (specdec_accept_workspace_bytes).  noise_codes_kernel draws the noise on torch's exponential_ grid before
+// pass 1 and keeps of each E only a 16-bit code, the upper half of its float bits, so that E lies in
+// [lo(code), hi(code)) (truncation keeps the order of positive floats).  tail_codes_kernel then streams each
+// request's tail row, its q row and its codes, bounds every element's ratio w / E from both sides, and draws
+// exactly (the Philox block again, torch's transform, the quotient tail_accept_kernel takes) only the elements
+// whose upper bound reaches the best lower bound: every other element provably loses, so the winner is the one
+// tail_accept_kernel finds, bit for bit.
+constexpr int kCodeVec = 8;           // elements per lane and group (16 bytes of codes)
+constexpr int kCodeGroups = 2;        // groups per lane and item
+constexpr int kCodeItem = 32 * kCodeVec * kCodeGroups;   // elements of one warp's item (512)
+constexpr int kCodeCtasPerSm = 3;
+
+// Code of one uniform r in (0, 1] of the exponential draw: E = torch's transform of r lies in [lo, hi), lo = code
+// << 16 and hi = (code + 1) << 16 read as floats.
+__device__ __forceinline__ unsigned short noise_code(float r) {
+  return static_cast<unsigned short>(__float_as_uint(torch_exponential_clamped(r)) >> 16);
+}
+
+// The [B, V] exponential draw at (seed, offset_E), as 16-bit codes (kFloats = false) or as the floats themselves
+// (a test hook): launched with torch's grid (e_grid blocks of 256), each thread one Philox block per grid-stride
+// round, element idx + (4 n + ii) S of round n taking lane ii.
+template <bool kFloats>
+__global__ void __launch_bounds__(kThreads) noise_codes_kernel(Args a, float* floats) {
+  const unsigned S = kRngBlock * gridDim.x;
+  const unsigned idx = blockIdx.x * kRngBlock + threadIdx.x;
+  const unsigned N = (unsigned)a.e_numel;
+  const unsigned long long c0 = a.offset_E >> 2;
+  for (int n = 0; n < a.e_rounds; ++n) {
+    const unsigned li0 = idx + 4u * (unsigned)n * S;
+    if (li0 >= N) break;
+    const float4 r4 = philox_uniform4(a.seed, c0, idx, n);
+    const float r[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+    for (int ii = 0; ii < 4; ++ii) {
+      const unsigned li = li0 + (unsigned)ii * S;
+      if (li < N) {
+        if constexpr (kFloats) {
+          floats[li] = torch_exponential_clamped(r[ii]);
+        } else {
+          a.codes[li] = noise_code(r[ii]);
+        }
+      }
+    }
+  }
+}
+
+// Exact race key of element v of request b's tail row: torch's E regenerated from its Philox block, then the
+// quotient and key exactly as tail_accept_kernel forms them.
+// S = 256 * torch's grid, c0 = offset / 4.
+__device__ __forceinline__ unsigned long long exact_race_key(unsigned long long seed, unsigned long long c0, unsigned S,
+                                                          unsigned V, unsigned b, unsigned v, float w) {
+  const unsigned li = b * V + v;
+  const unsigned m = li / S;
+  const float4 r4 = philox_uniform4(seed, c0, li - m * S, (int)(m >> 2));
+  const unsigned lane = m & 3u;
+  const float r = lane == 0 ? r4.x : lane == 1 ? r4.y : lane == 2 ? r4.z : r4.w;
+  const float e = torch_exponential_clamped(r);
+  const unsigned bits = __float_as_uint(__fdividef(w, e)) & 0x7fffffffu;
+  return (static_cast<unsigned long long>(bits | 0x80000000u) << 32) | (0xffffffffu - v);
+}
+
+template <typename T>
+__device__ __forceinline__ void load_x8(const T* row, unsigned v, float (&f)[8]) {
+  if constexpr (sizeof(T) == 4) {
+    float h[4];
+    unpack16(ldg16(row + v), h);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) f[j] = h[j];
+    unpack16(ldg16(row + v + 4), h);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) f[4 + j] = h[j];
+  } else if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    unpack16_bf16(ldg16(row + v), f);
+  } else {
+    unpack16_f16(ldg16(row + v), f);
+  }
+}
+
+// One warp per item of kCodeItem elements of one request's row, items strided over the grid's warps.  Per lane
+// kCodeGroups groups of 8 consecutive elements: weights and codes held in registers while the warp's lower bound
+// forms (the largest w / hi of its elements, and the best ratio any item of the request has published), then the
+// candidate test w >= LB lo with margins that cover the approximate quotients.  A request whose item has no
+// positive lower bound races its positive weights and its first element exactly (all-zero weights: the first
+// index wins, as in torch).
+template <typename T>
+__global__ void __launch_bounds__(kThreads, kCodeCtasPerSm) tail_codes_kernel(Args a) {
+  __shared__ int s_last;
+  __shared__ float2 s_list[kThreads / 32][kCodeItem];   // per warp: (element, weight) of its item's candidates
+  const volatile int* status = a.status;
+  if (status[0] != 0) return;                   // pass 1 rejected its inputs
+  const int lane = threadIdx.x & 31;
+  float2* my_list = s_list[threadIdx.x >> 5];
+  const unsigned V = (unsigned)a.V;
+  const unsigned per_row = (V + kCodeItem - 1) / kCodeItem;
+  const unsigned items = per_row * (unsigned)a.B;
+  const unsigned nwarps = gridDim.x * (kThreads / 32);
+  for (unsigned item = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); item < items; item += nwarps) {
+    const unsigned b = item / per_row;
+    const unsigned v0 = (item - b * per_row) * kCodeItem;
+    const ReqDesc rd = a.desc[b];
+    const unsigned long long published = __ldcg(&a.tail_key[b]);
+    TailDesc d;
+    d.m = rd.m;
+    d.inv_s = 1.0f / rd.s;
+    d.thr = rd.thr;
+    d.temp = rd.temp;
+    const T* xrow = static_cast<const T*>(a.x) + rd.x_row * (long long)V;
+    const float* qrow = rd.q_row < 0 ? nullptr : a.q + rd.q_row * (long long)V;
+    const unsigned short* crow = a.codes + (size_t)b * V;
+    float w[kCodeGroups][kCodeVec];
+    unsigned cw[kCodeGroups][kCodeVec / 2];     // codes, two per word (element 2j in the low half)
+    float lb = 0.0f;
+#pragma unroll
+    for (int g = 0; g < kCodeGroups; ++g) {
+      const unsigned v = v0 + (unsigned)g * (32 * kCodeVec) + (unsigned)lane * kCodeVec;
+      float x[kCodeVec], q[kCodeVec];
+      if (a.codes_vec && v < V) {                 // V % 8 == 0: the whole group is in range
+        load_x8<T>(xrow, v, x);
+        if (qrow) {
+          float h[4];
+          unpack16(ldg16(qrow + v), h);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) q[j] = h[j];
+          unpack16(ldg16(qrow + v + 4), h);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) q[4 + j] = h[j];
+        }
+        const uint4 c = ldg16(crow + v);
+        cw[g][0] = c.x;
+        cw[g][1] = c.y;
+        cw[g][2] = c.z;
+        cw[g][3] = c.w;
+      } else {
+#pragma unroll
+        for (int j = 0; j < kCodeVec; ++j) {
+          const bool in = v + j < V;
+          x[j] = in ? to_f32(xrow[v + j]) : 0.0f;
+          q[j] = in && qrow ? qrow[v + j] : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < kCodeVec / 2; ++j) {   // 1.0 past the row (w is 0 there)
+          const unsigned c0 = v + 2 * j < V ? crow[v + 2 * j] : 0x3f80u;
+          const unsigned c1 = v + 2 * j + 1 < V ? crow[v + 2 * j + 1] : 0x3f80u;
+          cw[g][j] = c0 | (c1 << 16);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kCodeVec; ++j) {
+        const bool in = v + j < V;
+        const float wj = in ? tail_weight(x[j], q[j], d, a.probs_mode, qrow != nullptr) : 0.0f;
+        w[g][j] = wj;
+        const unsigned code = (j & 1) ? cw[g][j / 2] >> 16 : cw[g][j / 2] & 0xffffu;
+        const float hi = __uint_as_float((code + 1u) << 16);
+        lb = fmaxf(lb, __fdividef(wj, hi));
+      }
+    }
+    // the warp's lower bound of the request's largest ratio: its own elements' w / hi (shrunk past the
+    // quotients' error; subnormal bounds dropped) and the best exact ratio published so far
+    lb = warp_max_f32(lb) * (1.0f - 1e-5f);
+    if (!(lb >= 1.17549435e-38f)) lb = 0.0f;
+    const float pub = published ? __uint_as_float(static_cast<unsigned>(published >> 32) & 0x7fffffffu) : 0.0f;
+    const float LB = fmaxf(lb, pub);
+    // candidates into the warp's list; drawn exactly once the weights' registers are free
+    unsigned n_cand = 0;
+#pragma unroll
+    for (int g = 0; g < kCodeGroups; ++g) {
+#pragma unroll
+      for (int j = 0; j < kCodeVec; ++j) {
+        const unsigned v = v0 + (unsigned)g * (32 * kCodeVec) + (unsigned)lane * kCodeVec + (unsigned)j;
+        const unsigned code = (j & 1) ? cw[g][j / 2] >> 16 : cw[g][j / 2] & 0xffffu;
+        const float lo = __uint_as_float(code << 16);
+        const bool cand = v < V && (LB > 0.0f ? w[g][j] * (1.0f + 2e-5f) >= LB * lo : (w[g][j] > 0.0f || v == v0));
+        const unsigned ballot = __ballot_sync(0xffffffffu, cand);
+        if (cand) {
+          const unsigned at = n_cand + __popc(ballot & ((1u << lane) - 1u));
+          my_list[at] = make_float2(__uint_as_float(v), w[g][j]);
+        }
+        n_cand += __popc(ballot);
+      }
+    }
+    __syncwarp();
+    unsigned long long best = 0ull;
+    for (unsigned i = lane; i < n_cand; i += 32) {
+      const float2 c = my_list[i];
+      const unsigned long long key = exact_race_key(a.seed, a.offset_E >> 2, kRngBlock * (unsigned)a.e_grid, V, b,
+                                                    __float_as_uint(c.x), c.y);
+      best = key > best ? key : best;
+    }
+    __syncwarp();
+    best = warp_max_u64_redux(best);
+    if (lane == 0 && best > published) atomicMax(&a.tail_key[b], best);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned ticket = atomicAdd(a.tail_ticket, 1u);
+    s_last = ticket == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int i = threadIdx.x; i < a.B; i += kThreads) {
+    const unsigned long long kk = atomicExch(&a.tail_key[i], 0ull);
     a.tail[i] = (long long)argmax_key_index(kk);
   }
   if (threadIdx.x == 0) atomicExch(a.tail_ticket, 0u);
@@ -1410,22 +1628,38 @@ static void bind_workspace(Args& a, void* ws) {
   a.kept_ids = reinterpret_cast<int*>(base + L.kept_ids);
 }
 
-template <typename T>
-static int launch_tail(Args& a, const DeviceInfo& info, bool race, cudaStream_t stream) {
+// torch's grid and grid-stride rounds of the [B, V] exponential draw.
+static void exponential_grid(Args& a, const DeviceInfo& info) {
   a.e_numel = (long long)a.B * a.V;
   a.e_grid = torch_rng_grid(a.e_numel, info);
   const long long S = (long long)kRngBlock * a.e_grid;
   a.e_rounds = (int)((a.e_numel - 1) / (S * 4) + 1);
   a.e_sq = (unsigned)(S / a.V);
   a.e_sr = (unsigned)(S % a.V);
+}
+
+template <typename T>
+static int launch_tail(Args& a, const DeviceInfo& info, bool race, cudaStream_t stream) {
+  exponential_grid(a, info);
   if (race) {
     race_kernel<<<a.e_grid, kThreads, 0, stream>>>(a);
+  } else if (a.codes) {
+    const long long warps = (long long)a.B * ((a.V + kCodeItem - 1) / kCodeItem);
+    long long grid = (warps + kThreads / 32 - 1) / (kThreads / 32);
+    const long long cap = (long long)info.sm_count * kCodeCtasPerSm;
+    if (grid > cap) grid = cap;
+    tail_codes_kernel<T><<<(unsigned)grid, kThreads, 0, stream>>>(a);
   } else {
     const size_t smem = (sizeof(TailDesc) + sizeof(unsigned long long) + sizeof(float)) * a.B;
     tail_accept_kernel<T><<<a.e_grid, kThreads, smem, stream>>>(a);
   }
   SPECDEC_LAUNCH_CHECK();
   return kOk;
+}
+
+// Bytes of the noise codes tail_codes_kernel races over, placed after the fixed layout.
+static size_t noise_code_bytes(long long B, long long V) {
+  return (((size_t)B * (size_t)V * sizeof(unsigned short)) + 255) & ~size_t(255);
 }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -1449,6 +1683,11 @@ using namespace specdec::sampler;
 extern "C" {
 
 size_t specdec_sampler_workspace_bytes(long long T) { return layout(T).total; }
+
+size_t specdec_accept_workspace_bytes(long long T, long long B, long long V) {
+  if (T < 1 || B < 1 || V < 1) return 0;
+  return layout(T).total + noise_code_bytes(B, V);
+}
 
 unsigned long long specdec_philox_increment(long long numel) {
   DeviceInfo info;
@@ -1558,8 +1797,20 @@ int specdec_accept(const void* x, int x_is_probs, int dtype, long long T, long l
   choose_chunks(a, info);
   a.vec_ok = aligned16(x) && ((V * (long long)dtype_bytes(dtype)) % 16 == 0);
   bind_workspace(a, workspace);
+  // noise codes when the workspace holds them, the noise is drawn in-kernel at a block boundary (torch's offsets
+  // are multiples of 4) and no row truncates (truncating calls race their kept sets, the whole row only rarely)
+  const size_t codes_at = layout(T).total;
+  if (E == nullptr && (offset_E & 3ull) == 0 && !a.truncate && workspace_bytes >= codes_at + noise_code_bytes(B, V)) {
+    a.codes = reinterpret_cast<unsigned short*>(static_cast<char*>(workspace) + codes_at);
+    a.codes_vec = a.vec_ok && V % 8 == 0 && aligned16(q) && aligned16(a.codes);
+  }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   SPECDEC_CUDA_TRY(cudaMemsetAsync(a.status, 0, 2 * sizeof(int), s));
+  if (a.codes) {
+    exponential_grid(a, info);
+    noise_codes_kernel<false><<<a.e_grid, kThreads, 0, s>>>(a, nullptr);
+    SPECDEC_LAUNCH_CHECK();
+  }
   return SPECDEC_DISPATCH_DTYPE(dtype, [&] {
     if (a.probs_mode) {
       decide_probs_kernel<Tx><<<(unsigned)B, 64, 0, s>>>(a);
@@ -1625,6 +1876,26 @@ int specdec_race(const float* weights, long long R, long long V, const float* E,
   a.E = E; a.seed = seed; a.offset_E = offset_E; a.tail = out;
   bind_workspace(a, workspace);
   return launch_tail<float>(a, info, true, static_cast<cudaStream_t>(stream));
+}
+
+int specdec_exponential_codes(unsigned long long seed, unsigned long long offset, long long numel,
+                              unsigned short* codes, float* values, void* stream) {
+  SPECDEC_CHECK_ARG((codes != nullptr) != (values != nullptr), "exactly one of codes and values must be non-null");
+  SPECDEC_CHECK_ARG(numel >= 1 && numel < (1ll << 31), "numel %lld out of range", numel);
+  SPECDEC_CHECK_ARG((offset & 3ull) == 0, "offset %llu is not a multiple of 4", offset);
+  DeviceInfo info;
+  if (int st = device_info(&info)) return st;
+  Args a{};
+  a.B = 1; a.V = numel; a.seed = seed; a.offset_E = offset; a.codes = codes;
+  exponential_grid(a, info);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (codes) {
+    noise_codes_kernel<false><<<a.e_grid, kThreads, 0, s>>>(a, nullptr);
+  } else {
+    noise_codes_kernel<true><<<a.e_grid, kThreads, 0, s>>>(a, values);
+  }
+  SPECDEC_LAUNCH_CHECK();
+  return kOk;
 }
 
 }  // extern "C"

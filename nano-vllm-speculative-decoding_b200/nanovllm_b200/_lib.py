@@ -30,6 +30,8 @@ SIGNATURES = {
     "specdec_last_error": (ctypes.c_char_p, []),
     "specdec_device_supported": (_c_int, []),
     "specdec_sampler_workspace_bytes": (_c_size, [_c_ll]),
+    "specdec_accept_workspace_bytes": (_c_size, [_c_ll, _c_ll, _c_ll]),
+    "specdec_exponential_codes": (_c_int, [_c_ull, _c_ull, _c_ll, _c_void_p, _c_void_p, _c_void_p]),
     "specdec_philox_increment": (_c_ull, [_c_ll]),
     "specdec_probs": (_c_int, [_c_void_p, _c_int, _c_ll, _c_ll, _c_ll, _c_void_p, _c_void_p, _c_void_p, _c_int,
                                _c_int, _c_void_p, _c_void_p, _c_size, _c_void_p]),

@@ -201,7 +201,10 @@ def _accept(x: torch.Tensor, x_is_probs: bool, q: torch.Tensor, drafts: torch.Te
         temps = sampling.temperatures.contiguous()
         top_k, top_p = _params_per_row(sampling)
         max_top_k, has_top_p = sampling.max_top_k, sampling.has_top_p
-    ws = _workspace(device, rows)
+    if noise is None:   # in-kernel draws: room for the noise codes the tail race streams
+        ws = Workspace.get(device, _lib.lib().specdec_accept_workspace_bytes(rows, batch, vocab))
+    else:
+        ws = _workspace(device, rows)
     check(_lib.lib().specdec_accept(ptr(x), int(x_is_probs), DTYPE_CODES[x.dtype], rows, vocab, ptr(q), ptr(drafts),
                                     batch, k, ptr(lens), ptr(temps), ptr(top_k), ptr(top_p), max_top_k,
                                     int(has_top_p), ptr(u), ptr(noise), seed, offsets[0], offsets[1],
