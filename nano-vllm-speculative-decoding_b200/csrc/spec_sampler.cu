@@ -150,6 +150,23 @@ __device__ __forceinline__ float torch_exponential_clamped(float r) {
   return e < floor_v ? floor_v : e;
 }
 
+// The four uniforms of call n of curand's Philox4x32-10 stream (seed, subsequence idx, offset 4 c0): the Philox
+// block (Salmon et al., SC 2011) at counter (c0 + n, idx) under key seed, computed by curand's own block function
+// and uniform transform, without the state bookkeeping of curand_uniform4.
+__device__ __forceinline__ float4 philox_uniform4(unsigned long long seed, unsigned long long c0, unsigned idx,
+                                                  int n) {
+  const unsigned long long c = c0 + (unsigned long long)n;
+  const uint4 ctr = make_uint4((unsigned)c, (unsigned)(c >> 32), idx, 0u);
+  const uint2 key = make_uint2((unsigned)seed, (unsigned)(seed >> 32));
+  return _curand_uniform4(curand_Philox4x32_10(ctr, key));
+}
+
+// Code of one uniform r in (0, 1] of the exponential draw: E = torch's transform of r lies in [lo, hi), lo = code
+// << 16 and hi = (code + 1) << 16 read as floats.
+__device__ __forceinline__ unsigned short noise_code(float r) {
+  return static_cast<unsigned short>(__float_as_uint(torch_exponential_clamped(r)) >> 16);
+}
+
 // Uniform number li of a torch.rand draw of `numel` floats whose grid has `grid` blocks of 256 threads.
 __device__ float torch_rand_at(unsigned long long seed, unsigned long long offset, long long li, int grid) {
   const long long S = (long long)kRngBlock * grid;
@@ -958,16 +975,6 @@ __device__ __forceinline__ void tail_issue_loads(const Args& a, const TailDesc* 
   }
 }
 
-// The four uniforms of call n of curand's Philox4x32-10 stream (seed, subsequence idx, offset 4 c0): the Philox
-// block (Salmon et al., SC 2011) at counter (c0 + n, idx) under key seed, computed by curand's own block function
-// and uniform transform, without the state bookkeeping of curand_uniform4.
-__device__ __forceinline__ float4 philox_uniform4(unsigned long long seed, unsigned long long c0, unsigned idx,
-                                                  int n) {
-  const unsigned long long c = c0 + (unsigned long long)n;
-  const uint4 ctr = make_uint4((unsigned)c, (unsigned)(c >> 32), idx, 0u);
-  const uint2 key = make_uint2((unsigned)seed, (unsigned)(seed >> 32));
-  return _curand_uniform4(curand_Philox4x32_10(ctr, key));
-}
 
 // Race-element filter.  After its first round every CTA holds, per request, a lower bound lb of the request's
 // largest ratio (the best exact ratio any CTA had published by then).  An element with w < lb * E cannot win, and
@@ -1143,13 +1150,8 @@ __global__ void __launch_bounds__(kThreads, 4) tail_accept_kernel(Args a) {
 constexpr int kCodeVec = 8;           // elements per lane and group (16 bytes of codes)
 constexpr int kCodeGroups = 2;        // groups per lane and item
 constexpr int kCodeItem = 32 * kCodeVec * kCodeGroups;   // elements of one warp's item (512)
-constexpr int kCodeCtasPerSm = 3;
+constexpr int kCodeCtasPerSm = 2;
 
-// Code of one uniform r in (0, 1] of the exponential draw: E = torch's transform of r lies in [lo, hi), lo = code
-// << 16 and hi = (code + 1) << 16 read as floats.
-__device__ __forceinline__ unsigned short noise_code(float r) {
-  return static_cast<unsigned short>(__float_as_uint(torch_exponential_clamped(r)) >> 16);
-}
 
 // The [B, V] exponential draw at (seed, offset_E), as 16-bit codes (kFloats = false) or as the floats themselves
 // (a test hook): launched with torch's grid (e_grid blocks of 256), each thread one Philox block per grid-stride
@@ -1211,120 +1213,283 @@ __device__ __forceinline__ void load_x8(const T* row, unsigned v, float (&f)[8])
   }
 }
 
-// One warp per item of kCodeItem elements of one request's row, items strided over the grid's warps.  Per lane
-// kCodeGroups groups of 8 consecutive elements: weights and codes held in registers while the warp's lower bound
-// forms (the largest w / hi of its elements, and the best ratio any item of the request has published), then the
-// candidate test w >= LB lo with margins that cover the approximate quotients.  A request whose item has no
-// positive lower bound races its positive weights and its first element exactly (all-zero weights: the first
-// index wins, as in torch).
+// Weights of 8 consecutive elements under one item's descriptor, with tail_weight's flags fixed per item (the same
+// operations on the same inputs, so the same floats as tail_weight).
+template <bool kProbs, bool kUnit, bool kResidual>
+__device__ __forceinline__ void weights8(const float (&x)[8], const float (&q)[8], const TailDesc& d, float (&w)[8]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    float p;
+    if constexpr (kProbs) {
+      p = x[j];
+    } else {
+      const float f = kUnit ? x[j] : scale_logit(x[j], d.temp);
+      p = f >= d.thr ? exp_compensated(f - d.m) * d.inv_s : 0.0f;
+    }
+    w[j] = kResidual ? fmaxf(p - q[j], 0.0f) : p;
+  }
+}
+
+template <bool kResidual>
+__device__ __forceinline__ void weights8_any(int mode, const float (&x)[8], const float (&q)[8], const TailDesc& d,
+                                             float (&w)[8]) {
+  if (mode == 0) {
+    weights8<true, true, kResidual>(x, q, d, w);
+  } else if (mode == 1) {
+    weights8<false, true, kResidual>(x, q, d, w);
+  } else {
+    weights8<false, false, kResidual>(x, q, d, w);
+  }
+}
+
+// Float bits of the lower end of the code range of element j of a packed pair word (element 2i in the low half).
+__device__ __forceinline__ unsigned code_lo_bits(unsigned word, int j) {
+  return (j & 1) ? (word & 0xffff0000u) : (word << 16);
+}
+
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+// The race of one warp's item once its values are in registers: x, q (0 where there is no residual) and the
+// codes of the lane's kCodeGroups groups of 8 consecutive elements starting at `base` (+ 256 per group).  Per
+// element only an upper bound of the ratio, ub = w / lo (a reciprocal), and per lane its maximum.  Since a code's
+// range has hi / lo <= 129 / 128 (7 mantissa bits), ub * 128 / 129 bounds the same ratio from below, so the warp's
+// largest ub, scaled so, or the best exact ratio any item of the request has published is a lower bound LB of
+// the request's largest ratio, and so is `known`, the best key the warp knows for the request (published by other
+// warps when its run of the row began, or found by itself since).  Only a lane whose largest ub reaches LB (past
+// the quotients' error) can hold the winner: such lanes (one or two per item, none once `known` dominates) hand
+// all their elements to the warp's candidate list, which is drawn exactly into `known`.  An item with no positive bound races its
+// positive weights and its first element exactly (all-zero weights: the first index wins, as in torch).
+__device__ __forceinline__ void race_item(const Args& a, float2* my_list, int lane, unsigned b, unsigned v0,
+                                          unsigned base, unsigned V, const TailDesc& d, bool residual,
+                                          unsigned long long& known, float (&x)[kCodeGroups][kCodeVec],
+                                          float (&q)[kCodeGroups][kCodeVec],
+                                          const unsigned (&cw)[kCodeGroups][kCodeVec / 2]) {
+  const int mode = a.probs_mode ? 0 : (d.temp == 1.0f ? 1 : 2);
+  float w[kCodeGroups][kCodeVec];
+  float ub = 0.0f;
+#pragma unroll
+  for (int g = 0; g < kCodeGroups; ++g) {
+    if (residual) {
+      weights8_any<true>(mode, x[g], q[g], d, w[g]);
+    } else {
+      weights8_any<false>(mode, x[g], q[g], d, w[g]);
+    }
+    const bool in = base + (unsigned)g * (32 * kCodeVec) < V;
+#pragma unroll
+    for (int j = 0; j < kCodeVec; ++j) {
+      if (!in || base + (unsigned)g * (32 * kCodeVec) + j >= V) w[g][j] = 0.0f;   // past the row
+      ub = fmaxf(ub, w[g][j] * rcp_approx(__uint_as_float(code_lo_bits(cw[g][j / 2], j))));
+    }
+  }
+  // ub_max * 128/129 bounds the best w / hi from below; shrunk past the reciprocal's and the exact quotients'
+  // error, subnormal bounds dropped
+  float lb = warp_max_f32(ub) * (128.0f / 129.0f) * (1.0f - 1e-5f);
+  if (!(lb >= 1.17549435e-38f)) lb = 0.0f;
+  const float pub = known ? __uint_as_float(static_cast<unsigned>(known >> 32) & 0x7fffffffu) : 0.0f;
+  const float LB = fmaxf(lb, pub);
+  unsigned n_cand = 0;
+  if (LB > 0.0f) {
+    const bool mine = ub * (1.0f + 1e-5f) >= LB;
+    const unsigned ballot = __ballot_sync(0xffffffffu, mine);
+    if (mine) {   // all the lane's elements, at its rank's slots (past the row: an empty weight at V)
+      float2* slot = my_list + kCodeGroups * kCodeVec * __popc(ballot & ((1u << lane) - 1u));
+#pragma unroll
+      for (int g = 0; g < kCodeGroups; ++g) {
+#pragma unroll
+        for (int j = 0; j < kCodeVec; ++j) {
+          const unsigned v = base + (unsigned)g * (32 * kCodeVec) + (unsigned)j;
+          slot[g * kCodeVec + j] = make_float2(__uint_as_float(v < V ? v : V), w[g][j]);
+        }
+      }
+    }
+    n_cand = kCodeGroups * kCodeVec * __popc(ballot);
+  } else {
+#pragma unroll
+    for (int g = 0; g < kCodeGroups; ++g) {
+#pragma unroll
+      for (int j = 0; j < kCodeVec; ++j) {
+        const unsigned v = base + (unsigned)g * (32 * kCodeVec) + (unsigned)j;
+        const bool cand = v < V && (w[g][j] > 0.0f || v == v0);
+        const unsigned ballot = __ballot_sync(0xffffffffu, cand);
+        if (cand) my_list[n_cand + __popc(ballot & ((1u << lane) - 1u))] = make_float2(__uint_as_float(v), w[g][j]);
+        n_cand += __popc(ballot);
+      }
+    }
+  }
+  __syncwarp();
+  unsigned long long best = 0ull;
+  for (unsigned i = lane; i < n_cand; i += 32) {
+    const float2 c = my_list[i];
+    const unsigned v = __float_as_uint(c.x);
+    if (v < V) {
+      const unsigned long long key =
+          exact_race_key(a.seed, a.offset_E >> 2, kRngBlock * (unsigned)a.e_grid, V, b, v, c.y);
+      best = key > best ? key : best;
+    }
+  }
+  __syncwarp();
+  best = warp_max_u64_redux(best);
+  known = best > known ? best : known;
+}
+
+// One item's 16-byte vectors for one lane (the fast path: V % 8 == 0 and 16-byte aligned rows, so a group of 8 is
+// wholly in or out of the row).
 template <typename T>
+struct CodeLoads {
+  uint4 x[kCodeGroups][sizeof(T) == 4 ? 2 : 1];
+  uint4 q[kCodeGroups][2];
+  uint4 c[kCodeGroups];
+};
+
+template <typename T>
+__device__ __forceinline__ void issue_item(const Args& a, const TailDesc* s_td, unsigned item, unsigned per_row,
+                                           unsigned V, int lane, CodeLoads<T>& L) {
+  const unsigned b = item / per_row;
+  const unsigned base = (item - b * per_row) * kCodeItem + (unsigned)lane * kCodeVec;
+  const T* xrow = static_cast<const T*>(s_td[b].xrow);
+  const float* qrow = s_td[b].qrow;
+  const unsigned short* crow = a.codes + (size_t)b * V;
+  const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+  for (int g = 0; g < kCodeGroups; ++g) {
+    const unsigned v = base + (unsigned)g * (32 * kCodeVec);
+    const bool in = v < V;
+#pragma unroll
+    for (int h = 0; h < (sizeof(T) == 4 ? 2 : 1); ++h) L.x[g][h] = in ? ldg16(xrow + v + 4 * h) : zero;
+    L.q[g][0] = in && qrow ? ldg16(qrow + v) : zero;
+    L.q[g][1] = in && qrow ? ldg16(qrow + v + 4) : zero;
+    L.c[g] = in ? ldg16(crow + v) : make_uint4(0x3f803f80u, 0x3f803f80u, 0x3f803f80u, 0x3f803f80u);   // 1.0
+  }
+}
+
+// Items of kCodeItem elements of the requests' rows, a contiguous run of them per warp.  The requests'
+// descriptors sit in shared memory; on the fast path (kVec) the next item's loads are issued before the current
+// item is raced, so every warp keeps an item's bytes in flight while it computes.
+template <typename T, bool kVec>
 __global__ void __launch_bounds__(kThreads, kCodeCtasPerSm) tail_codes_kernel(Args a) {
+  extern __shared__ __align__(16) unsigned char codes_smem[];
+  TailDesc* s_td = reinterpret_cast<TailDesc*>(codes_smem);
   __shared__ int s_last;
   __shared__ float2 s_list[kThreads / 32][kCodeItem];   // per warp: (element, weight) of its item's candidates
   const volatile int* status = a.status;
   if (status[0] != 0) return;                   // pass 1 rejected its inputs
+  const unsigned V = (unsigned)a.V;
+  for (int i = threadIdx.x; i < a.B; i += kThreads) {
+    const ReqDesc rd = a.desc[i];
+    TailDesc t;
+    t.m = rd.m;
+    t.inv_s = 1.0f / rd.s;
+    t.thr = rd.thr;
+    t.temp = rd.temp;
+    t.xrow = static_cast<const T*>(a.x) + rd.x_row * (long long)V;
+    t.qrow = rd.q_row < 0 ? nullptr : a.q + rd.q_row * (long long)V;
+    s_td[i] = t;
+  }
+  __syncthreads();
   const int lane = threadIdx.x & 31;
   float2* my_list = s_list[threadIdx.x >> 5];
-  const unsigned V = (unsigned)a.V;
   const unsigned per_row = (V + kCodeItem - 1) / kCodeItem;
   const unsigned items = per_row * (unsigned)a.B;
-  const unsigned nwarps = gridDim.x * (kThreads / 32);
-  for (unsigned item = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); item < items; item += nwarps) {
-    const unsigned b = item / per_row;
-    const unsigned v0 = (item - b * per_row) * kCodeItem;
-    const ReqDesc rd = a.desc[b];
-    const unsigned long long published = __ldcg(&a.tail_key[b]);
-    TailDesc d;
-    d.m = rd.m;
-    d.inv_s = 1.0f / rd.s;
-    d.thr = rd.thr;
-    d.temp = rd.temp;
-    const T* xrow = static_cast<const T*>(a.x) + rd.x_row * (long long)V;
-    const float* qrow = rd.q_row < 0 ? nullptr : a.q + rd.q_row * (long long)V;
-    const unsigned short* crow = a.codes + (size_t)b * V;
-    float w[kCodeGroups][kCodeVec];
-    unsigned cw[kCodeGroups][kCodeVec / 2];     // codes, two per word (element 2j in the low half)
-    float lb = 0.0f;
+  // each warp races a contiguous run of items (mostly of one request's row), keeping the best key it knows for
+  // the request in registers and publishing it once per run of the row
+  const unsigned long long nw = (unsigned long long)gridDim.x * (kThreads / 32);
+  const unsigned long long wg = (unsigned long long)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
+  unsigned item = (unsigned)(items * wg / nw);
+  const unsigned item_end = (unsigned)(items * (wg + 1) / nw);
+  unsigned row = 0xffffffffu;
+  unsigned long long known = 0ull, published = 0ull;
+  auto enter_row = [&](unsigned b) {
+    if (b == row) return;
+    if (row != 0xffffffffu && lane == 0 && known > published) atomicMax(&a.tail_key[row], known);
+    row = b;
+    published = __ldcg(&a.tail_key[b]);
+    known = published;
+  };
+  if constexpr (kVec) {
+    // two load sets, alternated (no register copies): an item's loads are issued one item ahead of its race
+    auto race_loaded = [&](unsigned it, const CodeLoads<T>& L) {
+      const unsigned b = it / per_row;
+      const unsigned v0 = (it - b * per_row) * kCodeItem;
+      enter_row(b);
+      float x[kCodeGroups][kCodeVec], q[kCodeGroups][kCodeVec];
+      unsigned cw[kCodeGroups][kCodeVec / 2];
 #pragma unroll
-    for (int g = 0; g < kCodeGroups; ++g) {
-      const unsigned v = v0 + (unsigned)g * (32 * kCodeVec) + (unsigned)lane * kCodeVec;
-      float x[kCodeVec], q[kCodeVec];
-      if (a.codes_vec && v < V) {                 // V % 8 == 0: the whole group is in range
-        load_x8<T>(xrow, v, x);
-        if (qrow) {
+      for (int g = 0; g < kCodeGroups; ++g) {
+        if constexpr (sizeof(T) == 4) {
           float h[4];
-          unpack16(ldg16(qrow + v), h);
+          unpack16(L.x[g][0], h);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) q[j] = h[j];
-          unpack16(ldg16(qrow + v + 4), h);
+          for (int j = 0; j < 4; ++j) x[g][j] = h[j];
+          unpack16(L.x[g][1], h);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) q[4 + j] = h[j];
+          for (int j = 0; j < 4; ++j) x[g][4 + j] = h[j];
+        } else if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+          unpack16_bf16(L.x[g][0], x[g]);
+        } else {
+          unpack16_f16(L.x[g][0], x[g]);
         }
-        const uint4 c = ldg16(crow + v);
-        cw[g][0] = c.x;
-        cw[g][1] = c.y;
-        cw[g][2] = c.z;
-        cw[g][3] = c.w;
-      } else {
+        float h[4];
+        unpack16(L.q[g][0], h);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) q[g][j] = h[j];
+        unpack16(L.q[g][1], h);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) q[g][4 + j] = h[j];
+        cw[g][0] = L.c[g].x;
+        cw[g][1] = L.c[g].y;
+        cw[g][2] = L.c[g].z;
+        cw[g][3] = L.c[g].w;
+      }
+      const TailDesc& d = s_td[b];
+      race_item(a, my_list, lane, b, v0, v0 + (unsigned)lane * kCodeVec, V, d, d.qrow != nullptr, known, x, q, cw);
+    };
+    CodeLoads<T> la, lb;
+    if (item < item_end) issue_item<T>(a, s_td, item, per_row, V, lane, la);
+    while (item < item_end) {
+      if (item + 1 < item_end) issue_item<T>(a, s_td, item + 1, per_row, V, lane, lb);
+      race_loaded(item, la);
+      if (++item >= item_end) break;
+      if (item + 1 < item_end) issue_item<T>(a, s_td, item + 1, per_row, V, lane, la);
+      race_loaded(item, lb);
+      ++item;
+    }
+  } else {
+    for (; item < item_end; ++item) {
+      const unsigned b = item / per_row;
+      const unsigned v0 = (item - b * per_row) * kCodeItem;
+      enter_row(b);
+      const TailDesc& d = s_td[b];
+      const T* xrow = static_cast<const T*>(d.xrow);
+      const float* qrow = d.qrow;
+      const unsigned short* crow = a.codes + (size_t)b * V;
+      const unsigned base = v0 + (unsigned)lane * kCodeVec;
+      float x[kCodeGroups][kCodeVec], q[kCodeGroups][kCodeVec];
+      unsigned cw[kCodeGroups][kCodeVec / 2];
+#pragma unroll
+      for (int g = 0; g < kCodeGroups; ++g) {
+        const unsigned v = base + (unsigned)g * (32 * kCodeVec);
 #pragma unroll
         for (int j = 0; j < kCodeVec; ++j) {
           const bool in = v + j < V;
-          x[j] = in ? to_f32(xrow[v + j]) : 0.0f;
-          q[j] = in && qrow ? qrow[v + j] : 0.0f;
+          x[g][j] = in ? to_f32(xrow[v + j]) : 0.0f;
+          q[g][j] = in && qrow ? qrow[v + j] : 0.0f;
         }
 #pragma unroll
-        for (int j = 0; j < kCodeVec / 2; ++j) {   // 1.0 past the row (w is 0 there)
+        for (int j = 0; j < kCodeVec / 2; ++j) {   // 1.0 past the row
           const unsigned c0 = v + 2 * j < V ? crow[v + 2 * j] : 0x3f80u;
           const unsigned c1 = v + 2 * j + 1 < V ? crow[v + 2 * j + 1] : 0x3f80u;
           cw[g][j] = c0 | (c1 << 16);
         }
       }
-#pragma unroll
-      for (int j = 0; j < kCodeVec; ++j) {
-        const bool in = v + j < V;
-        const float wj = in ? tail_weight(x[j], q[j], d, a.probs_mode, qrow != nullptr) : 0.0f;
-        w[g][j] = wj;
-        const unsigned code = (j & 1) ? cw[g][j / 2] >> 16 : cw[g][j / 2] & 0xffffu;
-        const float hi = __uint_as_float((code + 1u) << 16);
-        lb = fmaxf(lb, __fdividef(wj, hi));
-      }
+      race_item(a, my_list, lane, b, v0, base, V, d, qrow != nullptr, known, x, q, cw);
     }
-    // the warp's lower bound of the request's largest ratio: its own elements' w / hi (shrunk past the
-    // quotients' error; subnormal bounds dropped) and the best exact ratio published so far
-    lb = warp_max_f32(lb) * (1.0f - 1e-5f);
-    if (!(lb >= 1.17549435e-38f)) lb = 0.0f;
-    const float pub = published ? __uint_as_float(static_cast<unsigned>(published >> 32) & 0x7fffffffu) : 0.0f;
-    const float LB = fmaxf(lb, pub);
-    // candidates into the warp's list; drawn exactly once the weights' registers are free
-    unsigned n_cand = 0;
-#pragma unroll
-    for (int g = 0; g < kCodeGroups; ++g) {
-#pragma unroll
-      for (int j = 0; j < kCodeVec; ++j) {
-        const unsigned v = v0 + (unsigned)g * (32 * kCodeVec) + (unsigned)lane * kCodeVec + (unsigned)j;
-        const unsigned code = (j & 1) ? cw[g][j / 2] >> 16 : cw[g][j / 2] & 0xffffu;
-        const float lo = __uint_as_float(code << 16);
-        const bool cand = v < V && (LB > 0.0f ? w[g][j] * (1.0f + 2e-5f) >= LB * lo : (w[g][j] > 0.0f || v == v0));
-        const unsigned ballot = __ballot_sync(0xffffffffu, cand);
-        if (cand) {
-          const unsigned at = n_cand + __popc(ballot & ((1u << lane) - 1u));
-          my_list[at] = make_float2(__uint_as_float(v), w[g][j]);
-        }
-        n_cand += __popc(ballot);
-      }
-    }
-    __syncwarp();
-    unsigned long long best = 0ull;
-    for (unsigned i = lane; i < n_cand; i += 32) {
-      const float2 c = my_list[i];
-      const unsigned long long key = exact_race_key(a.seed, a.offset_E >> 2, kRngBlock * (unsigned)a.e_grid, V, b,
-                                                    __float_as_uint(c.x), c.y);
-      best = key > best ? key : best;
-    }
-    __syncwarp();
-    best = warp_max_u64_redux(best);
-    if (lane == 0 && best > published) atomicMax(&a.tail_key[b], best);
   }
+  if (row != 0xffffffffu && lane == 0 && known > published) atomicMax(&a.tail_key[row], known);
+  __threadfence();   // this warp's published keys before the CTA's ticket
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
@@ -1648,7 +1813,16 @@ static int launch_tail(Args& a, const DeviceInfo& info, bool race, cudaStream_t 
     long long grid = (warps + kThreads / 32 - 1) / (kThreads / 32);
     const long long cap = (long long)info.sm_count * kCodeCtasPerSm;
     if (grid > cap) grid = cap;
-    tail_codes_kernel<T><<<(unsigned)grid, kThreads, 0, stream>>>(a);
+    // the descriptors (up to 32 KB) beside the static candidate lists (32 KB) pass the 48 KB default
+    const size_t smem = sizeof(TailDesc) * a.B;
+    const int smem_max = (int)(sizeof(TailDesc) * kMaxRequests);
+    if (a.codes_vec) {
+      if (int st = ensure_dynamic_smem<tail_codes_kernel<T, true>>(smem_max)) return st;
+      tail_codes_kernel<T, true><<<(unsigned)grid, kThreads, smem, stream>>>(a);
+    } else {
+      if (int st = ensure_dynamic_smem<tail_codes_kernel<T, false>>(smem_max)) return st;
+      tail_codes_kernel<T, false><<<(unsigned)grid, kThreads, smem, stream>>>(a);
+    }
   } else {
     const size_t smem = (sizeof(TailDesc) + sizeof(unsigned long long) + sizeof(float)) * a.B;
     tail_accept_kernel<T><<<a.e_grid, kThreads, smem, stream>>>(a);

@@ -122,6 +122,12 @@ def test_code_race_matches_on_small_and_ragged_vocabularies(V):
         both(x, False, q, d, lens, temps, 77 + seed)
 
 
+def test_code_race_matches_at_the_request_limit():
+    """1024 requests: the descriptors fill the race's 32 KB of shared memory."""
+    x, q, d, lens, temps = make(11, 1024, 2, 1000, torch.bfloat16, True, temp=0.8)
+    both(x, False, q, d, lens, temps, 12)
+
+
 def test_code_race_matches_with_bonus_rows_and_one_request():
     x, q, d, lens, temps = make(4, 64, 7, 151936, torch.bfloat16, False, draft_from_p=True)
     n, t = both(x, False, q, d, lens, temps, 5)
