@@ -87,6 +87,7 @@ struct NormRopeArgs {
 // the warp that owns the K row of the same head.
 __global__ void __launch_bounds__(256) norm_rope_store_kernel(const NormRopeArgs a) {
   griddep_launch_dependents();   // a dependent launched early (verify attention) may start its prologue
+  griddep_wait();                // launched as a dependent of the projection that wrote its input
   const int lane = threadIdx.x & 31;
   const long long item = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int heads = a.Hq + a.Hkv;
@@ -138,6 +139,8 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* __res
                                                       __nv_bfloat16* __restrict__ residual_out, int width, float eps) {
   constexpr int kMaxVec = 4;   // 4 x 8 elements per thread: width <= 256 * 32 = 8192
   __shared__ float red[8];
+  griddep_launch_dependents();
+  griddep_wait();                // launched as a dependent of the kernel that wrote x
   const long long t = blockIdx.x;
   const uint4* xv = reinterpret_cast<const uint4*>(x + t * width);
   const uint4* rv = residual ? reinterpret_cast<const uint4*>(residual + t * width) : nullptr;
@@ -220,6 +223,8 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* __res
 // a / (1 + e^-a) with the hardware exp2 and a fast quotient: a few fp32 ulp, far below the bf16 rounding.
 __global__ void __launch_bounds__(256) silu_mul_kernel(const __nv_bfloat16* gate_up, __nv_bfloat16* out, long long T,
                                                        int I) {
+  griddep_launch_dependents();
+  griddep_wait();                // launched as a dependent of the projection that wrote gate_up
   const long long nvec_row = I / 8;
   const long long i = (long long)blockIdx.x * 256 + threadIdx.x;
   if (i >= T * nvec_row) return;
@@ -293,7 +298,8 @@ int specdec_norm_rope_store(const void* x, long long x_layer_stride, long long x
   a.err = err;
   const long long items = (long long)T * (num_q_heads + num_kv_heads);
   dim3 grid((unsigned)((items + 7) / 8), (unsigned)layers);
-  fused::norm_rope_store_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  SPECDEC_CUDA_TRY(launch_dependent(fused::norm_rope_store_kernel, grid, dim3(256), static_cast<cudaStream_t>(stream),
+                                    a));
   SPECDEC_LAUNCH_CHECK();
   return kOk;
 }
@@ -305,10 +311,11 @@ int specdec_rmsnorm(const void* x, const void* residual, const void* weight, voi
   SPECDEC_CHECK_ARG(width % 8 == 0 && width <= 8192 && width > 0, "width %d must be a multiple of 8 up to 8192",
                     width);
   if (T <= 0) return kOk;
-  fused::rmsnorm_kernel<<<(unsigned)T, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(residual),
-      static_cast<const __nv_bfloat16*>(weight), static_cast<__nv_bfloat16*>(out),
-      static_cast<__nv_bfloat16*>(residual_out), width, eps);
+  SPECDEC_CUDA_TRY(launch_dependent(fused::rmsnorm_kernel, dim3((unsigned)T), dim3(256),
+                                    static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(x),
+                                    static_cast<const __nv_bfloat16*>(residual),
+                                    static_cast<const __nv_bfloat16*>(weight), static_cast<__nv_bfloat16*>(out),
+                                    static_cast<__nv_bfloat16*>(residual_out), width, eps));
   SPECDEC_LAUNCH_CHECK();
   return kOk;
 }
@@ -318,8 +325,9 @@ int specdec_silu_mul(const void* gate_up, void* out, long long T, int intermedia
   SPECDEC_CHECK_ARG(intermediate % 8 == 0 && intermediate > 0, "intermediate must be a positive multiple of 8");
   if (T <= 0) return kOk;
   const long long n = T * (intermediate / 8);
-  fused::silu_mul_kernel<<<(unsigned)((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(gate_up), static_cast<__nv_bfloat16*>(out), T, intermediate);
+  SPECDEC_CUDA_TRY(launch_dependent(fused::silu_mul_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256),
+                                    static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(gate_up),
+                                    static_cast<__nv_bfloat16*>(out), T, intermediate));
   SPECDEC_LAUNCH_CHECK();
   return kOk;
 }
