@@ -1191,8 +1191,8 @@ def main() -> int:
     roofline = attention_roofline(torch, w, pk["hbm_gbs"])
     roofline["peak_source"] = pk["source"]
     accept = accept_timing(torch, w)
-    launches_per_step = w.shape.layers * 5 + 1 + 2      # per layer: 2 norms, qk-norm/rope/store, attention,
-                                                        # silu; final norm; sampler stats + tail
+    launches_per_step = w.shape.layers * 5 + 1 + 3      # per layer: 2 norms, qk-norm/rope/store, attention,
+                                                        # silu; final norm; sampler noise codes + stats + tail
     h2d = (num_tokens * (8 + 8 + 4) + 2 * (batch + 1) * 4 + batch * w.width * 4)
     d2h = batch * (K_DRAFTS + 2) * 8
     round_nbytes = round_bytes(w, num_tokens)
