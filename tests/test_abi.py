@@ -37,6 +37,17 @@ def test_host_queries_run_without_a_gpu(lib):
     assert lib.specdec_last_error() is not None
 
 
+def test_accept_workspace_adds_the_noise_codes(lib):
+    """The accept's workspace with room for the tail race's noise codes: the sampler workspace plus 2 bytes per
+    element of the [B, V] noise, rounded to 256 bytes; 0 for sizes that are not positive."""
+    for T, B, V in [(512, 64, 151936), (1, 1, 7), (16384, 1024, 1000)]:
+        codes = (B * V * 2 + 255) // 256 * 256
+        assert lib.specdec_accept_workspace_bytes(T, B, V) == lib.specdec_sampler_workspace_bytes(T) + codes
+    assert lib.specdec_accept_workspace_bytes(0, 64, 151936) == 0
+    assert lib.specdec_accept_workspace_bytes(512, 0, 151936) == 0
+    assert lib.specdec_accept_workspace_bytes(512, 64, -1) == 0
+
+
 def _attention_multi(lib, outs, num_outs):
     """specdec_paged_attention_multi with plausible (never dereferenced) addresses: only the host validation
     runs, so a call must be rejected before any CUDA call."""
