@@ -48,6 +48,8 @@ constexpr int kRngBlock = 256;       // torch's block_size_bound for distributio
 constexpr int kStatusBadLens = 1;     // a length outside 1..k+1, or lengths not summing to T
 constexpr int kStatusBadDraft = 2;    // a draft id outside [0, V)
 constexpr int kStatusBadTopK = 3;     // a row's top_k above the in-kernel cap
+constexpr int kStatusTimeout = 5;     // a wait of the early-exit pass 1 ran out (zero the workspace again)
+constexpr long long kRowWaitPolls = 1ll << 22;   // polls of a row counter (~64 ns apart) before giving up
 
 struct RowStat {   // per verified row: softmax max / sum over the kept entries, truncation threshold
   float m, s, thr, pad;
@@ -62,7 +64,8 @@ struct ReqDesc {   // per request: where its tail distribution lives
 // Self-cleaning tables (tickets, argmax keys) sit at fixed offsets at the front, so a workspace zeroed once at
 // allocation stays valid across calls of any shape; per-call scratch follows.
 struct Layout {
-  size_t status, req_ticket, tail_key, tail_ticket, row_key, rows, partial, desc, kept_n, kept_ids, total;
+  size_t status, req_ticket, tail_key, tail_ticket, row_key, row_cnt, row_done, rows, partial, desc, kept_n, kept_ids,
+      total;
 };
 static constexpr Layout layout(int64_t T) {
   Layout L{};
@@ -77,6 +80,8 @@ static constexpr Layout layout(int64_t T) {
   L.tail_key = take(sizeof(unsigned long long) * kMaxRequests);
   L.tail_ticket = take(256);
   L.row_key = take(sizeof(unsigned long long) * kMaxRows);
+  L.row_cnt = take(sizeof(unsigned) * kMaxRows);
+  L.row_done = take(sizeof(unsigned) * kMaxRows);
   L.rows = take(sizeof(RowStat) * (size_t)(T > 0 ? T : 1));
   L.partial = take(sizeof(float2) * (size_t)(T > 0 ? T : 1) * kMaxChunks);
   L.desc = take(sizeof(ReqDesc) * kMaxRequests);
@@ -121,6 +126,8 @@ struct Args {
   unsigned long long* tail_key;
   unsigned* tail_ticket;
   unsigned long long* row_key;
+  unsigned* row_cnt;        // [T] early-exit pass 1: chunks that published the row (reset once all have read it)
+  unsigned* row_done;       // [T] chunks past the row's wait
   RowStat* rows;
   float2* partial;
   ReqDesc* desc;
@@ -528,6 +535,140 @@ __global__ void __launch_bounds__(kThreads, kStatsCtasPerSm) stats_kernel(Args a
   __threadfence();
   decide_request<T>(a, b, start, len, true);
   if (threadIdx.x == 0) atomicExch(&a.req_ticket[b], 0u);
+}
+
+// ---------------------------------------------------------------------------------------- pass 1, early exit
+// The accept test walks a request's drafts in order and stops at the first rejection (spec_sampler.py:142-147),
+// so the rows after it never matter.  Grid (C, B): the C CTAs of request b stream its rows in order, chunk c of
+// each; after publishing a row's chunk partial, every CTA of the request waits (bounded) until all C have, merges
+// the row's (max, sum), and takes the draft's accept test itself (the same inputs and arithmetic in every CTA, so
+// the same outcome); at the first rejection, or at the last verified row, chunk 0 writes the request's result.
+// Launched cooperatively (every CTA resident at once), which the waits need.
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Thread 0: polls until *cnt reaches target; false after kRowWaitPolls polls.
+__device__ bool wait_row_count(const unsigned* cnt, unsigned target) {
+  for (long long i = 0; i < kRowWaitPolls; ++i) {
+    if (ld_acquire_u32(cnt) >= target) return true;
+    __nanosleep(64);
+  }
+  return false;
+}
+
+constexpr int kEarlyCtasPerSm = 3;   // the walk's decision code beside the streaming loop: up to 85 registers
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, kEarlyCtasPerSm) stats_early_kernel(Args a) {
+  __shared__ int s_start[kMaxRequests + 1];
+  __shared__ int s_flag;      // 0 go on, 1 the request is decided, 2 bad input or a wait that ran out
+  __shared__ RowStat s_rs;
+  // the walk's state lives in shared memory, so that no register holds it across the streaming loop
+  __shared__ int s_j, s_row0, s_len;
+  __shared__ float s_temp;
+  __shared__ float s_u[32], s_q[32], s_x[32];   // per draft: its uniform, q and target logit (loaded up front)
+  const int b = blockIdx.y;
+  if (a.lens != nullptr && !starts_from_lens<kThreads>(a.lens, a.B, a.k + 1, a.T, s_start)) {
+    if (threadIdx.x == 0) report(a, kStatusBadLens);
+    return;
+  }
+  // every draft id is checked (the reference indexes them all): a bad one ends the whole request in every CTA.
+  // Lane j loads draft j's uniform, q and target logit, so a row's decision waits on nothing but the row.
+  if (threadIdx.x < 32) {
+    const int row0 = a.lens == nullptr ? b * (a.k + 1) : s_start[b];
+    const int len = a.lens == nullptr ? a.k + 1 : s_start[b + 1] - s_start[b];
+    const int j = threadIdx.x;
+    bool bad = false;
+    if (j < a.k) {
+      const long long li = (long long)b * a.k + j;
+      const long long d = a.drafts[li];
+      bad = d < 0 || d >= a.V;
+      if (!bad && j < len - 1) {
+        s_u[j] = a.u ? a.u[li] : torch_rand_at(a.seed, a.offset_u, li, a.u_grid);
+        s_q[j] = a.q[li * a.V + d];
+        s_x[j] = to_f32(reinterpret_cast<const T*>(a.x)[(row0 + j) * a.V + d]);
+      }
+    }
+    bad = __any_sync(0xffffffffu, bad);
+    if (j == 0) {
+      s_flag = bad ? 2 : 0;
+      s_j = 0;
+      s_row0 = row0;
+      s_len = len;
+      s_temp = a.temperature[b];
+    }
+  }
+  __syncthreads();
+  if (s_flag) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) report(a, kStatusBadDraft);
+    return;
+  }
+  // row r's chunk: its (max, sum) published, then the row's arrival counter raised
+  auto publish_row = [&](int r) {
+    const long long t = s_row0 + r;
+    const int lo = blockIdx.x * a.chunk;
+    const int hi = min((long long)lo + a.chunk, a.V);
+    float m, s;
+    row_range_ms<T, kThreads>(reinterpret_cast<const T*>(a.x) + t * a.V, lo, hi, s_temp, a.vec_ok, m, s);
+    block_ms<kThreads>(m, s);
+    if (threadIdx.x == 0) {
+      a.partial[(size_t)t * kMaxChunks + blockIdx.x] = make_float2(m, s);
+      __threadfence();
+      atomicAdd(&a.row_cnt[t], 1u);
+    }
+  };
+  while (true) {
+    publish_row(s_j);
+    const int j = s_j;
+    const long long t = s_row0 + j;
+    const bool last_row = j == s_len - 1;
+    if (last_row && blockIdx.x != 0) return;   // the last verified row's stats matter to chunk 0 only
+    if (threadIdx.x == 0) s_flag = wait_row_count(&a.row_cnt[t], gridDim.x) ? 0 : 2;
+    __syncthreads();
+    if (s_flag == 2) {
+      if (threadIdx.x == 0) report(a, kStatusTimeout);
+      return;
+    }
+    if (threadIdx.x < 32) {
+      const RowStat rs = merge_row_warp(a, (int)t);
+      if (threadIdx.x == 0) {
+        int stop = 1;
+        if (!last_row) {   // prob_at's arithmetic on the preloaded logit
+          const float f = s_temp == 1.0f ? s_x[j] : scale_logit(s_x[j], s_temp);
+          stop = (s_u[j] * s_q[j] < prob_of_scaled(f, rs)) ? 0 : 1;   // u < min(1, p/q) without dividing
+        }
+        s_flag = stop;
+        s_rs = rs;
+        s_j = j + 1;
+        // the row's counters go back to zero once every CTA that waits on them is past the wait
+        if (last_row) {
+          a.row_cnt[t] = 0;
+        } else if (atomicAdd(&a.row_done[t], 1u) == gridDim.x - 1) {
+          a.row_cnt[t] = 0;
+          a.row_done[t] = 0;
+        }
+      }
+    }
+    __syncthreads();
+    if (s_flag) {
+      if (blockIdx.x == 0 && threadIdx.x == 0) {   // n_accept = j: drafts 0..j-1 accepted
+        a.n_accept[b] = j;
+        ReqDesc d;
+        d.x_row = t;
+        d.q_row = last_row ? -1 : (long long)b * a.k + j;
+        d.m = s_rs.m;
+        d.s = s_rs.s;
+        d.thr = s_rs.thr;
+        d.temp = s_temp;
+        a.desc[b] = d;
+        a.rows[t] = s_rs;
+      }
+      return;
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------------------- pass 1 (truncating)
@@ -1786,6 +1927,8 @@ static void bind_workspace(Args& a, void* ws) {
   a.tail_key = reinterpret_cast<unsigned long long*>(base + L.tail_key);
   a.tail_ticket = reinterpret_cast<unsigned*>(base + L.tail_ticket);
   a.row_key = reinterpret_cast<unsigned long long*>(base + L.row_key);
+  a.row_cnt = reinterpret_cast<unsigned*>(base + L.row_cnt);
+  a.row_done = reinterpret_cast<unsigned*>(base + L.row_done);
   a.rows = reinterpret_cast<RowStat*>(base + L.rows);
   a.partial = reinterpret_cast<float2*>(base + L.partial);
   a.desc = reinterpret_cast<ReqDesc*>(base + L.desc);
@@ -1828,6 +1971,37 @@ static int launch_tail(Args& a, const DeviceInfo& info, bool race, cudaStream_t 
     tail_accept_kernel<T><<<a.e_grid, kThreads, smem, stream>>>(a);
   }
   SPECDEC_LAUNCH_CHECK();
+  return kOk;
+}
+
+// The early-exit pass 1 (stats_early_kernel): C chunks per request with every CTA resident at once (a cooperative
+// launch), as many chunks as one wave holds, each at least 2048 elements.  kUnsupported when the requests alone do
+// not fit one wave (the caller then runs stats_kernel over every row).
+template <typename T>
+static int launch_early_stats(Args& a, const DeviceInfo& info, cudaStream_t stream) {
+  int per_sm = 0;
+  SPECDEC_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stats_early_kernel<T>, kThreads, 0));
+  const long long resident = (long long)per_sm * info.sm_count;
+  if (resident < a.B) return kUnsupported;
+  long long C = resident / a.B;
+  const long long cmax = (a.V + 2047) / 2048;
+  if (C > cmax) C = cmax;
+  if (C > kMaxChunks) C = kMaxChunks;
+  const int ve = a.dtype == kF32 ? 4 : 8;
+  long long chunk = (a.V + C - 1) / C;
+  chunk = (chunk + ve - 1) / ve * ve;
+  a.chunk = (int)chunk;
+  a.C = (int)((a.V + chunk - 1) / chunk);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)a.C, (unsigned)a.B);
+  cfg.blockDim = dim3(kThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  SPECDEC_CUDA_TRY(cudaLaunchKernelEx(&cfg, stats_early_kernel<T>, a));
   return kOk;
 }
 
@@ -1990,8 +2164,9 @@ int specdec_accept(const void* x, int x_is_probs, int dtype, long long T, long l
       decide_probs_kernel<Tx><<<(unsigned)B, 64, 0, s>>>(a);
     } else if (a.truncate) {
       topk_stats_kernel<Tx><<<(unsigned)T, kTopkThreads, 0, s>>>(a, 0);
-    } else {
-      stats_kernel<Tx><<<dim3(a.C, (unsigned)T), kThreads, 0, s>>>(a, 0);
+    } else if (int st = launch_early_stats<Tx>(a, info, s)) {
+      if (st != kUnsupported) return st;
+      stats_kernel<Tx><<<dim3(a.C, (unsigned)T), kThreads, 0, s>>>(a, 0);   // more requests than one wave holds
     }
     SPECDEC_LAUNCH_CHECK();
     if (a.truncate) {   // truncating rows: the race over each request's kept tokens, or (gated) over whole rows

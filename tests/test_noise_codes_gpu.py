@@ -176,3 +176,53 @@ def test_code_race_repeats_and_leaves_the_workspace_clean():
     assert torch.equal(outs[0][1], outs[2][1]) and torch.equal(outs[0][0], outs[2][0])
     fresh = accept(x, False, q, d, lens, temps, 43, (0, 8), L.specdec_sampler_workspace_bytes(rows))
     assert torch.equal(fresh[1], outs[1][1])
+
+
+def oracle_accept(logits, q, drafts, lens, temps, u, noise):
+    from oracle import spec_sampler as O
+    ln = lens.cpu().numpy()
+    p = O.probs_from_logits(logits.float().cpu().numpy(), np.repeat(temps.cpu().numpy(), ln))
+    args = (q.cpu().numpy(), drafts.cpu().numpy(), ln, u.cpu().numpy(), noise.cpu().numpy())
+    n, tail = O.accept_random_varlen(p, *args)
+    keep = ~O.near_tie_flags(p, *args)
+    return n, tail, keep
+
+
+@pytest.mark.parametrize("batch,k,V,accepting", [
+    (700, 2, 512, False),     # more requests than one wave holds: every row reduced (the full pass 1)
+    (64, 7, 151936, True),    # drafts the target likes: long walks of the early-exit pass
+    (64, 7, 151936, False),
+    (5, 4, 1001, True),       # ragged vocabulary, few requests: many chunks per row
+])
+def test_accept_passes_match_the_oracle(batch, k, V, accepting):
+    """specdec_accept's pass 1 in both forms against the oracle: the early-exit walk (each request's rows only up
+    to its first rejection, its chunks waiting on each other) and the full pass for batches past one wave."""
+    from nanovllm_b200 import spec_sampler as S
+    from types import SimpleNamespace
+    g = torch.Generator(device=DEV).manual_seed(batch + V)
+    lens = torch.randint(1, k + 2, (batch,), device=DEV, generator=g)
+    rows = int(lens.sum())
+    logits = (torch.randn(rows, V, device=DEV, generator=g) * 3).bfloat16()
+    q = torch.softmax(torch.randn(batch, k, V, device=DEV, generator=g) * 3, dim=-1)
+    drafts = torch.randint(V, (batch, k), device=DEV, generator=g)
+    if accepting:   # drafts = the target's argmax at each verified position, q ~ 0 there: most drafts accepted
+        starts = torch.cumsum(lens, 0) - lens
+        for b in range(batch):
+            for j in range(int(lens[b]) - 1):
+                drafts[b, j] = logits[starts[b] + j].float().argmax()
+        q = torch.full_like(q, 1e-9)
+    temps = torch.full((batch,), 0.9, device=DEV)
+    samp = S.sampling_tensors([SimpleNamespace(temperature=0.9, top_k=0, top_p=1.0)] * batch, DEV)
+    g1 = torch.Generator(device=DEV).manual_seed(7)
+    g2 = torch.Generator(device=DEV).manual_seed(7)
+    n, tail = S.accept_from_logits(logits, q, drafts, samp, lens, g1, draws="kernel")
+    u = torch.rand(batch, k, device=DEV, generator=g2)
+    noise = S.exponential_noise_(torch.empty(batch, V, device=DEV), g2)
+    from nanovllm_b200 import _lib
+    assert _lib.device_status(DEV) == 0
+    want_n, want_tail, keep = oracle_accept(logits, q, drafts, lens, temps, u, noise)
+    assert keep.mean() > 0.9
+    assert np.array_equal(n.cpu().numpy()[keep], want_n[keep])
+    assert np.array_equal(tail.cpu().numpy()[keep], want_tail[keep])
+    if accepting:
+        assert (n.cpu().numpy() == lens.cpu().numpy() - 1).mean() > 0.5
