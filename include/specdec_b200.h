@@ -58,9 +58,8 @@ int specdec_probs(const void* logits, int dtype, long long R, long long V, long 
 
 /* accept_random / accept_random_varlen (spec_sampler.py:114-150), and with x_is_probs = 0 the round driver's
  * fused probs_from_logits + accept (nanovllm/engine/speculative.py:450-462).  Without top-k, logits rows are
- * reduced only up to each request's first rejected draft (its later rows cannot change the result), its CTAs
- * launched cooperatively (all resident at once) and waiting on each other with a bounded wait; the workspace's
- * status word then reads 5 if a wait ran out (zero the workspace before reusing it).
+ * reduced only up to each request's first rejected draft (its later rows cannot change the result): one
+ * thread-block cluster per request walks its rows, when the requests fit one wave.
  * x [T, V]: fp32 probabilities (x_is_probs = 1) or logits of `dtype` with per-request temperature/top_k/top_p
  * [B].  q [B, k, V] fp32; drafts [B, k] int64; verified_lens [B] int64 in 1..k+1 summing to T, or NULL for
  * k + 1 each (T = B (k + 1)).  u [B, k] and E [B, V] (clamped Exp(1)) are the reference's two draws; when NULL

@@ -48,8 +48,6 @@ constexpr int kRngBlock = 256;       // torch's block_size_bound for distributio
 constexpr int kStatusBadLens = 1;     // a length outside 1..k+1, or lengths not summing to T
 constexpr int kStatusBadDraft = 2;    // a draft id outside [0, V)
 constexpr int kStatusBadTopK = 3;     // a row's top_k above the in-kernel cap
-constexpr int kStatusTimeout = 5;     // a wait of the early-exit pass 1 ran out (zero the workspace again)
-constexpr long long kRowWaitPolls = 1ll << 22;   // polls of a row counter (~64 ns apart) before giving up
 
 struct RowStat {   // per verified row: softmax max / sum over the kept entries, truncation threshold
   float m, s, thr, pad;
@@ -64,8 +62,7 @@ struct ReqDesc {   // per request: where its tail distribution lives
 // Self-cleaning tables (tickets, argmax keys) sit at fixed offsets at the front, so a workspace zeroed once at
 // allocation stays valid across calls of any shape; per-call scratch follows.
 struct Layout {
-  size_t status, req_ticket, tail_key, tail_ticket, row_key, row_cnt, row_done, rows, partial, desc, kept_n, kept_ids,
-      total;
+  size_t status, req_ticket, tail_key, tail_ticket, row_key, rows, partial, desc, kept_n, kept_ids, total;
 };
 static constexpr Layout layout(int64_t T) {
   Layout L{};
@@ -80,8 +77,6 @@ static constexpr Layout layout(int64_t T) {
   L.tail_key = take(sizeof(unsigned long long) * kMaxRequests);
   L.tail_ticket = take(256);
   L.row_key = take(sizeof(unsigned long long) * kMaxRows);
-  L.row_cnt = take(sizeof(unsigned) * kMaxRows);
-  L.row_done = take(sizeof(unsigned) * kMaxRows);
   L.rows = take(sizeof(RowStat) * (size_t)(T > 0 ? T : 1));
   L.partial = take(sizeof(float2) * (size_t)(T > 0 ? T : 1) * kMaxChunks);
   L.desc = take(sizeof(ReqDesc) * kMaxRequests);
@@ -126,8 +121,6 @@ struct Args {
   unsigned long long* tail_key;
   unsigned* tail_ticket;
   unsigned long long* row_key;
-  unsigned* row_cnt;        // [T] early-exit pass 1: chunks that published the row (reset once all have read it)
-  unsigned* row_done;       // [T] chunks past the row's wait
   RowStat* rows;
   float2* partial;
   ReqDesc* desc;
@@ -539,33 +532,55 @@ __global__ void __launch_bounds__(kThreads, kStatsCtasPerSm) stats_kernel(Args a
 
 // ---------------------------------------------------------------------------------------- pass 1, early exit
 // The accept test walks a request's drafts in order and stops at the first rejection (spec_sampler.py:142-147),
-// so the rows after it never matter.  Grid (C, B): the C CTAs of request b stream its rows in order, chunk c of
-// each; after publishing a row's chunk partial, every CTA of the request waits (bounded) until all C have, merges
-// the row's (max, sum), and takes the draft's accept test itself (the same inputs and arithmetic in every CTA, so
-// the same outcome); at the first rejection, or at the last verified row, chunk 0 writes the request's result.
-// Launched cooperatively (every CTA resident at once), which the waits need.
-__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+// so the rows after it never matter.  Grid (C, B) in thread-block clusters of C: the C CTAs of request b stream
+// its rows in order, chunk c of each; a row's C partial (max, sum) pairs meet in distributed shared memory at a
+// cluster barrier, every CTA merges them in the same order and takes the draft's accept test itself (the same
+// inputs and arithmetic, so the same outcome), and at the first rejection, or at the last verified row, chunk 0
+// writes the request's result.  The cluster's CTAs are co-scheduled by the hardware; nothing waits on memory.
+constexpr int kEarlyCtasPerSm = 3;   // the walk's decision code beside the streaming loop: up to 85 registers
+constexpr int kEarlyMaxCluster = 8;  // portable cluster size
+
+// Barrier over every thread of the cluster; the release / acquire pair makes each CTA's shared-memory writes
+// before it visible to the cluster's reads after it.
+__device__ __forceinline__ void cluster_barrier() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// The float2 at `local`'s offset in the shared memory of the cluster's CTA `rank`.
+__device__ __forceinline__ float2 ld_cluster_f2(const float2* local, unsigned rank) {
+  const unsigned addr = static_cast<unsigned>(__cvta_generic_to_shared(local));
+  unsigned remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(addr), "r"(rank));
+  float2 v;
+  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(remote) : "memory");
   return v;
 }
 
-// Thread 0: polls until *cnt reaches target; false after kRowWaitPolls polls.
-__device__ bool wait_row_count(const unsigned* cnt, unsigned target) {
-  for (long long i = 0; i < kRowWaitPolls; ++i) {
-    if (ld_acquire_u32(cnt) >= target) return true;
-    __nanosleep(64);
+// One warp: the (max, sum) of the cluster's C partials (lane c reads CTA c's).  The butterfly combine is
+// symmetric, so every lane, and every CTA of the cluster, gets the same floats.
+__device__ __forceinline__ float2 merge_cluster_partials(const float2* part, unsigned C) {
+  const unsigned lane = threadIdx.x & 31;
+  float m = -INFINITY, s = 0.0f;
+  if (lane < C) {
+    const float2 p = ld_cluster_f2(part, lane);
+    m = p.x;
+    s = p.y;
   }
-  return false;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    ms_combine(m, s, m2, s2);
+  }
+  return make_float2(m, s);
 }
-
-constexpr int kEarlyCtasPerSm = 3;   // the walk's decision code beside the streaming loop: up to 85 registers
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads, kEarlyCtasPerSm) stats_early_kernel(Args a) {
   __shared__ int s_start[kMaxRequests + 1];
-  __shared__ int s_flag;      // 0 go on, 1 the request is decided, 2 bad input or a wait that ran out
+  __shared__ int s_flag;      // 0 go on, 1 the request is decided, 2 a bad draft id
   __shared__ RowStat s_rs;
+  __shared__ float2 s_part;   // this CTA's (max, sum) of the current row, read by the whole cluster
   // the walk's state lives in shared memory, so that no register holds it across the streaming loop
   __shared__ int s_j, s_row0, s_len;
   __shared__ float s_temp;
@@ -573,9 +588,9 @@ __global__ void __launch_bounds__(kThreads, kEarlyCtasPerSm) stats_early_kernel(
   const int b = blockIdx.y;
   if (a.lens != nullptr && !starts_from_lens<kThreads>(a.lens, a.B, a.k + 1, a.T, s_start)) {
     if (threadIdx.x == 0) report(a, kStatusBadLens);
-    return;
+    return;                   // every CTA of every cluster leaves here
   }
-  // every draft id is checked (the reference indexes them all): a bad one ends the whole request in every CTA.
+  // every draft id is checked (the reference indexes them all): a bad one ends the request in all its CTAs.
   // Lane j loads draft j's uniform, q and target logit, so a row's decision waits on nothing but the row.
   if (threadIdx.x < 32) {
     const int row0 = a.lens == nullptr ? b * (a.k + 1) : s_start[b];
@@ -604,37 +619,27 @@ __global__ void __launch_bounds__(kThreads, kEarlyCtasPerSm) stats_early_kernel(
   __syncthreads();
   if (s_flag) {
     if (threadIdx.x == 0 && blockIdx.x == 0) report(a, kStatusBadDraft);
-    return;
+    return;                   // every CTA of this cluster leaves here
   }
-  // row r's chunk: its (max, sum) published, then the row's arrival counter raised
-  auto publish_row = [&](int r) {
-    const long long t = s_row0 + r;
-    const int lo = blockIdx.x * a.chunk;
-    const int hi = min((long long)lo + a.chunk, a.V);
-    float m, s;
-    row_range_ms<T, kThreads>(reinterpret_cast<const T*>(a.x) + t * a.V, lo, hi, s_temp, a.vec_ok, m, s);
-    block_ms<kThreads>(m, s);
-    if (threadIdx.x == 0) {
-      a.partial[(size_t)t * kMaxChunks + blockIdx.x] = make_float2(m, s);
-      __threadfence();
-      atomicAdd(&a.row_cnt[t], 1u);
-    }
-  };
   while (true) {
-    publish_row(s_j);
+    {
+      const long long t = s_row0 + s_j;
+      const int lo = blockIdx.x * a.chunk;
+      const int hi = min((long long)lo + a.chunk, a.V);
+      float m, s;
+      row_range_ms<T, kThreads>(reinterpret_cast<const T*>(a.x) + t * a.V, lo, hi, s_temp, a.vec_ok, m, s);
+      block_ms<kThreads>(m, s);
+      if (threadIdx.x == 0) s_part = make_float2(m, s);
+    }
+    cluster_barrier();        // every chunk's partial of the row is visible to the cluster
     const int j = s_j;
     const long long t = s_row0 + j;
     const bool last_row = j == s_len - 1;
-    if (last_row && blockIdx.x != 0) return;   // the last verified row's stats matter to chunk 0 only
-    if (threadIdx.x == 0) s_flag = wait_row_count(&a.row_cnt[t], gridDim.x) ? 0 : 2;
-    __syncthreads();
-    if (s_flag == 2) {
-      if (threadIdx.x == 0) report(a, kStatusTimeout);
-      return;
-    }
     if (threadIdx.x < 32) {
-      const RowStat rs = merge_row_warp(a, (int)t);
+      const float2 ms = merge_cluster_partials(&s_part, gridDim.x);
       if (threadIdx.x == 0) {
+        RowStat rs;
+        rs.m = ms.x; rs.s = ms.y; rs.thr = -INFINITY; rs.pad = 0.0f;
         int stop = 1;
         if (!last_row) {   // prob_at's arithmetic on the preloaded logit
           const float f = s_temp == 1.0f ? s_x[j] : scale_logit(s_x[j], s_temp);
@@ -643,16 +648,9 @@ __global__ void __launch_bounds__(kThreads, kEarlyCtasPerSm) stats_early_kernel(
         s_flag = stop;
         s_rs = rs;
         s_j = j + 1;
-        // the row's counters go back to zero once every CTA that waits on them is past the wait
-        if (last_row) {
-          a.row_cnt[t] = 0;
-        } else if (atomicAdd(&a.row_done[t], 1u) == gridDim.x - 1) {
-          a.row_cnt[t] = 0;
-          a.row_done[t] = 0;
-        }
       }
     }
-    __syncthreads();
+    cluster_barrier();        // the partials are read before any CTA overwrites (or leaves with) its own
     if (s_flag) {
       if (blockIdx.x == 0 && threadIdx.x == 0) {   // n_accept = j: drafts 0..j-1 accepted
         a.n_accept[b] = j;
@@ -1927,8 +1925,6 @@ static void bind_workspace(Args& a, void* ws) {
   a.tail_key = reinterpret_cast<unsigned long long*>(base + L.tail_key);
   a.tail_ticket = reinterpret_cast<unsigned*>(base + L.tail_ticket);
   a.row_key = reinterpret_cast<unsigned long long*>(base + L.row_key);
-  a.row_cnt = reinterpret_cast<unsigned*>(base + L.row_cnt);
-  a.row_done = reinterpret_cast<unsigned*>(base + L.row_done);
   a.rows = reinterpret_cast<RowStat*>(base + L.rows);
   a.partial = reinterpret_cast<float2*>(base + L.partial);
   a.desc = reinterpret_cast<ReqDesc*>(base + L.desc);
@@ -1974,9 +1970,10 @@ static int launch_tail(Args& a, const DeviceInfo& info, bool race, cudaStream_t 
   return kOk;
 }
 
-// The early-exit pass 1 (stats_early_kernel): C chunks per request with every CTA resident at once (a cooperative
-// launch), as many chunks as one wave holds, each at least 2048 elements.  kUnsupported when the requests alone do
-// not fit one wave (the caller then runs stats_kernel over every row).
+// The early-exit pass 1 (stats_early_kernel): clusters of C CTAs, one per request, C as large as one wave of the
+// requests allows (at most the portable cluster size; each chunk at least 2048 elements).  kUnsupported when the
+// requests alone do not fit one wave (the caller then runs stats_kernel over every row, which has no sequential
+// walk to stretch over several waves).
 template <typename T>
 static int launch_early_stats(Args& a, const DeviceInfo& info, cudaStream_t stream) {
   int per_sm = 0;
@@ -1986,7 +1983,7 @@ static int launch_early_stats(Args& a, const DeviceInfo& info, cudaStream_t stre
   long long C = resident / a.B;
   const long long cmax = (a.V + 2047) / 2048;
   if (C > cmax) C = cmax;
-  if (C > kMaxChunks) C = kMaxChunks;
+  if (C > kEarlyMaxCluster) C = kEarlyMaxCluster;
   const int ve = a.dtype == kF32 ? 4 : 8;
   long long chunk = (a.V + C - 1) / C;
   chunk = (chunk + ve - 1) / ve * ve;
@@ -1997,8 +1994,10 @@ static int launch_early_stats(Args& a, const DeviceInfo& info, cudaStream_t stre
   cfg.blockDim = dim3(kThreads);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)a.C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   SPECDEC_CUDA_TRY(cudaLaunchKernelEx(&cfg, stats_early_kernel<T>, a));

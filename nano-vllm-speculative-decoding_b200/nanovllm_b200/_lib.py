@@ -168,8 +168,7 @@ class Workspace:
 
 def device_status(device: torch.device, name: str = "sampler") -> int:
     """The device-side input-check word of the last sampler call on this device (synchronises): 0 ok,
-    1 verified lengths outside 1..k+1 or not summing to T, 2 a draft id outside [0, V), 3 a top_k above the cap,
-    5 a bounded wait of the accept's early-exit pass ran out (the workspace must be zeroed again)."""
+    1 verified lengths outside 1..k+1 or not summing to T, 2 a draft id outside [0, V), 3 a top_k above the cap."""
     key = (device.index if device.index is not None else torch.cuda.current_device(), name)
     buf = Workspace._buffers.get(key)
     return 0 if buf is None else int(buf[:4].view(torch.int32).item())
