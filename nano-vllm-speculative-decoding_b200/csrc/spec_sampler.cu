@@ -539,6 +539,7 @@ __global__ void __launch_bounds__(kThreads, kStatsCtasPerSm) stats_kernel(Args a
 // writes the request's result.  The cluster's CTAs are co-scheduled by the hardware; nothing waits on memory.
 constexpr int kEarlyCtasPerSm = 3;   // the walk's decision code beside the streaming loop: up to 85 registers
 constexpr int kEarlyMaxCluster = 8;  // portable cluster size
+constexpr int kNoiseCtasPerSm = 4;   // the noise codes kernel beside the early-exit pass: CTAs per SM
 
 // Barrier over every thread of the cluster; the release / acquire pair makes each CTA's shared-memory writes
 // before it visible to the cluster's reads after it.
@@ -586,6 +587,7 @@ __global__ void __launch_bounds__(kThreads, kEarlyCtasPerSm) stats_early_kernel(
   __shared__ float s_temp;
   __shared__ float s_u[32], s_q[32], s_x[32];   // per draft: its uniform, q and target logit (loaded up front)
   const int b = blockIdx.y;
+  griddep_launch_dependents();   // the noise codes kernel may start beside the walk
   if (a.lens != nullptr && !starts_from_lens<kThreads>(a.lens, a.B, a.k + 1, a.T, s_start)) {
     if (threadIdx.x == 0) report(a, kStatusBadLens);
     return;                   // every CTA of every cluster leaves here
@@ -1297,27 +1299,31 @@ constexpr int kCodeCtasPerSm = 2;
 // round, element idx + (4 n + ii) S of round n taking lane ii.
 template <bool kFloats>
 __global__ void __launch_bounds__(kThreads) noise_codes_kernel(Args a, float* floats) {
-  const unsigned S = kRngBlock * gridDim.x;
-  const unsigned idx = blockIdx.x * kRngBlock + threadIdx.x;
+  const unsigned S = kRngBlock * (unsigned)a.e_grid;   // torch's grid; this launch's grid strides over it
   const unsigned N = (unsigned)a.e_numel;
   const unsigned long long c0 = a.offset_E >> 2;
-  for (int n = 0; n < a.e_rounds; ++n) {
-    const unsigned li0 = idx + 4u * (unsigned)n * S;
-    if (li0 >= N) break;
-    const float4 r4 = philox_uniform4(a.seed, c0, idx, n);
-    const float r[4] = {r4.x, r4.y, r4.z, r4.w};
+  for (unsigned idx = blockIdx.x * kRngBlock + threadIdx.x; idx < S; idx += gridDim.x * kRngBlock) {
+    for (int n = 0; n < a.e_rounds; ++n) {
+      const unsigned li0 = idx + 4u * (unsigned)n * S;
+      if (li0 >= N) break;
+      const float4 r4 = philox_uniform4(a.seed, c0, idx, n);
+      const float r[4] = {r4.x, r4.y, r4.z, r4.w};
 #pragma unroll
-    for (int ii = 0; ii < 4; ++ii) {
-      const unsigned li = li0 + (unsigned)ii * S;
-      if (li < N) {
-        if constexpr (kFloats) {
-          floats[li] = torch_exponential_clamped(r[ii]);
-        } else {
-          a.codes[li] = noise_code(r[ii]);
+      for (int ii = 0; ii < 4; ++ii) {
+        const unsigned li = li0 + (unsigned)ii * S;
+        if (li < N) {
+          if constexpr (kFloats) {
+            floats[li] = torch_exponential_clamped(r[ii]);
+          } else {
+            a.codes[li] = noise_code(r[ii]);
+          }
         }
       }
     }
   }
+  // launched as a dependent of the accept's pass 1 (beside which it runs): its end then also implies pass 1's,
+  // whose decisions the tail race reads with the codes (returns at once for an ordinary launch)
+  griddep_wait();
 }
 
 // Exact race key of element v of request b's tail row: torch's E regenerated from its Philox block, then the
@@ -2153,19 +2159,32 @@ int specdec_accept(const void* x, int x_is_probs, int dtype, long long T, long l
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   SPECDEC_CUDA_TRY(cudaMemsetAsync(a.status, 0, 2 * sizeof(int), s));
-  if (a.codes) {
-    exponential_grid(a, info);
-    noise_codes_kernel<false><<<a.e_grid, kThreads, 0, s>>>(a, nullptr);
+  if (a.codes) exponential_grid(a, info);
+  // the noise codes: before pass 1, or beside the early-exit pass as its programmatic dependent (the walk leaves
+  // most issue slots idle; the codes kernel waits for the pass only at its end)
+  auto draw_codes = [&](bool beside) -> int {
+    if (!a.codes) return kOk;
+    if (beside) {
+      SPECDEC_CUDA_TRY(launch_dependent(noise_codes_kernel<false>, dim3((unsigned)(info.sm_count * kNoiseCtasPerSm)),
+                                        dim3(kThreads), s, a, static_cast<float*>(nullptr)));
+    } else {
+      noise_codes_kernel<false><<<a.e_grid, kThreads, 0, s>>>(a, nullptr);
+    }
     SPECDEC_LAUNCH_CHECK();
-  }
+    return kOk;
+  };
   return SPECDEC_DISPATCH_DTYPE(dtype, [&] {
     if (a.probs_mode) {
+      if (int st = draw_codes(false)) return st;
       decide_probs_kernel<Tx><<<(unsigned)B, 64, 0, s>>>(a);
     } else if (a.truncate) {
       topk_stats_kernel<Tx><<<(unsigned)T, kTopkThreads, 0, s>>>(a, 0);
     } else if (int st = launch_early_stats<Tx>(a, info, s)) {
       if (st != kUnsupported) return st;
+      if (int st2 = draw_codes(false)) return st2;
       stats_kernel<Tx><<<dim3(a.C, (unsigned)T), kThreads, 0, s>>>(a, 0);   // more requests than one wave holds
+    } else if (int st2 = draw_codes(true)) {
+      return st2;
     }
     SPECDEC_LAUNCH_CHECK();
     if (a.truncate) {   // truncating rows: the race over each request's kept tokens, or (gated) over whole rows
