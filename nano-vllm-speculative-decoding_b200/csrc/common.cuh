@@ -77,12 +77,12 @@ __device__ __forceinline__ void griddep_launch_dependents() { asm volatile("grid
 // while that work drains, so the kernel must call griddep_wait() before it reads anything the preceding work
 // writes.  Saves the launch gap after each library GEMM in the layer loop.
 template <typename... KArgs, typename... Args>
-static cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t stream,
-                                    Args... args) {
+static cudaError_t launch_dependent_smem(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                         cudaStream_t stream, Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -90,6 +90,11 @@ static cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 bl
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t stream,
+                                    Args... args) {
+  return launch_dependent_smem(kernel, grid, block, 0, stream, args...);
 }
 
 __device__ __forceinline__ uint4 ldg16(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }

@@ -1322,7 +1322,9 @@ __global__ void __launch_bounds__(kThreads) noise_codes_kernel(Args a, float* fl
     }
   }
   // launched as a dependent of the accept's pass 1 (beside which it runs): its end then also implies pass 1's,
-  // whose decisions the tail race reads with the codes (returns at once for an ordinary launch)
+  // whose decisions the tail race reads with the codes (returns at once for an ordinary launch).  The race, a
+  // dependent of this kernel, may start launching as its CTAs finish.
+  griddep_launch_dependents();
   griddep_wait();
 }
 
@@ -1520,6 +1522,7 @@ __global__ void __launch_bounds__(kThreads, kCodeCtasPerSm) tail_codes_kernel(Ar
   TailDesc* s_td = reinterpret_cast<TailDesc*>(codes_smem);
   __shared__ int s_last;
   __shared__ float2 s_list[kThreads / 32][kCodeItem];   // per warp: (element, weight) of its item's candidates
+  griddep_wait();                               // launched as a dependent of the pass that wrote its inputs
   const volatile int* status = a.status;
   if (status[0] != 0) return;                   // pass 1 rejected its inputs
   const unsigned V = (unsigned)a.V;
@@ -1961,13 +1964,11 @@ static int launch_tail(Args& a, const DeviceInfo& info, bool race, cudaStream_t 
     // the descriptors (up to 32 KB) beside the static candidate lists (32 KB) pass the 48 KB default
     const size_t smem = sizeof(TailDesc) * a.B;
     const int smem_max = (int)(sizeof(TailDesc) * kMaxRequests);
-    if (a.codes_vec) {
-      if (int st = ensure_dynamic_smem<tail_codes_kernel<T, true>>(smem_max)) return st;
-      tail_codes_kernel<T, true><<<(unsigned)grid, kThreads, smem, stream>>>(a);
-    } else {
-      if (int st = ensure_dynamic_smem<tail_codes_kernel<T, false>>(smem_max)) return st;
-      tail_codes_kernel<T, false><<<(unsigned)grid, kThreads, smem, stream>>>(a);
-    }
+    auto kernel = a.codes_vec ? tail_codes_kernel<T, true> : tail_codes_kernel<T, false>;
+    if (int st = a.codes_vec ? ensure_dynamic_smem<tail_codes_kernel<T, true>>(smem_max)
+                             : ensure_dynamic_smem<tail_codes_kernel<T, false>>(smem_max))
+      return st;
+    SPECDEC_CUDA_TRY(launch_dependent_smem(kernel, dim3((unsigned)grid), dim3(kThreads), smem, stream, a));
   } else {
     const size_t smem = (sizeof(TailDesc) + sizeof(unsigned long long) + sizeof(float)) * a.B;
     tail_accept_kernel<T><<<a.e_grid, kThreads, smem, stream>>>(a);
