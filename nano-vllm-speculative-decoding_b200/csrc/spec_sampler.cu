@@ -109,6 +109,7 @@ struct Args {
   float* probs_out;         // [T, V] for specdec_probs
   // layout
   int C, chunk, vec_ok;
+  int early_rows;           // stats_early_kernel: rows a cluster reduces per step (C / early_rows CTAs per row)
   int u_grid;               // torch grid (blocks of 256) of the [B, k] uniform draw
   int e_grid, e_rounds;     // torch grid and grid-stride rounds of the [B, V] exponential draw
   long long e_numel;
@@ -540,6 +541,7 @@ __global__ void __launch_bounds__(kThreads, kStatsCtasPerSm) stats_kernel(Args a
 constexpr int kEarlyCtasPerSm = 3;   // the walk's decision code beside the streaming loop: up to 85 registers
 constexpr int kEarlyMaxCluster = 8;  // portable cluster size
 constexpr int kNoiseCtasPerSm = 4;   // the noise codes kernel beside the early-exit pass: CTAs per SM
+constexpr int kEarlyRowsPerStep = 2; // rows the early-exit pass reduces per step (when the cluster splits evenly)
 
 // Barrier over every thread of the cluster; the release / acquire pair makes each CTA's shared-memory writes
 // before it visible to the cluster's reads after it.
@@ -555,25 +557,6 @@ __device__ __forceinline__ float2 ld_cluster_f2(const float2* local, unsigned ra
   float2 v;
   asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(remote) : "memory");
   return v;
-}
-
-// One warp: the (max, sum) of the cluster's C partials (lane c reads CTA c's).  The butterfly combine is
-// symmetric, so every lane, and every CTA of the cluster, gets the same floats.
-__device__ __forceinline__ float2 merge_cluster_partials(const float2* part, unsigned C) {
-  const unsigned lane = threadIdx.x & 31;
-  float m = -INFINITY, s = 0.0f;
-  if (lane < C) {
-    const float2 p = ld_cluster_f2(part, lane);
-    m = p.x;
-    s = p.y;
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
-    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
-    ms_combine(m, s, m2, s2);
-  }
-  return make_float2(m, s);
 }
 
 template <typename T>
@@ -623,38 +606,67 @@ __global__ void __launch_bounds__(kThreads, kEarlyCtasPerSm) stats_early_kernel(
     if (threadIdx.x == 0 && blockIdx.x == 0) report(a, kStatusBadDraft);
     return;                   // every CTA of this cluster leaves here
   }
+  // each step reduces the next K rows at once, P = C / K CTAs (chunks) per row; the decisions then go row by row
+  const int K = a.early_rows, P = (int)gridDim.x / K;
+  const int my_row = (int)blockIdx.x / P, my_chunk = (int)blockIdx.x % P;
   while (true) {
     {
-      const long long t = s_row0 + s_j;
-      const int lo = blockIdx.x * a.chunk;
-      const int hi = min((long long)lo + a.chunk, a.V);
-      float m, s;
-      row_range_ms<T, kThreads>(reinterpret_cast<const T*>(a.x) + t * a.V, lo, hi, s_temp, a.vec_ok, m, s);
-      block_ms<kThreads>(m, s);
+      const int jr = s_j + my_row;
+      float m = -INFINITY, s = 0.0f;    // a row past the request's last contributes nothing
+      if (jr < s_len) {
+        const long long t = s_row0 + jr;
+        const int lo = my_chunk * a.chunk;
+        const int hi = min((long long)lo + a.chunk, a.V);
+        row_range_ms<T, kThreads>(reinterpret_cast<const T*>(a.x) + t * a.V, lo, hi, s_temp, a.vec_ok, m, s);
+        block_ms<kThreads>(m, s);
+      }
       if (threadIdx.x == 0) s_part = make_float2(m, s);
     }
-    cluster_barrier();        // every chunk's partial of the row is visible to the cluster
-    const int j = s_j;
-    const long long t = s_row0 + j;
-    const bool last_row = j == s_len - 1;
+    cluster_barrier();        // every chunk's partial of the step's rows is visible to the cluster
     if (threadIdx.x < 32) {
-      const float2 ms = merge_cluster_partials(&s_part, gridDim.x);
-      if (threadIdx.x == 0) {
-        RowStat rs;
-        rs.m = ms.x; rs.s = ms.y; rs.thr = -INFINITY; rs.pad = 0.0f;
-        int stop = 1;
-        if (!last_row) {   // prob_at's arithmetic on the preloaded logit
-          const float f = s_temp == 1.0f ? s_x[j] : scale_logit(s_x[j], s_temp);
-          stop = (s_u[j] * s_q[j] < prob_of_scaled(f, rs)) ? 0 : 1;   // u < min(1, p/q) without dividing
+      const int lane = threadIdx.x;
+      float pm = -INFINITY, ps = 0.0f;
+      if (lane < (int)gridDim.x) {   // the cluster spans the grid's x dimension: rank = blockIdx.x
+        const float2 p = ld_cluster_f2(&s_part, lane);
+        pm = p.x;
+        ps = p.y;
+      }
+      int decided = -1;
+      RowStat rs_dec;
+      rs_dec.m = 0.0f; rs_dec.s = 1.0f; rs_dec.thr = -INFINITY; rs_dec.pad = 0.0f;
+      for (int r = 0; r < K; ++r) {   // warp-uniform; every lane (and CTA) merges in the same order
+        float m = -INFINITY, s = 0.0f;
+        for (int c = 0; c < P; ++c) {
+          const float m2 = __shfl_sync(0xffffffffu, pm, r * P + c);
+          const float s2 = __shfl_sync(0xffffffffu, ps, r * P + c);
+          ms_combine(m, s, m2, s2);
         }
-        s_flag = stop;
-        s_rs = rs;
-        s_j = j + 1;
+        const int j = s_j + r;
+        if (decided >= 0 || j >= s_len) continue;
+        RowStat rs;
+        rs.m = m; rs.s = s; rs.thr = -INFINITY; rs.pad = 0.0f;
+        bool stop = j == s_len - 1;
+        if (!stop) {   // prob_at's arithmetic on the preloaded logit
+          const float f = s_temp == 1.0f ? s_x[j] : scale_logit(s_x[j], s_temp);
+          stop = !(s_u[j] * s_q[j] < prob_of_scaled(f, rs));   // u < min(1, p/q) without dividing
+        }
+        if (stop) {
+          decided = j;
+          rs_dec = rs;
+        }
+      }
+      if (lane == 0) {
+        s_flag = decided >= 0 ? 1 : 0;
+        s_rs = rs_dec;
+        s_j = decided >= 0 ? decided : s_j + K;
       }
     }
     cluster_barrier();        // the partials are read before any CTA overwrites (or leaves with) its own
     if (s_flag) {
       if (blockIdx.x == 0 && threadIdx.x == 0) {   // n_accept = j: drafts 0..j-1 accepted
+        const int j = s_j;
+        const long long t = s_row0 + j;
+        const bool last_row = j == s_len - 1;
         a.n_accept[b] = j;
         ReqDesc d;
         d.x_row = t;
@@ -1991,11 +2003,16 @@ static int launch_early_stats(Args& a, const DeviceInfo& info, cudaStream_t stre
   const long long cmax = (a.V + 2047) / 2048;
   if (C > cmax) C = cmax;
   if (C > kEarlyMaxCluster) C = kEarlyMaxCluster;
+  // K rows per step when the cluster splits evenly (fewer steps of fixed cost; a decided request wastes at most
+  // K - 1 rows), P = C / K chunks per row
+  const int K = (C % kEarlyRowsPerStep == 0) ? kEarlyRowsPerStep : 1;
+  const long long P = C / K;
   const int ve = a.dtype == kF32 ? 4 : 8;
-  long long chunk = (a.V + C - 1) / C;
+  long long chunk = (a.V + P - 1) / P;
   chunk = (chunk + ve - 1) / ve * ve;
   a.chunk = (int)chunk;
-  a.C = (int)((a.V + chunk - 1) / chunk);
+  a.early_rows = K;
+  a.C = (int)(K * ((a.V + chunk - 1) / chunk));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)a.C, (unsigned)a.B);
   cfg.blockDim = dim3(kThreads);
