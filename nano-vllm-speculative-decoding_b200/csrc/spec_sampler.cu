@@ -109,7 +109,6 @@ struct Args {
   float* probs_out;         // [T, V] for specdec_probs
   // layout
   int C, chunk, vec_ok;
-  int early_rows;           // stats_early_kernel: rows a cluster reduces per step (C / early_rows CTAs per row)
   int u_grid;               // torch grid (blocks of 256) of the [B, k] uniform draw
   int e_grid, e_rounds;     // torch grid and grid-stride rounds of the [B, V] exponential draw
   long long e_numel;
@@ -541,7 +540,6 @@ __global__ void __launch_bounds__(kThreads, kStatsCtasPerSm) stats_kernel(Args a
 constexpr int kEarlyCtasPerSm = 3;   // the walk's decision code beside the streaming loop: up to 85 registers
 constexpr int kEarlyMaxCluster = 8;  // portable cluster size
 constexpr int kNoiseCtasPerSm = 4;   // the noise codes kernel beside the early-exit pass: CTAs per SM
-constexpr int kEarlyRowsPerStep = 2; // rows the early-exit pass reduces per step (when the cluster splits evenly)
 
 // Barrier over every thread of the cluster; the release / acquire pair makes each CTA's shared-memory writes
 // before it visible to the cluster's reads after it.
@@ -559,6 +557,14 @@ __device__ __forceinline__ float2 ld_cluster_f2(const float2* local, unsigned ra
   return v;
 }
 
+// Rows per step after the first: the largest divisor of the cluster size C not above the rows left (at least 1).
+__device__ __forceinline__ int early_rows_per_step(int C, int left) {
+  int k = 1;
+  for (int d = 2; d <= C; ++d)
+    if (C % d == 0 && d <= left) k = d;
+  return k;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads, kEarlyCtasPerSm) stats_early_kernel(Args a) {
   __shared__ int s_start[kMaxRequests + 1];
@@ -566,7 +572,7 @@ __global__ void __launch_bounds__(kThreads, kEarlyCtasPerSm) stats_early_kernel(
   __shared__ RowStat s_rs;
   __shared__ float2 s_part;   // this CTA's (max, sum) of the current row, read by the whole cluster
   // the walk's state lives in shared memory, so that no register holds it across the streaming loop
-  __shared__ int s_j, s_row0, s_len;
+  __shared__ int s_j, s_row0, s_len, s_k;
   __shared__ float s_temp;
   __shared__ float s_u[32], s_q[32], s_x[32];   // per draft: its uniform, q and target logit (loaded up front)
   const int b = blockIdx.y;
@@ -598,6 +604,7 @@ __global__ void __launch_bounds__(kThreads, kEarlyCtasPerSm) stats_early_kernel(
       s_j = 0;
       s_row0 = row0;
       s_len = len;
+      s_k = (gridDim.x % 2 == 0 && len >= 2) ? 2 : 1;
       s_temp = a.temperature[b];
     }
   }
@@ -606,20 +613,25 @@ __global__ void __launch_bounds__(kThreads, kEarlyCtasPerSm) stats_early_kernel(
     if (threadIdx.x == 0 && blockIdx.x == 0) report(a, kStatusBadDraft);
     return;                   // every CTA of this cluster leaves here
   }
-  // each step reduces the next K rows at once, P = C / K CTAs (chunks) per row; the decisions then go row by row
-  const int K = a.early_rows, P = (int)gridDim.x / K;
-  const int my_row = (int)blockIdx.x / P, my_chunk = (int)blockIdx.x % P;
+  // each step reduces the next K rows at once, P = C / K CTAs (chunks) per row; the decisions then go row by row.
+  // K is two at first (most walks end within two rows), then the most rows the cluster can give a CTA each of
+  // (the walks that get that far tend to go on)
   while (true) {
+    const int K = s_k, P = (int)gridDim.x / K;
+    const int my_row = (int)blockIdx.x / P, my_chunk = (int)blockIdx.x % P;
     {
+      constexpr int ve = sizeof(T) == 4 ? 4 : 8;
+      const long long chunk = ((a.V + P - 1) / P + ve - 1) / ve * ve;
       const int jr = s_j + my_row;
-      float m = -INFINITY, s = 0.0f;    // a row past the request's last contributes nothing
-      if (jr < s_len) {
+      float m = -INFINITY, s = 0.0f;    // a row past the request's last, or an empty chunk, contributes nothing
+      const long long lo = my_chunk * chunk;
+      if (jr < s_len && lo < a.V) {
         const long long t = s_row0 + jr;
-        const int lo = my_chunk * a.chunk;
-        const int hi = min((long long)lo + a.chunk, a.V);
-        row_range_ms<T, kThreads>(reinterpret_cast<const T*>(a.x) + t * a.V, lo, hi, s_temp, a.vec_ok, m, s);
-        block_ms<kThreads>(m, s);
+        const long long hi = min(lo + chunk, a.V);
+        row_range_ms<T, kThreads>(reinterpret_cast<const T*>(a.x) + t * a.V, (int)lo, (int)hi, s_temp, a.vec_ok, m,
+                                  s);
       }
+      block_ms<kThreads>(m, s);
       if (threadIdx.x == 0) s_part = make_float2(m, s);
     }
     cluster_barrier();        // every chunk's partial of the step's rows is visible to the cluster
@@ -659,6 +671,7 @@ __global__ void __launch_bounds__(kThreads, kEarlyCtasPerSm) stats_early_kernel(
         s_flag = decided >= 0 ? 1 : 0;
         s_rs = rs_dec;
         s_j = decided >= 0 ? decided : s_j + K;
+        s_k = early_rows_per_step((int)gridDim.x, s_len - s_j);
       }
     }
     cluster_barrier();        // the partials are read before any CTA overwrites (or leaves with) its own
@@ -2003,16 +2016,7 @@ static int launch_early_stats(Args& a, const DeviceInfo& info, cudaStream_t stre
   const long long cmax = (a.V + 2047) / 2048;
   if (C > cmax) C = cmax;
   if (C > kEarlyMaxCluster) C = kEarlyMaxCluster;
-  // K rows per step when the cluster splits evenly (fewer steps of fixed cost; a decided request wastes at most
-  // K - 1 rows), P = C / K chunks per row
-  const int K = (C % kEarlyRowsPerStep == 0) ? kEarlyRowsPerStep : 1;
-  const long long P = C / K;
-  const int ve = a.dtype == kF32 ? 4 : 8;
-  long long chunk = (a.V + P - 1) / P;
-  chunk = (chunk + ve - 1) / ve * ve;
-  a.chunk = (int)chunk;
-  a.early_rows = K;
-  a.C = (int)(K * ((a.V + chunk - 1) / chunk));
+  a.C = (int)C;   // the kernel picks each step's rows and chunks
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)a.C, (unsigned)a.B);
   cfg.blockDim = dim3(kThreads);
