@@ -193,6 +193,8 @@ def oracle_accept(logits, q, drafts, lens, temps, u, noise):
     (64, 7, 151936, True),    # drafts the target likes: long walks of the early-exit pass
     (64, 7, 151936, False),
     (5, 4, 1001, True),       # ragged vocabulary, few requests: many chunks per row
+    (300, 3, 4096, True),     # one CTA per request (clusters of 1)
+    (148, 5, 8192, True),     # clusters of 3: one row in the first step, then three
 ])
 def test_accept_passes_match_the_oracle(batch, k, V, accepting):
     """specdec_accept's pass 1 in both forms against the oracle: the early-exit walk (each request's rows only up
