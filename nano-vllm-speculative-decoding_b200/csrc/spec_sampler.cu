@@ -11,18 +11,23 @@
 //                                                  bonus position; verified = j < len - 1
 //
 // Design (B200): the path is HBM-bound integer/float streaming, so it never touches the tensor cores.
-//   pass 1  (stats)  grid (chunks x rows): every verified row of logits is read once with 16-byte loads and
-//                    reduced to a softmax (max, sum) partial per chunk.  Rows that truncate (top_k > 0) are
-//                    handled by one 512-thread CTA per row that radix-selects the k-th value over L2-resident
-//                    re-reads.  The last CTA to finish a request (an atomic ticket per request) merges the
-//                    partials, computes p and q at the k drafts, draws or reads the uniforms, and decides the
-//                    accepted prefix - so acceptance costs no extra launch.
-//   pass 2  (tail)   grid = torch's own grid for exponential_ over [B, V]: thread i regenerates exactly the
-//                    Exp(1) numbers torch's CUDA generator would have written (Philox4x32-10 subsequence i,
-//                    curand_uniform4, torch's log transform, clamp at 1e-10), so the [B, V] noise is never
-//                    materialised in HBM.  Each element computes w = p (bonus) or (p - q)+, the ratio w / E in
-//                    IEEE fp32, and an argmax key; warps reduce per request into shared memory, CTAs into one
-//                    64-bit atomicMax per request, and the last CTA writes the tail tokens.
+//   pass 1  (stats)  early exit (stats_early_kernel, whenever the requests fit one wave): one thread-block
+//                    cluster per request walks its verified rows in order, a chunk per CTA, meets each row's
+//                    partial (max, sum) pairs in distributed shared memory and takes the accept test there, and
+//                    stops at the first rejected draft - the later rows are never read.  Otherwise grid
+//                    (chunks x rows): every verified row is read once with 16-byte loads and reduced to a
+//                    partial per chunk; the last CTA of a request (an atomic ticket) merges the partials and
+//                    decides the accepted prefix.  Rows that truncate (top_k > 0) are handled by one 512-thread
+//                    CTA per row that radix-selects the k-th value over L2-resident re-reads.
+//   pass 2  (tail)   the race over the request's tail row (bonus p or residual (p - q)+) against torch's
+//                    exact Exp(1) draws, regenerated in-kernel (Philox4x32-10 at torch's counters and grid,
+//                    torch's __logf transform, clamp at 1e-10), so the [B, V] noise is never read from HBM as
+//                    floats: with room in the workspace the draws are first kept as 16-bit codes that bound each
+//                    one (noise_codes_kernel, beside the early-exit pass) and the race streams the rows and codes,
+//                    drawing exactly only the elements that can still win (tail_codes_kernel); without it every
+//                    element is drawn in place (tail_accept_kernel).  The ratio w / E, an argmax key per request
+//                    (first index on ties), one 64-bit atomicMax per request and warp run; the last CTA writes the
+//                    tail tokens.
 // Explicit u / E pointers replace the in-kernel draws (parity mode) without changing anything else.
 #include "common.cuh"
 
